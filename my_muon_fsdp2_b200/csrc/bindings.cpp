@@ -1,0 +1,460 @@
+// PyTorch bindings: adapts torch tensors to the plain launch API in kernels.h.
+// Every function checks devices, dtypes and contiguity and enqueues on the current stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cstring>
+#include <vector>
+
+#include "kernels.h"
+
+namespace {
+
+using torch::Tensor;
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "mmf: ", name, " must be a CUDA tensor");
+}
+void check_bf16_contig(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == torch::kBFloat16, "mmf: ", name, " must be bfloat16");
+  TORCH_CHECK(t.is_contiguous(), "mmf: ", name, " must be contiguous");
+}
+const float* opt_f32_ptr(const c10::optional<Tensor>& t, const char* name) {
+  if (!t.has_value()) return nullptr;
+  check_cuda(*t, name);
+  TORCH_CHECK(t->scalar_type() == torch::kFloat32 && t->is_contiguous(), "mmf: ", name, " must be contiguous fp32");
+  return t->data_ptr<float>();
+}
+
+// Copy a vector of POD descriptors to the device through a pinned staging tensor.
+template <typename T>
+Tensor upload(const std::vector<T>& v, const torch::Device& dev) {
+  const int64_t bytes = static_cast<int64_t>(v.size() * sizeof(T));
+  Tensor host = torch::empty({bytes}, torch::dtype(torch::kUInt8).pinned_memory(true));
+  std::memcpy(host.data_ptr(), v.data(), bytes);
+  return host.to(dev, /*non_blocking=*/true);
+}
+
+Tensor ptr_table(const std::vector<Tensor>& ts) {
+  TORCH_CHECK(!ts.empty(), "mmf: empty pointer table");
+  std::vector<int64_t> ptrs;
+  ptrs.reserve(ts.size());
+  for (const auto& t : ts) {
+    check_cuda(t, "tensor");
+    ptrs.push_back(reinterpret_cast<int64_t>(t.data_ptr()));
+  }
+  Tensor host = torch::empty({static_cast<int64_t>(ptrs.size())}, torch::dtype(torch::kInt64).pinned_memory(true));
+  std::memcpy(host.data_ptr(), ptrs.data(), ptrs.size() * sizeof(int64_t));
+  return host.to(ts[0].device(), true);
+}
+
+void gemm_dims(const Tensor& A, const Tensor& B, bool b_mn, int& batch, int& M, int& N, int& K) {
+  TORCH_CHECK(A.dim() == 3 && B.dim() == 3, "mmf: GEMM operands must be [batch, rows, cols]");
+  batch = static_cast<int>(A.size(0));
+  M = static_cast<int>(A.size(1));
+  K = static_cast<int>(A.size(2));
+  TORCH_CHECK(B.size(0) == batch, "mmf: batch mismatch");
+  if (b_mn) {
+    TORCH_CHECK(B.size(1) == K, "mmf: K mismatch (B is [batch, K, N])");
+    N = static_cast<int>(B.size(2));
+  } else {
+    TORCH_CHECK(B.size(2) == K, "mmf: K mismatch (B is [batch, N, K])");
+    N = static_cast<int>(B.size(1));
+  }
+}
+
+void tc_gemm_ws(Tensor A, Tensor B, bool b_mn_major, Tensor D, c10::optional<Tensor> C,
+                c10::optional<Tensor> alpha_vec, double alpha, c10::optional<Tensor> beta_vec, double beta,
+                bool symmetric) {
+  check_bf16_contig(A, "A");
+  check_bf16_contig(B, "B");
+  check_bf16_contig(D, "D");
+  const c10::cuda::CUDAGuard guard(A.device());
+  mmf::GemmWsArgs a{};
+  gemm_dims(A, B, b_mn_major, a.batch, a.M, a.N, a.K);
+  TORCH_CHECK(D.dim() == 3 && D.size(0) == a.batch && D.size(1) == a.M && D.size(2) == a.N, "mmf: D shape mismatch");
+  if (C.has_value()) {
+    check_bf16_contig(*C, "C");
+    TORCH_CHECK(C->sizes() == D.sizes(), "mmf: C shape mismatch");
+    TORCH_CHECK(C->data_ptr() != D.data_ptr(), "mmf: C must not alias D");
+  }
+  a.A = A.data_ptr();
+  a.B = B.data_ptr();
+  a.b_mn_major = b_mn_major;
+  a.D = D.data_ptr();
+  a.C = C.has_value() ? C->data_ptr() : nullptr;
+  a.alpha_vec = opt_f32_ptr(alpha_vec, "alpha_vec");
+  a.alpha = static_cast<float>(alpha);
+  a.beta_vec = opt_f32_ptr(beta_vec, "beta_vec");
+  a.beta = static_cast<float>(beta);
+  a.symmetric = symmetric;
+  mmf::tc_gemm_ws(a, cur_stream());
+}
+
+void tc_gemm_out(Tensor A, Tensor B, bool b_mn_major, c10::optional<Tensor> C, c10::optional<Tensor> alpha_vec,
+                 double alpha, c10::optional<Tensor> beta_vec, double beta, Tensor out_ptrs, int64_t nseg,
+                 c10::optional<Tensor> out_meta, int64_t out_ld,
+                 bool out_f32, bool out_transposed, int64_t m_true, int64_t n_true, c10::optional<Tensor> p_scale_vec,
+                 double p_scale, c10::optional<Tensor> v_scale_vec, double v_scale) {
+  check_bf16_contig(A, "A");
+  check_bf16_contig(B, "B");
+  const c10::cuda::CUDAGuard guard(A.device());
+  mmf::GemmOutArgs a{};
+  gemm_dims(A, B, b_mn_major, a.batch, a.M, a.N, a.K);
+  if (C.has_value()) {
+    check_bf16_contig(*C, "C");
+    TORCH_CHECK(C->dim() == 3 && C->size(0) == a.batch && C->size(1) == a.M && C->size(2) == a.N,
+                "mmf: C shape mismatch");
+  }
+  check_cuda(out_ptrs, "out_ptrs");
+  TORCH_CHECK(nseg >= 1, "mmf: nseg must be >= 1");
+  TORCH_CHECK(out_ptrs.scalar_type() == torch::kInt64 && out_ptrs.numel() == a.batch * nseg,
+              "mmf: out_ptrs must be int64[batch * nseg]");
+  if (out_meta.has_value())
+    TORCH_CHECK(out_meta->is_cuda() && out_meta->scalar_type() == torch::kInt64 && out_meta->numel() == 3 * a.batch,
+                "mmf: out_meta must be a CUDA int64[batch * 3]");
+  a.A = A.data_ptr();
+  a.B = B.data_ptr();
+  a.b_mn_major = b_mn_major;
+  a.C = C.has_value() ? C->data_ptr() : nullptr;
+  a.alpha_vec = opt_f32_ptr(alpha_vec, "alpha_vec");
+  a.alpha = static_cast<float>(alpha);
+  a.beta_vec = opt_f32_ptr(beta_vec, "beta_vec");
+  a.beta = static_cast<float>(beta);
+  a.out_ptrs = out_ptrs.data_ptr<int64_t>();
+  a.nseg = static_cast<int>(nseg);
+  a.out_meta = out_meta.has_value() ? out_meta->data_ptr<int64_t>() : nullptr;
+  a.out_ld = out_ld;
+  a.out_f32 = out_f32;
+  a.out_transposed = out_transposed;
+  a.m_true = static_cast<int>(m_true);
+  a.n_true = static_cast<int>(n_true);
+  a.p_scale_vec = opt_f32_ptr(p_scale_vec, "p_scale_vec");
+  a.p_scale = static_cast<float>(p_scale);
+  a.v_scale_vec = opt_f32_ptr(v_scale_vec, "v_scale_vec");
+  a.v_scale = static_cast<float>(v_scale);
+  mmf::tc_gemm_out(a, cur_stream());
+}
+
+// grads/bufs/params: per-matrix tensors (bufs/params may be empty lists).  dst: optional bf16
+// workspace; per-matrix destination = dst_base_offsets[i] elements into dst.
+void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<Tensor> params,
+               c10::optional<Tensor> dst, std::vector<int64_t> dst_offsets, std::vector<int64_t> dst_row0,
+               std::vector<int64_t> transposed, int64_t dst_ld, std::vector<double> p_scale,
+               std::vector<double> v_scale, int64_t mode, bool nesterov, double mu, double wd_coupled,
+               c10::optional<Tensor> sumsq) {
+  const int n = static_cast<int>(grads.size());
+  if (n == 0) return;
+  const auto dev = grads[0].device();
+  const c10::cuda::CUDAGuard guard(dev);
+  TORCH_CHECK(bufs.empty() || (int)bufs.size() == n, "mmf: bufs size");
+  TORCH_CHECK(params.empty() || (int)params.size() == n, "mmf: params size");
+  const bool grad_f32 = grads[0].scalar_type() == torch::kFloat32;
+  const bool param_f32 = !params.empty() && params[0].scalar_type() == torch::kFloat32;
+  std::vector<mmf::PrepDesc> d(n);
+  int max_tiles = 1;
+  for (int i = 0; i < n; ++i) {
+    const Tensor& g = grads[i];
+    check_cuda(g, "grad");
+    TORCH_CHECK(g.is_contiguous() && g.dim() == 2, "mmf: grads must be contiguous 2-D");
+    TORCH_CHECK((g.scalar_type() == torch::kFloat32) == grad_f32 &&
+                    (g.scalar_type() == torch::kFloat32 || g.scalar_type() == torch::kBFloat16),
+                "mmf: grads must all be fp32 or all bf16");
+    d[i].grad = reinterpret_cast<int64_t>(g.data_ptr());
+    d[i].rows = static_cast<int32_t>(g.size(0));
+    d[i].cols = static_cast<int32_t>(g.size(1));
+    if (!bufs.empty()) {
+      TORCH_CHECK(bufs[i].scalar_type() == torch::kFloat32 && bufs[i].is_contiguous() && bufs[i].numel() == g.numel(),
+                  "mmf: momentum buffers must be contiguous fp32 of the grad's size");
+      d[i].buf = reinterpret_cast<int64_t>(bufs[i].data_ptr());
+    }
+    if (!params.empty()) {
+      TORCH_CHECK(params[i].is_contiguous() && params[i].numel() == g.numel() &&
+                      (params[i].scalar_type() == torch::kFloat32) == param_f32,
+                  "mmf: params must be contiguous, same size, same dtype");
+      d[i].param = reinterpret_cast<int64_t>(params[i].data_ptr());
+    }
+    if (dst.has_value()) {
+      d[i].dst = reinterpret_cast<int64_t>(dst->data_ptr()) + dst_offsets[i] * 2;
+      d[i].dst_row0 = static_cast<int32_t>(dst_row0[i]);
+      d[i].transposed = static_cast<int32_t>(transposed[i]);
+      d[i].dst_ld = dst_ld;
+    } else {
+      TORCH_CHECK(!params.empty(), "mmf: direct apply needs params");
+      d[i].p_scale = static_cast<float>(p_scale[i]);
+      d[i].v_scale = static_cast<float>(v_scale[i]);
+    }
+    const int tiles = ((d[i].rows + 63) / 64) * ((d[i].cols + 63) / 64);
+    if (tiles > max_tiles) max_tiles = tiles;
+  }
+  if (mode != 0) TORCH_CHECK(!bufs.empty(), "mmf: momentum modes need buffers");
+  if (dst.has_value()) check_bf16_contig(*dst, "dst");
+  Tensor dd = upload(d, dev);
+  mmf::PrepArgs a{};
+  a.descs = reinterpret_cast<const mmf::PrepDesc*>(dd.data_ptr());
+  a.n = n;
+  a.max_tiles = max_tiles;
+  a.grad_f32 = grad_f32;
+  a.param_f32 = param_f32;
+  a.mode = static_cast<int>(mode);
+  a.nesterov = nesterov ? 1 : 0;
+  a.mu = static_cast<float>(mu);
+  a.wd_coupled = static_cast<float>(wd_coupled);
+  a.sumsq = sumsq.has_value() ? sumsq->data_ptr<float>() : nullptr;
+  mmf::muon_prep(a, cur_stream());
+}
+
+void ns_scale(Tensor sumsq, int64_t n, int64_t nparts, double eps, Tensor s, c10::optional<Tensor> s2) {
+  check_cuda(sumsq, "sumsq");
+  const c10::cuda::CUDAGuard guard(sumsq.device());
+  mmf::ns_scale(sumsq.data_ptr<float>(), static_cast<int>(n), static_cast<int>(nparts), static_cast<float>(eps),
+                s.data_ptr<float>(), s2.has_value() ? s2->data_ptr<float>() : nullptr, cur_stream());
+}
+
+void ws_to_out(Tensor X, c10::optional<Tensor> s_vec, Tensor out_ptrs, int64_t nseg, c10::optional<Tensor> out_meta,
+               int64_t out_ld, bool out_f32,
+               bool out_transposed, int64_t m_true, int64_t n_true, c10::optional<Tensor> p_scale_vec, double p_scale,
+               c10::optional<Tensor> v_scale_vec, double v_scale) {
+  check_bf16_contig(X, "X");
+  const c10::cuda::CUDAGuard guard(X.device());
+  mmf::WsOutArgs a{};
+  a.X = X.data_ptr();
+  a.batch = static_cast<int>(X.size(0));
+  a.Mp = static_cast<int>(X.size(1));
+  a.Np = static_cast<int>(X.size(2));
+  a.s_vec = opt_f32_ptr(s_vec, "s_vec");
+  TORCH_CHECK(nseg >= 1 && out_ptrs.numel() == a.batch * nseg, "mmf: out_ptrs must be int64[batch * nseg]");
+  a.out_ptrs = out_ptrs.data_ptr<int64_t>();
+  a.nseg = static_cast<int>(nseg);
+  a.out_meta = out_meta.has_value() ? out_meta->data_ptr<int64_t>() : nullptr;
+  a.out_ld = out_ld;
+  a.out_f32 = out_f32;
+  a.out_transposed = out_transposed;
+  a.m_true = static_cast<int>(m_true);
+  a.n_true = static_cast<int>(n_true);
+  a.p_scale_vec = opt_f32_ptr(p_scale_vec, "p_scale_vec");
+  a.p_scale = static_cast<float>(p_scale);
+  a.v_scale_vec = opt_f32_ptr(v_scale_vec, "v_scale_vec");
+  a.v_scale = static_cast<float>(v_scale);
+  mmf::ws_to_out(a, cur_stream());
+}
+
+void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> exp_avgs,
+           std::vector<Tensor> exp_avg_sqs, double lr, double beta1, double beta2, double eps, double weight_decay,
+           double bias_correction1, double bias_correction2_sqrt) {
+  const int n = static_cast<int>(params.size());
+  if (n == 0) return;
+  const auto dev = params[0].device();
+  const c10::cuda::CUDAGuard guard(dev);
+  TORCH_CHECK((int)grads.size() == n && (int)exp_avgs.size() == n && (int)exp_avg_sqs.size() == n,
+              "mmf: adamw list sizes differ");
+  const bool p32 = params[0].scalar_type() == torch::kFloat32;
+  const bool g32 = grads[0].scalar_type() == torch::kFloat32;
+  std::vector<mmf::AdamDesc> d(n);
+  int64_t max_numel = 1;
+  for (int i = 0; i < n; ++i) {
+    TORCH_CHECK(params[i].is_cuda() && params[i].is_contiguous() && grads[i].is_contiguous() &&
+                    exp_avgs[i].is_contiguous() && exp_avg_sqs[i].is_contiguous(),
+                "mmf: adamw tensors must be contiguous CUDA tensors");
+    TORCH_CHECK((params[i].scalar_type() == torch::kFloat32) == p32 && (grads[i].scalar_type() == torch::kFloat32) == g32,
+                "mmf: adamw dtypes must be uniform within a launch");
+    TORCH_CHECK(exp_avgs[i].scalar_type() == torch::kFloat32 && exp_avg_sqs[i].scalar_type() == torch::kFloat32,
+                "mmf: adamw moments must be fp32");
+    TORCH_CHECK(grads[i].numel() == params[i].numel(), "mmf: adamw grad size");
+    d[i].param = reinterpret_cast<int64_t>(params[i].data_ptr());
+    d[i].grad = reinterpret_cast<int64_t>(grads[i].data_ptr());
+    d[i].exp_avg = reinterpret_cast<int64_t>(exp_avgs[i].data_ptr());
+    d[i].exp_avg_sq = reinterpret_cast<int64_t>(exp_avg_sqs[i].data_ptr());
+    d[i].numel = params[i].numel();
+    if (d[i].numel > max_numel) max_numel = d[i].numel;
+  }
+  Tensor dd = upload(d, dev);
+  mmf::AdamArgs a{};
+  a.descs = reinterpret_cast<const mmf::AdamDesc*>(dd.data_ptr());
+  a.n = n;
+  a.max_numel = max_numel;
+  a.param_f32 = p32;
+  a.grad_f32 = g32;
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.eps = static_cast<float>(eps);
+  a.weight_decay = static_cast<float>(weight_decay);
+  a.bias_correction1 = static_cast<float>(bias_correction1);
+  a.bias_correction2_sqrt = static_cast<float>(bias_correction2_sqrt);
+  mmf::adamw_multi(a, cur_stream());
+}
+
+// --------------------------------- model ops --------------------------------------------
+std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
+  check_bf16_contig(x, "x");
+  check_bf16_contig(w, "w");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int cols = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / cols);
+  TORCH_CHECK(w.numel() == cols, "mmf: rmsnorm weight size");
+  Tensor y = torch::empty_like(x);
+  Tensor rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  mmf::rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), rows, cols,
+                   static_cast<float>(eps), cur_stream());
+  return {y, rstd};
+}
+
+std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
+  check_bf16_contig(dy, "dy");
+  check_bf16_contig(x, "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int cols = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / cols);
+  const int prow = std::max(1, std::min(rows, 296));
+  Tensor dx = torch::empty_like(x);
+  Tensor part = torch::empty({prow, cols}, x.options().dtype(torch::kFloat32));
+  Tensor dw = torch::empty({cols}, w.options());
+  mmf::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dx.data_ptr(),
+                   part.data_ptr<float>(), rows, cols, prow, cur_stream());
+  mmf::colsum_partials(part.data_ptr<float>(), prow, cols, dw.data_ptr(), w.scalar_type() == torch::kFloat32,
+                       cur_stream());
+  return {dx, dw};
+}
+
+std::vector<Tensor> layernorm_fwd(Tensor x, Tensor w, c10::optional<Tensor> b, double eps) {
+  check_bf16_contig(x, "x");
+  check_bf16_contig(w, "w");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int cols = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / cols);
+  Tensor y = torch::empty_like(x);
+  Tensor mean = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  Tensor rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  mmf::layernorm_fwd(x.data_ptr(), w.data_ptr(), b.has_value() ? b->data_ptr() : nullptr, y.data_ptr(),
+                     mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, cols, static_cast<float>(eps), cur_stream());
+  return {y, mean, rstd};
+}
+
+std::vector<Tensor> layernorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor mean, Tensor rstd, bool has_bias) {
+  check_bf16_contig(dy, "dy");
+  check_bf16_contig(x, "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int cols = static_cast<int>(x.size(-1));
+  const int rows = static_cast<int>(x.numel() / cols);
+  const int prow = std::max(1, std::min(rows, 296));
+  Tensor dx = torch::empty_like(x);
+  Tensor pw = torch::empty({prow, cols}, x.options().dtype(torch::kFloat32));
+  Tensor pb = torch::empty({prow, cols}, x.options().dtype(torch::kFloat32));
+  mmf::layernorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr(), mean.data_ptr<float>(), rstd.data_ptr<float>(),
+                     dx.data_ptr(), pw.data_ptr<float>(), pb.data_ptr<float>(), rows, cols, prow, cur_stream());
+  Tensor dw = torch::empty({cols}, w.options());
+  mmf::colsum_partials(pw.data_ptr<float>(), prow, cols, dw.data_ptr(), w.scalar_type() == torch::kFloat32,
+                       cur_stream());
+  Tensor db;
+  if (has_bias) {
+    db = torch::empty({cols}, w.options());
+    mmf::colsum_partials(pb.data_ptr<float>(), prow, cols, db.data_ptr(), w.scalar_type() == torch::kFloat32,
+                         cur_stream());
+  }
+  return {dx, dw, db};
+}
+
+// x viewed as [tokens, heads, head_dim] with arbitrary token/head strides (elements).
+void rope_(Tensor x, int64_t tokens, int64_t heads, int64_t head_dim, int64_t seq_len, double theta, bool inverse,
+           int64_t token_stride, int64_t head_stride) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16, "mmf: rope input must be bf16");
+  const c10::cuda::CUDAGuard guard(x.device());
+  mmf::rope_inplace(x.data_ptr(), static_cast<int>(tokens), static_cast<int>(heads), static_cast<int>(head_dim),
+                    static_cast<int>(seq_len), static_cast<float>(theta), inverse, token_stride, head_stride,
+                    cur_stream());
+}
+
+Tensor swiglu_fwd(Tensor g, Tensor u) {
+  check_bf16_contig(g, "gate");
+  check_bf16_contig(u, "up");
+  const c10::cuda::CUDAGuard guard(g.device());
+  Tensor o = torch::empty_like(g);
+  mmf::swiglu_fwd(g.data_ptr(), u.data_ptr(), o.data_ptr(), g.numel(), cur_stream());
+  return o;
+}
+std::vector<Tensor> swiglu_bwd(Tensor d, Tensor g, Tensor u) {
+  check_bf16_contig(d, "dout");
+  const c10::cuda::CUDAGuard guard(g.device());
+  Tensor dg = torch::empty_like(g), du = torch::empty_like(u);
+  mmf::swiglu_bwd(d.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(), g.numel(), cur_stream());
+  return {dg, du};
+}
+Tensor gelu_fwd(Tensor x) {
+  check_bf16_contig(x, "x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor y = torch::empty_like(x);
+  mmf::gelu_fwd(x.data_ptr(), y.data_ptr(), x.numel(), cur_stream());
+  return y;
+}
+Tensor gelu_bwd(Tensor dy, Tensor x) {
+  check_bf16_contig(dy, "dy");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Tensor dx = torch::empty_like(x);
+  mmf::gelu_bwd(dy.data_ptr(), x.data_ptr(), dx.data_ptr(), x.numel(), cur_stream());
+  return dx;
+}
+
+// logits [rows, >=vocab] bf16 (row stride ld), targets int64 [rows]. Returns per-row loss.
+Tensor cross_entropy_(Tensor logits, Tensor targets, int64_t vocab, double grad_scale, int64_t ignore_index) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == torch::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
+              "mmf: logits must be bf16 [rows, vocab] with unit column stride");
+  TORCH_CHECK(targets.scalar_type() == torch::kInt64 && targets.is_contiguous(), "mmf: targets must be int64");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int rows = static_cast<int>(logits.size(0));
+  Tensor loss = torch::empty({rows}, logits.options().dtype(torch::kFloat32));
+  mmf::cross_entropy_fwd_bwd(logits.data_ptr(), targets.data_ptr<int64_t>(), loss.data_ptr<float>(), rows,
+                             static_cast<int>(vocab), logits.stride(0), static_cast<float>(grad_scale),
+                             static_cast<int>(ignore_index), cur_stream());
+  return loss;
+}
+
+void power_iteration(Tensor W, Tensor u, Tensor v, Tensor sigma, int64_t iters, double eps, Tensor work) {
+  check_cuda(W, "W");
+  TORCH_CHECK(W.dim() == 2 && W.is_contiguous(), "mmf: W must be contiguous 2-D");
+  TORCH_CHECK(W.scalar_type() == torch::kFloat32 || W.scalar_type() == torch::kBFloat16, "mmf: W dtype");
+  const c10::cuda::CUDAGuard guard(W.device());
+  TORCH_CHECK(work.numel() >= std::max(W.size(0), W.size(1)) + 1, "mmf: work too small");
+  mmf::power_iteration(W.data_ptr(), W.scalar_type() == torch::kFloat32, static_cast<int>(W.size(0)),
+                       static_cast<int>(W.size(1)), u.data_ptr<float>(), v.data_ptr<float>(), sigma.data_ptr<float>(),
+                       static_cast<int>(iters), static_cast<float>(eps), work.data_ptr<float>(), cur_stream());
+}
+
+int64_t device_error(int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  return mmf::read_and_clear_device_error(static_cast<int>(device), cur_stream());
+}
+
+int64_t launch_count() { return static_cast<int64_t>(mmf::launch_count()); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of my_muon_fsdp2_b200";
+  m.def("ptr_table", &ptr_table);
+  m.def("tc_gemm_ws", &tc_gemm_ws);
+  m.def("tc_gemm_out", &tc_gemm_out);
+  m.def("muon_prep", &muon_prep);
+  m.def("ns_scale", &ns_scale);
+  m.def("ws_to_out", &ws_to_out);
+  m.def("adamw", &adamw);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("rope_", &rope_);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("gelu_fwd", &gelu_fwd);
+  m.def("gelu_bwd", &gelu_bwd);
+  m.def("cross_entropy_", &cross_entropy_);
+  m.def("power_iteration", &power_iteration);
+  m.def("device_error", &device_error);
+  m.def("launch_count", &launch_count);
+}

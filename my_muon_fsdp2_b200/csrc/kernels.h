@@ -1,0 +1,183 @@
+// Host-side launch API of the native kernels.  Only plain C++/CUDA types cross this boundary,
+// so the .cu translation units compile without the PyTorch headers; bindings.cpp adapts
+// torch tensors to these calls.  Every launcher enqueues on the given stream and returns
+// immediately; argument errors are thrown as std::runtime_error.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mmf {
+
+// ----------------------------------------------------------------------------------------
+// Device error word shared by all kernels (bounded waits record their timeout code here).
+int* device_error_word(int device);
+int read_and_clear_device_error(int device, cudaStream_t stream);
+
+// Number of kernel launches issued by this library since process start (host counter).
+uint64_t launch_count();
+void count_launch();
+
+// ----------------------------------------------------------------------------------------
+// tcgen05 GEMM:   V[b] = alpha_b * (A[b] @ Bop[b]) + beta_b * C[b]
+//   A    : [batch, M, K] bf16 row-major (K contiguous)
+//   Bop  : b_mn_major == false -> [batch, N, K] bf16 row-major (product uses Bop^T)
+//          b_mn_major == true  -> [batch, K, N] bf16 row-major (product uses Bop as is)
+//   C    : optional [batch, M, N] bf16 (may alias A when symmetric)
+//   alpha_b = alpha * (alpha_vec ? alpha_vec[b] : 1), beta_b likewise.
+// Requirements (checked): M % 128 == 0, N % 256 == 0, K % 64 == 0, 16-byte aligned bases.
+//
+// Epilogue "workspace" mode: D[b] = bf16(V[b]).  With symmetric == true (M == N and the
+// product is symmetric, e.g. X X^T or A A for symmetric A) only tiles touching the upper
+// triangle are computed and each upper element is also written to its mirror position.
+struct GemmWsArgs {
+  const void* A;
+  const void* B;
+  bool b_mn_major;
+  void* D;
+  const void* C;
+  int batch, M, N, K;
+  const float* alpha_vec;
+  float alpha;
+  const float* beta_vec;
+  float beta;
+  bool symmetric;
+};
+void tc_gemm_ws(const GemmWsArgs& args, cudaStream_t stream);
+
+// Epilogue "output" mode: for every element (i, j) with i < m_true, j < n_true, with
+// (r, c) = transposed_b ? (j, i) : (i, j) the element's position in the destination matrix,
+//   seg = r / seg_rows_b,  T = out_ptrs[b * nseg + seg],  idx = (r - seg * seg_rows_b) * ld_b + c
+//   T[idx] = p_scale_b * T[idx] + v_scale_b * V[b][i][j]      (old value not read if p_scale_b == 0)
+// Row segments let one launch scatter each rank's row shard into a different buffer (a local
+// all-to-all staging segment or a peer's receive buffer).  Per-batch (ld, transposed,
+// seg_rows) come from out_meta[3*b .. 3*b+2] when out_meta is non-null, else from the scalars.
+struct GemmOutArgs {
+  const void* A;
+  const void* B;
+  bool b_mn_major;
+  const void* C;
+  int batch, M, N, K;
+  const float* alpha_vec;
+  float alpha;
+  const float* beta_vec;
+  float beta;
+  const int64_t* out_ptrs;  // device array [batch * nseg]
+  int nseg;
+  const int64_t* out_meta;  // device array [batch * 3] or null
+  int64_t out_ld;
+  bool out_f32;
+  bool out_transposed;
+  int m_true, n_true;
+  const float* p_scale_vec;  // device [batch] or null (-> p_scale)
+  float p_scale;
+  const float* v_scale_vec;  // device [batch] or null (-> v_scale)
+  float v_scale;
+};
+void tc_gemm_out(const GemmOutArgs& args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------------
+// Muon pre-NS multi-tensor kernel.  For matrix b (a row block of rows_b x cols_b elements):
+//   mode 0 (copy):      u = g
+//   mode 1 (ema):       buf = mu*buf + (1-mu)*g'            (lerp form)
+//   mode 2 (heavy-ball):buf = mu*buf + g'
+//   g' = g + wd_coupled * p  (only if wd_coupled != 0)
+//   u = nesterov ? g' + mu*buf : buf   (modes 1, 2)
+// then u is written as bf16 into dst_b at [dst_row0 + r][c] (or transposed [c][dst_row0 + r])
+// with leading dimension dst_ld, and sum(u^2) is accumulated into sumsq[b] (fp32 atomics).
+// If dst_b == 0 the update is applied directly: p = p_scale*p + v_scale*u (1-D params).
+struct PrepDesc {
+  int64_t grad;      // device pointer
+  int64_t buf;       // fp32 momentum (0 in copy mode)
+  int64_t param;     // param pointer (for coupled wd / direct apply), may be 0
+  int64_t dst;       // bf16 destination base (0 -> direct apply)
+  int32_t rows, cols;
+  int32_t dst_row0;
+  int32_t transposed;
+  int64_t dst_ld;
+  float p_scale, v_scale;  // direct-apply coefficients
+};
+struct PrepArgs {
+  const PrepDesc* descs;  // device array [n]
+  int n;
+  int max_tiles;          // max over b of ceil(rows/64)*ceil(cols/64)
+  int grad_f32;           // grad dtype: 0 bf16, 1 f32
+  int param_f32;          // param dtype: 0 bf16, 1 f32
+  int mode;
+  int nesterov;
+  float mu;
+  float wd_coupled;
+  float* sumsq;           // device [n] (may be null)
+};
+void muon_prep(const PrepArgs& args, cudaStream_t stream);
+
+// s[b] = 1 / (sqrt(sumsq[b]) + eps), s2[b] = s[b]^2 ; optionally sums `nparts` partials per
+// matrix laid out as sumsq[p * n + b].
+void ns_scale(const float* sumsq, int n, int nparts, float eps, float* s, float* s2, cudaStream_t stream);
+
+// Elementwise copy of an (unscaled) bf16 workspace matrix to output pointers, applying
+// T = p_scale*T + v_scale*s[b]*X (used when steps == 0 and for received NS results).
+struct WsOutArgs {
+  const void* X;  // [batch, Mp, Np] bf16 workspace
+  int batch, Mp, Np;
+  const float* s_vec;  // may be null
+  const int64_t* out_ptrs;  // [batch * nseg]
+  int nseg;
+  const int64_t* out_meta;  // [batch * 3] (ld, transposed, seg_rows) or null
+  int64_t out_ld;
+  bool out_f32, out_transposed;
+  int m_true, n_true;
+  const float* p_scale_vec;
+  float p_scale;
+  const float* v_scale_vec;
+  float v_scale;
+};
+void ws_to_out(const WsOutArgs& args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------------
+// Multi-tensor AdamW (decoupled weight decay), fp32 moments, bf16 or fp32 params/grads.
+struct AdamDesc {
+  int64_t param, grad, exp_avg, exp_avg_sq;
+  int64_t numel;
+};
+struct AdamArgs {
+  const AdamDesc* descs;
+  int n;
+  int64_t max_numel;
+  int param_f32, grad_f32;
+  float lr, beta1, beta2, eps, weight_decay;
+  float bias_correction1, bias_correction2_sqrt;  // host-computed
+};
+void adamw_multi(const AdamArgs& args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------------
+// Model kernels (bf16 activations, fp32 statistics).
+void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int cols, float eps,
+                 cudaStream_t stream);
+void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw_partial,
+                 int rows, int cols, int partial_rows, cudaStream_t stream);
+void layernorm_fwd(const void* x, const void* w, const void* b, void* y, float* mean, float* rstd, int rows,
+                   int cols, float eps, cudaStream_t stream);
+void layernorm_bwd(const void* dy, const void* x, const void* w, const float* mean, const float* rstd, void* dx,
+                   float* dw_partial, float* db_partial, int rows, int cols, int partial_rows,
+                   cudaStream_t stream);
+void colsum_partials(const float* partial, int prow, int cols, void* out, bool out_f32, cudaStream_t stream);
+// RoPE on x [tokens, heads, head_dim] (bf16, in place), positions = token % seq_len.
+void rope_inplace(void* x, int tokens, int heads, int head_dim, int seq_len, float theta, bool inverse,
+                  int64_t token_stride, int64_t head_stride, cudaStream_t stream);
+void swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, cudaStream_t stream);
+void swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate, void* dup, int64_t n,
+                cudaStream_t stream);
+void gelu_fwd(const void* x, void* y, int64_t n, cudaStream_t stream);
+void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t stream);
+// Softmax cross entropy over bf16 logits rows; writes per-row loss (fp32) and, when
+// grad_scale != 0, overwrites logits with d(loss_sum*grad_scale)/dlogits (bf16).
+void cross_entropy_fwd_bwd(void* logits, const int64_t* targets, float* loss_rows, int rows, int vocab,
+                           int64_t ld, float grad_scale, int ignore_index, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------------
+// Spectral: batched power iteration helpers (GEMV with fused normalisation).
+void power_iteration(const void* W, bool w_f32, int m, int n, float* u, float* v, float* sigma, int iters,
+                     float eps, float* work, cudaStream_t stream);
+
+}  // namespace mmf

@@ -1,0 +1,341 @@
+// Optimizer-side memory-bound kernels (multi-tensor, one launch per parameter group):
+//   * muon_prep   : momentum / Nesterov / coupled weight decay fused with the bf16 cast of the
+//                   NS input, the (optional) transpose into the wide orientation, and the
+//                   per-matrix sum of squares for the Frobenius pre-normalisation.
+//                   Replaces optimizer.py:142-150 + utils.py:79-89 (several ATen passes).
+//   * ns_scale    : 1 / (||G||_F + 1e-7) per matrix (summing per-rank partials when sharded).
+//   * ws_to_out   : bf16 workspace -> parameter / output tensors with axpby.
+//   * adamw_multi : fused AdamW over all tensors of a group (examples/mixed_adamw.py:310-355
+//                   semantics with a correct bias correction).
+//   * power_iteration : device-resident power iteration for the spectral norm
+//                   (src/muon_fsdp/spectral.py:48-111) without host synchronisation.
+#include <cuda_bf16.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace mmf {
+
+namespace {
+
+template <bool F32>
+__device__ __forceinline__ float ld_val(const void* base, int64_t i) {
+  if (F32) return reinterpret_cast<const float*>(base)[i];
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+}
+template <bool F32>
+__device__ __forceinline__ void st_val(void* base, int64_t i, float v) {
+  if (F32)
+    reinterpret_cast<float*>(base)[i] = v;
+  else
+    reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+}
+
+__device__ __forceinline__ float block_sum_256(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x < 32) {
+    s = (l < (int)(blockDim.x >> 5)) ? red[l] : 0.f;
+    s = warp_sum(s);
+  }
+  __syncthreads();
+  return s;  // valid in thread 0
+}
+
+constexpr int PT = 64;  // prep tile edge
+
+template <bool GRAD_F32, bool PARAM_F32>
+__global__ void __launch_bounds__(256) muon_prep_kernel(const PrepArgs a) {
+  const PrepDesc d = a.descs[blockIdx.y];
+  const int tiles_c = (d.cols + PT - 1) / PT;
+  const int tiles = ((d.rows + PT - 1) / PT) * tiles_c;
+  __shared__ float tile[PT][PT + 1];
+  __shared__ float red[8];
+  const int tx = threadIdx.x & (PT - 1);
+  const int ty = threadIdx.x >> 6;  // 0..3
+  const void* G = reinterpret_cast<const void*>(d.grad);
+  float* BUF = reinterpret_cast<float*>(d.buf);
+  void* P = reinterpret_cast<void*>(d.param);
+  __nv_bfloat16* DST = reinterpret_cast<__nv_bfloat16*>(d.dst);
+  const float mu = a.mu;
+  float sq = 0.f;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int r0 = (t / tiles_c) * PT, c0 = (t % tiles_c) * PT;
+    const int c = c0 + tx;
+#pragma unroll 4
+    for (int rr = ty; rr < PT; rr += 4) {
+      const int r = r0 + rr;
+      float u = 0.f;
+      if (r < d.rows && c < d.cols) {
+        const int64_t i = static_cast<int64_t>(r) * d.cols + c;
+        float g = ld_val<GRAD_F32>(G, i);
+        if (a.wd_coupled != 0.f && P) g = fmaf(a.wd_coupled, ld_val<PARAM_F32>(P, i), g);
+        if (a.mode == 0) {
+          u = g;
+        } else {
+          float b = BUF[i];
+          b = (a.mode == 1) ? fmaf(mu, b - g, g) /* mu*b + (1-mu)*g */ : fmaf(mu, b, g);
+          BUF[i] = b;
+          u = a.nesterov ? fmaf(mu, b, g) : b;
+        }
+        if (!DST) {
+          const float pv = (d.p_scale != 0.f) ? ld_val<PARAM_F32>(P, i) : 0.f;
+          st_val<PARAM_F32>(P, i, fmaf(d.p_scale, pv, d.v_scale * u));
+        } else if (!d.transposed) {
+          const __nv_bfloat16 ub = __float2bfloat16_rn(u);
+          DST[static_cast<int64_t>(d.dst_row0 + r) * d.dst_ld + c] = ub;
+        }
+        sq = fmaf(u, u, sq);
+      }
+      if (DST && d.transposed) tile[rr][tx] = u;
+    }
+    if (DST && d.transposed) {
+      __syncthreads();
+      // write tile transposed: dst[(c0 + cc) * ld + dst_row0 + r0 + tx]
+      const int r = r0 + tx;
+#pragma unroll 4
+      for (int cc = ty; cc < PT; cc += 4) {
+        const int cg = c0 + cc;
+        if (r < d.rows && cg < d.cols)
+          DST[static_cast<int64_t>(cg) * d.dst_ld + d.dst_row0 + r] = __float2bfloat16_rn(tile[tx][cc]);
+      }
+      __syncthreads();
+    }
+  }
+  if (a.sumsq) {
+    const float s = block_sum_256(sq, red);
+    if (threadIdx.x == 0 && s != 0.f) atomicAdd(&a.sumsq[blockIdx.y], s);
+  }
+}
+
+__global__ void ns_scale_kernel(const float* sumsq, int n, int nparts, float eps, float* s, float* s2) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= n) return;
+  float acc = 0.f;
+  for (int p = 0; p < nparts; ++p) acc += sumsq[static_cast<int64_t>(p) * n + b];
+  const float v = 1.f / (sqrtf(acc) + eps);
+  s[b] = v;
+  if (s2) s2[b] = v * v;
+}
+
+template <bool OUT_F32>
+__global__ void ws_to_out_kernel(const WsOutArgs a) {
+  const int b = blockIdx.y;
+  const __nv_bfloat16* X = reinterpret_cast<const __nv_bfloat16*>(a.X) + static_cast<int64_t>(b) * a.Mp * a.Np;
+  const float sc = a.s_vec ? a.s_vec[b] : 1.f;
+  const float ps = a.p_scale * (a.p_scale_vec ? a.p_scale_vec[b] : 1.f);
+  const float vs = a.v_scale * (a.v_scale_vec ? a.v_scale_vec[b] : 1.f) * sc;
+  int64_t ld = a.out_ld, seg_rows = int64_t(1) << 40;
+  int tr = a.out_transposed ? 1 : 0;
+  if (a.out_meta) {
+    ld = a.out_meta[3 * b];
+    tr = static_cast<int>(a.out_meta[3 * b + 1]);
+    seg_rows = a.out_meta[3 * b + 2];
+  }
+  const int64_t* segp = a.out_ptrs + static_cast<int64_t>(b) * (a.nseg < 1 ? 1 : a.nseg);
+  const int64_t total = static_cast<int64_t>(a.m_true) * a.n_true;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(e / a.n_true), j = static_cast<int>(e % a.n_true);
+    const float v = __bfloat162float(X[static_cast<int64_t>(i) * a.Np + j]);
+    const int64_t r = tr ? j : i, cc = tr ? i : j;
+    const int seg = (a.nseg > 1) ? static_cast<int>(r / seg_rows) : 0;
+    void* T = reinterpret_cast<void*>(segp[seg]);
+    const int64_t idx = (r - seg * seg_rows) * ld + cc;
+    const float old = (ps != 0.f) ? ld_val<OUT_F32>(T, idx) : 0.f;
+    st_val<OUT_F32>(T, idx, fmaf(ps, old, vs * v));
+  }
+}
+
+template <bool P_F32, bool G_F32>
+__global__ void __launch_bounds__(256) adamw_kernel(const AdamArgs a) {
+  const AdamDesc d = a.descs[blockIdx.y];
+  void* P = reinterpret_cast<void*>(d.param);
+  const void* G = reinterpret_cast<const void*>(d.grad);
+  float* M = reinterpret_cast<float*>(d.exp_avg);
+  float* V = reinterpret_cast<float*>(d.exp_avg_sq);
+  const float step_size = a.lr / a.bias_correction1;
+  const float decay = 1.f - a.lr * a.weight_decay;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < d.numel;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float g = ld_val<G_F32>(G, i);
+    float m = M[i], v = V[i];
+    m = fmaf(a.beta1, m - g, g);
+    v = fmaf(a.beta2, v - g * g, g * g);
+    M[i] = m;
+    V[i] = v;
+    float p = ld_val<P_F32>(P, i) * decay;
+    const float denom = sqrtf(v) / a.bias_correction2_sqrt + a.eps;
+    p = fmaf(-step_size, m / denom, p);
+    st_val<P_F32>(P, i, p);
+  }
+}
+
+// ---------------------------- power iteration helpers ------------------------------------
+// y[r] = sum_c W[r, c] x[c]     (one warp per row)
+template <bool F32>
+__global__ void gemv_rows_kernel(const void* W, int m, int n, const float* x, float* y) {
+  const int warps = blockDim.x >> 5;
+  const int r = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int l = threadIdx.x & 31;
+  if (r >= m) return;
+  float acc = 0.f;
+  for (int c = l; c < n; c += 32) acc = fmaf(ld_val<F32>(W, static_cast<int64_t>(r) * n + c), x[c], acc);
+  acc = warp_sum(acc);
+  if (l == 0) y[r] = acc;
+}
+// y[c] = sum_r W[r, c] x[r]     (one thread per column, rows split over blockIdx.y, atomics)
+template <bool F32>
+__global__ void gemv_cols_kernel(const void* W, int m, int n, const float* x, float* y, int rows_per_block) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  const int r0 = blockIdx.y * rows_per_block;
+  const int r1 = min(m, r0 + rows_per_block);
+  float acc = 0.f;
+  for (int r = r0; r < r1; ++r) acc = fmaf(ld_val<F32>(W, static_cast<int64_t>(r) * n + c), x[r], acc);
+  atomicAdd(&y[c], acc);
+}
+// x /= max(||x||, eps) in place (single block); optionally also writes ||x|| into *norm_out.
+__global__ void normalize_kernel(float* x, int n, float eps, float* norm_out) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s = fmaf(x[i], x[i], s);
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float nrm = sqrtf(red[0]);
+  const float inv = 1.f / fmaxf(nrm, eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] *= inv;
+  if (norm_out && threadIdx.x == 0) *norm_out = nrm;
+}
+__global__ void dot_kernel(const float* a, const float* b, int n, float* out) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s = fmaf(a[i], b[i], s);
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) *out = t;
+  }
+}
+
+int grid_for(int64_t work, int threads, int cap) {
+  int64_t g = (work + threads - 1) / threads;
+  if (g < 1) g = 1;
+  if (g > cap) g = cap;
+  return static_cast<int>(g);
+}
+
+void check_launch(const char* what) {
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: ") + what + " launch failed: " + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+void muon_prep(const PrepArgs& a, cudaStream_t stream) {
+  if (a.n <= 0) return;
+  if (a.n > 65535) throw std::runtime_error("mmf: muon_prep supports at most 65535 tensors per launch");
+  const int gx = a.max_tiles < 1 ? 1 : (a.max_tiles > 4096 ? 4096 : a.max_tiles);
+  dim3 grid(gx, a.n);
+  if (a.grad_f32) {
+    if (a.param_f32)
+      muon_prep_kernel<true, true><<<grid, 256, 0, stream>>>(a);
+    else
+      muon_prep_kernel<true, false><<<grid, 256, 0, stream>>>(a);
+  } else {
+    if (a.param_f32)
+      muon_prep_kernel<false, true><<<grid, 256, 0, stream>>>(a);
+    else
+      muon_prep_kernel<false, false><<<grid, 256, 0, stream>>>(a);
+  }
+  check_launch("muon_prep");
+}
+
+void ns_scale(const float* sumsq, int n, int nparts, float eps, float* s, float* s2, cudaStream_t stream) {
+  if (n <= 0) return;
+  ns_scale_kernel<<<(n + 127) / 128, 128, 0, stream>>>(sumsq, n, nparts, eps, s, s2);
+  check_launch("ns_scale");
+}
+
+void ws_to_out(const WsOutArgs& a, cudaStream_t stream) {
+  if (a.batch <= 0) return;
+  dim3 grid(grid_for(static_cast<int64_t>(a.m_true) * a.n_true, 256, 2048), a.batch);
+  if (a.out_f32)
+    ws_to_out_kernel<true><<<grid, 256, 0, stream>>>(a);
+  else
+    ws_to_out_kernel<false><<<grid, 256, 0, stream>>>(a);
+  check_launch("ws_to_out");
+}
+
+void adamw_multi(const AdamArgs& a, cudaStream_t stream) {
+  if (a.n <= 0) return;
+  if (a.n > 65535) throw std::runtime_error("mmf: adamw_multi supports at most 65535 tensors per launch");
+  dim3 grid(grid_for(a.max_numel, 256, 1184), a.n);
+  if (a.param_f32) {
+    if (a.grad_f32)
+      adamw_kernel<true, true><<<grid, 256, 0, stream>>>(a);
+    else
+      adamw_kernel<true, false><<<grid, 256, 0, stream>>>(a);
+  } else {
+    if (a.grad_f32)
+      adamw_kernel<false, true><<<grid, 256, 0, stream>>>(a);
+    else
+      adamw_kernel<false, false><<<grid, 256, 0, stream>>>(a);
+  }
+  check_launch("adamw_multi");
+}
+
+// work must hold max(m, n) + 1 floats.  u [m], v [n] (v holds the start vector on entry).
+void power_iteration(const void* W, bool w_f32, int m, int n, float* u, float* v, float* sigma, int iters, float eps,
+                     float* work, cudaStream_t stream) {
+  const int rows_per_block = 256;
+  auto rows = [&](const float* x, float* y) {
+    if (w_f32)
+      gemv_rows_kernel<true><<<(m + 7) / 8, 256, 0, stream>>>(W, m, n, x, y);
+    else
+      gemv_rows_kernel<false><<<(m + 7) / 8, 256, 0, stream>>>(W, m, n, x, y);
+    check_launch("gemv_rows");
+  };
+  auto cols = [&](const float* x, float* y) {
+    cudaMemsetAsync(y, 0, sizeof(float) * n, stream);
+    dim3 g((n + 255) / 256, (m + rows_per_block - 1) / rows_per_block);
+    if (w_f32)
+      gemv_cols_kernel<true><<<g, 256, 0, stream>>>(W, m, n, x, y, rows_per_block);
+    else
+      gemv_cols_kernel<false><<<g, 256, 0, stream>>>(W, m, n, x, y, rows_per_block);
+    check_launch("gemv_cols");
+  };
+  normalize_kernel<<<1, 1024, 0, stream>>>(v, n, eps, nullptr);
+  check_launch("normalize");
+  for (int it = 0; it < iters; ++it) {
+    rows(v, u);
+    normalize_kernel<<<1, 1024, 0, stream>>>(u, m, eps, nullptr);
+    check_launch("normalize");
+    cols(u, v);
+    normalize_kernel<<<1, 1024, 0, stream>>>(v, n, eps, nullptr);
+    check_launch("normalize");
+  }
+  // sigma = u^T W v
+  rows(v, work);
+  dot_kernel<<<1, 1024, 0, stream>>>(u, work, m, sigma);
+  check_launch("dot");
+}
+
+}  // namespace mmf

@@ -1,0 +1,524 @@
+// Persistent, warp-specialised bf16 GEMM on the sm_100a 5th-generation tensor core.
+//
+//   warp 0      : TMA producer (one elected lane) — 4-stage smem ring, 128B-swizzled tiles
+//   warp 1      : TMEM allocator + MMA issuer (one lane issues tcgen05.mma, M=128 N=256 K=16)
+//   warps 2..5  : epilogue — tcgen05.ld from TMEM, fused axpby / SYRK mirror / param update
+//
+// The accumulator lives in TMEM (2 x 256 fp32 columns, double buffered), so the epilogue of
+// tile t overlaps the main loop of tile t+1.  Every mbarrier wait is bounded (see
+// tc_common.cuh); a timeout records an error code and unwinds instead of hanging.
+//
+// This kernel is the building block of the Newton–Schulz chain that replaces the reference's
+// three torch.matmul calls per iteration (src/muon_fsdp/utils.py:96-99):
+//   A = X X^T            -> symmetric mode, alpha = Frobenius scale^2 on the first iteration
+//   B = c A A + b A      -> symmetric mode, beta term reads A
+//   X' = B X + a X       -> B operand read MN-major straight from row-major X
+// and the final iteration's epilogue applies the Muon update to the parameters directly
+// (src/muon_fsdp/optimizer.py:157-170 semantics) in "output" mode.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace mmf {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+
+struct GemmParams {
+  int M, N, K, batch;
+  int tiles_m, tiles_n, tiles_per_batch, num_tiles;
+  int symmetric;
+  int mode;  // 0 workspace, 1 output
+  __nv_bfloat16* D;
+  const __nv_bfloat16* C;
+  const float* alpha_vec;
+  float alpha;
+  const float* beta_vec;
+  float beta;
+  const int64_t* out_ptrs;
+  int nseg;
+  const int64_t* out_meta;
+  int64_t out_ld;
+  int out_f32, out_transposed, m_true, n_true;
+  const float* p_scale_vec;
+  float p_scale;
+  const float* v_scale_vec;
+  float v_scale;
+  int* err;
+};
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& b, int& tm, int& tn) {
+  b = t / p.tiles_per_batch;
+  int r = t - b * p.tiles_per_batch;
+  if (!p.symmetric) {
+    tm = r / p.tiles_n;
+    tn = r - tm * p.tiles_n;
+    return;
+  }
+  // Symmetric output: row block i (BM rows) needs column blocks tn >= i*BM/BN = i/2.
+  int i = 0;
+#pragma unroll 1
+  while (true) {
+    const int cnt = p.tiles_n - (i >> 1);
+    if (r < cnt) {
+      tm = i;
+      tn = (i >> 1) + r;
+      return;
+    }
+    r -= cnt;
+    ++i;
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w = s[q];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(h[e]);
+      v[q * 8 + 2 * e] = f.x;
+      v[q * 8 + 2 * e + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+    d[q] = w;
+  }
+}
+
+template <bool B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&tfull[j], 1);
+      mbar_init(&tempty[j], 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int k_blocks = p.K / BK;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued = 0;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int b, tm, tn;
+        tile_coords(p, t, b, tm, tn);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_3d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, tm * BM, b);
+          if (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_3d(sB + stage * B_BYTES + c * (BK * 64 * 2), &tmB, &full[stage], tn * BN + c * 64, kb * BK,
+                          b);
+          } else {
+            tma_load_3d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, tn * BN, b);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Unwinding: let the loads already in flight land before the CTA can exit.
+        for (int s = 0; s < STAGES && s < issued; ++s) {
+          int st = (stage + STAGES - 1 - s) % STAGES;
+          uint32_t ph = (st < stage) ? phase : (phase ^ 1u);
+          mbar_wait(&full[st], ph, p.err, ERR_TMA_EMPTY_TIMEOUT, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ---------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, ERR_MMA_FULL_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc_kmajor(a_addr + kk * 32);
+            const uint64_t bd = B_MN ? sdesc_mnmajor(b_addr + kk * 16 * 128, BK * 64 * 2) : sdesc_kmajor(b_addr + kk * 32);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Drain: make sure every issued MMA finished before TMEM can be released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else {
+    // ------------------------------ epilogue -----------------------------------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int b, tm, tn;
+      tile_coords(p, t, b, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
+      tc_fence_after();
+      const int row = tm * BM + q * 32 + lane;
+      const float alpha_b = p.alpha * (p.alpha_vec ? p.alpha_vec[b] : 1.f);
+      const float beta_b = p.C ? p.beta * (p.beta_vec ? p.beta_vec[b] : 1.f) : 0.f;
+      const int64_t mn = static_cast<int64_t>(p.M) * p.N;
+      const __nv_bfloat16* Crow = p.C ? p.C + b * mn + static_cast<int64_t>(row) * p.N : nullptr;
+      const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      if (p.mode == 0) {
+        __nv_bfloat16* Db = p.D + b * mn;
+#pragma unroll 1
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          float v[32];
+          tmem_ld_32cols(t_row + chunk * 32, v);
+          const int col0 = tn * BN + chunk * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha_b;
+          if (beta_b != 0.f) {
+            float c[32];
+            load_bf16x32(Crow + col0, c);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = fmaf(beta_b, c[i], v[i]);
+          }
+          if (!p.symmetric || col0 >= row) {
+            store_bf16x32(Db + static_cast<int64_t>(row) * p.N + col0, v);
+          } else if (col0 + 31 >= row) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i >= row) Db[static_cast<int64_t>(row) * p.N + col0 + i] = __float2bfloat16_rn(v[i]);
+          }
+          if (p.symmetric && col0 + 31 > row) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i > row) Db[static_cast<int64_t>(col0 + i) * p.N + row] = __float2bfloat16_rn(v[i]);
+          }
+        }
+      } else {
+        const float ps = p.p_scale * (p.p_scale_vec ? p.p_scale_vec[b] : 1.f);
+        const float vs = p.v_scale * (p.v_scale_vec ? p.v_scale_vec[b] : 1.f);
+        int64_t ld = p.out_ld, seg_rows = int64_t(1) << 40;
+        int tr = p.out_transposed;
+        if (p.out_meta) {
+          ld = p.out_meta[3 * b];
+          tr = static_cast<int>(p.out_meta[3 * b + 1]);
+          seg_rows = p.out_meta[3 * b + 2];
+        }
+        const int64_t* segp = p.out_ptrs + static_cast<int64_t>(b) * p.nseg;
+        const bool row_ok = row < p.m_true;
+#pragma unroll 1
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          float v[32];
+          tmem_ld_32cols(t_row + chunk * 32, v);
+          const int col0 = tn * BN + chunk * 32;
+          if (!row_ok || col0 >= p.n_true) continue;
+          float c[32];
+          if (beta_b != 0.f) load_bf16x32(Crow + col0, c);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = col0 + i;
+            if (col >= p.n_true) break;
+            float val = alpha_b * v[i];
+            if (beta_b != 0.f) val = fmaf(beta_b, c[i], val);
+            const int64_t r = tr ? col : row;
+            const int64_t cc = tr ? row : col;
+            const int seg = (p.nseg > 1) ? static_cast<int>(r / seg_rows) : 0;
+            char* T = reinterpret_cast<char*>(segp[seg]);
+            const int64_t idx = (r - seg * seg_rows) * ld + cc;
+            if (p.out_f32) {
+              float* tp = reinterpret_cast<float*>(T) + idx;
+              const float old = (ps != 0.f) ? *tp : 0.f;
+              *tp = fmaf(ps, old, vs * val);
+            } else {
+              __nv_bfloat16* tp = reinterpret_cast<__nv_bfloat16*>(T) + idx;
+              const float old = (ps != 0.f) ? __bfloat162float(*tp) : 0.f;
+              *tp = __float2bfloat16_rn(fmaf(ps, old, vs * val));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ------------------------------------ host side ------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn) throw std::runtime_error("mmf: cuTensorMapEncodeTiled is not available from the CUDA driver");
+  return fn;
+}
+
+CUtensorMap make_map_bf16_3d(const void* base, uint64_t inner, uint64_t outer, uint64_t batch, uint32_t box_inner,
+                             uint32_t box_outer) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("mmf: TMA base must be 16-byte aligned");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  cuuint64_t strides[2] = {inner * 2, inner * outer * 2};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("mmf: cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return m;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  bool attr_set[2] = {false, false};
+};
+DeviceInfo& dev_info(int dev) {
+  static DeviceInfo infos[64];
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  DeviceInfo& d = infos[dev];
+  if (d.sms == 0) cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+  return d;
+}
+
+void check_shape(int batch, int M, int N, int K) {
+  if (batch <= 0 || M <= 0 || N <= 0 || K <= 0) throw std::runtime_error("mmf: empty GEMM");
+  if (M % BM || N % BN || K % BK)
+    throw std::runtime_error("mmf: tc_gemm needs M%128==0, N%256==0, K%64==0 (got M=" + std::to_string(M) +
+                             " N=" + std::to_string(N) + " K=" + std::to_string(K) + ")");
+}
+
+void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceInfo& di = dev_info(dev);
+  p.tiles_m = p.M / BM;
+  p.tiles_n = p.N / BN;
+  if (p.symmetric) {
+    if (p.M != p.N) throw std::runtime_error("mmf: symmetric GEMM needs M == N");
+    int cnt = 0;
+    for (int i = 0; i < p.tiles_m; ++i) cnt += p.tiles_n - (i >> 1);
+    p.tiles_per_batch = cnt;
+  } else {
+    p.tiles_per_batch = p.tiles_m * p.tiles_n;
+  }
+  p.num_tiles = p.tiles_per_batch * p.batch;
+  p.err = device_error_word(dev);
+  CUtensorMap ma = make_map_bf16_3d(A, p.K, p.M, p.batch, BK, BM);
+  CUtensorMap mb = b_mn ? make_map_bf16_3d(B, p.N, p.K, p.batch, 64, BK) : make_map_bf16_3d(B, p.K, p.N, p.batch, BK, BN);
+  const int grid = p.num_tiles < di.sms ? p.num_tiles : di.sms;
+  if (b_mn) {
+    if (!di.attr_set[1]) {
+      cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      di.attr_set[1] = true;
+    }
+    tc_gemm_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  } else {
+    if (!di.attr_set[0]) {
+      cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      di.attr_set[0] = true;
+    }
+    tc_gemm_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+  }
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: tc_gemm launch failed: ") + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+// ------------------------------- error word / counters -----------------------------------
+__device__ int g_mmf_error_word;
+
+int* device_error_word(int device) {
+  static int* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  if (!ptrs[device]) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != device) cudaSetDevice(device);
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_mmf_error_word);
+    if (cur != device) cudaSetDevice(cur);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    ptrs[device] = static_cast<int*>(p);
+  }
+  return ptrs[device];
+}
+
+int read_and_clear_device_error(int device, cudaStream_t stream) {
+  int* p = device_error_word(device);
+  int v = 0;
+  cudaMemcpyAsync(&v, p, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  cudaStreamSynchronize(stream);
+  if (v != 0) {
+    cudaMemsetAsync(p, 0, sizeof(int), stream);
+    cudaStreamSynchronize(stream);
+  }
+  return v;
+}
+
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launch_count() { return g_launches.load(); }
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void tc_gemm_ws(const GemmWsArgs& a, cudaStream_t stream) {
+  check_shape(a.batch, a.M, a.N, a.K);
+  GemmParams p{};
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.batch = a.batch;
+  p.symmetric = a.symmetric ? 1 : 0;
+  p.mode = 0;
+  p.D = static_cast<__nv_bfloat16*>(a.D);
+  p.C = static_cast<const __nv_bfloat16*>(a.C);
+  p.alpha_vec = a.alpha_vec;
+  p.alpha = a.alpha;
+  p.beta_vec = a.beta_vec;
+  p.beta = a.beta;
+  if ((reinterpret_cast<uintptr_t>(a.D) & 15) || (a.C && (reinterpret_cast<uintptr_t>(a.C) & 15)))
+    throw std::runtime_error("mmf: D/C must be 16-byte aligned");
+  launch(p, a.A, a.B, a.b_mn_major, stream);
+}
+
+void tc_gemm_out(const GemmOutArgs& a, cudaStream_t stream) {
+  check_shape(a.batch, a.M, a.N, a.K);
+  if (a.m_true > a.M || a.n_true > a.N) throw std::runtime_error("mmf: true extent exceeds padded GEMM extent");
+  GemmParams p{};
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.batch = a.batch;
+  p.symmetric = 0;
+  p.mode = 1;
+  p.C = static_cast<const __nv_bfloat16*>(a.C);
+  p.alpha_vec = a.alpha_vec;
+  p.alpha = a.alpha;
+  p.beta_vec = a.beta_vec;
+  p.beta = a.beta;
+  p.out_ptrs = a.out_ptrs;
+  p.nseg = a.nseg < 1 ? 1 : a.nseg;
+  p.out_meta = a.out_meta;
+  p.out_ld = a.out_ld;
+  p.out_f32 = a.out_f32 ? 1 : 0;
+  p.out_transposed = a.out_transposed ? 1 : 0;
+  p.m_true = a.m_true;
+  p.n_true = a.n_true;
+  p.p_scale_vec = a.p_scale_vec;
+  p.p_scale = a.p_scale;
+  p.v_scale_vec = a.v_scale_vec;
+  p.v_scale = a.v_scale;
+  launch(p, a.A, a.B, a.b_mn_major, stream);
+}
+
+}  // namespace mmf

@@ -1,0 +1,176 @@
+"""Collective primitives with single-process fallbacks.
+
+API parity with the reference's two comm layers:
+``src/fsdp2_utils/comm.py:18-267`` (is_distributed, get_world_size, get_rank, get_local_rank,
+all_gather, all_gather_grads, scatter, scatter_updates, all_reduce, all_reduce_sum,
+all_reduce_avg, broadcast, barrier) and ``src/muon_fsdp/distributed.py:13-170``
+(is_available, all_gather_grads, scatter_updates).
+
+Differences (deliberate):
+* ``scatter_updates`` works (the reference passes an unsupported ``src_tensor=`` kwarg,
+  distributed.py:161-166) and, because every rank already holds the identical full update in
+  the NS-replication scheme, it slices locally instead of shipping data from rank 0.
+* Rows that do not divide by the world size follow ``torch.chunk`` (FSDP2's own sharding)
+  instead of raising.
+* Gathers are bucketed: all tensors of one dtype go through a single
+  ``all_gather_into_tensor`` instead of one collective per tensor.
+"""
+from __future__ import annotations
+
+import os
+from collections import OrderedDict
+from typing import List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def is_available() -> bool:
+    """True when torch.distributed is available *and* initialised."""
+    return dist.is_available() and dist.is_initialized()
+
+
+is_distributed = is_available
+
+
+def get_world_size(group: Optional[dist.ProcessGroup] = None) -> int:
+    return dist.get_world_size(group) if is_available() else 1
+
+
+def get_rank(group: Optional[dist.ProcessGroup] = None) -> int:
+    return dist.get_rank(group) if is_available() else 0
+
+
+def get_local_rank() -> int:
+    """Rank within the node (LOCAL_RANK from the launcher, else the global rank)."""
+    if not is_available():
+        return 0
+    lr = os.environ.get("LOCAL_RANK")
+    if lr is not None:
+        return int(lr)
+    try:
+        return dist.get_node_local_rank()  # torch >= 2.4
+    except Exception:
+        return get_rank()
+
+
+def chunk_rows(rows: int, world: int) -> List[int]:
+    """Row counts per rank under ``torch.chunk`` semantics (FSDP2's Shard(0) layout)."""
+    cs = (rows + world - 1) // world if world > 0 else rows
+    out = []
+    for r in range(world):
+        lo = min(r * cs, rows)
+        hi = min((r + 1) * cs, rows)
+        out.append(hi - lo)
+    return out
+
+
+def chunk_offset(rows: int, world: int, rank: int) -> int:
+    cs = (rows + world - 1) // world
+    return min(rank * cs, rows)
+
+
+def all_gather(tensors: Sequence[torch.Tensor], group: Optional[dist.ProcessGroup] = None) -> List[torch.Tensor]:
+    """All-gather each tensor along dim 0 (equal local sizes), one bucketed collective per dtype."""
+    tensors = list(tensors)
+    if not is_available() or get_world_size(group) == 1 or not tensors:
+        return tensors
+    ws = get_world_size(group)
+    out: List[Optional[torch.Tensor]] = [None] * len(tensors)
+    buckets: "OrderedDict[tuple, List[int]]" = OrderedDict()
+    for i, t in enumerate(tensors):
+        buckets.setdefault((t.dtype, t.device), []).append(i)
+    for (dtype, device), idxs in buckets.items():
+        flat = [tensors[i].contiguous().reshape(-1) for i in idxs]
+        sizes = [f.numel() for f in flat]
+        send = torch.cat(flat) if len(flat) > 1 else flat[0]
+        recv = send.new_empty(ws * send.numel())
+        dist.all_gather_into_tensor(recv, send, group=group)
+        recv = recv.view(ws, -1)
+        off = 0
+        for i, n in zip(idxs, sizes):
+            t = tensors[i]
+            parts = recv[:, off:off + n].reshape(ws, *t.shape)
+            out[i] = parts.reshape(ws * t.shape[0], *t.shape[1:]) if t.dim() > 0 else parts.reshape(ws)
+            off += n
+    return out  # type: ignore[return-value]
+
+
+def all_gather_grads(grads: Sequence[torch.Tensor], group: Optional[dist.ProcessGroup] = None) -> List[torch.Tensor]:
+    """Gather row-sharded gradients into full matrices (``muon_fsdp.distributed.all_gather_grads``)."""
+    return all_gather(grads, group=group)
+
+
+def scatter(tensors: Sequence[torch.Tensor], src_rank: int = 0,
+            group: Optional[dist.ProcessGroup] = None) -> List[torch.Tensor]:
+    """Split each full tensor along dim 0 and give every rank its chunk (sent from ``src_rank``)."""
+    tensors = list(tensors)
+    if not is_available() or get_world_size(group) == 1:
+        return tensors
+    ws, rank = get_world_size(group), get_rank(group)
+    out = []
+    for t in tensors:
+        t = t.contiguous()
+        if t.shape[0] % ws != 0:
+            raise ValueError(f"dim 0 ({t.shape[0]}) must be divisible by world_size ({ws}) for scatter")
+        chunk = t.shape[0] // ws
+        recv = t.new_empty((chunk,) + tuple(t.shape[1:]))
+        src_global = dist.get_global_rank(group, src_rank) if group is not None else src_rank
+        scatter_list = list(t.split(chunk)) if rank == src_rank else None
+        dist.scatter(recv, scatter_list=scatter_list, src=src_global, group=group)
+        out.append(recv)
+    return out
+
+
+def scatter_updates(updates: Sequence[torch.Tensor], src_rank: int = 0,
+                    group: Optional[dist.ProcessGroup] = None) -> List[torch.Tensor]:
+    """Each rank's ``torch.chunk`` row slice of identical full updates (no communication)."""
+    updates = list(updates)
+    if not is_available() or get_world_size(group) == 1:
+        return updates
+    ws, rank = get_world_size(group), get_rank(group)
+    out = []
+    for u in updates:
+        rows = u.shape[0]
+        off = chunk_offset(rows, ws, rank)
+        n = chunk_rows(rows, ws)[rank]
+        out.append(u[off:off + n].contiguous())
+    return out
+
+
+def all_reduce(tensor: torch.Tensor, op=None, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+    if not is_available() or get_world_size(group) == 1:
+        return tensor
+    dist.all_reduce(tensor, op=op if op is not None else dist.ReduceOp.SUM, group=group)
+    return tensor
+
+
+def all_reduce_sum(tensor: torch.Tensor, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+    return all_reduce(tensor, dist.ReduceOp.SUM if is_available() else None, group)
+
+
+def all_reduce_avg(tensor: torch.Tensor, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+    if not is_available() or get_world_size(group) == 1:
+        return tensor
+    all_reduce(tensor, dist.ReduceOp.SUM, group)
+    tensor.div_(get_world_size(group))
+    return tensor
+
+
+def broadcast(tensor: torch.Tensor, src: int = 0, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+    if not is_available() or get_world_size(group) == 1:
+        return tensor
+    dist.broadcast(tensor, src=src, group=group)
+    return tensor
+
+
+def barrier(group: Optional[dist.ProcessGroup] = None) -> None:
+    if is_available():
+        dist.barrier(group=group)
+
+
+__all__ = [
+    "is_available", "is_distributed", "get_world_size", "get_rank", "get_local_rank", "chunk_rows",
+    "chunk_offset", "all_gather", "all_gather_grads", "scatter", "scatter_updates", "all_reduce",
+    "all_reduce_sum", "all_reduce_avg", "broadcast", "barrier",
+]
