@@ -144,7 +144,7 @@ void tc_gemm_out(Tensor A, Tensor B, bool b_mn_major, c10::optional<Tensor> C, c
 // workspace; per-matrix destination = dst_base_offsets[i] elements into dst.
 void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<Tensor> params,
                c10::optional<Tensor> dst, std::vector<int64_t> dst_offsets, std::vector<int64_t> dst_row0,
-               std::vector<int64_t> transposed, int64_t dst_ld, std::vector<double> p_scale,
+               std::vector<int64_t> transposed, std::vector<int64_t> dst_ld, std::vector<double> p_scale,
                std::vector<double> v_scale, int64_t mode, bool nesterov, double mu, double wd_coupled,
                c10::optional<Tensor> sumsq) {
   const int n = static_cast<int>(grads.size());
@@ -182,7 +182,7 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
       d[i].dst = reinterpret_cast<int64_t>(dst->data_ptr()) + dst_offsets[i] * 2;
       d[i].dst_row0 = static_cast<int32_t>(dst_row0[i]);
       d[i].transposed = static_cast<int32_t>(transposed[i]);
-      d[i].dst_ld = dst_ld;
+      d[i].dst_ld = dst_ld.size() == 1 ? dst_ld[0] : dst_ld[i];
     } else {
       TORCH_CHECK(!params.empty(), "mmf: direct apply needs params");
       d[i].p_scale = static_cast<float>(p_scale[i]);
@@ -192,6 +192,12 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
     if (tiles > max_tiles) max_tiles = tiles;
   }
   if (mode != 0) TORCH_CHECK(!bufs.empty(), "mmf: momentum modes need buffers");
+  if (dst.has_value())
+    TORCH_CHECK((int)dst_offsets.size() == n && (int)dst_row0.size() == n && (int)transposed.size() == n &&
+                    (dst_ld.size() == 1 || (int)dst_ld.size() == n),
+                "mmf: per-tensor destination lists must match the number of tensors");
+  else
+    TORCH_CHECK((int)p_scale.size() == n && (int)v_scale.size() == n, "mmf: per-tensor scale lists size");
   if (dst.has_value()) check_bf16_contig(*dst, "dst");
   Tensor dd = upload(d, dev);
   mmf::PrepArgs a{};

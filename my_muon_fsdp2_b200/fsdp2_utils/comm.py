@@ -1,0 +1,16 @@
+"""``fsdp2_utils.comm``."""
+from ..parallel.comm import (  # noqa: F401
+    all_gather,
+    all_gather_grads,
+    all_reduce,
+    all_reduce_avg,
+    all_reduce_sum,
+    barrier,
+    broadcast,
+    get_local_rank,
+    get_rank,
+    get_world_size,
+    is_distributed,
+    scatter,
+    scatter_updates,
+)

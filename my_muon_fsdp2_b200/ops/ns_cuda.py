@@ -123,7 +123,7 @@ def newton_schulz_batched(
         srcs = [_as_supported(mats[i]) for i in idxs]
         if len({t.dtype for t in srcs}) != 1:
             srcs = [t.float() for t in srcs]
-        E.muon_prep(srcs, [], [], X0, [b * Mp * Np for b in range(B)], [0] * B, [int(tall)] * B, Np, [], [], 0,
+        E.muon_prep(srcs, [], [], X0, [b * Mp * Np for b in range(B)], [0] * B, [int(tall)] * B, [Np], [], [], 0,
                     False, 0.0, 0.0, sumsq)
         s = torch.empty(B, dtype=torch.float32, device=dev)
         s2 = torch.empty_like(s)

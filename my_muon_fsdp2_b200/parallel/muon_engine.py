@@ -1,0 +1,432 @@
+"""Muon step engine: momentum + Newton–Schulz + parameter update for plain or FSDP2-sharded params.
+
+This is the B200 replacement of the reference's "NS replication" step
+(``src/muon_fsdp/fsdp.py:253-450``: per-parameter all-gather of the raw gradient, identical NS on
+every rank, row slice).  Instead of replicating the NS work ``world_size`` times, each matrix is
+given one *owner* rank (longest-processing-time-first assignment on its NS FLOP count), so the
+chain runs once per matrix and the ranks split the FLOPs:
+
+1. every rank updates the momentum of its local row shards (``muon_prep`` kernel: momentum,
+   Nesterov, coupled weight decay, bf16 cast, per-matrix sum of squares) and writes the bf16
+   NS input for matrix *j* into the staging segment of ``owner(j)``;
+2. the per-matrix partial sums of squares are all-reduced (a few hundred floats);
+3. the staged shards reach their owners (``comm="nccl"``: one ``all_to_all_single`` for all
+   matrices; ``comm="p2p"``: the owner's assembly kernel reads the shards straight out of the
+   peers' symmetric-memory buffers over NVLink);
+4. each owner stacks its matrices by shape and runs the batched tcgen05 chain; the last GEMM's
+   epilogue scatters every rank's row shard of the orthogonalised update into that rank's
+   return segment (local buffer for NCCL, the peer's symmetric buffer for P2P);
+5. after the return exchange each rank applies ``p = (1 - lr*wd) * p - lr_eff * O`` to its shard
+   (``muon_prep`` in direct-apply mode).
+
+Unsharded (plain) parameters, or a world of one, take the local path: the momentum kernel
+writes directly into the NS workspace and the last GEMM epilogue updates the parameters.
+
+CPU tensors (gloo process groups, tests) run the same schedule with PyTorch math in fp32.
+"""
+from __future__ import annotations
+
+import math
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..ops.newton_schulz import NS_COEFFICIENTS, NS_EPS, _ns_torch
+from .comm import chunk_offset, chunk_rows
+from .dtensor import is_dtensor
+
+MODE_COPY, MODE_EMA, MODE_HEAVYBALL = 0, 1, 2
+
+
+@dataclass
+class MuonHyper:
+    """Momentum form shared by one engine call (one parameter group)."""
+
+    mode: int = MODE_EMA  # EMA (lerp) or heavy-ball (buf = mu*buf + g)
+    momentum: float = 0.95
+    nesterov: bool = False
+    wd_coupled: float = 0.0  # g <- g + wd * p before the momentum update
+    ns_steps: int = 5
+
+
+@dataclass
+class MuonTask:
+    """One parameter: its update is p <- decay * p - lr_eff * U."""
+
+    param: torch.Tensor
+    grad: torch.Tensor
+    buf: Optional[torch.Tensor]  # fp32 momentum (local shard) or None in copy mode
+    lr_eff: float
+    decay: float = 1.0
+    orthogonalize: bool = True
+    # filled by the engine
+    local_param: Optional[torch.Tensor] = field(default=None, repr=False)
+    local_grad: Optional[torch.Tensor] = field(default=None, repr=False)
+
+
+def ns_flops(rows: int, cols: int, steps: int) -> float:
+    m, n = min(rows, cols), max(rows, cols)
+    return steps * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def assign_owners(costs: Sequence[float], world: int) -> List[int]:
+    """Longest-processing-time-first: biggest matrix to the least-loaded rank (ties -> lowest rank)."""
+    load = [0.0] * world
+    owners = [0] * len(costs)
+    for j in sorted(range(len(costs)), key=lambda i: (-costs[i], i)):
+        r = min(range(world), key=lambda k: (load[k], k))
+        owners[j] = r
+        load[r] += costs[j]
+    return owners
+
+
+def _local(t: torch.Tensor) -> torch.Tensor:
+    return t.to_local() if is_dtensor(t) else t
+
+
+def _as2d(t: torch.Tensor) -> torch.Tensor:
+    if t.dim() == 2:
+        return t
+    if t.dim() <= 1:
+        return t.reshape(1, -1)
+    return t.reshape(t.shape[0], -1)
+
+
+class MuonEngine:
+    """Executes Muon steps for lists of :class:`MuonTask` (see module docstring)."""
+
+    def __init__(self, process_group: Optional[dist.ProcessGroup] = None, comm: str = "auto",
+                 max_workspace_bytes: int = 8 << 30):
+        if comm not in ("auto", "nccl", "p2p"):
+            raise ValueError(f"comm must be 'auto', 'nccl' or 'p2p', got {comm!r}")
+        self.group = process_group
+        self.comm = comm
+        self.max_workspace_bytes = int(max_workspace_bytes)
+        self._p2p = None
+        self.last_stats: Dict[str, float] = {}
+
+    # ------------------------------------------------------------------ helpers
+    def _world(self, tasks: Sequence[MuonTask]) -> Tuple[int, int, Optional[dist.ProcessGroup]]:
+        sharded = [t for t in tasks if is_dtensor(t.param)]
+        if not sharded:
+            return 1, 0, None
+        group = self.group
+        if group is None:
+            mesh = sharded[0].param.device_mesh
+            group = mesh.get_group(mesh.ndim - 1) if mesh.ndim > 1 else mesh.get_group()
+        return dist.get_world_size(group), dist.get_rank(group), group
+
+    # ------------------------------------------------------------------ public
+    @torch.no_grad()
+    def step(self, tasks: Sequence[MuonTask], hp: MuonHyper) -> None:
+        tasks = [t for t in tasks if t.grad is not None]
+        if not tasks:
+            return
+        for t in tasks:
+            if t.grad.is_sparse:
+                raise RuntimeError("Muon does not support sparse gradients")
+            t.local_param = _local(t.param)
+            t.local_grad = _local(t.grad)
+        world, rank, group = self._world(tasks)
+        is_cuda = tasks[0].local_param.is_cuda
+        elementwise = [t for t in tasks if not (t.orthogonalize and t.param.dim() == 2)]
+        matrices = [t for t in tasks if t.orthogonalize and t.param.dim() == 2]
+        if elementwise:
+            self._elementwise(elementwise, hp, is_cuda)
+        if not matrices:
+            return
+        sharded = [t for t in matrices if is_dtensor(t.param)]
+        local = [t for t in matrices if not is_dtensor(t.param)]
+        if world == 1:
+            local = local + sharded
+            sharded = []
+        if local:
+            if is_cuda:
+                self._local_cuda(local, hp)
+            else:
+                self._local_cpu(local, hp)
+        if sharded:
+            self._sharded(sharded, hp, world, rank, group, is_cuda)
+
+    # ------------------------------------------------------------------ elementwise (no NS)
+    def _elementwise(self, tasks: List[MuonTask], hp: MuonHyper, is_cuda: bool) -> None:
+        if is_cuda:
+            from .._ext import ext
+
+            E = ext()
+            for key, ts in _group_by(tasks, lambda t: (t.local_grad.dtype, t.local_param.dtype)).items():
+                grads = [_as2d(t.local_grad.contiguous()) for t in ts]
+                params = [_as2d(t.local_param) for t in ts]
+                bufs = [_as2d(t.buf) for t in ts] if hp.mode != MODE_COPY else []
+                E.muon_prep(grads, bufs, params, None, [], [], [], [0], [_decay_float(t.decay) for t in ts],
+                            [-t.lr_eff for t in ts], hp.mode, hp.nesterov, hp.momentum, hp.wd_coupled, None)
+            return
+        for t in tasks:
+            u = _momentum_torch(t, hp)
+            p = t.local_param
+            _decay_(p, t.decay)
+            p.add_(u.to(p.dtype).reshape(p.shape), alpha=-t.lr_eff)
+
+    # ------------------------------------------------------------------ local paths
+    def _local_cpu(self, tasks: List[MuonTask], hp: MuonHyper) -> None:
+        for t in tasks:
+            u = _momentum_torch(t, hp)
+            o = _ns_torch(u, hp.ns_steps)
+            p = t.local_param
+            _decay_(p, t.decay)
+            p.add_(o.to(p.dtype), alpha=-t.lr_eff)
+
+    def _local_cuda(self, tasks: List[MuonTask], hp: MuonHyper) -> None:
+        from .._ext import ext
+        from ..ops.ns_cuda import round_up, run_ns_group, wide_shape
+
+        E = ext()
+        dev = tasks[0].local_param.device
+        groups = _group_by(tasks, lambda t: (tuple(t.local_param.shape), t.local_grad.dtype, t.local_param.dtype))
+        for (shape, gdt, pdt), ts in groups.items():
+            rows, cols = shape
+            mw, nw, tall = wide_shape(rows, cols)
+            Mp, Np = round_up(mw), round_up(nw)
+            per = 2 * Mp * Np * 2 + 2 * Mp * Mp * 2
+            chunk = max(1, min(len(ts), self.max_workspace_bytes // max(per, 1)))
+            for c0 in range(0, len(ts), chunk):
+                sub = ts[c0:c0 + chunk]
+                B = len(sub)
+                padded = (Mp != mw) or (Np != nw)
+                X0 = (torch.zeros if padded else torch.empty)(B, Mp, Np, dtype=torch.bfloat16, device=dev)
+                sumsq = torch.zeros(B, dtype=torch.float32, device=dev)
+                grads = [t.local_grad.contiguous() for t in sub]
+                params = [t.local_param for t in sub]
+                bufs = [t.buf for t in sub] if hp.mode != MODE_COPY else []
+                E.muon_prep(grads, bufs, params if hp.wd_coupled != 0 else [], X0,
+                            [b * Mp * Np for b in range(B)], [0] * B, [int(tall)] * B, [Np], [], [], hp.mode,
+                            hp.nesterov, hp.momentum, hp.wd_coupled, sumsq)
+                s = torch.empty(B, dtype=torch.float32, device=dev)
+                s2 = torch.empty_like(s)
+                E.ns_scale(sumsq, B, 1, NS_EPS, s, s2)
+                ptrs = E.ptr_table(params)
+                pvec = _decay_vec([t.decay for t in sub], dev)
+                vvec = torch.tensor([-t.lr_eff for t in sub], dtype=torch.float32).to(dev, non_blocking=True)
+                run_ns_group(X0, s, s2, hp.ns_steps, ptrs, cols, pdt == torch.float32, tall, mw, nw,
+                             p_scale=1.0, v_scale=1.0, p_scale_vec=pvec, v_scale_vec=vvec)
+
+    # ------------------------------------------------------------------ sharded path
+    def _sharded(self, tasks: List[MuonTask], hp: MuonHyper, world: int, rank: int,
+                 group: dist.ProcessGroup, is_cuda: bool) -> None:
+        n = len(tasks)
+        shapes = [tuple(t.param.shape) for t in tasks]
+        owners = assign_owners([ns_flops(r, c, hp.ns_steps) for r, c in shapes], world)
+        rows_of = [chunk_rows(r, world) for r, _ in shapes]
+        for j, t in enumerate(tasks):
+            if t.local_param.shape[0] != rows_of[j][rank]:
+                raise RuntimeError(
+                    "MuonEngine expects FSDP2 Shard(0) parameters laid out like torch.chunk "
+                    f"(param {j}: local rows {t.local_param.shape[0]} != {rows_of[j][rank]})")
+        owned = [[j for j in range(n) if owners[j] == o] for o in range(world)]
+        # element counts of shard (j, r)
+        cnt = [[rows_of[j][r] * shapes[j][1] for r in range(world)] for j in range(n)]
+        dev = tasks[0].local_param.device
+        xdtype = torch.bfloat16 if is_cuda else torch.float32
+        # ---- 1. local momentum into the send layout [dest][j in owned(dest)][my rows x cols]
+        send_split = [sum(cnt[j][rank] for j in owned[d]) for d in range(world)]
+        send = torch.empty(sum(send_split), dtype=xdtype, device=dev)
+        send_off: Dict[int, int] = {}
+        off = 0
+        for d in range(world):
+            for j in owned[d]:
+                send_off[j] = off
+                off += cnt[j][rank]
+        sumsq = torch.zeros(n, dtype=torch.float32, device=dev)
+        if is_cuda:
+            self._cuda_local_momentum(tasks, hp, send, send_off, sumsq)
+        else:
+            for j, t in enumerate(tasks):
+                u = _momentum_torch(t, hp).float()
+                sumsq[j] = (u * u).sum()
+                send[send_off[j]:send_off[j] + cnt[j][rank]].copy_(u.reshape(-1))
+        # ---- 2. global Frobenius norms
+        dist.all_reduce(sumsq, group=group)
+        # ---- 3. shards -> owners
+        recv_split = [sum(cnt[j][r] for j in owned[rank]) for r in range(world)]
+        recv = torch.empty(sum(recv_split), dtype=xdtype, device=dev)
+        dist.all_to_all_single(recv, send, recv_split, send_split, group=group)
+        recv_base = [sum(recv_split[:r]) for r in range(world)]
+        # position of shard (j, r) inside recv
+        shard_at: Dict[Tuple[int, int], int] = {}
+        for r in range(world):
+            o = recv_base[r]
+            for j in owned[rank]:
+                shard_at[(j, r)] = o
+                o += cnt[j][r]
+        # ---- 4. NS on owned matrices; results scattered into the return layout
+        #      back layout: [dest d][j in owned(me)][rows_d(j) x cols]
+        back_split = [sum(cnt[j][d] for j in owned[rank]) for d in range(world)]
+        back = torch.empty(sum(back_split), dtype=xdtype, device=dev)
+        back_base = [sum(back_split[:d]) for d in range(world)]
+        back_at: Dict[Tuple[int, int], int] = {}
+        for d in range(world):
+            o = back_base[d]
+            for j in owned[rank]:
+                back_at[(j, d)] = o
+                o += cnt[j][d]
+        if owned[rank]:
+            if is_cuda:
+                self._cuda_owner_ns(tasks, hp, owned[rank], shapes, rows_of, cnt, world, recv, shard_at, back,
+                                    back_at, sumsq)
+            else:
+                for j in owned[rank]:
+                    rws, cls = shapes[j]
+                    full = torch.cat([recv[shard_at[(j, r)]:shard_at[(j, r)] + cnt[j][r]].view(rows_of[j][r], cls)
+                                      for r in range(world)])
+                    o = _ns_torch(full, hp.ns_steps)
+                    for d in range(world):
+                        r0 = chunk_offset(rws, world, d)
+                        back[back_at[(j, d)]:back_at[(j, d)] + cnt[j][d]].copy_(
+                            o[r0:r0 + rows_of[j][d]].reshape(-1))
+        # ---- 5. updates back to the shard holders and apply
+        ret_split = [sum(cnt[j][rank] for j in owned[o]) for o in range(world)]
+        ret = torch.empty(sum(ret_split), dtype=xdtype, device=dev)
+        dist.all_to_all_single(ret, back, ret_split, back_split, group=group)
+        ret_at: Dict[int, int] = {}
+        o_ = 0
+        for o in range(world):
+            for j in owned[o]:
+                ret_at[j] = o_
+                o_ += cnt[j][rank]
+        if is_cuda:
+            self._cuda_apply(tasks, ret, ret_at, cnt, rank)
+        else:
+            for j, t in enumerate(tasks):
+                p = t.local_param
+                u = ret[ret_at[j]:ret_at[j] + cnt[j][rank]].view(p.shape)
+                _decay_(p, t.decay)
+                p.add_(u.to(p.dtype), alpha=-t.lr_eff)
+        self.last_stats = {"matrices": float(n), "owned": float(len(owned[rank])),
+                           "exchange_bytes": float((send.numel() + ret.numel()) * send.element_size())}
+
+    # ---- CUDA pieces of the sharded path
+    def _cuda_local_momentum(self, tasks, hp, send, send_off, sumsq) -> None:
+        from .._ext import ext
+
+        E = ext()
+        idx = list(range(len(tasks)))
+        for key, js in _group_by(idx, lambda j: (tasks[j].local_grad.dtype, tasks[j].local_param.dtype)).items():
+            live = [j for j in js if tasks[j].local_param.numel() > 0]
+            if not live:
+                continue
+            grads = [tasks[j].local_grad.contiguous() for j in live]
+            params = [tasks[j].local_param for j in live]
+            bufs = [tasks[j].buf for j in live] if hp.mode != MODE_COPY else []
+            part = torch.zeros(len(live), dtype=torch.float32, device=send.device)
+            E.muon_prep(grads, bufs, params if hp.wd_coupled != 0 else [], send, [send_off[j] for j in live],
+                        [0] * len(live), [0] * len(live), [tasks[j].local_param.shape[1] for j in live], [], [],
+                        hp.mode, hp.nesterov, hp.momentum,
+                        hp.wd_coupled, part)
+            sumsq.index_copy_(0, torch.tensor(live, device=send.device), part)
+
+    def _cuda_owner_ns(self, tasks, hp, mine, shapes, rows_of, cnt, world, recv, shard_at, back, back_at,
+                       sumsq) -> None:
+        from .._ext import ext
+        from ..ops.ns_cuda import round_up, run_ns_group, wide_shape
+
+        E = ext()
+        dev = recv.device
+        # group owned matrices by their wide shape (tall ones transposed), so e.g. w1/w3 (14336x4096)
+        # and w2 (4096x14336) of a SwiGLU FFN share one batched chain
+        groups = _group_by(mine, lambda j: wide_shape(*shapes[j])[:2])
+        for (mw, nw), js in groups.items():
+            Mp, Np = round_up(mw), round_up(nw)
+            per = 2 * Mp * Np * 2 + 2 * Mp * Mp * 2
+            chunk = max(1, min(len(js), self.max_workspace_bytes // max(per, 1)))
+            for c0 in range(0, len(js), chunk):
+                sub = js[c0:c0 + chunk]
+                B = len(sub)
+                padded = (Mp != mw) or (Np != nw)
+                X0 = (torch.zeros if padded else torch.empty)(B, Mp, Np, dtype=torch.bfloat16, device=dev)
+                srcs, offs, row0, trs = [], [], [], []
+                for b, j in enumerate(sub):
+                    rws, cls = shapes[j]
+                    tall = rws > cls
+                    for r in range(world):
+                        if rows_of[j][r] == 0:
+                            continue
+                        st = shard_at[(j, r)]
+                        srcs.append(recv[st:st + cnt[j][r]].view(rows_of[j][r], cls))
+                        offs.append(b * Mp * Np)
+                        row0.append(chunk_offset(rws, world, r))
+                        trs.append(int(tall))
+                E.muon_prep(srcs, [], [], X0, offs, row0, trs, [Np], [], [], MODE_COPY, False, 0.0, 0.0, None)
+                ssq = sumsq.index_select(0, torch.tensor(sub, device=dev))
+                s = torch.empty(B, dtype=torch.float32, device=dev)
+                s2 = torch.empty_like(s)
+                E.ns_scale(ssq, B, 1, NS_EPS, s, s2)
+                seg_views, meta = [], []
+                for j in sub:
+                    rws, cls = shapes[j]
+                    cs = (rws + world - 1) // world
+                    for d in range(world):
+                        st = back_at[(j, d)]
+                        # empty trailing shards still need a valid pointer
+                        seg_views.append(back[st:st + max(cnt[j][d], 1)] if cnt[j][d] else back[:1])
+                    meta += [cls, int(rws > cls), cs]
+                ptrs = E.ptr_table(seg_views)
+                meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
+                run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
+                             nseg=world, out_meta=meta_t)
+
+    def _cuda_apply(self, tasks, ret, ret_at, cnt, rank) -> None:
+        from .._ext import ext
+
+        E = ext()
+        idx = [j for j in range(len(tasks)) if tasks[j].local_param.numel() > 0]
+        for key, js in _group_by(idx, lambda j: tasks[j].local_param.dtype).items():
+            srcs = [ret[ret_at[j]:ret_at[j] + cnt[j][rank]].view(tasks[j].local_param.shape) for j in js]
+            params = [tasks[j].local_param for j in js]
+            E.muon_prep(srcs, [], params, None, [], [], [], [0], [_decay_float(tasks[j].decay) for j in js],
+                        [-tasks[j].lr_eff for j in js], MODE_COPY, False, 0.0, 0.0, None)
+
+
+# ---------------------------------------------------------------------- helpers
+def _group_by(items, key) -> "OrderedDict":
+    out: "OrderedDict" = OrderedDict()
+    for it in items:
+        out.setdefault(key(it), []).append(it)
+    return out
+
+
+def _momentum_torch(t: MuonTask, hp: MuonHyper) -> torch.Tensor:
+    """Reference momentum math (optimizer.py:142-150 / fsdp.py:330-341) on the local shard."""
+    g = t.local_grad
+    if hp.wd_coupled != 0:
+        g = g + hp.wd_coupled * t.local_param
+    if hp.mode == MODE_COPY:
+        return g
+    buf = t.buf
+    gb = g.to(buf.dtype)
+    if hp.mode == MODE_EMA:
+        buf.lerp_(gb, 1 - hp.momentum)
+    else:
+        buf.mul_(hp.momentum).add_(gb)
+    if hp.nesterov:
+        return gb + hp.momentum * buf
+    return buf.clone()
+
+
+def _decay_(p: torch.Tensor, decay) -> None:
+    if isinstance(decay, torch.Tensor):
+        p.mul_(decay.to(p.dtype))
+    elif decay != 1.0:
+        p.mul_(decay)
+
+
+def _decay_float(decay) -> float:
+    return float(decay.item()) if isinstance(decay, torch.Tensor) else float(decay)
+
+
+def _decay_vec(decays, dev) -> torch.Tensor:
+    if all(not isinstance(d, torch.Tensor) for d in decays):
+        return torch.tensor([float(d) for d in decays], dtype=torch.float32).to(dev, non_blocking=True)
+    return torch.stack([torch.as_tensor(d, dtype=torch.float32, device=dev).reshape(()) for d in decays])
