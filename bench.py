@@ -1,0 +1,281 @@
+"""Headline benchmark: Llama-3-8B FSDP2 + Muon training throughput (tokens/s) on N B200 GPUs.
+
+Workload (one optimizer step per rank): 4 micro-batches (grad accumulation) of 1 sequence x 4096
+uniform random tokens, bf16 parameters/compute, fp32 Muon momentum; Muon (lr 0.02, momentum
+0.95, weight decay 0.01, 5 NS steps) on every attention/FFN matrix, AdamW (lr 1e-3, wd 0.01) on
+embeddings, norms and the LM head.  FSDP2 ``fully_shard`` on every decoder layer and the root.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Timing: W untimed steps, then K steps bracketed by barrier + synchronize, timed with CUDA events
+on the launching stream; the MAX over ranks is reported.  The per-step working set (16 GB of
+weights, tens of GB of activations) is far larger than the 126 MB L2, so no L2 flush is needed.
+A second K-step loop measures the same metric end to end through ``Trainer.train_step`` (host
+->device copy of the pinned token batch and a device->host read of the loss every step).
+Rank 0 prints one JSON line.
+
+``--impl reference`` runs the unmodified reference package (installed under baseline/_ref) on a
+stock ``transformers`` Llama with the same config, FSDP2 wrapping, data and hyper-parameters.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import socket
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+METRIC = "Llama-8B FSDP2+Muon tokens/s at 1/2/4/8 B200; Muon optimizer.step() ms"
+MODEL_DESC = "Llama-3-8B (32 layers, d4096, 32q/8kv heads, hd128, SwiGLU 14336, RMSNorm, RoPE 500000, vocab 128256)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--grad-accum", type=int, default=4)
+    ap.add_argument("--micro-bs", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=32, help="debug only: fewer layers is not the named config")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def init_dist():
+    if "RANK" not in os.environ:
+        os.environ.update(RANK="0", WORLD_SIZE="1", LOCAL_RANK="0", MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(free_port()))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
+    return dist.get_rank(), dist.get_world_size(), local
+
+
+def baseline_value():
+    try:
+        with open(os.path.join(HERE, "BASELINE.json")) as f:
+            pub = json.load(f).get("published") or {}
+        v = pub.get("tokens_per_s") if isinstance(pub, dict) else None
+        return float(v) if v else None
+    except Exception:
+        return None
+
+
+def synthetic_tokens(step: int, ga: int, mbs: int, seq: int, vocab: int, rank: int, device="cpu"):
+    g = torch.Generator().manual_seed(10007 * step + rank)
+    return torch.randint(0, vocab, (ga, mbs, seq + 1), generator=g).to(device)
+
+
+# ------------------------------------------------------------------------------ our arm
+def build_ours(args, world, local):
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from my_muon_fsdp2_b200 import FusedAdamW, MuonOptimizer
+    from my_muon_fsdp2_b200.models.llama import Llama, LlamaConfig, apply_fsdp
+
+    cfg = LlamaConfig.llama3_8b()
+    cfg.n_layers = args.layers
+    mesh = init_device_mesh("cuda", (world,))
+    with torch.device("meta"):
+        model = Llama(cfg).to(torch.bfloat16)
+    apply_fsdp(model, mesh)
+    model.to_empty(device=torch.device("cuda", local))
+    model.init_weights(seed=0)
+    muon_names = set(model.muon_param_names())
+    muon_p = [p for n, p in model.named_parameters() if n in muon_names]
+    adam_p = [p for n, p in model.named_parameters() if n not in muon_names]
+    opts = [MuonOptimizer(muon_p, lr=0.02, momentum=0.95, weight_decay=0.01, nesterov=False, ns_steps=5),
+            FusedAdamW(adam_p, lr=1e-3, weight_decay=0.01)]
+    return model, opts, cfg.vocab_size
+
+
+def launch_counter():
+    from my_muon_fsdp2_b200._ext import launch_count
+
+    return launch_count
+
+
+# ------------------------------------------------------------------------ reference arm
+def build_reference(args, world, local):
+    ref = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "muon_fsdp")):
+        raise RuntimeError("reference package not installed under baseline/_ref")
+    sys.path.insert(0, ref)
+    import muon_fsdp  # noqa: F401  (the unmodified reference)
+    from muon_fsdp import MuonOptimizer as RefMuon
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.fsdp import fully_shard
+    from transformers import LlamaConfig as HFConfig
+    from transformers import LlamaForCausalLM
+
+    hf = HFConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=args.layers,
+                  num_attention_heads=32, num_key_value_heads=8, rope_theta=500000.0, max_position_embeddings=8192,
+                  rms_norm_eps=1e-5, tie_word_embeddings=False, attn_implementation="sdpa", use_cache=False)
+    mesh = init_device_mesh("cuda", (world,))
+    with torch.device("meta"):
+        model = LlamaForCausalLM(hf).to(torch.bfloat16)
+    for layer in model.model.layers:
+        fully_shard(layer, mesh=mesh)
+    fully_shard(model, mesh=mesh)
+    model.to_empty(device=torch.device("cuda", local))
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            loc = p.to_local()
+            if "norm" in n:
+                loc.fill_(1.0)
+            else:
+                loc.normal_(0.0, 0.02)
+    muon_p = [p for n, p in model.named_parameters() if p.dim() == 2 and (".self_attn." in n or ".mlp." in n)]
+    ids = {id(p) for p in muon_p}
+    adam_p = [p for p in model.parameters() if id(p) not in ids]
+    opts = [RefMuon(muon_p, lr=0.02, momentum=0.95, weight_decay=0.01, nesterov=False, ns_steps=5),
+            torch.optim.AdamW(adam_p, lr=1e-3, weight_decay=0.01)]
+    return model, opts, hf.vocab_size
+
+
+class RefTrainer:
+    """The reference has no trainer API for this model; its examples' loop (train_gpt.py:330-383)."""
+
+    def __init__(self, model, opts, ga, step_timer=None):
+        self.model, self.opts, self.ga, self.step_timer = model, opts, ga, step_timer
+
+    def step_on_device(self, tokens):
+        total = None
+        for i in range(self.ga):
+            self.model.set_requires_gradient_sync(i == self.ga - 1)
+            t = tokens[i]
+            loss = self.model(input_ids=t[:, :-1], labels=t[:, :-1]).loss / self.ga
+            loss.backward()
+            total = loss.detach() if total is None else total + loss.detach()
+        if self.step_timer is not None:
+            self.step_timer.start()
+        for o in self.opts:
+            o.step()
+        if self.step_timer is not None:
+            self.step_timer.stop()
+        for o in self.opts:
+            o.zero_grad(set_to_none=True)
+        return total
+
+    def train_step(self, batch):
+        return float(self.step_on_device(batch.to("cuda", non_blocking=True)).item())
+
+
+# ---------------------------------------------------------------------------------- main
+def main():
+    args = parse()
+    rank, world, local = init_dist()
+    from my_muon_fsdp2_b200.utils.clocks import ClockSampler, physical_gpu_index
+    from my_muon_fsdp2_b200.utils.timing import EventTimer, max_over_ranks
+
+    ga, mbs, seq = args.grad_accum, args.micro_bs, args.seq
+    tokens_per_step = world * ga * mbs * seq
+    try:
+        if args.impl == "reference":
+            model, opts, vocab = build_reference(args, world, local)
+            count = None
+        else:
+            model, opts, vocab = build_ours(args, world, local)
+            count = launch_counter()
+    except Exception as e:  # reference cannot be built/installed: say so in one line
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}))
+            dist.destroy_process_group()
+            return
+        raise
+    opt_timer = EventTimer()
+    if args.impl == "reference":
+        trainer = RefTrainer(model, opts, ga, step_timer=opt_timer)
+    else:
+        from my_muon_fsdp2_b200.train import Trainer
+
+        trainer = Trainer(model, opts, grad_accum=ga, step_timer=opt_timer)
+
+    dev_batches = [synthetic_tokens(s, ga, mbs, seq, vocab, rank, device="cuda") for s in range(2)]
+    for s in range(args.warmup):
+        trainer.step_on_device(dev_batches[s % 2])
+    torch.cuda.synchronize()
+    if args.impl == "ours":
+        from my_muon_fsdp2_b200._ext import check_device_error
+
+        check_device_error(local)
+    opt_timer.pairs.clear()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(physical_gpu_index(local))
+    clocks.start()
+    n0 = count() if count else 0
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for s in range(args.steps):
+        loss = trainer.step_on_device(dev_batches[s % 2])
+    end.record()
+    torch.cuda.synchronize()
+    launches = (count() - n0) if count else None
+    clk = clocks.stop()
+    dist.barrier()
+    dev_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    opt_ms = max_over_ranks(opt_timer.mean_ms())
+    final_loss = float(loss.item())
+
+    e2e = None
+    if not args.no_e2e:
+        host = [synthetic_tokens(100 + s, ga, mbs, seq, vocab, rank).pin_memory() for s in range(2)]
+        trainer.train_step(host[0])  # settle
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for s in range(args.steps):
+            trainer.train_step(host[s % 2])
+        t1.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        e2e = {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": host[0].numel() * host[0].element_size(), "d2h_bytes_per_step": 4,
+               "ms_per_step": e2e_ms, "api": ("my_muon_fsdp2_b200.train.Trainer.train_step" if args.impl == "ours"
+                                               else "reference example loop (no trainer API in the reference)")}
+
+    if rank == 0:
+        value = tokens_per_step / (dev_ms / 1e3)
+        base = baseline_value()
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / base) if base else None, "dtype": "bf16",
+            "data": "synthetic uniform random tokens; random-init weights",
+            "optimizer_step_ms": opt_ms,
+            "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
+                       "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
+                       "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",
+                       "tokens_per_step": tokens_per_step,
+                       "l2": "no flush: per-step working set (16 GB bf16 weights + activations) >> 126 MB L2",
+                       "optimizers": "Muon(attn+FFN matrices, lr .02, mom .95, wd .01, ns 5) + AdamW(rest, lr 1e-3)"},
+            "clocks": clk, "e2e": e2e, "gpu_launches": launches, "final_loss": final_loss,
+        }
+        if args.impl == "reference":
+            out["impl"] = "reference"
+        print(json.dumps(out))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,57 @@
+"""Training-step API (parity with the reference trainers' loop, examples/train_gpt.py:298-402).
+
+``Trainer.train_step(batch)`` is the end-to-end call a user makes: it copies the step's
+token batch from (pinned) host memory to the GPU, runs ``grad_accum`` micro-batches of
+forward/backward (FSDP2 gradient sync only on the last one), steps every optimizer, clears
+gradients and returns the loss as a Python float (one device->host read).
+"""
+from __future__ import annotations
+
+from typing import Iterable, List, Optional, Sequence
+
+import torch
+import torch.nn as nn
+
+from ..parallel.fsdp_utils import is_fsdp_module
+
+
+class Trainer:
+    def __init__(self, model: nn.Module, optimizers: Sequence, grad_accum: int = 1, device=None,
+                 step_timer=None):
+        self.model = model
+        self.optimizers = list(optimizers)
+        self.grad_accum = int(grad_accum)
+        self.device = torch.device(device) if device is not None else next(model.parameters()).device
+        self.step_timer = step_timer  # optional EventTimer around the optimizer steps
+        self.fsdp = is_fsdp_module(model)
+
+    def _micro(self, tokens: torch.Tensor, i: int):
+        last = i == self.grad_accum - 1
+        if self.fsdp:
+            self.model.set_requires_gradient_sync(last)
+        t = tokens[i]
+        loss = self.model(t[:, :-1], t[:, 1:]) / self.grad_accum
+        loss.backward()
+        return loss
+
+    def step_on_device(self, tokens: torch.Tensor) -> torch.Tensor:
+        """One optimizer step on a device batch [grad_accum, micro_bs, seq+1]; returns the loss
+        (device tensor, no synchronisation)."""
+        total = None
+        for i in range(self.grad_accum):
+            l = self._micro(tokens, i).detach()
+            total = l if total is None else total + l
+        if self.step_timer is not None:
+            self.step_timer.start()
+        for opt in self.optimizers:
+            opt.step()
+        if self.step_timer is not None:
+            self.step_timer.stop()
+        for opt in self.optimizers:
+            opt.zero_grad(set_to_none=True)
+        return total
+
+    def train_step(self, batch: torch.Tensor) -> float:
+        """End-to-end step from a host batch [grad_accum, micro_bs, seq+1] (int64)."""
+        tokens = batch.to(self.device, non_blocking=True)
+        return float(self.step_on_device(tokens).item())
