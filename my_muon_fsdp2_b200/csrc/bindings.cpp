@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "kernels.h"
+#include "symm_comm.h"
 
 namespace {
 
@@ -155,6 +156,13 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
   TORCH_CHECK(params.empty() || (int)params.size() == n, "mmf: params size");
   const bool grad_f32 = grads[0].scalar_type() == torch::kFloat32;
   const bool param_f32 = !params.empty() && params[0].scalar_type() == torch::kFloat32;
+  if (dst.has_value()) {
+    TORCH_CHECK((int)dst_offsets.size() == n && (int)dst_row0.size() == n && (int)transposed.size() == n &&
+                    (dst_ld.size() == 1 || (int)dst_ld.size() == n),
+                "mmf: per-tensor destination lists must match the number of tensors");
+  } else {
+    TORCH_CHECK((int)p_scale.size() == n && (int)v_scale.size() == n, "mmf: per-tensor scale lists size");
+  }
   std::vector<mmf::PrepDesc> d(n);
   int max_tiles = 1;
   for (int i = 0; i < n; ++i) {
@@ -191,13 +199,9 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
     const int tiles = ((d[i].rows + 63) / 64) * ((d[i].cols + 63) / 64);
     if (tiles > max_tiles) max_tiles = tiles;
   }
-  if (mode != 0) TORCH_CHECK(!bufs.empty(), "mmf: momentum modes need buffers");
-  if (dst.has_value())
-    TORCH_CHECK((int)dst_offsets.size() == n && (int)dst_row0.size() == n && (int)transposed.size() == n &&
-                    (dst_ld.size() == 1 || (int)dst_ld.size() == n),
-                "mmf: per-tensor destination lists must match the number of tensors");
-  else
-    TORCH_CHECK((int)p_scale.size() == n && (int)v_scale.size() == n, "mmf: per-tensor scale lists size");
+  if (mode != 0) {
+    TORCH_CHECK(!bufs.empty(), "mmf: momentum modes need buffers");
+  }
   if (dst.has_value()) check_bf16_contig(*dst, "dst");
   Tensor dd = upload(d, dev);
   mmf::PrepArgs a{};
@@ -432,6 +436,27 @@ void power_iteration(Tensor W, Tensor u, Tensor v, Tensor sigma, int64_t iters, 
                        static_cast<int>(iters), static_cast<float>(eps), work.data_ptr<float>(), cur_stream());
 }
 
+// pad_ptrs / payload_ptrs: device int64 tensors of per-rank addresses (symmetric memory).
+void symm_barrier(Tensor pad_ptrs, int64_t rank, int64_t ws, int64_t epoch, int64_t slot_base,
+                  c10::optional<Tensor> payload, c10::optional<Tensor> payload_ptrs, double timeout_s) {
+  check_cuda(pad_ptrs, "pad_ptrs");
+  TORCH_CHECK(pad_ptrs.scalar_type() == torch::kInt64 && pad_ptrs.numel() == ws, "mmf: pad_ptrs must be int64[ws]");
+  const float* pl = nullptr;
+  int n = 0;
+  const int64_t* pp = nullptr;
+  if (payload.has_value()) {
+    TORCH_CHECK(payload_ptrs.has_value() && payload_ptrs->numel() == ws, "mmf: payload needs payload_ptrs[ws]");
+    TORCH_CHECK(payload->scalar_type() == torch::kFloat32 && payload->is_contiguous(), "mmf: payload must be fp32");
+    pl = payload->data_ptr<float>();
+    n = static_cast<int>(payload->numel());
+    pp = payload_ptrs->data_ptr<int64_t>();
+  }
+  const c10::cuda::CUDAGuard guard(pad_ptrs.device());
+  mmf::symm_barrier(pad_ptrs.data_ptr<int64_t>(), static_cast<int>(rank), static_cast<int>(ws),
+                    static_cast<uint32_t>(epoch), static_cast<int>(slot_base), pl, n, pp,
+                    static_cast<uint64_t>(timeout_s * 1e9), cur_stream());
+}
+
 int64_t device_error(int64_t device) {
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   return mmf::read_and_clear_device_error(static_cast<int>(device), cur_stream());
@@ -461,6 +486,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gelu_bwd", &gelu_bwd);
   m.def("cross_entropy_", &cross_entropy_);
   m.def("power_iteration", &power_iteration);
+  m.def("symm_barrier", &symm_barrier);
   m.def("device_error", &device_error);
   m.def("launch_count", &launch_count);
 }

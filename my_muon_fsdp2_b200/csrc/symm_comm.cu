@@ -1,0 +1,84 @@
+// Cross-GPU signalling over NVLink peer memory (buffers from PyTorch symmetric memory).
+//
+// symm_barrier: every rank writes `epoch` into slot [slot_base + my_rank] of every peer's
+// signal pad (release, system scope) and then waits until all ws slots of its own pad reach
+// `epoch` (acquire, system scope).  Optionally, before signalling, it copies a small fp32
+// payload (the per-matrix partial sums of squares of the Muon step) into row `my_rank` of
+// every peer's payload buffer, so that after the barrier each rank holds all ranks' rows.
+//
+// Waits are bounded: after MMF_WAIT_TIMEOUT_NS the kernel records ERR_PEER_FLAG_TIMEOUT in
+// the error word and returns (no trap, no hang); the host raises on the next check.
+// Plain loads/stores only; no multimem and no TMA here.
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "kernels.h"
+#include "symm_comm.h"
+#include "tc_common.cuh"
+
+namespace mmf {
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void symm_barrier_kernel(const int64_t* __restrict__ pad_ptrs, int rank, int ws, uint32_t epoch,
+                                    int slot_base, const float* __restrict__ payload, int n_payload,
+                                    const int64_t* __restrict__ payload_ptrs, int* err, uint64_t timeout_ns) {
+  // 1. payload rows into every peer (all threads cooperate), then make them visible system-wide
+  if (payload != nullptr && n_payload > 0) {
+    for (int64_t e = threadIdx.x; e < static_cast<int64_t>(ws) * n_payload; e += blockDim.x) {
+      const int peer = static_cast<int>(e / n_payload);
+      const int i = static_cast<int>(e % n_payload);
+      float* dst = reinterpret_cast<float*>(payload_ptrs[peer]);
+      dst[static_cast<int64_t>(rank) * n_payload + i] = payload[i];
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  // 2. signal every peer
+  for (int peer = threadIdx.x; peer < ws; peer += blockDim.x) {
+    uint32_t* pad = reinterpret_cast<uint32_t*>(pad_ptrs[peer]);
+    st_release_sys(pad + slot_base + rank, epoch);
+  }
+  // 3. wait for every peer's signal in my own pad (bounded)
+  const uint32_t* mine = reinterpret_cast<const uint32_t*>(pad_ptrs[rank]);
+  for (int peer = threadIdx.x; peer < ws; peer += blockDim.x) {
+    const uint32_t* slot = mine + slot_base + peer;
+    if (static_cast<int32_t>(ld_acquire_sys(slot) - epoch) >= 0) continue;
+    const uint64_t t0 = globaltimer_ns();
+    while (static_cast<int32_t>(ld_acquire_sys(slot) - epoch) < 0) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        atomicCAS(err, 0, ERR_PEER_FLAG_TIMEOUT);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+}
+
+}  // namespace
+
+void symm_barrier(const int64_t* pad_ptrs, int rank, int ws, uint32_t epoch, int slot_base, const float* payload,
+                  int n_payload, const int64_t* payload_ptrs, uint64_t timeout_ns, cudaStream_t stream) {
+  if (ws < 1 || rank < 0 || rank >= ws) throw std::runtime_error("mmf: bad rank/world for symm_barrier");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  symm_barrier_kernel<<<1, 256, 0, stream>>>(pad_ptrs, rank, ws, epoch, slot_base, payload, n_payload, payload_ptrs,
+                                             device_error_word(dev), timeout_ns);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: symm_barrier launch failed: ") + cudaGetErrorString(e));
+}
+
+}  // namespace mmf

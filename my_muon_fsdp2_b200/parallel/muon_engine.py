@@ -149,7 +149,20 @@ class MuonEngine:
             else:
                 self._local_cpu(local, hp)
         if sharded:
-            self._sharded(sharded, hp, world, rank, group, is_cuda)
+            if is_cuda and self._use_p2p(group):
+                self._sharded_p2p(sharded, hp, world, rank, group)
+            else:
+                self._sharded(sharded, hp, world, rank, group, is_cuda)
+
+    def _use_p2p(self, group) -> bool:
+        if self.comm == "nccl":
+            return False
+        from .symm import p2p_supported
+
+        ok = p2p_supported(group)
+        if self.comm == "p2p" and not ok:
+            raise RuntimeError("comm='p2p' needs an NCCL process group on CUDA devices")
+        return ok
 
     # ------------------------------------------------------------------ elementwise (no NS)
     def _elementwise(self, tasks: List[MuonTask], hp: MuonHyper, is_cuda: bool) -> None:
@@ -306,6 +319,101 @@ class MuonEngine:
                 p.add_(u.to(p.dtype), alpha=-t.lr_eff)
         self.last_stats = {"matrices": float(n), "owned": float(len(owned[rank])),
                            "exchange_bytes": float((send.numel() + ret.numel()) * send.element_size())}
+
+    # ------------------------------------------------------------------ sharded, P2P
+    def _sharded_p2p(self, tasks: List[MuonTask], hp: MuonHyper, world: int, rank: int,
+                     group: dist.ProcessGroup) -> None:
+        """Same schedule as :meth:`_sharded`, with the exchange done by our kernels over NVLink:
+        momentum -> own symmetric buffer; barrier (+ partial norms to every peer); owner assembly
+        reads peer shards (P2P loads); final NS epilogue stores each rank's rows into that rank's
+        buffer (P2P stores); barrier; local apply."""
+        from .._ext import ext
+        from ..ops.ns_cuda import round_up, run_ns_group, wide_shape
+        from .symm import workspace_for
+
+        E = ext()
+        n = len(tasks)
+        dev = tasks[0].local_param.device
+        shapes = [tuple(t.param.shape) for t in tasks]
+        owners = assign_owners([ns_flops(r, c, hp.ns_steps) for r, c in shapes], world)
+        rows_of = [chunk_rows(r, world) for r, _ in shapes]
+        for j, t in enumerate(tasks):
+            if t.local_param.shape[0] != rows_of[j][rank]:
+                raise RuntimeError("MuonEngine expects FSDP2 Shard(0) parameters laid out like torch.chunk")
+        cnt = [[rows_of[j][r] * shapes[j][1] for r in range(world)] for j in range(n)]
+        off = [[0] * n for _ in range(world)]
+        for r in range(world):
+            o = 0
+            for j in range(n):
+                off[r][j] = o
+                o += cnt[j][r]
+        total = max(sum(cnt[j][r] for j in range(n)) for r in range(world))
+        sw = workspace_for(group, dev)
+        sw.ensure(total, n)
+        # 1. momentum of local shards -> own symmetric buffer; partial sums of squares
+        part = torch.zeros(n, dtype=torch.float32, device=dev)
+        idx = [j for j in range(n) if cnt[j][rank] > 0]
+        for key, js in _group_by(idx, lambda j: (tasks[j].local_grad.dtype, tasks[j].local_param.dtype)).items():
+            grads = [tasks[j].local_grad.contiguous() for j in js]
+            params = [tasks[j].local_param for j in js]
+            bufs = [tasks[j].buf for j in js] if hp.mode != MODE_COPY else []
+            sub = torch.zeros(len(js), dtype=torch.float32, device=dev)
+            E.muon_prep(grads, bufs, params if hp.wd_coupled != 0 else [], sw.buf, [off[rank][j] for j in js],
+                        [0] * len(js), [0] * len(js), [shapes[j][1] for j in js], [], [], hp.mode, hp.nesterov,
+                        hp.momentum, hp.wd_coupled, sub)
+            part.index_copy_(0, torch.tensor(js, device=dev), sub)
+        # 2. barrier: every rank's shards are in place; all partial norms delivered to all ranks
+        sw.barrier(payload=part)
+        rows_ssq = sw.payload_rows()  # [world, n]
+        mine = [j for j in range(n) if owners[j] == rank]
+        groups = _group_by(mine, lambda j: wide_shape(*shapes[j])[:2])
+        for (mw, nw), js in groups.items():
+            Mp, Np = round_up(mw), round_up(nw)
+            per = 2 * Mp * Np * 2 + 2 * Mp * Mp * 2
+            chunk = max(1, min(len(js), self.max_workspace_bytes // max(per, 1)))
+            for c0 in range(0, len(js), chunk):
+                sub_js = js[c0:c0 + chunk]
+                B = len(sub_js)
+                padded = (Mp != mw) or (Np != nw)
+                X0 = (torch.zeros if padded else torch.empty)(B, Mp, Np, dtype=torch.bfloat16, device=dev)
+                srcs, offs, row0, trs = [], [], [], []
+                for b, j in enumerate(sub_js):
+                    rws, cls = shapes[j]
+                    for r in range(world):
+                        if rows_of[j][r] == 0:
+                            continue
+                        # 3. P2P loads: the assembly kernel reads rank r's shard in place
+                        srcs.append(sw.peer_view(r, off[r][j], (rows_of[j][r], cls)))
+                        offs.append(b * Mp * Np)
+                        row0.append(chunk_offset(rws, world, r))
+                        trs.append(int(rws > cls))
+                E.muon_prep(srcs, [], [], X0, offs, row0, trs, [Np], [], [], MODE_COPY, False, 0.0, 0.0, None)
+                jt = torch.tensor(sub_js, device=dev)
+                ssq = rows_ssq.index_select(1, jt).contiguous()  # [world, B]
+                s = torch.empty(B, dtype=torch.float32, device=dev)
+                s2 = torch.empty_like(s)
+                E.ns_scale(ssq, B, world, NS_EPS, s, s2)
+                addrs, meta = [], []
+                for j in sub_js:
+                    rws, cls = shapes[j]
+                    for d in range(world):
+                        # 4. P2P stores: rows of rank d go straight into rank d's buffer
+                        addrs.append(sw.peer_addr(d, off[d][j]))
+                    meta += [cls, int(rws > cls), (rws + world - 1) // world]
+                ptrs = torch.tensor(addrs, dtype=torch.int64).to(dev, non_blocking=True)
+                meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
+                run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
+                             nseg=world, out_meta=meta_t)
+        # 5. barrier: all owners' results have landed
+        sw.barrier()
+        # 6. local apply from the own buffer
+        for key, js in _group_by(idx, lambda j: tasks[j].local_param.dtype).items():
+            srcs = [sw.peer_view(rank, off[rank][j], tuple(tasks[j].local_param.shape)) for j in js]
+            params = [tasks[j].local_param for j in js]
+            E.muon_prep(srcs, [], params, None, [], [], [], [0], [_decay_float(tasks[j].decay) for j in js],
+                        [-tasks[j].lr_eff for j in js], MODE_COPY, False, 0.0, 0.0, None)
+        self.last_stats = {"matrices": float(n), "owned": float(len(mine)), "exchange_bytes": float(2 * 2 * total),
+                           "comm": "p2p"}
 
     # ---- CUDA pieces of the sharded path
     def _cuda_local_momentum(self, tasks, hp, send, send_off, sumsq) -> None:
