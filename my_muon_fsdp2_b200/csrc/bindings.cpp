@@ -165,6 +165,7 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
   }
   std::vector<mmf::PrepDesc> d(n);
   int max_tiles = 1;
+  bool vec8 = true;
   for (int i = 0; i < n; ++i) {
     const Tensor& g = grads[i];
     check_cuda(g, "grad");
@@ -198,6 +199,10 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
     }
     const int tiles = ((d[i].rows + 63) / 64) * ((d[i].cols + 63) / 64);
     if (tiles > max_tiles) max_tiles = tiles;
+    auto al16 = [](int64_t p) { return (p & 15) == 0; };
+    bool v = (d[i].cols % 8 == 0) && al16(d[i].grad) && al16(d[i].buf) && al16(d[i].param);
+    if (dst.has_value()) v = v && al16(d[i].dst) && (d[i].dst_ld % 8 == 0) && (d[i].dst_row0 % 8 == 0);
+    if (!v) vec8 = false;
   }
   if (mode != 0) {
     TORCH_CHECK(!bufs.empty(), "mmf: momentum modes need buffers");
@@ -215,6 +220,7 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
   a.mu = static_cast<float>(mu);
   a.wd_coupled = static_cast<float>(wd_coupled);
   a.sumsq = sumsq.has_value() ? sumsq->data_ptr<float>() : nullptr;
+  a.vec8 = vec8 ? 1 : 0;
   mmf::muon_prep(a, cur_stream());
 }
 

@@ -108,6 +108,7 @@ struct PrepArgs {
   float mu;
   float wd_coupled;
   float* sumsq;           // device [n] (may be null)
+  int vec8;               // all tensors allow 16-byte vector access (host-checked)
 };
 void muon_prep(const PrepArgs& args, cudaStream_t stream);
 

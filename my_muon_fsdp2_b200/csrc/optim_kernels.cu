@@ -50,15 +50,53 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
 
 constexpr int PT = 64;  // prep tile edge
 
-template <bool GRAD_F32, bool PARAM_F32>
+// 8-wide vector helpers (16-byte bf16 / 2 x 16-byte fp32 accesses)
+template <bool F32>
+__device__ __forceinline__ void ld8(const void* base, int64_t i, float* v) {
+  if (F32) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
+    float4 a = p[0], b = p[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(base) + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(h[e]);
+      v[2 * e] = f.x;
+      v[2 * e + 1] = f.y;
+    }
+  }
+}
+template <bool F32>
+__device__ __forceinline__ void st8(void* base, int64_t i, const float* v) {
+  if (F32) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 w;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + i) = w;
+  }
+}
+
+// VEC == 8: each thread handles 8 consecutive columns (requires cols % 8 == 0, 16-byte aligned
+// tensors, dst_ld % 8 == 0 and dst_row0 % 8 == 0 — checked on the host).  Loads from peer
+// memory (the P2P assembly of the sharded Muon step) are 16-byte requests.
+template <bool GRAD_F32, bool PARAM_F32, int VEC>
 __global__ void __launch_bounds__(256) muon_prep_kernel(const PrepArgs a) {
   const PrepDesc d = a.descs[blockIdx.y];
   const int tiles_c = (d.cols + PT - 1) / PT;
   const int tiles = ((d.rows + PT - 1) / PT) * tiles_c;
   __shared__ float tile[PT][PT + 1];
   __shared__ float red[8];
-  const int tx = threadIdx.x & (PT - 1);
-  const int ty = threadIdx.x >> 6;  // 0..3
+  constexpr int TPR = PT / VEC;          // threads per tile row
+  constexpr int RPP = 256 / TPR;         // rows per pass
+  const int tx = threadIdx.x % TPR;
+  const int ty = threadIdx.x / TPR;
   const void* G = reinterpret_cast<const void*>(d.grad);
   float* BUF = reinterpret_cast<float*>(d.buf);
   void* P = reinterpret_cast<void*>(d.param);
@@ -67,43 +105,82 @@ __global__ void __launch_bounds__(256) muon_prep_kernel(const PrepArgs a) {
   float sq = 0.f;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int r0 = (t / tiles_c) * PT, c0 = (t % tiles_c) * PT;
-    const int c = c0 + tx;
-#pragma unroll 4
-    for (int rr = ty; rr < PT; rr += 4) {
+    const int c = c0 + tx * VEC;
+#pragma unroll 2
+    for (int rr = ty; rr < PT; rr += RPP) {
       const int r = r0 + rr;
-      float u = 0.f;
+      float u[VEC];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) u[e] = 0.f;
       if (r < d.rows && c < d.cols) {
         const int64_t i = static_cast<int64_t>(r) * d.cols + c;
-        float g = ld_val<GRAD_F32>(G, i);
-        if (a.wd_coupled != 0.f && P) g = fmaf(a.wd_coupled, ld_val<PARAM_F32>(P, i), g);
-        if (a.mode == 0) {
-          u = g;
+        float g[VEC];
+        if (VEC == 8) {
+          ld8<GRAD_F32>(G, i, g);
         } else {
-          float b = BUF[i];
-          b = (a.mode == 1) ? fmaf(mu, b - g, g) /* mu*b + (1-mu)*g */ : fmaf(mu, b, g);
-          BUF[i] = b;
-          u = a.nesterov ? fmaf(mu, b, g) : b;
+          g[0] = ld_val<GRAD_F32>(G, i);
+        }
+        if (a.wd_coupled != 0.f && P) {
+          float pv[VEC];
+          if (VEC == 8) ld8<PARAM_F32>(P, i, pv); else pv[0] = ld_val<PARAM_F32>(P, i);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) g[e] = fmaf(a.wd_coupled, pv[e], g[e]);
+        }
+        if (a.mode == 0) {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) u[e] = g[e];
+        } else {
+          float b[VEC];
+          if (VEC == 8) ld8<true>(BUF, i, b); else b[0] = BUF[i];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            b[e] = (a.mode == 1) ? fmaf(mu, b[e] - g[e], g[e]) : fmaf(mu, b[e], g[e]);
+            u[e] = a.nesterov ? fmaf(mu, b[e], g[e]) : b[e];
+          }
+          if (VEC == 8) st8<true>(BUF, i, b); else BUF[i] = b[0];
         }
         if (!DST) {
-          const float pv = (d.p_scale != 0.f) ? ld_val<PARAM_F32>(P, i) : 0.f;
-          st_val<PARAM_F32>(P, i, fmaf(d.p_scale, pv, d.v_scale * u));
+          float pv[VEC];
+          if (d.p_scale != 0.f) {
+            if (VEC == 8) ld8<PARAM_F32>(P, i, pv); else pv[0] = ld_val<PARAM_F32>(P, i);
+          } else {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) pv[e] = 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) pv[e] = fmaf(d.p_scale, pv[e], d.v_scale * u[e]);
+          if (VEC == 8) st8<PARAM_F32>(P, i, pv); else st_val<PARAM_F32>(P, i, pv[0]);
         } else if (!d.transposed) {
-          const __nv_bfloat16 ub = __float2bfloat16_rn(u);
-          DST[static_cast<int64_t>(d.dst_row0 + r) * d.dst_ld + c] = ub;
+          const int64_t o = static_cast<int64_t>(d.dst_row0 + r) * d.dst_ld + c;
+          if (VEC == 8) st8<false>(DST, o, u); else DST[o] = __float2bfloat16_rn(u[0]);
         }
-        sq = fmaf(u, u, sq);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) sq = fmaf(u[e], u[e], sq);
       }
-      if (DST && d.transposed) tile[rr][tx] = u;
+      if (DST && d.transposed) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) tile[rr][tx * VEC + e] = u[e];
+      }
     }
     if (DST && d.transposed) {
       __syncthreads();
-      // write tile transposed: dst[(c0 + cc) * ld + dst_row0 + r0 + tx]
-      const int r = r0 + tx;
-#pragma unroll 4
-      for (int cc = ty; cc < PT; cc += 4) {
+      // transposed write: destination row (c0 + cc), columns dst_row0 + r0 + [rr0, rr0 + VEC)
+#pragma unroll 2
+      for (int cc = ty; cc < PT; cc += RPP) {
         const int cg = c0 + cc;
-        if (r < d.rows && cg < d.cols)
-          DST[static_cast<int64_t>(cg) * d.dst_ld + d.dst_row0 + r] = __float2bfloat16_rn(tile[tx][cc]);
+        const int rr0 = tx * VEC;
+        if (cg < d.cols) {
+          const int64_t o = static_cast<int64_t>(cg) * d.dst_ld + d.dst_row0 + r0 + rr0;
+          if (VEC == 8 && r0 + rr0 + 8 <= d.rows) {
+            float v8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v8[e] = tile[rr0 + e][cc];
+            st8<false>(DST, o, v8);
+          } else {
+            for (int e = 0; e < VEC; ++e)
+              if (r0 + rr0 + e < d.rows) DST[o + e] = __float2bfloat16_rn(tile[rr0 + e][cc]);
+          }
+        }
       }
       __syncthreads();
     }
@@ -254,17 +331,21 @@ void muon_prep(const PrepArgs& a, cudaStream_t stream) {
   if (a.n > 65535) throw std::runtime_error("mmf: muon_prep supports at most 65535 tensors per launch");
   const int gx = a.max_tiles < 1 ? 1 : (a.max_tiles > 4096 ? 4096 : a.max_tiles);
   dim3 grid(gx, a.n);
-  if (a.grad_f32) {
-    if (a.param_f32)
-      muon_prep_kernel<true, true><<<grid, 256, 0, stream>>>(a);
-    else
-      muon_prep_kernel<true, false><<<grid, 256, 0, stream>>>(a);
+#define MMF_PREP(GF, PF, V) muon_prep_kernel<GF, PF, V><<<grid, 256, 0, stream>>>(a)
+  if (a.vec8) {
+    if (a.grad_f32) {
+      if (a.param_f32) MMF_PREP(true, true, 8); else MMF_PREP(true, false, 8);
+    } else {
+      if (a.param_f32) MMF_PREP(false, true, 8); else MMF_PREP(false, false, 8);
+    }
   } else {
-    if (a.param_f32)
-      muon_prep_kernel<false, true><<<grid, 256, 0, stream>>>(a);
-    else
-      muon_prep_kernel<false, false><<<grid, 256, 0, stream>>>(a);
+    if (a.grad_f32) {
+      if (a.param_f32) MMF_PREP(true, true, 1); else MMF_PREP(true, false, 1);
+    } else {
+      if (a.param_f32) MMF_PREP(false, true, 1); else MMF_PREP(false, false, 1);
+    }
   }
+#undef MMF_PREP
   check_launch("muon_prep");
 }
 

@@ -306,6 +306,44 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!row_ok || col0 >= p.n_true) continue;
           float c[32];
           if (beta_b != 0.f) load_bf16x32(Crow + col0, c);
+          if (!tr && col0 + 32 <= p.n_true && (ld & 7) == 0) {
+            // contiguous 32-element run of one destination row: 16-byte vector accesses
+            const int seg = (p.nseg > 1) ? static_cast<int>(row / seg_rows) : 0;
+            char* T = reinterpret_cast<char*>(segp[seg]);
+            const int64_t idx = (static_cast<int64_t>(row) - seg * seg_rows) * ld + col0;
+            float val[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              val[i] = alpha_b * v[i];
+              if (beta_b != 0.f) val[i] = fmaf(beta_b, c[i], val[i]);
+              val[i] *= vs;
+            }
+            if (p.out_f32) {
+              float4* tp = reinterpret_cast<float4*>(reinterpret_cast<float*>(T) + idx);
+              if ((reinterpret_cast<uintptr_t>(tp) & 15) == 0) {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) {
+                  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                  if (ps != 0.f) o = tp[q4];
+                  tp[q4] = make_float4(fmaf(ps, o.x, val[4 * q4]), fmaf(ps, o.y, val[4 * q4 + 1]),
+                                       fmaf(ps, o.z, val[4 * q4 + 2]), fmaf(ps, o.w, val[4 * q4 + 3]));
+                }
+                continue;
+              }
+            } else {
+              __nv_bfloat16* tp = reinterpret_cast<__nv_bfloat16*>(T) + idx;
+              if ((reinterpret_cast<uintptr_t>(tp) & 15) == 0) {
+                if (ps != 0.f) {
+                  float o[32];
+                  load_bf16x32(tp, o);
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) val[i] = fmaf(ps, o[i], val[i]);
+                }
+                store_bf16x32(tp, val);
+                continue;
+              }
+            }
+          }
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int col = col0 + i;
