@@ -272,6 +272,7 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
   const bool g32 = grads[0].scalar_type() == torch::kFloat32;
   std::vector<mmf::AdamDesc> d(n);
   int64_t max_numel = 1;
+  bool vec4 = true;
   for (int i = 0; i < n; ++i) {
     TORCH_CHECK(params[i].is_cuda() && params[i].is_contiguous() && grads[i].is_contiguous() &&
                     exp_avgs[i].is_contiguous() && exp_avg_sqs[i].is_contiguous(),
@@ -287,6 +288,10 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
     d[i].exp_avg_sq = reinterpret_cast<int64_t>(exp_avg_sqs[i].data_ptr());
     d[i].numel = params[i].numel();
     if (d[i].numel > max_numel) max_numel = d[i].numel;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (d[i].numel % 4 != 0 || !al(params[i].data_ptr()) || !al(grads[i].data_ptr()) || !al(exp_avgs[i].data_ptr()) ||
+        !al(exp_avg_sqs[i].data_ptr()))
+      vec4 = false;
   }
   Tensor dd = upload(d, dev);
   mmf::AdamArgs a{};
@@ -302,6 +307,7 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
   a.weight_decay = static_cast<float>(weight_decay);
   a.bias_correction1 = static_cast<float>(bias_correction1);
   a.bias_correction2_sqrt = static_cast<float>(bias_correction2_sqrt);
+  a.vec4 = vec4 ? 1 : 0;
   mmf::adamw_multi(a, cur_stream());
 }
 

@@ -148,6 +148,7 @@ struct AdamArgs {
   int param_f32, grad_f32;
   float lr, beta1, beta2, eps, weight_decay;
   float bias_correction1, bias_correction2_sqrt;  // host-computed
+  int vec4;  // every tensor has numel % 4 == 0 and 16-byte aligned storage
 };
 void adamw_multi(const AdamArgs& args, cudaStream_t stream);
 

@@ -19,6 +19,25 @@ namespace {
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
 
+// 8 x bf16 <-> 8 x float through one 16-byte access
+__device__ __forceinline__ void ld_bf8(const __nv_bfloat16* p, float* v) {
+  uint4 w = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float2 f = __bfloat1622float2(h[e]);
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void st_bf8(__nv_bfloat16* p, const float* v) {
+  uint4 w;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+  *reinterpret_cast<uint4*>(p) = w;
+}
+
 // Block-wide sum for blockDim.x <= 1024 (result broadcast to all threads).
 __device__ __forceinline__ float block_allsum(float v, float* red) {
   v = warp_sum(v);
@@ -53,6 +72,41 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* _
   for (int c = threadIdx.x; c < cols; c += blockDim.x) y[off + c] = __float2bfloat16_rn(bf(x[off + c]) * r * bf(w[c]));
 }
 
+// Vector variant: the row stays in registers (cols % 8 == 0 and cols <= 256 * 8 * RV).
+template <int RV>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_vec_kernel(const __nv_bfloat16* __restrict__ x,
+                                                              const __nv_bfloat16* __restrict__ w,
+                                                              __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
+                                                              int cols, float eps) {
+  __shared__ float red[33];
+  const int64_t off = static_cast<int64_t>(blockIdx.x) * cols;
+  float v[RV][8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < RV; ++k) {
+    const int c = (threadIdx.x + 256 * k) * 8;
+    if (c < cols) {
+      ld_bf8(x + off + c, v[k]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(v[k][e], v[k][e], s);
+    }
+  }
+  s = block_allsum(s, red);
+  const float r = rsqrtf(s / cols + eps);
+  if (threadIdx.x == 0) rstd[blockIdx.x] = r;
+#pragma unroll
+  for (int k = 0; k < RV; ++k) {
+    const int c = (threadIdx.x + 256 * k) * 8;
+    if (c < cols) {
+      float wv[8], o[8];
+      ld_bf8(w + c, wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[k][e] * r * wv[e];
+      st_bf8(y + off + c, o);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
                                                           const __nv_bfloat16* __restrict__ x,
                                                           const __nv_bfloat16* __restrict__ w,
@@ -77,6 +131,65 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
   }
   __syncthreads();
   for (int c = threadIdx.x; c < cols; c += blockDim.x) dw_part[static_cast<int64_t>(blockIdx.x) * cols + c] = dw_acc[c];
+}
+
+// Vector variant of the backward (cols % 8 == 0 and cols <= 256 * 8 * RV).
+template <int RV>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                              const __nv_bfloat16* __restrict__ x,
+                                                              const __nv_bfloat16* __restrict__ w,
+                                                              const float* __restrict__ rstd,
+                                                              __nv_bfloat16* __restrict__ dx,
+                                                              float* __restrict__ dw_part, int rows, int cols) {
+  __shared__ float red[33];
+  float acc[RV][8], wv[RV][8];
+#pragma unroll
+  for (int k = 0; k < RV; ++k) {
+    const int c = (threadIdx.x + 256 * k) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[k][e] = 0.f;
+    if (c < cols) ld_bf8(w + c, wv[k]);
+  }
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int64_t off = static_cast<int64_t>(r) * cols;
+    const float rs = rstd[r];
+    float g[RV][8], xv[RV][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < RV; ++k) {
+      const int c = (threadIdx.x + 256 * k) * 8;
+      if (c < cols) {
+        ld_bf8(dy + off + c, g[k]);
+        ld_bf8(x + off + c, xv[k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot = fmaf(g[k][e] * wv[k][e], xv[k][e], dot);
+      }
+    }
+    dot = block_allsum(dot, red);
+    const float k3 = dot * rs * rs * rs / cols;
+#pragma unroll
+    for (int k = 0; k < RV; ++k) {
+      const int c = (threadIdx.x + 256 * k) * 8;
+      if (c < cols) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          o[e] = rs * g[k][e] * wv[k][e] - xv[k][e] * k3;
+          acc[k][e] = fmaf(g[k][e], xv[k][e] * rs, acc[k][e]);
+        }
+        st_bf8(dx + off + c, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < RV; ++k) {
+    const int c = (threadIdx.x + 256 * k) * 8;
+    if (c < cols) {
+      float4* dst = reinterpret_cast<float4*>(dw_part + static_cast<int64_t>(blockIdx.x) * cols + c);
+      dst[0] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+      dst[1] = make_float4(acc[k][4], acc[k][5], acc[k][6], acc[k][7]);
+    }
+  }
 }
 
 // --------------------------------- LayerNorm ---------------------------------------------
@@ -156,32 +269,64 @@ __global__ void colsum_kernel(const float* __restrict__ part, int prow, int cols
 }
 
 // ------------------------------------ RoPE -----------------------------------------------
+// One thread per (token, frequency i): the angle is computed once and applied to every head.
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, int tokens, int heads, int head_dim, int seq_len,
                             float log2_theta, float sign, int64_t token_stride, int64_t head_stride) {
   const int half = head_dim >> 1;
-  const int64_t total = static_cast<int64_t>(tokens) * heads * half;
+  const int64_t total = static_cast<int64_t>(tokens) * half;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int i = static_cast<int>(e % half);
-    const int64_t th = e / half;
-    const int h = static_cast<int>(th % heads);
-    const int t = static_cast<int>(th / heads);
+    const int t = static_cast<int>(e / half);
     const int pos = t % seq_len;
-    // inv_freq = theta^(-2i/d)
-    const float inv_freq = exp2f(-log2_theta * (2.f * i) / head_dim);
+    const float inv_freq = exp2f(-log2_theta * (2.f * i) / head_dim);  // theta^(-2i/d)
     float sn, cs;
     sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
     sn *= sign;
-    __nv_bfloat16* p = x + t * token_stride + h * head_stride;
-    const float x1 = bf(p[i]), x2 = bf(p[i + half]);
-    p[i] = __float2bfloat16_rn(x1 * cs - x2 * sn);
-    p[i + half] = __float2bfloat16_rn(x2 * cs + x1 * sn);
+    __nv_bfloat16* base = x + t * token_stride + i;
+    for (int h = 0; h < heads; ++h) {
+      __nv_bfloat16* p = base + h * head_stride;
+      const float x1 = bf(p[0]), x2 = bf(p[half]);
+      p[0] = __float2bfloat16_rn(x1 * cs - x2 * sn);
+      p[half] = __float2bfloat16_rn(x2 * cs + x1 * sn);
+    }
   }
 }
 
 // ------------------------------- activations ---------------------------------------------
 __device__ __forceinline__ float sigmoidf_(float g) { return 1.f / (1.f + expf(-g)); }
 
+__global__ void swiglu_fwd_vec_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ u,
+                                      __nv_bfloat16* __restrict__ o, int64_t n8) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float gv[8], uv[8], ov[8];
+    ld_bf8(g + 8 * i, gv);
+    ld_bf8(u + 8 * i, uv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ov[e] = gv[e] * sigmoidf_(gv[e]) * uv[e];
+    st_bf8(o + 8 * i, ov);
+  }
+}
+__global__ void swiglu_bwd_vec_kernel(const __nv_bfloat16* __restrict__ d, const __nv_bfloat16* __restrict__ g,
+                                      const __nv_bfloat16* __restrict__ u, __nv_bfloat16* __restrict__ dg,
+                                      __nv_bfloat16* __restrict__ du, int64_t n8) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float dv[8], gv[8], uv[8], a[8], b[8];
+    ld_bf8(d + 8 * i, dv);
+    ld_bf8(g + 8 * i, gv);
+    ld_bf8(u + 8 * i, uv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float sg = sigmoidf_(gv[e]);
+      a[e] = dv[e] * uv[e] * sg * (1.f + gv[e] * (1.f - sg));
+      b[e] = dv[e] * gv[e] * sg;
+    }
+    st_bf8(dg + 8 * i, a);
+    st_bf8(du + 8 * i, b);
+  }
+}
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ u,
                                   __nv_bfloat16* __restrict__ o, int64_t n) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -223,6 +368,7 @@ __global__ void gelu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv
 
 // ------------------------------- cross entropy -------------------------------------------
 // One block per row.  Online (max, sum-exp) over the row, then the gradient pass.
+template <bool VEC>
 __global__ void __launch_bounds__(1024) ce_kernel(__nv_bfloat16* __restrict__ logits, const int64_t* __restrict__ tgt,
                                                   float* __restrict__ loss_rows, int vocab, int64_t ld,
                                                   float grad_scale, int ignore_index) {
@@ -232,13 +378,29 @@ __global__ void __launch_bounds__(1024) ce_kernel(__nv_bfloat16* __restrict__ lo
   __nv_bfloat16* L = logits + row * ld;
   const int64_t t = tgt[row];
   float m = -INFINITY, s = 0.f;
-  for (int c = threadIdx.x; c < vocab; c += blockDim.x) {
-    const float v = bf(L[c]);
-    if (v > m) {
-      s = s * expf(m - v) + 1.f;
-      m = v;
-    } else {
-      s += expf(v - m);
+  if (VEC) {
+    for (int c = threadIdx.x * 8; c < vocab; c += blockDim.x * 8) {
+      float v[8];
+      ld_bf8(L + c, v);
+      float mx = v[0];
+#pragma unroll
+      for (int e = 1; e < 8; ++e) mx = fmaxf(mx, v[e]);
+      if (mx > m) {
+        s *= expf(m - mx);
+        m = mx;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += expf(v[e] - m);
+    }
+  } else {
+    for (int c = threadIdx.x; c < vocab; c += blockDim.x) {
+      const float v = bf(L[c]);
+      if (v > m) {
+        s = s * expf(m - v) + 1.f;
+        m = v;
+      } else {
+        s += expf(v - m);
+      }
     }
   }
   // combine (m, s) across the warp then the block
@@ -282,14 +444,32 @@ __global__ void __launch_bounds__(1024) ce_kernel(__nv_bfloat16* __restrict__ lo
   __syncthreads();  // the target logit must be read before it is overwritten
   if (grad_scale != 0.f) {
     const float inv = 1.f / se;
-    for (int c = threadIdx.x; c < vocab; c += blockDim.x) {
-      float gv = 0.f;
-      if (!ignored) {
-        gv = expf(bf(L[c]) - mx) * inv;
-        if (c == t) gv -= 1.f;
-        gv *= grad_scale;
+    if (VEC) {
+      for (int c = threadIdx.x * 8; c < vocab; c += blockDim.x * 8) {
+        float v[8];
+        ld_bf8(L + c, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float gv = 0.f;
+          if (!ignored) {
+            gv = expf(v[e] - mx) * inv;
+            if (c + e == t) gv -= 1.f;
+            gv *= grad_scale;
+          }
+          v[e] = gv;
+        }
+        st_bf8(L + c, v);
       }
-      L[c] = __float2bfloat16_rn(gv);
+    } else {
+      for (int c = threadIdx.x; c < vocab; c += blockDim.x) {
+        float gv = 0.f;
+        if (!ignored) {
+          gv = expf(bf(L[c]) - mx) * inv;
+          if (c == t) gv -= 1.f;
+          gv *= grad_scale;
+        }
+        L[c] = __float2bfloat16_rn(gv);
+      }
     }
   }
 }
@@ -300,6 +480,8 @@ int grid_for(int64_t work, int threads, int cap) {
   if (g > cap) g = cap;
   return static_cast<int>(g);
 }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 void check_launch(const char* what) {
   count_launch();
@@ -312,15 +494,28 @@ void check_launch(const char* what) {
 void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int cols, float eps,
                  cudaStream_t stream) {
   if (rows <= 0) return;
-  rmsnorm_fwd_kernel<<<rows, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
-                                               static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
-                                               rstd, cols, eps);
+  const bool vec = (cols % 8 == 0) && cols <= 256 * 8 * 4 && aligned16(x) && aligned16(w) && aligned16(y);
+  if (vec)
+    rmsnorm_fwd_vec_kernel<4><<<rows, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
+                                                        static_cast<const __nv_bfloat16*>(w),
+                                                        static_cast<__nv_bfloat16*>(y), rstd, cols, eps);
+  else
+    rmsnorm_fwd_kernel<<<rows, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x),
+                                                 static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
+                                                 rstd, cols, eps);
   check_launch("rmsnorm_fwd");
 }
 
 void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw_partial,
                  int rows, int cols, int partial_rows, cudaStream_t stream) {
   if (rows <= 0) return;
+  if ((cols % 8 == 0) && cols <= 256 * 8 * 4 && aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx)) {
+    rmsnorm_bwd_vec_kernel<4><<<partial_rows, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
+        static_cast<const __nv_bfloat16*>(w), rstd, static_cast<__nv_bfloat16*>(dx), dw_partial, rows, cols);
+    check_launch("rmsnorm_bwd");
+    return;
+  }
   const size_t smem = sizeof(float) * cols;
   if (smem > 200 * 1024) throw std::runtime_error("mmf: rmsnorm_bwd width too large");
   if (smem > 48 * 1024) cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -364,7 +559,7 @@ void rope_inplace(void* x, int tokens, int heads, int head_dim, int seq_len, flo
                   int64_t token_stride, int64_t head_stride, cudaStream_t stream) {
   if (tokens <= 0) return;
   if (head_dim % 2) throw std::runtime_error("mmf: rope needs an even head_dim");
-  const int64_t work = static_cast<int64_t>(tokens) * heads * (head_dim / 2);
+  const int64_t work = static_cast<int64_t>(tokens) * (head_dim / 2);
   rope_kernel<<<grid_for(work, 256, 148 * 16), 256, 0, stream>>>(static_cast<__nv_bfloat16*>(x), tokens, heads,
                                                                  head_dim, seq_len, log2f(theta),
                                                                  inverse ? -1.f : 1.f, token_stride, head_stride);
@@ -373,6 +568,13 @@ void rope_inplace(void* x, int tokens, int heads, int head_dim, int seq_len, flo
 
 void swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, cudaStream_t stream) {
   if (n <= 0) return;
+  if (n % 8 == 0 && aligned16(gate) && aligned16(up) && aligned16(out)) {
+    swiglu_fwd_vec_kernel<<<grid_for(n / 8, 256, 148 * 16), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up),
+        static_cast<__nv_bfloat16*>(out), n / 8);
+    check_launch("swiglu_fwd");
+    return;
+  }
   swiglu_fwd_kernel<<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up), static_cast<__nv_bfloat16*>(out), n);
   check_launch("swiglu_fwd");
@@ -381,6 +583,14 @@ void swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, cudaStre
 void swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate, void* dup, int64_t n,
                 cudaStream_t stream) {
   if (n <= 0) return;
+  if (n % 8 == 0 && aligned16(dout) && aligned16(gate) && aligned16(up) && aligned16(dgate) && aligned16(dup)) {
+    swiglu_bwd_vec_kernel<<<grid_for(n / 8, 256, 148 * 16), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(gate),
+        static_cast<const __nv_bfloat16*>(up), static_cast<__nv_bfloat16*>(dgate), static_cast<__nv_bfloat16*>(dup),
+        n / 8);
+    check_launch("swiglu_bwd");
+    return;
+  }
   swiglu_bwd_kernel<<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(gate),
       static_cast<const __nv_bfloat16*>(up), static_cast<__nv_bfloat16*>(dgate), static_cast<__nv_bfloat16*>(dup), n);
@@ -404,8 +614,13 @@ void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t s
 void cross_entropy_fwd_bwd(void* logits, const int64_t* targets, float* loss_rows, int rows, int vocab, int64_t ld,
                            float grad_scale, int ignore_index, cudaStream_t stream) {
   if (rows <= 0) return;
-  ce_kernel<<<rows, 1024, 0, stream>>>(static_cast<__nv_bfloat16*>(logits), targets, loss_rows, vocab, ld, grad_scale,
-                                       ignore_index);
+  const bool vec = (vocab % 8 == 0) && (ld % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  if (vec)
+    ce_kernel<true><<<rows, 1024, 0, stream>>>(static_cast<__nv_bfloat16*>(logits), targets, loss_rows, vocab, ld,
+                                               grad_scale, ignore_index);
+  else
+    ce_kernel<false><<<rows, 1024, 0, stream>>>(static_cast<__nv_bfloat16*>(logits), targets, loss_rows, vocab, ld,
+                                                grad_scale, ignore_index);
   check_launch("cross_entropy");
 }
 

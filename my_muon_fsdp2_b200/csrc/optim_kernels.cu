@@ -230,7 +230,33 @@ __global__ void ws_to_out_kernel(const WsOutArgs a) {
   }
 }
 
-template <bool P_F32, bool G_F32>
+template <bool F32>
+__device__ __forceinline__ void ld4(const void* base, int64_t i, float* v) {
+  if (F32) {
+    float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  } else {
+    uint2 w = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(base) + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+    float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  }
+}
+template <bool F32>
+__device__ __forceinline__ void st4(void* base, int64_t i, const float* v) {
+  if (F32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + i) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+    uint2 w;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+    h[0] = __floats2bfloat162_rn(v[0], v[1]);
+    h[1] = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(base) + i) = w;
+  }
+}
+
+// VEC == 4 needs numel % 4 == 0 and 16-byte aligned tensors (host-checked per launch).
+template <bool P_F32, bool G_F32, int VEC>
 __global__ void __launch_bounds__(256) adamw_kernel(const AdamArgs a) {
   const AdamDesc d = a.descs[blockIdx.y];
   void* P = reinterpret_cast<void*>(d.param);
@@ -239,18 +265,38 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamArgs a) {
   float* V = reinterpret_cast<float*>(d.exp_avg_sq);
   const float step_size = a.lr / a.bias_correction1;
   const float decay = 1.f - a.lr * a.weight_decay;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < d.numel;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float g = ld_val<G_F32>(G, i);
-    float m = M[i], v = V[i];
-    m = fmaf(a.beta1, m - g, g);
-    v = fmaf(a.beta2, v - g * g, g * g);
-    M[i] = m;
-    V[i] = v;
-    float p = ld_val<P_F32>(P, i) * decay;
-    const float denom = sqrtf(v) / a.bias_correction2_sqrt + a.eps;
-    p = fmaf(-step_size, m / denom, p);
-    st_val<P_F32>(P, i, p);
+  const int64_t nv = d.numel / VEC;
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < nv;
+       j += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = j * VEC;
+    float g[VEC], m[VEC], v[VEC], p[VEC];
+    if (VEC == 4) {
+      ld4<G_F32>(G, i, g);
+      ld4<true>(M, i, m);
+      ld4<true>(V, i, v);
+      ld4<P_F32>(P, i, p);
+    } else {
+      g[0] = ld_val<G_F32>(G, i);
+      m[0] = M[i];
+      v[0] = V[i];
+      p[0] = ld_val<P_F32>(P, i);
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      m[e] = fmaf(a.beta1, m[e] - g[e], g[e]);
+      v[e] = fmaf(a.beta2, v[e] - g[e] * g[e], g[e] * g[e]);
+      const float denom = sqrtf(v[e]) / a.bias_correction2_sqrt + a.eps;
+      p[e] = fmaf(-step_size, m[e] / denom, p[e] * decay);
+    }
+    if (VEC == 4) {
+      st4<true>(M, i, m);
+      st4<true>(V, i, v);
+      st4<P_F32>(P, i, p);
+    } else {
+      M[i] = m[0];
+      V[i] = v[0];
+      st_val<P_F32>(P, i, p[0]);
+    }
   }
 }
 
@@ -368,18 +414,21 @@ void ws_to_out(const WsOutArgs& a, cudaStream_t stream) {
 void adamw_multi(const AdamArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
   if (a.n > 65535) throw std::runtime_error("mmf: adamw_multi supports at most 65535 tensors per launch");
-  dim3 grid(grid_for(a.max_numel, 256, 1184), a.n);
+  const int vec = a.vec4 ? 4 : 1;
+  dim3 grid(grid_for(a.max_numel / vec, 256, 1184), a.n);
+#define MMF_ADAM(PF, GF)                                                      \
+  do {                                                                        \
+    if (a.vec4)                                                               \
+      adamw_kernel<PF, GF, 4><<<grid, 256, 0, stream>>>(a);                   \
+    else                                                                      \
+      adamw_kernel<PF, GF, 1><<<grid, 256, 0, stream>>>(a);                   \
+  } while (0)
   if (a.param_f32) {
-    if (a.grad_f32)
-      adamw_kernel<true, true><<<grid, 256, 0, stream>>>(a);
-    else
-      adamw_kernel<true, false><<<grid, 256, 0, stream>>>(a);
+    if (a.grad_f32) MMF_ADAM(true, true); else MMF_ADAM(true, false);
   } else {
-    if (a.grad_f32)
-      adamw_kernel<false, true><<<grid, 256, 0, stream>>>(a);
-    else
-      adamw_kernel<false, false><<<grid, 256, 0, stream>>>(a);
+    if (a.grad_f32) MMF_ADAM(false, true); else MMF_ADAM(false, false);
   }
+#undef MMF_ADAM
   check_launch("adamw_multi");
 }
 

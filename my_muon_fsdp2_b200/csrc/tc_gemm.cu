@@ -40,6 +40,7 @@ constexpr uint32_t TMEM_COLS = 512;
 struct GemmParams {
   int M, N, K, batch;
   int tiles_m, tiles_n, tiles_per_batch, num_tiles;
+  int band;
   int symmetric;
   int mode;  // 0 workspace, 1 output
   __nv_bfloat16* D;
@@ -64,8 +65,15 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& b, 
   b = t / p.tiles_per_batch;
   int r = t - b * p.tiles_per_batch;
   if (!p.symmetric) {
-    tm = r / p.tiles_n;
-    tn = r - tm * p.tiles_n;
+    // Column bands of `band` tile columns, M fastest inside a band: the CTAs running at the
+    // same time share a narrow slab of the (large) B operand and all of the (small) A operand,
+    // so B is read from DRAM about once instead of once per row block.
+    const int span = p.band * p.tiles_m;
+    const int bi = r / span;
+    const int rr = r - bi * span;
+    const int w = min(p.band, p.tiles_n - bi * p.band);
+    tn = bi * p.band + rr % w;
+    tm = rr / w;
     return;
   }
   // Symmetric output: row block i (BM rows) needs column blocks tn >= i*BM/BN = i/2.
@@ -447,6 +455,11 @@ void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t
     p.tiles_per_batch = cnt;
   } else {
     p.tiles_per_batch = p.tiles_m * p.tiles_n;
+  }
+  {
+    // band width: enough tile columns that one wave of CTAs covers whole bands
+    int band = (di.sms + p.tiles_m - 1) / p.tiles_m;
+    p.band = band < 1 ? 1 : (band > p.tiles_n ? p.tiles_n : band);
   }
   p.num_tiles = p.tiles_per_batch * p.batch;
   p.err = device_error_word(dev);
