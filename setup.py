@@ -28,7 +28,6 @@ SOURCES = [
     "model_kernels.cu",
     "attention.cu",
     "symm_comm.cu",
-    "noalloc.cu",
 ]
 
 
