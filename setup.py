@@ -28,6 +28,7 @@ SOURCES = [
     "model_kernels.cu",
     "attention.cu",
     "symm_comm.cu",
+    "noalloc.cu",
 ]
 
 
