@@ -39,6 +39,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--comm", choices=["auto", "nccl", "p2p"], default="auto")
     ap.add_argument("--ns-steps", type=int, default=5)
+    ap.add_argument("--gemm-variant", type=int, default=0, help="0 auto, 1 single-CTA, 2 CTA pair")
     return ap.parse_args()
 
 
@@ -88,7 +89,10 @@ def main():
     params = [torch.nn.Parameter(shard(torch.zeros_like(t))) for t in fulls]
     grads = [shard(t) for t in fulls]
     if args.impl == "ours":
+        from my_muon_fsdp2_b200._ext import ext
         from my_muon_fsdp2_b200.parallel.muon_engine import MODE_COPY, MuonEngine, MuonHyper, MuonTask
+
+        ext().set_gemm_variant(args.gemm_variant)
 
         engine = MuonEngine(comm=args.comm)
         hp = MuonHyper(mode=MODE_COPY, ns_steps=args.ns_steps)

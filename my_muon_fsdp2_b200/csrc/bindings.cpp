@@ -499,6 +499,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_", &cross_entropy_);
   m.def("power_iteration", &power_iteration);
   m.def("symm_barrier", &symm_barrier);
+  m.def("set_gemm_variant", [](int64_t v) { mmf::set_gemm_variant(static_cast<int>(v)); });
+  m.def("gemm_variant", []() { return static_cast<int64_t>(mmf::gemm_variant()); });
   m.def("device_error", &device_error);
   m.def("launch_count", &launch_count);
 }

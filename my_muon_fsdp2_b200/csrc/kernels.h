@@ -45,6 +45,11 @@ struct GemmWsArgs {
 };
 void tc_gemm_ws(const GemmWsArgs& args, cudaStream_t stream);
 
+// GEMM kernel variant: 0 = automatic (CTA pair when the problem has enough 256-row tiles),
+// 1 = single-CTA 128x256 tiles, 2 = CTA pair (cta_group::2) 256x256 tiles.
+void set_gemm_variant(int v);
+int gemm_variant();
+
 // Epilogue "output" mode: for every element (i, j) with i < m_true, j < n_true, with
 // (r, c) = transposed_b ? (j, i) : (i, j) the element's position in the destination matrix,
 //   seg = r / seg_rows_b,  T = out_ptrs[b * nseg + seg],  idx = (r - seg * seg_rows_b) * ld_b + c

@@ -118,6 +118,125 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v
   }
 }
 
+// Epilogue of one output tile for one thread: `row` is the thread's output row, `t_row` the
+// TMEM address of its accumulator lane (column 0 of the tile), tn the tile column block.
+// Warp-collective (tcgen05.ld): all 32 lanes of the warp must call it together.
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, int b, int row, int tn, uint32_t t_row) {
+      const float alpha_b = p.alpha * (p.alpha_vec ? p.alpha_vec[b] : 1.f);
+      const float beta_b = p.C ? p.beta * (p.beta_vec ? p.beta_vec[b] : 1.f) : 0.f;
+      const int64_t mn = static_cast<int64_t>(p.M) * p.N;
+      const __nv_bfloat16* Crow = p.C ? p.C + b * mn + static_cast<int64_t>(row) * p.N : nullptr;
+      if (p.mode == 0) {
+        __nv_bfloat16* Db = p.D + b * mn;
+#pragma unroll 1
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          float v[32];
+          tmem_ld_32cols(t_row + chunk * 32, v);
+          const int col0 = tn * BN + chunk * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha_b;
+          if (beta_b != 0.f) {
+            float c[32];
+            load_bf16x32(Crow + col0, c);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = fmaf(beta_b, c[i], v[i]);
+          }
+          if (!p.symmetric || col0 >= row) {
+            store_bf16x32(Db + static_cast<int64_t>(row) * p.N + col0, v);
+          } else if (col0 + 31 >= row) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i >= row) Db[static_cast<int64_t>(row) * p.N + col0 + i] = __float2bfloat16_rn(v[i]);
+          }
+          if (p.symmetric && col0 + 31 > row) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i > row) Db[static_cast<int64_t>(col0 + i) * p.N + row] = __float2bfloat16_rn(v[i]);
+          }
+        }
+      } else {
+        const float ps = p.p_scale * (p.p_scale_vec ? p.p_scale_vec[b] : 1.f);
+        const float vs = p.v_scale * (p.v_scale_vec ? p.v_scale_vec[b] : 1.f);
+        int64_t ld = p.out_ld, seg_rows = int64_t(1) << 40;
+        int tr = p.out_transposed;
+        if (p.out_meta) {
+          ld = p.out_meta[3 * b];
+          tr = static_cast<int>(p.out_meta[3 * b + 1]);
+          seg_rows = p.out_meta[3 * b + 2];
+        }
+        const int64_t* segp = p.out_ptrs + static_cast<int64_t>(b) * p.nseg;
+        const bool row_ok = row < p.m_true;
+#pragma unroll 1
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          float v[32];
+          tmem_ld_32cols(t_row + chunk * 32, v);
+          const int col0 = tn * BN + chunk * 32;
+          if (!row_ok || col0 >= p.n_true) continue;
+          float c[32];
+          if (beta_b != 0.f) load_bf16x32(Crow + col0, c);
+          if (!tr && col0 + 32 <= p.n_true && (ld & 7) == 0) {
+            // contiguous 32-element run of one destination row: 16-byte vector accesses
+            const int seg = (p.nseg > 1) ? static_cast<int>(row / seg_rows) : 0;
+            char* T = reinterpret_cast<char*>(segp[seg]);
+            const int64_t idx = (static_cast<int64_t>(row) - seg * seg_rows) * ld + col0;
+            float val[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              val[i] = alpha_b * v[i];
+              if (beta_b != 0.f) val[i] = fmaf(beta_b, c[i], val[i]);
+              val[i] *= vs;
+            }
+            if (p.out_f32) {
+              float4* tp = reinterpret_cast<float4*>(reinterpret_cast<float*>(T) + idx);
+              if ((reinterpret_cast<uintptr_t>(tp) & 15) == 0) {
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) {
+                  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+                  if (ps != 0.f) o = tp[q4];
+                  tp[q4] = make_float4(fmaf(ps, o.x, val[4 * q4]), fmaf(ps, o.y, val[4 * q4 + 1]),
+                                       fmaf(ps, o.z, val[4 * q4 + 2]), fmaf(ps, o.w, val[4 * q4 + 3]));
+                }
+                continue;
+              }
+            } else {
+              __nv_bfloat16* tp = reinterpret_cast<__nv_bfloat16*>(T) + idx;
+              if ((reinterpret_cast<uintptr_t>(tp) & 15) == 0) {
+                if (ps != 0.f) {
+                  float o[32];
+                  load_bf16x32(tp, o);
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) val[i] = fmaf(ps, o[i], val[i]);
+                }
+                store_bf16x32(tp, val);
+                continue;
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = col0 + i;
+            if (col >= p.n_true) break;
+            float val = alpha_b * v[i];
+            if (beta_b != 0.f) val = fmaf(beta_b, c[i], val);
+            const int64_t r = tr ? col : row;
+            const int64_t cc = tr ? row : col;
+            const int seg = (p.nseg > 1) ? static_cast<int>(r / seg_rows) : 0;
+            char* T = reinterpret_cast<char*>(segp[seg]);
+            const int64_t idx = (r - seg * seg_rows) * ld + cc;
+            if (p.out_f32) {
+              float* tp = reinterpret_cast<float*>(T) + idx;
+              const float old = (ps != 0.f) ? *tp : 0.f;
+              *tp = fmaf(ps, old, vs * val);
+            } else {
+              __nv_bfloat16* tp = reinterpret_cast<__nv_bfloat16*>(T) + idx;
+              const float old = (ps != 0.f) ? __bfloat162float(*tp) : 0.f;
+              *tp = __float2bfloat16_rn(fmaf(ps, old, vs * val));
+            }
+          }
+        }
+      }
+}
+
 template <bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -260,121 +379,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(p, t, b, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
       tc_fence_after();
-      const int row = tm * BM + q * 32 + lane;
-      const float alpha_b = p.alpha * (p.alpha_vec ? p.alpha_vec[b] : 1.f);
-      const float beta_b = p.C ? p.beta * (p.beta_vec ? p.beta_vec[b] : 1.f) : 0.f;
-      const int64_t mn = static_cast<int64_t>(p.M) * p.N;
-      const __nv_bfloat16* Crow = p.C ? p.C + b * mn + static_cast<int64_t>(row) * p.N : nullptr;
-      const uint32_t t_row = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      if (p.mode == 0) {
-        __nv_bfloat16* Db = p.D + b * mn;
-#pragma unroll 1
-        for (int chunk = 0; chunk < BN / 32; ++chunk) {
-          float v[32];
-          tmem_ld_32cols(t_row + chunk * 32, v);
-          const int col0 = tn * BN + chunk * 32;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha_b;
-          if (beta_b != 0.f) {
-            float c[32];
-            load_bf16x32(Crow + col0, c);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = fmaf(beta_b, c[i], v[i]);
-          }
-          if (!p.symmetric || col0 >= row) {
-            store_bf16x32(Db + static_cast<int64_t>(row) * p.N + col0, v);
-          } else if (col0 + 31 >= row) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i >= row) Db[static_cast<int64_t>(row) * p.N + col0 + i] = __float2bfloat16_rn(v[i]);
-          }
-          if (p.symmetric && col0 + 31 > row) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i > row) Db[static_cast<int64_t>(col0 + i) * p.N + row] = __float2bfloat16_rn(v[i]);
-          }
-        }
-      } else {
-        const float ps = p.p_scale * (p.p_scale_vec ? p.p_scale_vec[b] : 1.f);
-        const float vs = p.v_scale * (p.v_scale_vec ? p.v_scale_vec[b] : 1.f);
-        int64_t ld = p.out_ld, seg_rows = int64_t(1) << 40;
-        int tr = p.out_transposed;
-        if (p.out_meta) {
-          ld = p.out_meta[3 * b];
-          tr = static_cast<int>(p.out_meta[3 * b + 1]);
-          seg_rows = p.out_meta[3 * b + 2];
-        }
-        const int64_t* segp = p.out_ptrs + static_cast<int64_t>(b) * p.nseg;
-        const bool row_ok = row < p.m_true;
-#pragma unroll 1
-        for (int chunk = 0; chunk < BN / 32; ++chunk) {
-          float v[32];
-          tmem_ld_32cols(t_row + chunk * 32, v);
-          const int col0 = tn * BN + chunk * 32;
-          if (!row_ok || col0 >= p.n_true) continue;
-          float c[32];
-          if (beta_b != 0.f) load_bf16x32(Crow + col0, c);
-          if (!tr && col0 + 32 <= p.n_true && (ld & 7) == 0) {
-            // contiguous 32-element run of one destination row: 16-byte vector accesses
-            const int seg = (p.nseg > 1) ? static_cast<int>(row / seg_rows) : 0;
-            char* T = reinterpret_cast<char*>(segp[seg]);
-            const int64_t idx = (static_cast<int64_t>(row) - seg * seg_rows) * ld + col0;
-            float val[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              val[i] = alpha_b * v[i];
-              if (beta_b != 0.f) val[i] = fmaf(beta_b, c[i], val[i]);
-              val[i] *= vs;
-            }
-            if (p.out_f32) {
-              float4* tp = reinterpret_cast<float4*>(reinterpret_cast<float*>(T) + idx);
-              if ((reinterpret_cast<uintptr_t>(tp) & 15) == 0) {
-#pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) {
-                  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-                  if (ps != 0.f) o = tp[q4];
-                  tp[q4] = make_float4(fmaf(ps, o.x, val[4 * q4]), fmaf(ps, o.y, val[4 * q4 + 1]),
-                                       fmaf(ps, o.z, val[4 * q4 + 2]), fmaf(ps, o.w, val[4 * q4 + 3]));
-                }
-                continue;
-              }
-            } else {
-              __nv_bfloat16* tp = reinterpret_cast<__nv_bfloat16*>(T) + idx;
-              if ((reinterpret_cast<uintptr_t>(tp) & 15) == 0) {
-                if (ps != 0.f) {
-                  float o[32];
-                  load_bf16x32(tp, o);
-#pragma unroll
-                  for (int i = 0; i < 32; ++i) val[i] = fmaf(ps, o[i], val[i]);
-                }
-                store_bf16x32(tp, val);
-                continue;
-              }
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int col = col0 + i;
-            if (col >= p.n_true) break;
-            float val = alpha_b * v[i];
-            if (beta_b != 0.f) val = fmaf(beta_b, c[i], val);
-            const int64_t r = tr ? col : row;
-            const int64_t cc = tr ? row : col;
-            const int seg = (p.nseg > 1) ? static_cast<int>(r / seg_rows) : 0;
-            char* T = reinterpret_cast<char*>(segp[seg]);
-            const int64_t idx = (r - seg * seg_rows) * ld + cc;
-            if (p.out_f32) {
-              float* tp = reinterpret_cast<float*>(T) + idx;
-              const float old = (ps != 0.f) ? *tp : 0.f;
-              *tp = fmaf(ps, old, vs * val);
-            } else {
-              __nv_bfloat16* tp = reinterpret_cast<__nv_bfloat16*>(T) + idx;
-              const float old = (ps != 0.f) ? __bfloat162float(*tp) : 0.f;
-              *tp = __float2bfloat16_rn(fmaf(ps, old, vs * val));
-            }
-          }
-        }
-      }
+      epilogue_tile(p, b, tm * BM + q * 32 + lane, tn, tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -390,6 +395,208 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// ======================================================================================
+// CTA-pair variant (cta_group::2): a cluster of 2 CTAs computes a 256 x 256 tile; each CTA
+// stages its 128 rows of A and its 128-column half of B (6-stage ring, 32 KB/stage), the
+// leader CTA (rank 0) issues M=256 N=256 K=16 MMAs that read both CTAs' smem, and each CTA's
+// epilogue drains its own 128 TMEM lanes.  Halves the per-SM B traffic of the 1-CTA kernel.
+//   full[s]  : leader only; both CTAs' TMA bytes land on it (leader arms 64 KB)
+//   empty[s] : both CTAs; the leader's commit arrives on both (multicast commit)
+//   tfull[j] : both CTAs; multicast commit after the tile's last MMA
+//   tempty[j]: leader only, count 8 (4 epilogue warps x 2 CTAs; CTA 1 arrives remotely)
+// ======================================================================================
+constexpr int P_BM = 256;           // rows per CTA pair
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2;   // 16 KB per CTA
+constexpr int P_B_BYTES = 128 * BK * 2;   // 16 KB per CTA (half of N = 256)
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ void tile_coords_pair(const GemmParams& p, int t, int& b, int& tm, int& tn) {
+  b = t / p.tiles_per_batch;
+  int r = t - b * p.tiles_per_batch;
+  if (!p.symmetric) {
+    const int span = p.band * p.tiles_m;
+    const int bi = r / span;
+    const int rr = r - bi * span;
+    const int w = min(p.band, p.tiles_n - bi * p.band);
+    tn = bi * p.band + rr % w;
+    tm = rr / w;
+    return;
+  }
+  // square 256 x 256 tiles: row block i needs column blocks tn >= i
+  int i = 0;
+#pragma unroll 1
+  while (true) {
+    const int cnt = p.tiles_n - i;
+    if (r < cnt) {
+      tm = i;
+      tn = i + r;
+      return;
+    }
+    r -= cnt;
+    ++i;
+  }
+}
+
+template <bool B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + P_STAGES * P_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + P_STAGES * P_B_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&tfull[j], 1);
+      mbar_init(&tempty[j], 8);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive / TMA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int k_blocks = p.K / BK;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer (both CTAs) -------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = cluster; t < p.num_tiles && ok; t += nclusters) {
+        int b, tm, tn;
+        tile_coords_pair(p, t, b, tm, tn);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          tma_load_3d_pair(sA + stage * P_A_BYTES, &tmA, fb, kb * BK, tm * P_BM + rank * 128, b);
+          if (B_MN) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+              tma_load_3d_pair(sB + stage * P_B_BYTES + c * (BK * 64 * 2), &tmB, fb, tn * BN + rank * 128 + c * 64,
+                               kb * BK, b);
+          } else {
+            tma_load_3d_pair(sB + stage * P_B_BYTES, &tmB, fb, kb * BK, tn * BN + rank * 128, b);
+          }
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer (leader CTA only) ---------------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, BN, false, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = cluster; t < p.num_tiles && ok; t += nclusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.err, ERR_MMA_FULL_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * P_A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * P_B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc_kmajor(a_addr + kk * 32);
+            const uint64_t bd = B_MN ? sdesc_mnmajor(b_addr + kk * 16 * 128, BK * 64 * 2) : sdesc_kmajor(b_addr + kk * 32);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      umma_commit_pair(drain, 0x1);
+      mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else {
+    // ------------------------------ epilogue (both CTAs) -----------------------------
+    const int q = warp & 3;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster; t < p.num_tiles; t += nclusters) {
+      int b, tm, tn;
+      tile_coords_pair(p, t, b, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
+      tc_fence_after();
+      epilogue_tile(p, b, tm * P_BM + static_cast<int>(rank) * 128 + q * 32 + lane, tn,
+                    tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // the leader's MMAs read CTA 1's smem: nobody leaves before both are done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -424,7 +631,7 @@ CUtensorMap make_map_bf16_3d(const void* base, uint64_t inner, uint64_t outer, u
 
 struct DeviceInfo {
   int sms = 0;
-  bool attr_set[2] = {false, false};
+  bool attr_set[4] = {false, false, false, false};
 };
 DeviceInfo& dev_info(int dev) {
   static DeviceInfo infos[64];
@@ -442,42 +649,90 @@ void check_shape(int batch, int M, int N, int K) {
                              " N=" + std::to_string(N) + " K=" + std::to_string(K) + ")");
 }
 
+std::atomic<int> g_variant{0};  // 0 auto, 1 single-CTA, 2 CTA pair
+
+int pair_tiles(const GemmParams& p) {
+  const int tm = p.M / P_BM, tn = p.N / BN;
+  return (p.symmetric ? tm * (tm + 1) / 2 : tm * tn) * p.batch;
+}
+
 void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   DeviceInfo& di = dev_info(dev);
-  p.tiles_m = p.M / BM;
+  p.err = device_error_word(dev);
+  int variant = g_variant.load();
+  if (variant == 0) {
+    // the CTA pair needs 256-row blocks and enough tiles to keep most SMs busy
+    variant = (p.M % P_BM == 0 && pair_tiles(p) >= di.sms / 2) ? 2 : 1;
+  }
+  if (variant == 2 && p.M % P_BM != 0) variant = 1;
+  const bool pair = variant == 2;
+  const int bm = pair ? P_BM : BM;
+  p.tiles_m = p.M / bm;
   p.tiles_n = p.N / BN;
   if (p.symmetric) {
     if (p.M != p.N) throw std::runtime_error("mmf: symmetric GEMM needs M == N");
     int cnt = 0;
-    for (int i = 0; i < p.tiles_m; ++i) cnt += p.tiles_n - (i >> 1);
+    for (int i = 0; i < p.tiles_m; ++i) cnt += pair ? (p.tiles_n - i) : (p.tiles_n - (i >> 1));
     p.tiles_per_batch = cnt;
   } else {
     p.tiles_per_batch = p.tiles_m * p.tiles_n;
   }
+  p.num_tiles = p.tiles_per_batch * p.batch;
   {
-    // band width: enough tile columns that one wave of CTAs covers whole bands
-    int band = (di.sms + p.tiles_m - 1) / p.tiles_m;
+    const int units = pair ? di.sms / 2 : di.sms;  // concurrently running tiles
+    int band = (units + p.tiles_m - 1) / p.tiles_m;
     p.band = band < 1 ? 1 : (band > p.tiles_n ? p.tiles_n : band);
   }
-  p.num_tiles = p.tiles_per_batch * p.batch;
-  p.err = device_error_word(dev);
-  CUtensorMap ma = make_map_bf16_3d(A, p.K, p.M, p.batch, BK, BM);
-  CUtensorMap mb = b_mn ? make_map_bf16_3d(B, p.N, p.K, p.batch, 64, BK) : make_map_bf16_3d(B, p.K, p.N, p.batch, BK, BN);
-  const int grid = p.num_tiles < di.sms ? p.num_tiles : di.sms;
-  if (b_mn) {
-    if (!di.attr_set[1]) {
-      cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-      di.attr_set[1] = true;
+  const int a_rows = pair ? 128 : BM;
+  const int b_rows = pair ? 128 : BN;
+  CUtensorMap ma = make_map_bf16_3d(A, p.K, p.M, p.batch, BK, a_rows);
+  CUtensorMap mb = b_mn ? make_map_bf16_3d(B, p.N, p.K, p.batch, 64, BK) : make_map_bf16_3d(B, p.K, p.N, p.batch, BK, b_rows);
+  if (!pair) {
+    const int grid = p.num_tiles < di.sms ? p.num_tiles : di.sms;
+    if (b_mn) {
+      if (!di.attr_set[1]) {
+        cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        di.attr_set[1] = true;
+      }
+      tc_gemm_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+    } else {
+      if (!di.attr_set[0]) {
+        cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        di.attr_set[0] = true;
+      }
+      tc_gemm_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
     }
-    tc_gemm_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
   } else {
-    if (!di.attr_set[0]) {
-      cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-      di.attr_set[0] = true;
+    const int clusters = p.num_tiles < di.sms / 2 ? p.num_tiles : di.sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t le;
+    if (b_mn) {
+      if (!di.attr_set[3]) {
+        cudaFuncSetAttribute(tc_gemm_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+        di.attr_set[3] = true;
+      }
+      le = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<true>, ma, mb, p);
+    } else {
+      if (!di.attr_set[2]) {
+        cudaFuncSetAttribute(tc_gemm_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+        di.attr_set[2] = true;
+      }
+      le = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<false>, ma, mb, p);
     }
-    tc_gemm_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+    if (le != cudaSuccess) throw std::runtime_error(std::string("mmf: tc_gemm pair launch failed: ") + cudaGetErrorString(le));
   }
   count_launch();
   cudaError_t e = cudaGetLastError();
@@ -521,6 +776,9 @@ int read_and_clear_device_error(int device, cudaStream_t stream) {
 static std::atomic<uint64_t> g_launches{0};
 uint64_t launch_count() { return g_launches.load(); }
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void set_gemm_variant(int v) { g_variant.store(v); }
+int gemm_variant() { return g_variant.load(); }
 
 void tc_gemm_ws(const GemmWsArgs& a, cudaStream_t stream) {
   check_shape(a.batch, a.M, a.N, a.K);

@@ -13,11 +13,20 @@ def E():
     return ext()
 
 
+@pytest.fixture(params=[1, 2], ids=["cta1", "cta_pair"], autouse=True)
+def gemm_variant(request):
+    """Run every GEMM test with the single-CTA and with the CTA-pair (cta_group::2) kernel."""
+    E().set_gemm_variant(request.param)
+    yield request.param
+    E().set_gemm_variant(0)
+
+
 def _bf(*shape):
     return torch.randn(*shape, device="cuda").to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("batch,M,N,K", [(1, 128, 256, 64), (2, 256, 512, 320), (3, 384, 256, 1024)])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 128, 256, 64), (2, 256, 512, 320), (3, 384, 256, 1024),
+                                         (1, 512, 768, 4096)])
 def test_kmajor_plain(batch, M, N, K):
     A, B = _bf(batch, M, K), _bf(batch, N, K)
     D = torch.empty(batch, M, N, dtype=torch.bfloat16, device="cuda")
@@ -29,7 +38,7 @@ def test_kmajor_plain(batch, M, N, K):
     check_device_error(0)
 
 
-@pytest.mark.parametrize("batch,M,N,K", [(1, 128, 256, 64), (2, 256, 512, 192)])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 128, 256, 64), (2, 256, 512, 192), (1, 768, 1024, 512)])
 def test_mnmajor_axpby(batch, M, N, K):
     A, Bk = _bf(batch, M, K), _bf(batch, K, N)
     C = _bf(batch, M, N)
@@ -40,7 +49,7 @@ def test_mnmajor_axpby(batch, M, N, K):
     assert rel_err(D, ref) < 1e-2
 
 
-@pytest.mark.parametrize("batch,M,K", [(1, 256, 256), (2, 512, 384), (1, 768, 128)])
+@pytest.mark.parametrize("batch,M,K", [(1, 256, 256), (2, 512, 384), (1, 768, 128), (1, 1024, 2048)])
 def test_symmetric_gram(batch, M, K):
     X = _bf(batch, M, K)
     D = torch.full((batch, M, M), float("nan"), dtype=torch.bfloat16, device="cuda")
