@@ -1,0 +1,734 @@
+// Causal flash attention (GQA) on the sm_100a 5th-generation tensor core.
+//
+// Forward, one CTA per (128-query block, query head, batch):
+//   warp 0      TMA producer: Q once; K_j / V_j per 128-key block into a 2-stage ring
+//   warp 1      single-thread tcgen05.mma issuer:  S_j = Q K_j^T  (TMEM, double buffered)
+//                                                   O  += P_j V_j   (TMEM, V read MN-major)
+//   warps 2..5  softmax: one query row per thread — S_j from TMEM, causal mask on the diagonal
+//               block, online max / sum in the exp2 domain, P_j (bf16) into 128B-swizzled smem,
+//               O rescaled in TMEM when the running max grows; epilogue O / l -> bf16, and the
+//               row log-sum-exp (natural log) for the backward pass.
+// All waits are bounded (tc_common.cuh).  Layouts: q [B, T, Hq, D], k/v [B, T, Hkv, D], o like q,
+// lse [B, Hq, T] fp32; T % 128 == 0, D in {64, 128}.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include "attention.h"
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace mmf {
+
+namespace {
+
+constexpr int QB = 128;  // query rows per CTA
+constexpr int KB = 128;  // keys per block
+constexpr int ATT_THREADS = 192;
+
+struct AttnParams {
+  int B, T, Hq, Hkv, D;
+  float scale_log2;  // softmax scale * log2(e)
+  __nv_bfloat16* o;
+  float* lse;
+  int* err;
+};
+
+template <int D>
+struct AttnSmem {
+  static constexpr int CH = D / 64;                 // 64-column swizzle chunks per row
+  static constexpr int TILE = 128 * D * 2;          // one [128 x D] bf16 tile
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + TILE;        // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * TILE;    // 2 stages
+  static constexpr int P_OFF = V_OFF + 2 * TILE;    // P: [128 q x 128 keys] bf16 = 32 KB
+  static constexpr int BAR_OFF = P_OFF + 128 * 128 * 2;
+  // >= 120 KB so that only one CTA (which holds all 512 TMEM columns) fits on an SM
+  static constexpr int BYTES = (BAR_OFF + 256 + 1024) > 120 * 1024 ? (BAR_OFF + 256 + 1024) : 120 * 1024;
+};
+
+// byte offset of element (row, col) inside a K-major 128B-swizzled tile made of [rows x 64]
+// chunks of 16 KB each (128 rows): the 16-byte unit index is XORed with (row % 8).
+__device__ __forceinline__ uint32_t swz_offset(int row, int col) {
+  const int chunk = col >> 6;
+  const int c = col & 63;
+  const int unit = (c >> 3) ^ (row & 7);
+  return static_cast<uint32_t>(chunk * (128 * 128) + row * 128 + unit * 16 + (c & 7) * 2);
+}
+
+template <int D>
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using L = AttnSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::Q_OFF;
+  uint8_t* sK = smem + L::K_OFF;
+  uint8_t* sV = smem + L::V_OFF;
+  uint8_t* sP = smem + L::P_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_empty = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = p.T / QB;
+  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);  // heaviest blocks first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int nblk = qb + 1;  // causal: key blocks 0..qb
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      constexpr uint32_t TILE = L::TILE;
+      mbar_arrive_expect_tx(q_full, TILE);
+#pragma unroll
+      for (int c = 0; c < L::CH; ++c) tma_load_4d(sQ + c * 16384, &tmQ, q_full, c * 64, h, qb * QB, b);
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
+#pragma unroll
+        for (int c = 0; c < L::CH; ++c) {
+          tma_load_4d(sK + st * TILE + c * 16384, &tmK, &kv_full[st], c * 64, hk, j * KB, b);
+          tma_load_4d(sV + st * TILE + c * 16384, &tmV, &kv_full[st], c * 64, hk, j * KB, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, KB, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
+      bool ok = mbar_wait(q_full, 0, p.err, ERR_MMA_FULL_TIMEOUT);
+      const uint32_t q_addr = smem_u32(sQ);
+      for (int j = 0; ok && j <= nblk; ++j) {
+        if (j < nblk) {
+          const int st = j & 1;
+          ok = mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT) &&
+               mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sK + st * L::TILE);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_bf16(tS[st], sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
+          }
+          umma_commit(&s_full[st]);
+        }
+        if (j >= 1) {
+          // O += P_{j-1} V_{j-1} once the softmax warps have written P_{j-1}
+          const int pj = j - 1, st = pj & 1;
+          if (!mbar_wait(p_full, pj & 1, p.err, ERR_MMA_FULL_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t p_addr = smem_u32(sP);
+          const uint32_t v_addr = smem_u32(sV + st * L::TILE);
+#pragma unroll
+          for (int kk = 0; kk < KB / 16; ++kk) {
+            const uint64_t ad = sdesc_kmajor(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32);
+            const uint64_t bd = sdesc_mnmajor(v_addr + kk * 16 * 128, 16384);
+            umma_bf16(tO, ad, bd, idesc_o, (pj | kk) ? 1u : 0u);
+          }
+          umma_commit(pv_done);
+          umma_commit(&kv_empty[st]);
+        }
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else {
+    // ------------------------------ softmax / epilogue ---------------------------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;            // row inside the query block
+    const int qi = qb * QB + r;             // query position
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    float m2 = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk && ok; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (j == qb);
+      // pass 1: row max of the scaled scores
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < KB / 32; ++c) {
+        float v[32];
+        tmem_ld_32cols(tS[st] + lane_off + c * 32, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const bool masked = diag && (j * KB + c * 32 + e > qi);
+          if (!masked) mx = fmaxf(mx, v[e] * p.scale_log2);
+        }
+      }
+      const float m_new = fmaxf(m2, mx);
+      const float alpha = (m2 == -INFINITY) ? 0.f : exp2f(m2 - m_new);
+      // P_{j-1} V_{j-1} must be done before O is rescaled and P is overwritten
+      if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld_32cols(tO + lane_off + c * 32, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] *= alpha;
+          tmem_st_32cols(tO + lane_off + c * 32, o);
+        }
+      }
+      // pass 2: probabilities -> swizzled bf16 P tile, row sum
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < KB / 32; ++c) {
+        float v[32];
+        tmem_ld_32cols(tS[st] + lane_off + c * 32, v);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 w;
+          __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            float pv[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int e = g * 8 + e2 * 2 + t;
+              const bool masked = diag && (j * KB + c * 32 + e > qi);
+              pv[t] = masked ? 0.f : exp2f(v[e] * p.scale_log2 - m_new);
+              sum += pv[t];
+            }
+            hw[e2] = __floats2bfloat162_rn(pv[0], pv[1]);
+          }
+          *reinterpret_cast<uint4*>(sP + swz_offset(r, c * 32 + g * 8)) = w;
+        }
+      }
+      l = l * alpha + sum;
+      m2 = m_new;
+      // S buffer free; P visible to the tensor core; O rescale stores complete
+      tc_fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_empty[st]);
+        mbar_arrive(p_full);
+      }
+    }
+    // epilogue: wait for the last P V, then O / l
+    if (ok && mbar_wait(pv_done, (nblk - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+      tc_fence_after();
+      const float inv = (l > 0.f) ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = p.o + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tmem_ld_32cols(tO + lane_off + c * 32, o);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 w;
+          __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(o[g * 8 + 2 * e2] * inv, o[g * 8 + 2 * e2 + 1] * inv);
+          *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = w;
+        }
+      }
+      // natural-log LSE: (m2 + log2(l)) * ln 2
+      p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + qi] = (m2 + log2f(l)) * 0.69314718055994531f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+
+// ======================================================================================
+// Backward, one CTA per (128-key block j, KV head, batch); loops over the query heads of the
+// GQA group and the query blocks i >= j (causal).  K_j and V_j stay in smem; per (head, i):
+//   MMA      S^T = K_j Q_i^T  -> TMEM tS        dP^T = V_j dO_i^T -> TMEM tdP
+//   softmax  (one key row per thread) P^T = exp2(S^T*scale*log2e - lse_i*log2e) (causal mask
+//            on the diagonal block), dS^T = P^T * (dP^T - delta_i); both bf16 into swizzled smem
+//   MMA      dV += P^T dO_i      dK += dS^T Q_i      (dO_i, Q_i read MN-major from the same tiles)
+//            dQ_i = dS K_j       (dS^T read as an MN-major A operand) -> TMEM tS
+//   softmax  warps add scale * dQ_i into the fp32 dQ accumulator (vector reductions)
+// dK (x scale) and dV are written once at the end (bf16); no atomics for them.
+// ======================================================================================
+struct AttnBwdParams {
+  int B, T, Hq, Hkv, D;
+  float scale, scale_log2;
+  const float* lse;    // [B, Hq, T]
+  const float* delta;  // [B, Hq, T]
+  float* dq_acc;       // [B, T, Hq, D] fp32, zero-initialised
+  __nv_bfloat16* dk;   // [B, T, Hkv, D]
+  __nv_bfloat16* dv;
+  int* err;
+};
+
+template <int D>
+struct BwdSmem {
+  static constexpr int CH = D / 64;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE;
+  static constexpr int Q_OFF = 2 * TILE;
+  static constexpr int DO_OFF = 3 * TILE;
+  static constexpr int PT_OFF = 4 * TILE;           // P^T [128 keys x 128 q] bf16
+  static constexpr int DST_OFF = PT_OFF + 32768;    // dS^T [128 keys x 128 q] bf16
+  static constexpr int STAT_OFF = DST_OFF + 32768;  // lse*log2e [128], delta [128]
+  static constexpr int BAR_OFF = STAT_OFF + 1024;
+  static constexpr int BYTES0 = BAR_OFF + 256 + 1024;
+  static constexpr int BYTES = BYTES0 > 120 * 1024 ? BYTES0 : 120 * 1024;
+};
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const AttnBwdParams p) {
+  using L = BwdSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + L::K_OFF;
+  uint8_t* sV = smem + L::V_OFF;
+  uint8_t* sQ = smem + L::Q_OFF;
+  uint8_t* sDO = smem + L::DO_OFF;
+  uint8_t* sPt = smem + L::PT_OFF;
+  uint8_t* sDSt = smem + L::DST_OFF;
+  float* sLse = reinterpret_cast<float*>(smem + L::STAT_OFF);
+  float* sDelta = sLse + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* sp_full = bars + 3;
+  uint64_t* ds_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_empty = bars + 6;
+  uint64_t* drain = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = p.T / QB;
+  const int j = blockIdx.x;  // key block (small j = most work, scheduled first)
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int G = p.Hq / p.Hkv;
+  const int per_head = nqb - j;
+  const int n_iter = G * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(qdo_empty, 1);
+    mbar_init(sp_full, 1);
+    mbar_init(ds_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * L::TILE);
+#pragma unroll
+      for (int c = 0; c < L::CH; ++c) {
+        tma_load_4d(sK + c * 16384, &tmK, kv_full, c * 64, hk, j * KB, b);
+        tma_load_4d(sV + c * 16384, &tmV, kv_full, c * 64, hk, j * KB, b);
+      }
+      for (int n = 0; n < n_iter; ++n) {
+        const int h = hk * G + n / per_head;
+        const int i = j + n % per_head;
+        if (!mbar_wait(qdo_empty, (n & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        mbar_arrive_expect_tx(qdo_full, 2 * L::TILE);
+#pragma unroll
+        for (int c = 0; c < L::CH; ++c) {
+          tma_load_4d(sQ + c * 16384, &tmQ, qdo_full, c * 64, h, i * QB, b);
+          tma_load_4d(sDO + c * 16384, &tmDO, qdo_full, c * 64, h, i * QB, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(128, 128, false, false);   // S^T, dP^T
+      constexpr uint32_t id_kv = idesc_bf16_f32(128, D, false, true);     // dV, dK (B MN-major)
+      constexpr uint32_t id_q = idesc_bf16_f32(128, D, true, true);       // dQ (A and B MN-major)
+      bool ok = mbar_wait(kv_full, 0, p.err, ERR_MMA_FULL_TIMEOUT);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      const uint32_t pt_addr = smem_u32(sPt), dst_addr = smem_u32(sDSt);
+      for (int n = 0; ok && n < n_iter; ++n) {
+        ok = mbar_wait(qdo_full, n & 1, p.err, ERR_MMA_FULL_TIMEOUT) &&
+             mbar_wait(dq_empty, (n & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tS, sdesc_kmajor(k_addr + off), sdesc_kmajor(q_addr + off), id_s, kk ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tDP, sdesc_kmajor(v_addr + off), sdesc_kmajor(do_addr + off), id_s, kk ? 1u : 0u);
+        }
+        umma_commit(sp_full);
+        if (!mbar_wait(ds_full, n & 1, p.err, ERR_MMA_FULL_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tDV, sdesc_kmajor(pt_addr + aoff), sdesc_mnmajor(do_addr + kk * 2048, 16384), id_kv,
+                    (n | kk) ? 1u : 0u);
+          umma_bf16(tDK, sdesc_kmajor(dst_addr + aoff), sdesc_mnmajor(q_addr + kk * 2048, 16384), id_kv,
+                    (n | kk) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 keys
+          umma_bf16(tS, sdesc_mnmajor(dst_addr + kk * 2048, 16384), sdesc_mnmajor(k_addr + kk * 2048, 16384), id_q,
+                    kk ? 1u : 0u);
+        }
+        umma_commit(dq_full);
+        umma_commit(qdo_empty);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else {
+    const int q = warp & 3;
+    const int kr = q * 32 + lane;  // key row (S^T / dP^T lane) and, for dQ, query row
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int tid = threadIdx.x - 64;  // 0..127
+    bool ok = true;
+    for (int n = 0; n < n_iter && ok; ++n) {
+      const int h = hk * G + n / per_head;
+      const int i = j + n % per_head;
+      // row statistics of query block i (previous iteration's readers are past this barrier)
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      {
+        const int64_t o = (static_cast<int64_t>(b) * p.Hq + h) * p.T + i * QB + tid;
+        sLse[tid] = p.lse[o] * 1.4426950408889634f;
+        sDelta[tid] = p.delta[o];
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!mbar_wait(sp_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (i == j);
+#pragma unroll 1
+      for (int c = 0; c < 128 / 32; ++c) {
+        float sv[32], dp[32];
+        tmem_ld_32cols(tS + lane_off + c * 32, sv);
+        tmem_ld_32cols(tDP + lane_off + c * 32, dp);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 wp, wd;
+          __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&wp);
+          __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int e = g * 8 + e2 * 2 + t;
+              const int qc = c * 32 + e;
+              const bool masked = diag && (qc < kr);
+              const float pr = masked ? 0.f : exp2f(sv[e] * p.scale_log2 - sLse[qc]);
+              pv[t] = pr;
+              dv[t] = pr * (dp[e] - sDelta[qc]);
+            }
+            hp[e2] = __floats2bfloat162_rn(pv[0], pv[1]);
+            hd[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
+          }
+          const uint32_t off = swz_offset(kr, c * 32 + g * 8);
+          *reinterpret_cast<uint4*>(sPt + off) = wp;
+          *reinterpret_cast<uint4*>(sDSt + off) = wd;
+        }
+      }
+      tc_fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+      // dQ_i partial (TMEM lanes = query rows) -> fp32 accumulator
+      if (!mbar_wait(dq_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float* dqrow = p.dq_acc + ((static_cast<int64_t>(b) * p.T + i * QB + kr) * p.Hq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        tmem_ld_32cols(tS + lane_off + c * 32, v);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          red_add_v4(dqrow + c * 32 + e, v[e] * p.scale, v[e + 1] * p.scale, v[e + 2] * p.scale, v[e + 3] * p.scale);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+    }
+    // dK_j (x scale) and dV_j: all MMAs finished (the last dq_full was waited above)
+    if (ok) {
+      tc_fence_after();
+      const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hkv + hk;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * D;
+        const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off;
+        const float f = which == 0 ? 1.f : p.scale;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld_32cols(tb + c * 32, v);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 w;
+            __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+            for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(v[g * 8 + 2 * e2] * f, v[g * 8 + 2 * e2 + 1] * f);
+            *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[b, h, t] = sum_d dO * O  (one warp per row)
+__global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dO,
+                                      float* __restrict__ delta, int B, int T, int H, int D) {
+  const int64_t rows = static_cast<int64_t>(B) * T * H;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const __nv_bfloat16* a = o + r * D;
+  const __nv_bfloat16* g = dO + r * D;
+  float s = 0.f;
+  for (int d = lane; d < D; d += 32) s = fmaf(__bfloat162float(a[d]), __bfloat162float(g[d]), s);
+  s = warp_sum(s);
+  if (lane == 0) {
+    const int h = static_cast<int>(r % H);
+    const int64_t bt = r / H;
+    const int t = static_cast<int>(bt % T);
+    const int bb = static_cast<int>(bt / T);
+    delta[(static_cast<int64_t>(bb) * H + h) * T + t] = s;
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// ------------------------------------ host side ------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn) throw std::runtime_error("mmf: cuTensorMapEncodeTiled unavailable");
+  return fn;
+}
+
+// [B, T, H, D] bf16 tensor, box {64 (D), 1 (head), 128 (T), 1}
+CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("mmf: attention tensors must be 16B aligned");
+  CUtensorMap m;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(T),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(H) * D * 2,
+                           static_cast<cuuint64_t>(T) * H * D * 2};
+  cuuint32_t box[4] = {64, 1, 128, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("mmf: attention tensor map encode failed: " + std::to_string((int)r));
+  return m;
+}
+
+template <int D>
+void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<D>::BYTES);
+    attr_set[dev] = true;
+  }
+  AttnParams p{};
+  p.B = a.B;
+  p.T = a.T;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.D = D;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.o = static_cast<__nv_bfloat16*>(a.o);
+  p.lse = a.lse;
+  p.err = device_error_word(dev);
+  CUtensorMap mq = map_bthd(a.q, a.B, a.T, a.Hq, D);
+  CUtensorMap mk = map_bthd(a.k, a.B, a.T, a.Hkv, D);
+  CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
+  dim3 grid(a.T / QB, a.Hq, a.B);
+  attn_fwd_kernel<D><<<grid, ATT_THREADS, AttnSmem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: attention launch failed: ") + cudaGetErrorString(e));
+}
+
+
+template <int D>
+void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
+    attr_set[dev] = true;
+  }
+  const int64_t rows = static_cast<int64_t>(a.B) * a.T * a.Hq;
+  attn_bwd_delta_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(a.o), static_cast<const __nv_bfloat16*>(a.dout), a.delta, a.B, a.T, a.Hq, D);
+  count_launch();
+  cudaMemsetAsync(a.dq_acc, 0, sizeof(float) * rows * D, stream);
+  AttnBwdParams p{};
+  p.B = a.B;
+  p.T = a.T;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.D = D;
+  p.scale = a.scale;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  p.lse = a.lse;
+  p.delta = a.delta;
+  p.dq_acc = a.dq_acc;
+  p.dk = static_cast<__nv_bfloat16*>(a.dk);
+  p.dv = static_cast<__nv_bfloat16*>(a.dv);
+  p.err = device_error_word(dev);
+  CUtensorMap mq = map_bthd(a.q, a.B, a.T, a.Hq, D);
+  CUtensorMap mk = map_bthd(a.k, a.B, a.T, a.Hkv, D);
+  CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
+  CUtensorMap mdo = map_bthd(a.dout, a.B, a.T, a.Hq, D);
+  dim3 grid(a.T / KB, a.Hkv, a.B);
+  attn_bwd_kernel<D><<<grid, ATT_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  count_launch();
+  const int64_t n = rows * D;
+  f32_to_bf16_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 16)), 256, 0, stream>>>(
+      a.dq_acc, static_cast<__nv_bfloat16*>(a.dq), n);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: attention bwd launch failed: ") + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+void attention_fwd(const AttnArgs& a, cudaStream_t stream) {
+  if (a.T % QB != 0) throw std::runtime_error("mmf: attention needs T % 128 == 0");
+  if (a.Hkv <= 0 || a.Hq % a.Hkv != 0) throw std::runtime_error("mmf: Hq must be a multiple of Hkv");
+  if (a.D == 128)
+    launch_fwd<128>(a, stream);
+  else if (a.D == 64)
+    launch_fwd<64>(a, stream);
+  else
+    throw std::runtime_error("mmf: attention supports head_dim 64 or 128");
+}
+
+}  // namespace mmf
+
+namespace mmf {
+void attention_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
+  if (a.T % KB != 0) throw std::runtime_error("mmf: attention needs T % 128 == 0");
+  if (a.Hkv <= 0 || a.Hq % a.Hkv != 0) throw std::runtime_error("mmf: Hq must be a multiple of Hkv");
+  if (a.D == 128)
+    launch_bwd<128>(a, stream);
+  else if (a.D == 64)
+    launch_bwd<64>(a, stream);
+  else
+    throw std::runtime_error("mmf: attention supports head_dim 64 or 128");
+}
+}  // namespace mmf

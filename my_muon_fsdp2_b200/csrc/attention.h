@@ -1,0 +1,36 @@
+// Causal GQA flash attention on tcgen05 (see attention.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mmf {
+
+struct AttnArgs {
+  const void* q;  // [B, T, Hq, D] bf16
+  const void* k;  // [B, T, Hkv, D] bf16
+  const void* v;  // [B, T, Hkv, D] bf16
+  void* o;        // [B, T, Hq, D] bf16
+  float* lse;     // [B, Hq, T] fp32 (natural log)
+  int B, T, Hq, Hkv, D;
+  float scale;
+};
+void attention_fwd(const AttnArgs& a, cudaStream_t stream);
+
+struct AttnBwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* dout;  // [B, T, Hq, D] bf16
+  const float* lse;  // [B, Hq, T]
+  float* delta;      // [B, Hq, T] scratch
+  float* dq_acc;     // [B, T, Hq, D] fp32 scratch
+  void* dq;          // [B, T, Hq, D] bf16
+  void* dk;          // [B, T, Hkv, D] bf16
+  void* dv;          // [B, T, Hkv, D] bf16
+  int B, T, Hq, Hkv, D;
+  float scale;
+};
+void attention_bwd(const AttnBwdArgs& a, cudaStream_t stream);
+
+}  // namespace mmf

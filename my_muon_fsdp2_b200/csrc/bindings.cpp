@@ -7,6 +7,7 @@
 #include <cstring>
 #include <vector>
 
+#include "attention.h"
 #include "kernels.h"
 #include "symm_comm.h"
 
@@ -469,6 +470,66 @@ void symm_barrier(Tensor pad_ptrs, int64_t rank, int64_t ws, int64_t epoch, int6
                     static_cast<uint64_t>(timeout_s * 1e9), cur_stream());
 }
 
+// q [B, T, Hq, D], k/v [B, T, Hkv, D] bf16 contiguous -> (o [B, T, Hq, D], lse [B, Hq, T])
+std::vector<Tensor> attention_fwd(Tensor q, Tensor k, Tensor v, double scale) {
+  check_bf16_contig(q, "q");
+  check_bf16_contig(k, "k");
+  check_bf16_contig(v, "v");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "mmf: attention tensors are [B, T, H, D]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  mmf::AttnArgs a{};
+  a.B = static_cast<int>(q.size(0));
+  a.T = static_cast<int>(q.size(1));
+  a.Hq = static_cast<int>(q.size(2));
+  a.D = static_cast<int>(q.size(3));
+  a.Hkv = static_cast<int>(k.size(2));
+  TORCH_CHECK(k.sizes() == v.sizes() && k.size(0) == a.B && k.size(1) == a.T && k.size(3) == a.D,
+              "mmf: k/v shapes must match q");
+  Tensor o = torch::empty_like(q);
+  Tensor lse = torch::empty({a.B, a.Hq, a.T}, q.options().dtype(torch::kFloat32));
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.o = o.data_ptr();
+  a.lse = lse.data_ptr<float>();
+  a.scale = static_cast<float>(scale);
+  mmf::attention_fwd(a, cur_stream());
+  return {o, lse};
+}
+
+std::vector<Tensor> attention_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, double scale) {
+  check_bf16_contig(dout, "dout");
+  check_bf16_contig(q, "q");
+  check_bf16_contig(k, "k");
+  check_bf16_contig(v, "v");
+  check_bf16_contig(o, "o");
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.is_contiguous(), "mmf: lse must be contiguous fp32");
+  const c10::cuda::CUDAGuard guard(q.device());
+  mmf::AttnBwdArgs a{};
+  a.B = static_cast<int>(q.size(0));
+  a.T = static_cast<int>(q.size(1));
+  a.Hq = static_cast<int>(q.size(2));
+  a.D = static_cast<int>(q.size(3));
+  a.Hkv = static_cast<int>(k.size(2));
+  Tensor dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  Tensor delta = torch::empty({a.B, a.Hq, a.T}, q.options().dtype(torch::kFloat32));
+  Tensor dq_acc = torch::empty({a.B, a.T, a.Hq, a.D}, q.options().dtype(torch::kFloat32));
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.o = o.data_ptr();
+  a.dout = dout.data_ptr();
+  a.lse = lse.data_ptr<float>();
+  a.delta = delta.data_ptr<float>();
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dq = dq.data_ptr();
+  a.dk = dk.data_ptr();
+  a.dv = dv.data_ptr();
+  a.scale = static_cast<float>(scale);
+  mmf::attention_bwd(a, cur_stream());
+  return {dq, dk, dv};
+}
+
 int64_t device_error(int64_t device) {
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   return mmf::read_and_clear_device_error(static_cast<int>(device), cur_stream());
@@ -499,6 +560,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_", &cross_entropy_);
   m.def("power_iteration", &power_iteration);
   m.def("symm_barrier", &symm_barrier);
+  m.def("attention_fwd", &attention_fwd);
+  m.def("attention_bwd", &attention_bwd);
   m.def("set_gemm_variant", [](int64_t v) { mmf::set_gemm_variant(static_cast<int>(v)); });
   m.def("gemm_variant", []() { return static_cast<int64_t>(mmf::gemm_variant()); });
   m.def("device_error", &device_error);

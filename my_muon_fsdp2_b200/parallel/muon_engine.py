@@ -260,8 +260,14 @@ class MuonEngine:
                 u = _momentum_torch(t, hp).float()
                 sumsq[j] = (u * u).sum()
                 send[send_off[j]:send_off[j] + cnt[j][rank]].copy_(u.reshape(-1))
-        # ---- 2. global Frobenius norms
-        dist.all_reduce(sumsq, group=group)
+        # ---- 2. global Frobenius norms (CUDA: gather the per-rank partials and sum them in rank
+        #      order on the owner, exactly like the P2P path, so both exchanges agree bit for bit)
+        parts = None
+        if is_cuda:
+            parts = torch.empty(world, n, dtype=torch.float32, device=dev)
+            dist.all_gather_into_tensor(parts, sumsq, group=group)
+        else:
+            dist.all_reduce(sumsq, group=group)
         # ---- 3. shards -> owners
         recv_split = [sum(cnt[j][r] for j in owned[rank]) for r in range(world)]
         recv = torch.empty(sum(recv_split), dtype=xdtype, device=dev)
@@ -288,7 +294,7 @@ class MuonEngine:
         if owned[rank]:
             if is_cuda:
                 self._cuda_owner_ns(tasks, hp, owned[rank], shapes, rows_of, cnt, world, recv, shard_at, back,
-                                    back_at, sumsq)
+                                    back_at, parts)
             else:
                 for j in owned[rank]:
                     rws, cls = shapes[j]
@@ -436,7 +442,7 @@ class MuonEngine:
             sumsq.index_copy_(0, torch.tensor(live, device=send.device), part)
 
     def _cuda_owner_ns(self, tasks, hp, mine, shapes, rows_of, cnt, world, recv, shard_at, back, back_at,
-                       sumsq) -> None:
+                       parts) -> None:
         from .._ext import ext
         from ..ops.ns_cuda import round_up, run_ns_group, wide_shape
 
@@ -467,10 +473,10 @@ class MuonEngine:
                         row0.append(chunk_offset(rws, world, r))
                         trs.append(int(tall))
                 E.muon_prep(srcs, [], [], X0, offs, row0, trs, [Np], [], [], MODE_COPY, False, 0.0, 0.0, None)
-                ssq = sumsq.index_select(0, torch.tensor(sub, device=dev))
+                ssq = parts.index_select(1, torch.tensor(sub, device=dev)).contiguous()  # [world, B]
                 s = torch.empty(B, dtype=torch.float32, device=dev)
                 s2 = torch.empty_like(s)
-                E.ns_scale(ssq, B, 1, NS_EPS, s, s2)
+                E.ns_scale(ssq, B, world, NS_EPS, s, s2)
                 seg_views, meta = [], []
                 for j in sub:
                     rws, cls = shapes[j]
