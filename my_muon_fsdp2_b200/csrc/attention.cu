@@ -28,6 +28,7 @@ namespace {
 constexpr int QB = 128;  // query rows per CTA
 constexpr int KB = 128;  // keys per block
 constexpr int ATT_THREADS = 192;
+constexpr int BWD_THREADS = 320;  // TMA warp, MMA warp, 8 elementwise warps (2 per TMEM lane quarter)
 
 struct AttnParams {
   int B, T, Hq, Hkv, D;
@@ -194,20 +195,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
       tc_fence_after();
       const bool diag = (j == qb);
-      // pass 1: row max of the scaled scores
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < KB / 32; ++c) {
-        float v[32];
-        tmem_ld_32cols(tS[st] + lane_off + c * 32, v);
+      // the whole 128-column S row in registers: 4 loads, one wait
+      float sv[KB];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const bool masked = diag && (j * KB + c * 32 + e > qi);
-          if (!masked) mx = fmaxf(mx, v[e] * p.scale_log2);
-        }
+      for (int c = 0; c < KB / 32; ++c) tmem_ld_32cols_async(tS[st] + lane_off + c * 32, sv + c * 32);
+      tmem_ld_wait();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < KB; ++e) {
+        sv[e] *= p.scale_log2;
+        if (diag && (j * KB + e > qi)) sv[e] = -INFINITY;
+        mx = fmaxf(mx, sv[e]);
       }
       const float m_new = fmaxf(m2, mx);
-      const float alpha = (m2 == -INFINITY) ? 0.f : exp2f(m2 - m_new);
+      const float alpha = (m2 == -INFINITY) ? 0.f : fast_exp2(m2 - m_new);
       // P_{j-1} V_{j-1} must be done before O is rescaled and P is overwritten
       if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
         ok = false;
@@ -215,39 +216,33 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
       tc_fence_after();
       if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          float o[32];
-          tmem_ld_32cols(tO + lane_off + c * 32, o);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] *= alpha;
-          tmem_st_32cols(tO + lane_off + c * 32, o);
+        for (int hh = 0; hh < D / 64; ++hh) {
+          float o[64];
+          tmem_ld_32cols_async(tO + lane_off + hh * 64, o);
+          tmem_ld_32cols_async(tO + lane_off + hh * 64 + 32, o + 32);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 64; ++e) o[e] *= alpha;
+          tmem_st_32cols_async(tO + lane_off + hh * 64, o);
+          tmem_st_32cols_async(tO + lane_off + hh * 64 + 32, o + 32);
         }
+        tmem_st_wait();
       }
-      // pass 2: probabilities -> swizzled bf16 P tile, row sum
+      // probabilities -> swizzled bf16 P tile, row sum
       float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < KB / 32; ++c) {
-        float v[32];
-        tmem_ld_32cols(tS[st] + lane_off + c * 32, v);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 w;
-          __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+      for (int g = 0; g < KB / 8; ++g) {
+        uint4 w;
+        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
 #pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            float pv[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int e = g * 8 + e2 * 2 + t;
-              const bool masked = diag && (j * KB + c * 32 + e > qi);
-              pv[t] = masked ? 0.f : exp2f(v[e] * p.scale_log2 - m_new);
-              sum += pv[t];
-            }
-            hw[e2] = __floats2bfloat162_rn(pv[0], pv[1]);
-          }
-          *reinterpret_cast<uint4*>(sP + swz_offset(r, c * 32 + g * 8)) = w;
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const float p0 = fast_exp2(sv[g * 8 + 2 * e2] - m_new);
+          const float p1 = fast_exp2(sv[g * 8 + 2 * e2 + 1] - m_new);
+          sum += p0 + p1;
+          hw[e2] = __floats2bfloat162_rn(p0, p1);
         }
+        *reinterpret_cast<uint4*>(sP + swz_offset(r, g * 8)) = w;
       }
       l = l * alpha + sum;
       m2 = m_new;
@@ -265,18 +260,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.f / l : 0.f;
       __nv_bfloat16* orow = p.o + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        tmem_ld_32cols(tO + lane_off + c * 32, o);
+      float o[D];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 w;
-          __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+      for (int c = 0; c < D / 32; ++c) tmem_ld_32cols_async(tO + lane_off + c * 32, o + c * 32);
+      tmem_ld_wait();
 #pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(o[g * 8 + 2 * e2] * inv, o[g * 8 + 2 * e2 + 1] * inv);
-          *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = w;
-        }
+      for (int g = 0; g < D / 8; ++g) {
+        uint4 w;
+        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(o[g * 8 + 2 * e2] * inv, o[g * 8 + 2 * e2 + 1] * inv);
+        *reinterpret_cast<uint4*>(orow + g * 8) = w;
       }
       // natural-log LSE: (m2 + log2(l)) * ln 2
       p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + qi] = (m2 + log2f(l)) * 0.69314718055994531f;
@@ -319,10 +313,9 @@ struct BwdSmem {
   static constexpr int TILE = 128 * D * 2;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = TILE;
-  static constexpr int Q_OFF = 2 * TILE;
-  static constexpr int DO_OFF = 3 * TILE;
-  static constexpr int PT_OFF = 4 * TILE;           // P^T [128 keys x 128 q] bf16
-  static constexpr int DST_OFF = PT_OFF + 32768;    // dS^T [128 keys x 128 q] bf16
+  static constexpr int Q_OFF = 2 * TILE;            // 2 buffers (prefetch of the next query block)
+  static constexpr int DO_OFF = 4 * TILE;           // 2 buffers
+  static constexpr int DST_OFF = 6 * TILE;          // dS^T [128 keys x 128 q] bf16 (P^T lives in TMEM)
   static constexpr int STAT_OFF = DST_OFF + 32768;  // lse*log2e [128], delta [128]
   static constexpr int BAR_OFF = STAT_OFF + 1024;
   static constexpr int BYTES0 = BAR_OFF + 256 + 1024;
@@ -335,7 +328,7 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 }
 
 template <int D>
-__global__ void __launch_bounds__(ATT_THREADS, 1)
+__global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const AttnBwdParams p) {
@@ -346,20 +339,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint8_t* sV = smem + L::V_OFF;
   uint8_t* sQ = smem + L::Q_OFF;
   uint8_t* sDO = smem + L::DO_OFF;
-  uint8_t* sPt = smem + L::PT_OFF;
   uint8_t* sDSt = smem + L::DST_OFF;
   float* sLse = reinterpret_cast<float*>(smem + L::STAT_OFF);
   float* sDelta = sLse + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* sp_full = bars + 3;
-  uint64_t* ds_full = bars + 4;
-  uint64_t* dq_full = bars + 5;
-  uint64_t* dq_empty = bars + 6;
-  uint64_t* drain = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* q_full = bars + 1;   // [2]
+  uint64_t* q_empty = bars + 3;  // [2]
+  uint64_t* do_full = bars + 5;   // [2]
+  uint64_t* do_empty = bars + 7;  // [2]
+  uint64_t* sp_full = bars + 9;
+  uint64_t* ds_full = bars + 10;
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_empty = bars + 12;
+  uint64_t* drain = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = p.T / QB;
@@ -371,12 +365,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qdo_full, 1);
-    mbar_init(qdo_empty, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&q_full[t], 1);
+      mbar_init(&q_empty[t], 1);
+      mbar_init(&do_full[t], 1);
+      mbar_init(&do_empty[t], 1);
+    }
     mbar_init(sp_full, 1);
-    mbar_init(ds_full, 4);
+    mbar_init(ds_full, 8);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 4);
+    mbar_init(dq_empty, 8);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -407,13 +405,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       for (int n = 0; n < n_iter; ++n) {
         const int h = hk * G + n / per_head;
         const int i = j + n % per_head;
-        if (!mbar_wait(qdo_empty, (n & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * L::TILE);
+        const int qs = n & 1;
+        if (!mbar_wait(&q_empty[qs], ((n >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&q_full[qs], L::TILE);
 #pragma unroll
-        for (int c = 0; c < L::CH; ++c) {
-          tma_load_4d(sQ + c * 16384, &tmQ, qdo_full, c * 64, h, i * QB, b);
-          tma_load_4d(sDO + c * 16384, &tmDO, qdo_full, c * 64, h, i * QB, b);
-        }
+        for (int c = 0; c < L::CH; ++c) tma_load_4d(sQ + qs * L::TILE + c * 16384, &tmQ, &q_full[qs], c * 64, h, i * QB, b);
+        if (!mbar_wait(&do_empty[qs], ((n >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&do_full[qs], L::TILE);
+#pragma unroll
+        for (int c = 0; c < L::CH; ++c)
+          tma_load_4d(sDO + qs * L::TILE + c * 16384, &tmDO, &do_full[qs], c * 64, h, i * QB, b);
       }
     }
   } else if (warp == 1) {
@@ -422,80 +423,92 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       constexpr uint32_t id_kv = idesc_bf16_f32(128, D, false, true);     // dV, dK (B MN-major)
       constexpr uint32_t id_q = idesc_bf16_f32(128, D, true, true);       // dQ (A and B MN-major)
       bool ok = mbar_wait(kv_full, 0, p.err, ERR_MMA_FULL_TIMEOUT);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
-      const uint32_t pt_addr = smem_u32(sPt), dst_addr = smem_u32(sDSt);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_base = smem_u32(sQ), do_base = smem_u32(sDO);
+      const uint32_t dst_addr = smem_u32(sDSt);
       for (int n = 0; ok && n < n_iter; ++n) {
-        ok = mbar_wait(qdo_full, n & 1, p.err, ERR_MMA_FULL_TIMEOUT) &&
-             mbar_wait(dq_empty, (n & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT);
-        if (!ok) break;
+        // S^T into tS (free: the elementwise warps finished reading it before ds_full(n-1))
+        const int qs = n & 1;
+        const uint32_t q_addr = q_base + qs * L::TILE;
+        const uint32_t do_addr = do_base + qs * L::TILE;
+        if (!mbar_wait(&q_full[qs], (n >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
           umma_bf16(tS, sdesc_kmajor(k_addr + off), sdesc_kmajor(q_addr + off), id_s, kk ? 1u : 0u);
         }
+        // dP^T into tDP once dQ of the previous iteration has been read out of it
+        if (!mbar_wait(dq_empty, (n & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) break;
+        if (!mbar_wait(&do_full[qs], (n >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
           umma_bf16(tDP, sdesc_kmajor(v_addr + off), sdesc_kmajor(do_addr + off), id_s, kk ? 1u : 0u);
         }
         umma_commit(sp_full);
-        if (!mbar_wait(ds_full, n & 1, p.err, ERR_MMA_FULL_TIMEOUT)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(ds_full, n & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows
           const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tDV, sdesc_kmajor(pt_addr + aoff), sdesc_mnmajor(do_addr + kk * 2048, 16384), id_kv,
-                    (n | kk) ? 1u : 0u);
+          // P^T from TMEM: query columns [64h, 64h+64) were packed into columns [64h, 64h+32) of tS
+          const uint32_t a_tm = tS + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8);
+          umma_bf16_ts(tDV, a_tm, sdesc_mnmajor(do_addr + kk * 2048, 16384), id_kv, (n | kk) ? 1u : 0u);
           umma_bf16(tDK, sdesc_kmajor(dst_addr + aoff), sdesc_mnmajor(q_addr + kk * 2048, 16384), id_kv,
                     (n | kk) ? 1u : 0u);
         }
+        // dQ_i = dS K_j into tDP (dP^T was consumed before ds_full)
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 keys
-          umma_bf16(tS, sdesc_mnmajor(dst_addr + kk * 2048, 16384), sdesc_mnmajor(k_addr + kk * 2048, 16384), id_q,
+          umma_bf16(tDP, sdesc_mnmajor(dst_addr + kk * 2048, 16384), sdesc_mnmajor(k_addr + kk * 2048, 16384), id_q,
                     kk ? 1u : 0u);
         }
         umma_commit(dq_full);
-        umma_commit(qdo_empty);
+        umma_commit(&q_empty[qs]);
+        umma_commit(&do_empty[qs]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
     }
   } else {
     const int q = warp & 3;
-    const int kr = q * 32 + lane;  // key row (S^T / dP^T lane) and, for dQ, query row
+    const int half = (warp - 2) >> 2;  // which 64 query columns (and D/2 output columns) this warp owns
+    const int kr = q * 32 + lane;      // key row (S^T / dP^T lane) and, for dQ, query row
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const int tid = threadIdx.x - 64;  // 0..127
+    const int tid = threadIdx.x - 64;  // 0..255
     bool ok = true;
     for (int n = 0; n < n_iter && ok; ++n) {
       const int h = hk * G + n / per_head;
       const int i = j + n % per_head;
-      // row statistics of query block i (previous iteration's readers are past this barrier)
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      // row statistics of query block i (the previous iteration's readers are past this barrier)
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       {
-        const int64_t o = (static_cast<int64_t>(b) * p.Hq + h) * p.T + i * QB + tid;
-        sLse[tid] = p.lse[o] * 1.4426950408889634f;
-        sDelta[tid] = p.delta[o];
+        const int64_t o = (static_cast<int64_t>(b) * p.Hq + h) * p.T + i * QB + (tid & 127);
+        if (tid < 128)
+          sLse[tid] = p.lse[o] * 1.4426950408889634f;
+        else
+          sDelta[tid - 128] = p.delta[o];
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       if (!mbar_wait(sp_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const bool diag = (i == j);
-#pragma unroll 1
-      for (int c = 0; c < 128 / 32; ++c) {
-        float sv[32], dp[32];
-        tmem_ld_32cols(tS + lane_off + c * 32, sv);
-        tmem_ld_32cols(tDP + lane_off + c * 32, dp);
+      {
+        const int c0 = half * 64;
+        float sv[64], dp[64];
+        tmem_ld_32cols_async(tS + lane_off + c0, sv);
+        tmem_ld_32cols_async(tS + lane_off + c0 + 32, sv + 32);
+        tmem_ld_32cols_async(tDP + lane_off + c0, dp);
+        tmem_ld_32cols_async(tDP + lane_off + c0 + 32, dp + 32);
+        tmem_ld_wait();
+        float ppk[32];  // P^T as bf16 pairs, reinterpreted as 32-bit TMEM words
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 wp, wd;
-          __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&wp);
+        for (int g = 0; g < 8; ++g) {
+          uint4 wd;
           __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
@@ -503,42 +516,45 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
               const int e = g * 8 + e2 * 2 + t;
-              const int qc = c * 32 + e;
+              const int qc = c0 + e;
               const bool masked = diag && (qc < kr);
-              const float pr = masked ? 0.f : exp2f(sv[e] * p.scale_log2 - sLse[qc]);
+              const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - sLse[qc]);
               pv[t] = pr;
               dv[t] = pr * (dp[e] - sDelta[qc]);
             }
-            hp[e2] = __floats2bfloat162_rn(pv[0], pv[1]);
+            __nv_bfloat162 pb = __floats2bfloat162_rn(pv[0], pv[1]);
+            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
             hd[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
           }
-          const uint32_t off = swz_offset(kr, c * 32 + g * 8);
-          *reinterpret_cast<uint4*>(sPt + off) = wp;
-          *reinterpret_cast<uint4*>(sDSt + off) = wd;
+          *reinterpret_cast<uint4*>(sDSt + swz_offset(kr, c0 + g * 8)) = wd;
         }
+        // packed P^T over this warp's own (already consumed) S columns
+        tmem_st_32cols_async(tS + lane_off + c0, ppk);
+        tmem_st_wait();
       }
       tc_fence_before();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full);
-      // dQ_i partial (TMEM lanes = query rows) -> fp32 accumulator
+      // dQ_i partial (in tDP; TMEM lanes = query rows) -> fp32 accumulator, this warp's D/2 columns
       if (!mbar_wait(dq_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float* dqrow = p.dq_acc + ((static_cast<int64_t>(b) * p.T + i * QB + kr) * p.Hq + h) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        tmem_ld_32cols(tS + lane_off + c * 32, v);
+      {
+        float* dqrow = p.dq_acc + ((static_cast<int64_t>(b) * p.T + i * QB + kr) * p.Hq + h) * D + half * (D / 2);
+        float v[D / 2];
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          red_add_v4(dqrow + c * 32 + e, v[e] * p.scale, v[e + 1] * p.scale, v[e + 2] * p.scale, v[e + 3] * p.scale);
+        for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tDP + lane_off + half * (D / 2) + c * 32, v + c * 32);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);  // tDP may be overwritten while the reductions drain
+#pragma unroll
+        for (int e = 0; e < D / 2; e += 4)
+          red_add_v4(dqrow + e, v[e] * p.scale, v[e + 1] * p.scale, v[e + 2] * p.scale, v[e + 3] * p.scale);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
     }
     // dK_j (x scale) and dV_j: all MMAs finished (the last dq_full was waited above)
     if (ok) {
@@ -546,21 +562,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hkv + hk;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
-        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * D;
-        const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off;
+        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * D + half * (D / 2);
+        const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off + half * (D / 2);
         const float f = which == 0 ? 1.f : p.scale;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tmem_ld_32cols(tb + c * 32, v);
+        float v[D / 2];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 w;
-            __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+        for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tb + c * 32, v + c * 32);
+        tmem_ld_wait();
 #pragma unroll
-            for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(v[g * 8 + 2 * e2] * f, v[g * 8 + 2 * e2 + 1] * f);
-            *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = w;
-          }
+        for (int g = 0; g < D / 16; ++g) {
+          uint4 w;
+          __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(v[g * 8 + 2 * e2] * f, v[g * 8 + 2 * e2 + 1] * f);
+          *reinterpret_cast<uint4*>(dst + g * 8) = w;
         }
       }
     }
@@ -695,7 +710,7 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
   CUtensorMap mdo = map_bthd(a.dout, a.B, a.T, a.Hq, D);
   dim3 grid(a.T / KB, a.Hkv, a.B);
-  attn_bwd_kernel<D><<<grid, ATT_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  attn_bwd_kernel<D><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
   count_launch();
   const int64_t n = rows * D;
   f32_to_bf16_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 16)), 256, 0, stream>>>(
