@@ -302,8 +302,8 @@ struct AttnBwdParams {
   const float* lse;    // [B, Hq, T]
   const float* delta;  // [B, Hq, T]
   float* dq_acc;       // [B, T, Hq, D] fp32, zero-initialised
-  __nv_bfloat16* dk;   // [B, T, Hkv, D]
-  __nv_bfloat16* dv;
+  float* dk_h;         // [B, T, Hq, D] fp32: dK of each query head (summed over the GQA group later)
+  float* dv_h;         // [B, T, Hq, D] fp32
   int* err;
 };
 
@@ -358,10 +358,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = p.T / QB;
   const int j = blockIdx.x;  // key block (small j = most work, scheduled first)
-  const int hk = blockIdx.y, b = blockIdx.z;
-  const int G = p.Hq / p.Hkv;
+  const int hq = blockIdx.y, b = blockIdx.z;
+  const int hk = hq / (p.Hq / p.Hkv);
   const int per_head = nqb - j;
-  const int n_iter = G * per_head;
+  const int n_iter = per_head;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -403,8 +403,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tma_load_4d(sV + c * 16384, &tmV, kv_full, c * 64, hk, j * KB, b);
       }
       for (int n = 0; n < n_iter; ++n) {
-        const int h = hk * G + n / per_head;
-        const int i = j + n % per_head;
+        const int h = hq;
+        const int i = j + n;
         const int qs = n & 1;
         if (!mbar_wait(&q_empty[qs], ((n >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
         mbar_arrive_expect_tx(&q_full[qs], L::TILE);
@@ -478,19 +478,22 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int tid = threadIdx.x - 64;  // 0..255
     bool ok = true;
+    // row statistics are prefetched one iteration ahead into a register (one value per thread)
+    const float* stat_src = (tid < 128) ? p.lse : p.delta;
+    const float stat_mul = (tid < 128) ? 1.4426950408889634f : 1.f;
+    const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + (tid & 127);
+    float stat_next = stat_src[stat_base + j * QB] * stat_mul;
     for (int n = 0; n < n_iter && ok; ++n) {
-      const int h = hk * G + n / per_head;
-      const int i = j + n % per_head;
-      // row statistics of query block i (the previous iteration's readers are past this barrier)
+      const int h = hq;
+      const int i = j + n;
+      // publish this iteration's statistics (the previous iteration's readers are past the barrier)
       asm volatile("bar.sync 1, 256;" ::: "memory");
-      {
-        const int64_t o = (static_cast<int64_t>(b) * p.Hq + h) * p.T + i * QB + (tid & 127);
-        if (tid < 128)
-          sLse[tid] = p.lse[o] * 1.4426950408889634f;
-        else
-          sDelta[tid - 128] = p.delta[o];
-      }
+      if (tid < 128)
+        sLse[tid] = stat_next;
+      else
+        sDelta[tid - 128] = stat_next;
       asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
       if (!mbar_wait(sp_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
         ok = false;
         break;
@@ -559,10 +562,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     // dK_j (x scale) and dV_j: all MMAs finished (the last dq_full was waited above)
     if (ok) {
       tc_fence_after();
-      const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hkv + hk;
+      const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hq + hq;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
-        __nv_bfloat16* dst = (which == 0 ? p.dv : p.dk) + row * D + half * (D / 2);
+        float* dst = (which == 0 ? p.dv_h : p.dk_h) + row * D + half * (D / 2);
         const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off + half * (D / 2);
         const float f = which == 0 ? 1.f : p.scale;
         float v[D / 2];
@@ -570,13 +573,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tb + c * 32, v + c * 32);
         tmem_ld_wait();
 #pragma unroll
-        for (int g = 0; g < D / 16; ++g) {
-          uint4 w;
-          __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(v[g * 8 + 2 * e2] * f, v[g * 8 + 2 * e2 + 1] * f);
-          *reinterpret_cast<uint4*>(dst + g * 8) = w;
-        }
+        for (int g = 0; g < D / 8; ++g)
+          *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4] * f, v[g * 4 + 1] * f, v[g * 4 + 2] * f, v[g * 4 + 3] * f);
       }
     }
   }
@@ -606,6 +604,26 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, const
     const int t = static_cast<int>(bt % T);
     const int bb = static_cast<int>(bt / T);
     delta[(static_cast<int64_t>(bb) * H + h) * T + t] = s;
+  }
+}
+
+// dk[b, t, hk, d] = sum_{g < G} dk_h[b, t, hk*G + g, d] (and dv), as bf16.
+__global__ void gqa_reduce_kernel(const float* __restrict__ dk_h, const float* __restrict__ dv_h,
+                                  __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int64_t rows_kv, int G,
+                                  int D) {
+  const int64_t n = rows_kv * D;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < n;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / D;  // (b, t, hk) row
+    const int d = static_cast<int>(e % D);
+    const int64_t base = (r * G) * D + d;
+    float a = 0.f, c = 0.f;
+    for (int g = 0; g < G; ++g) {
+      a += dk_h[base + static_cast<int64_t>(g) * D];
+      c += dv_h[base + static_cast<int64_t>(g) * D];
+    }
+    dk[e] = __float2bfloat16_rn(a);
+    dv[e] = __float2bfloat16_rn(c);
   }
 }
 
@@ -702,15 +720,19 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   p.lse = a.lse;
   p.delta = a.delta;
   p.dq_acc = a.dq_acc;
-  p.dk = static_cast<__nv_bfloat16*>(a.dk);
-  p.dv = static_cast<__nv_bfloat16*>(a.dv);
+  p.dk_h = a.dk_h;
+  p.dv_h = a.dv_h;
   p.err = device_error_word(dev);
   CUtensorMap mq = map_bthd(a.q, a.B, a.T, a.Hq, D);
   CUtensorMap mk = map_bthd(a.k, a.B, a.T, a.Hkv, D);
   CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
   CUtensorMap mdo = map_bthd(a.dout, a.B, a.T, a.Hq, D);
-  dim3 grid(a.T / KB, a.Hkv, a.B);
+  dim3 grid(a.T / KB, a.Hq, a.B);
   attn_bwd_kernel<D><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  count_launch();
+  const int64_t rows_kv = static_cast<int64_t>(a.B) * a.T * a.Hkv;
+  gqa_reduce_kernel<<<static_cast<unsigned>(std::min<int64_t>((rows_kv * D + 255) / 256, 148 * 16)), 256, 0, stream>>>(
+      a.dk_h, a.dv_h, static_cast<__nv_bfloat16*>(a.dk), static_cast<__nv_bfloat16*>(a.dv), rows_kv, a.Hq / a.Hkv, D);
   count_launch();
   const int64_t n = rows * D;
   f32_to_bf16_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 16)), 256, 0, stream>>>(

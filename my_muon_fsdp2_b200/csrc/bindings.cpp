@@ -514,6 +514,8 @@ std::vector<Tensor> attention_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Ten
   Tensor dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
   Tensor delta = torch::empty({a.B, a.Hq, a.T}, q.options().dtype(torch::kFloat32));
   Tensor dq_acc = torch::empty({a.B, a.T, a.Hq, a.D}, q.options().dtype(torch::kFloat32));
+  Tensor dk_h = torch::empty({a.B, a.T, a.Hq, a.D}, q.options().dtype(torch::kFloat32));
+  Tensor dv_h = torch::empty({a.B, a.T, a.Hq, a.D}, q.options().dtype(torch::kFloat32));
   a.q = q.data_ptr();
   a.k = k.data_ptr();
   a.v = v.data_ptr();
@@ -522,6 +524,8 @@ std::vector<Tensor> attention_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Ten
   a.lse = lse.data_ptr<float>();
   a.delta = delta.data_ptr<float>();
   a.dq_acc = dq_acc.data_ptr<float>();
+  a.dk_h = dk_h.data_ptr<float>();
+  a.dv_h = dv_h.data_ptr<float>();
   a.dq = dq.data_ptr();
   a.dk = dk.data_ptr();
   a.dv = dv.data_ptr();
