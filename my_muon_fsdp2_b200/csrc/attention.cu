@@ -477,6 +477,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int kr = q * 32 + lane;      // key row (S^T / dP^T lane) and, for dQ, query row
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int tid = threadIdx.x - 64;  // 0..255
+    // Every warp waits on the same mbarriers: a phase that completed is seen complete by all of
+    // them and one that never completes fails in all of them, so a timed-out wait makes every
+    // elementwise warp leave the loop at the same point and the named barriers stay matched.
     bool ok = true;
     // row statistics are prefetched one iteration ahead into a register (one value per thread)
     const float* stat_src = (tid < 128) ? p.lse : p.delta;
