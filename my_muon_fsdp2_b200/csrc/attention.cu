@@ -477,9 +477,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int kr = q * 32 + lane;      // key row (S^T / dP^T lane) and, for dQ, query row
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int tid = threadIdx.x - 64;  // 0..255
-    // Every warp waits on the same mbarriers: a phase that completed is seen complete by all of
-    // them and one that never completes fails in all of them, so a timed-out wait makes every
-    // elementwise warp leave the loop at the same point and the named barriers stay matched.
+    // Every warp waits on the same mbarriers with waits that only give up on their own timeout: a
+    // phase that completed is seen complete by all of them and one that never completes times
+    // out in all of them, so every elementwise warp leaves the loop at the same point and the
+    // named barriers stay matched.
     bool ok = true;
     // row statistics are prefetched one iteration ahead into a register (one value per thread)
     const float* stat_src = (tid < 128) ? p.lse : p.delta;
@@ -497,7 +498,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         sDelta[tid - 128] = stat_next;
       asm volatile("bar.sync 1, 256;" ::: "memory");
       if (n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
-      if (!mbar_wait(sp_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+      if (!mbar_wait(sp_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
         ok = false;
         break;
       }
@@ -543,7 +544,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full);
       // dQ_i partial (in tDP; TMEM lanes = query rows) -> fp32 accumulator, this warp's D/2 columns
-      if (!mbar_wait(dq_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+      if (!mbar_wait(dq_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
         ok = false;
         break;
       }

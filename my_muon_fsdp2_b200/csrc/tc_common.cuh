@@ -71,15 +71,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait on the phase with the given parity.  Returns false (and records `code` in
 // *err) if the phase did not complete within MMF_WAIT_TIMEOUT_NS, or if another CTA has
 // already recorded an error (so that one failure unwinds the whole grid quickly).
+// With check_err == false the wait ignores other CTAs' errors and only gives up on its own
+// timeout, so all warps that wait on the same phase reach the same verdict (needed where the
+// waiting warps later meet at a named barrier).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          uint64_t timeout_ns = MMF_WAIT_TIMEOUT_NS) {
+                                          uint64_t timeout_ns = MMF_WAIT_TIMEOUT_NS, bool check_err = true) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+    if (check_err && *reinterpret_cast<volatile int*>(err) != 0) return false;
     if (globaltimer_ns() - t0 > timeout_ns) {
       atomicCAS(err, 0, code);
       return false;
