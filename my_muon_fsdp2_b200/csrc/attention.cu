@@ -286,22 +286,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
 
 // ======================================================================================
-// Backward, one CTA per (128-key block j, KV head, batch); loops over the query heads of the
-// GQA group and the query blocks i >= j (causal).  K_j and V_j stay in smem; per (head, i):
+// Backward, part 1 (dK, dV): one CTA per (128-key block j, query head, batch); loops over the
+// query blocks i >= j (causal).  K_j and V_j stay in smem; Q_i / dO_i are double-buffered.
 //   MMA      S^T = K_j Q_i^T  -> TMEM tS        dP^T = V_j dO_i^T -> TMEM tdP
-//   softmax  (one key row per thread) P^T = exp2(S^T*scale*log2e - lse_i*log2e) (causal mask
-//            on the diagonal block), dS^T = P^T * (dP^T - delta_i); both bf16 into swizzled smem
-//   MMA      dV += P^T dO_i      dK += dS^T Q_i      (dO_i, Q_i read MN-major from the same tiles)
-//            dQ_i = dS K_j       (dS^T read as an MN-major A operand) -> TMEM tS
-//   softmax  warps add scale * dQ_i into the fp32 dQ accumulator (vector reductions)
-// dK (x scale) and dV are written once at the end (bf16); no atomics for them.
+//   softmax  (one key row per TMEM lane) P^T = exp2(S^T*scale*log2e - lse_i*log2e) (causal mask
+//            on the diagonal block), packed back into TMEM as bf16; dS^T = P^T * (dP^T - delta_i)
+//            as bf16 into a swizzled smem tile
+//   MMA      dV += P^T dO_i (A from TMEM)      dK += dS^T Q_i   (dO_i, Q_i read MN-major)
+// dK and dV of each query head are written once at the end as fp32 and summed over the GQA
+// group by gqa_reduce_kernel; no atomics.  dQ is computed by attn_bwd_dq_kernel (part 2).
 // ======================================================================================
 struct AttnBwdParams {
   int B, T, Hq, Hkv, D;
   float scale, scale_log2;
   const float* lse;    // [B, Hq, T]
   const float* delta;  // [B, Hq, T]
-  float* dq_acc;       // [B, T, Hq, D] fp32, zero-initialised
   float* dk_h;         // [B, T, Hq, D] fp32: dK of each query head (summed over the GQA group later)
   float* dv_h;         // [B, T, Hq, D] fp32
   int* err;
@@ -321,11 +320,6 @@ struct BwdSmem {
   static constexpr int BYTES0 = BAR_OFF + 256 + 1024;
   static constexpr int BYTES = BYTES0 > 120 * 1024 ? BYTES0 : 120 * 1024;
 };
-
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
 
 template <int D>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
@@ -350,10 +344,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* do_empty = bars + 7;  // [2]
   uint64_t* sp_full = bars + 9;
   uint64_t* ds_full = bars + 10;
-  uint64_t* dq_full = bars + 11;
-  uint64_t* dq_empty = bars + 12;
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = p.T / QB;
@@ -373,8 +365,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     }
     mbar_init(sp_full, 1);
     mbar_init(ds_full, 8);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 8);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -421,7 +411,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_bf16_f32(128, 128, false, false);   // S^T, dP^T
       constexpr uint32_t id_kv = idesc_bf16_f32(128, D, false, true);     // dV, dK (B MN-major)
-      constexpr uint32_t id_q = idesc_bf16_f32(128, D, true, true);       // dQ (A and B MN-major)
       bool ok = mbar_wait(kv_full, 0, p.err, ERR_MMA_FULL_TIMEOUT);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_base = smem_u32(sQ), do_base = smem_u32(sDO);
       const uint32_t dst_addr = smem_u32(sDSt);
@@ -437,8 +426,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
           umma_bf16(tS, sdesc_kmajor(k_addr + off), sdesc_kmajor(q_addr + off), id_s, kk ? 1u : 0u);
         }
-        // dP^T into tDP once dQ of the previous iteration has been read out of it
-        if (!mbar_wait(dq_empty, (n & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) break;
+        // dP^T into tDP (the elementwise warps read the previous one before ds_full)
         if (!mbar_wait(&do_full[qs], (n >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
         tc_fence_after();
 #pragma unroll
@@ -458,13 +446,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           umma_bf16(tDK, sdesc_kmajor(dst_addr + aoff), sdesc_mnmajor(q_addr + kk * 2048, 16384), id_kv,
                     (n | kk) ? 1u : 0u);
         }
-        // dQ_i = dS K_j into tDP (dP^T was consumed before ds_full)
-#pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 keys
-          umma_bf16(tDP, sdesc_mnmajor(dst_addr + kk * 2048, 16384), sdesc_mnmajor(k_addr + kk * 2048, 16384), id_q,
-                    kk ? 1u : 0u);
-        }
-        umma_commit(dq_full);
         umma_commit(&q_empty[qs]);
         umma_commit(&do_empty[qs]);
       }
@@ -543,27 +524,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full);
-      // dQ_i partial (in tDP; TMEM lanes = query rows) -> fp32 accumulator, this warp's D/2 columns
-      if (!mbar_wait(dq_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      {
-        float* dqrow = p.dq_acc + ((static_cast<int64_t>(b) * p.T + i * QB + kr) * p.Hq + h) * D + half * (D / 2);
-        float v[D / 2];
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tDP + lane_off + half * (D / 2) + c * 32, v + c * 32);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dq_empty);  // tDP may be overwritten while the reductions drain
-#pragma unroll
-        for (int e = 0; e < D / 2; e += 4)
-          red_add_v4(dqrow + e, v[e] * p.scale, v[e + 1] * p.scale, v[e + 2] * p.scale, v[e + 3] * p.scale);
-      }
     }
-    // dK_j (x scale) and dV_j: all MMAs finished (the last dq_full was waited above)
+    // the last dV/dK MMAs: the drain commit of the MMA thread is not visible here, so wait for the
+    // final Q/dO release (committed after them)
+    if (ok) ok = mbar_wait(&q_empty[(n_iter - 1) & 1], ((n_iter - 1) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
+                           MMF_WAIT_TIMEOUT_NS, false);
+    // dK_j (x scale) and dV_j
     if (ok) {
       tc_fence_after();
       const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hq + hq;
@@ -579,6 +545,251 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
         for (int g = 0; g < D / 8; ++g)
           *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4] * f, v[g * 4 + 1] * f, v[g * 4 + 2] * f, v[g * 4 + 3] * f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+
+// ======================================================================================
+// dQ kernel, one CTA per (128-query block i, query head, batch); loops over key blocks j <= i:
+//   MMA      S = Q_i K_j^T -> TMEM (double buffered)      dP = dO_i V_j^T -> TMEM
+//   softmax  (one query row per TMEM lane, two warps per lane quarter splitting the key columns)
+//            P = exp2(S*scale*log2e - lse*log2e) (causal mask on the diagonal), dS = P (dP - delta),
+//            bf16 into a swizzled smem tile
+//   MMA      dQ += dS K_j  (K_j read MN-major from its K-major tile)   -> TMEM, written once (bf16)
+// No atomics: each CTA owns its dQ rows.  Row statistics are per thread (its query row).
+// ======================================================================================
+template <int D>
+struct DqSmem {
+  static constexpr int CH = D / 64;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int DO_OFF = TILE;
+  static constexpr int K_OFF = 2 * TILE;   // 2 stages
+  static constexpr int V_OFF = 4 * TILE;   // 2 stages
+  static constexpr int DS_OFF = 6 * TILE;  // dS [128 q x 128 keys] bf16
+  static constexpr int BAR_OFF = DS_OFF + 32768;
+  static constexpr int BYTES0 = BAR_OFF + 256 + 1024;
+  static constexpr int BYTES = BYTES0 > 120 * 1024 ? BYTES0 : 120 * 1024;
+};
+
+struct AttnDqParams {
+  int B, T, Hq, Hkv;
+  float scale, scale_log2;
+  const float* lse;
+  const float* delta;
+  __nv_bfloat16* dq;
+  int* err;
+};
+
+template <int D>
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       const AttnDqParams p) {
+  using L = DqSmem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::Q_OFF;
+  uint8_t* sDO = smem + L::DO_OFF;
+  uint8_t* sK = smem + L::K_OFF;
+  uint8_t* sV = smem + L::V_OFF;
+  uint8_t* sDS = smem + L::DS_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* qdo_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2] S_j (and dP_j) ready
+  uint64_t* s_empty = bars + 7;   // [2] softmax done reading S buffer
+  uint64_t* dp_empty = bars + 9;  // softmax done reading dP
+  uint64_t* ds_full = bars + 10;  // dS written
+  uint64_t* ds_empty = bars + 11; // dQ MMA done reading dS
+  uint64_t* dq_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = p.T / QB;
+  const int i = nqb - 1 - static_cast<int>(blockIdx.x);  // heaviest first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int nblk = i + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qdo_full, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&kv_full[t], 1);
+      mbar_init(&kv_empty[t], 1);
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 8);
+    }
+    mbar_init(dp_empty, 8);
+    mbar_init(ds_full, 8);
+    mbar_init(ds_empty, 1);
+    mbar_init(dq_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tSb[2] = {tmem, tmem + 128};
+  const uint32_t tDP = tmem + 256, tDQ = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(qdo_full, 2 * L::TILE);
+#pragma unroll
+      for (int c = 0; c < L::CH; ++c) {
+        tma_load_4d(sQ + c * 16384, &tmQ, qdo_full, c * 64, h, i * QB, b);
+        tma_load_4d(sDO + c * 16384, &tmDO, qdo_full, c * 64, h, i * QB, b);
+      }
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::TILE);
+#pragma unroll
+        for (int c = 0; c < L::CH; ++c) {
+          tma_load_4d(sK + st * L::TILE + c * 16384, &tmK, &kv_full[st], c * 64, hk, j * KB, b);
+          tma_load_4d(sV + st * L::TILE + c * 16384, &tmV, &kv_full[st], c * 64, hk, j * KB, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(128, KB, false, false);
+      constexpr uint32_t id_q = idesc_bf16_f32(128, D, false, true);
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO), ds_addr = smem_u32(sDS);
+      // S_j and dP_j for block j; S is double-buffered, dP single (released by the softmax
+      // warps as soon as they have loaded it), so S_{j+1}/dP_{j+1} overlap the softmax of j.
+      auto issue_s_dp = [&](int j) -> bool {
+        const int st = j & 1;
+        const uint32_t k_addr = smem_u32(sK + st * L::TILE), v_addr = smem_u32(sV + st * L::TILE);
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) return false;
+        if (!mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tSb[st], sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), id_s, kk ? 1u : 0u);
+        }
+        if (!mbar_wait(dp_empty, (j & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tDP, sdesc_kmajor(do_addr + off), sdesc_kmajor(v_addr + off), id_s, kk ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+        return true;
+      };
+      bool ok = mbar_wait(qdo_full, 0, p.err, ERR_MMA_FULL_TIMEOUT) && issue_s_dp(0);
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int st = j & 1;
+        if (j + 1 < nblk && !issue_s_dp(j + 1)) break;
+        if (!mbar_wait(ds_full, j & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < KB / 16; ++kk) {  // K = keys
+          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tDQ, sdesc_kmajor(ds_addr + aoff), sdesc_mnmajor(k_addr + kk * 2048, 16384), id_q,
+                    (j | kk) ? 1u : 0u);
+        }
+        umma_commit(ds_empty);
+        umma_commit(&kv_empty[st]);
+      }
+      umma_commit(dq_done);
+    }
+  } else {
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;  // which 64 key columns this warp owns
+    const int r = q * 32 + lane;       // query row in the block
+    const int qi = i * QB + r;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int64_t so = (static_cast<int64_t>(b) * p.Hq + h) * p.T + qi;
+    const float lse2 = p.lse[so] * 1.4426950408889634f;
+    const float dlt = p.delta[so];
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (j == i);
+      const int c0 = half * 64;
+      float sv[64], dp[64];
+      tmem_ld_32cols_async(tSb[st] + lane_off + c0, sv);
+      tmem_ld_32cols_async(tSb[st] + lane_off + c0 + 32, sv + 32);
+      tmem_ld_32cols_async(tDP + lane_off + c0, dp);
+      tmem_ld_32cols_async(tDP + lane_off + c0 + 32, dp + 32);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_empty[st]);
+        mbar_arrive(dp_empty);
+      }
+      // the dS buffer must have been consumed by the previous dQ MMA
+      if (j >= 1 && !mbar_wait(ds_empty, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        uint4 w;
+        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          float dv[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int e = g * 8 + e2 * 2 + t;
+            const bool masked = diag && (j * KB + c0 + e > qi);
+            const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - lse2);
+            dv[t] = pr * (dp[e] - dlt);
+          }
+          hw[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
+        }
+        *reinterpret_cast<uint4*>(sDS + swz_offset(r, c0 + g * 8)) = w;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+    }
+    if (ok && mbar_wait(dq_done, 0, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+      tc_fence_after();
+      __nv_bfloat16* dst = p.dq + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D + half * (D / 2);
+      float v[D / 2];
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tDQ + lane_off + half * (D / 2) + c * 32, v + c * 32);
+      tmem_ld_wait();
+#pragma unroll
+      for (int g = 0; g < D / 16; ++g) {
+        uint4 w;
+        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2)
+          hw[e2] = __floats2bfloat162_rn(v[g * 8 + 2 * e2] * p.scale, v[g * 8 + 2 * e2 + 1] * p.scale);
+        *reinterpret_cast<uint4*>(dst + g * 8) = w;
       }
     }
   }
@@ -629,12 +840,6 @@ __global__ void gqa_reduce_kernel(const float* __restrict__ dk_h, const float* _
     dk[e] = __float2bfloat16_rn(a);
     dv[e] = __float2bfloat16_rn(c);
   }
-}
-
-__global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    y[i] = __float2bfloat16_rn(x[i]);
 }
 
 // ------------------------------------ host side ------------------------------------------
@@ -706,13 +911,13 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
     cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     attr_set[dev] = true;
   }
   const int64_t rows = static_cast<int64_t>(a.B) * a.T * a.Hq;
   attn_bwd_delta_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(a.o), static_cast<const __nv_bfloat16*>(a.dout), a.delta, a.B, a.T, a.Hq, D);
   count_launch();
-  cudaMemsetAsync(a.dq_acc, 0, sizeof(float) * rows * D, stream);
   AttnBwdParams p{};
   p.B = a.B;
   p.T = a.T;
@@ -723,7 +928,6 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.lse = a.lse;
   p.delta = a.delta;
-  p.dq_acc = a.dq_acc;
   p.dk_h = a.dk_h;
   p.dv_h = a.dv_h;
   p.err = device_error_word(dev);
@@ -734,13 +938,22 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   dim3 grid(a.T / KB, a.Hq, a.B);
   attn_bwd_kernel<D><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
   count_launch();
+  AttnDqParams pq{};
+  pq.B = a.B;
+  pq.T = a.T;
+  pq.Hq = a.Hq;
+  pq.Hkv = a.Hkv;
+  pq.scale = a.scale;
+  pq.scale_log2 = p.scale_log2;
+  pq.lse = a.lse;
+  pq.delta = a.delta;
+  pq.dq = static_cast<__nv_bfloat16*>(a.dq);
+  pq.err = p.err;
+  attn_bwd_dq_kernel<D><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, pq);
+  count_launch();
   const int64_t rows_kv = static_cast<int64_t>(a.B) * a.T * a.Hkv;
   gqa_reduce_kernel<<<static_cast<unsigned>(std::min<int64_t>((rows_kv * D + 255) / 256, 148 * 16)), 256, 0, stream>>>(
       a.dk_h, a.dv_h, static_cast<__nv_bfloat16*>(a.dk), static_cast<__nv_bfloat16*>(a.dv), rows_kv, a.Hq / a.Hkv, D);
-  count_launch();
-  const int64_t n = rows * D;
-  f32_to_bf16_kernel<<<static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 16)), 256, 0, stream>>>(
-      a.dq_acc, static_cast<__nv_bfloat16*>(a.dq), n);
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: attention bwd launch failed: ") + cudaGetErrorString(e));

@@ -24,7 +24,6 @@ struct AttnBwdArgs {
   const void* dout;  // [B, T, Hq, D] bf16
   const float* lse;  // [B, Hq, T]
   float* delta;      // [B, Hq, T] scratch
-  float* dq_acc;     // [B, T, Hq, D] fp32 scratch
   float* dk_h;       // [B, T, Hq, D] fp32 scratch (per-query-head dK)
   float* dv_h;       // [B, T, Hq, D] fp32 scratch
   void* dq;          // [B, T, Hq, D] bf16

@@ -513,7 +513,6 @@ std::vector<Tensor> attention_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Ten
   a.Hkv = static_cast<int>(k.size(2));
   Tensor dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
   Tensor delta = torch::empty({a.B, a.Hq, a.T}, q.options().dtype(torch::kFloat32));
-  Tensor dq_acc = torch::empty({a.B, a.T, a.Hq, a.D}, q.options().dtype(torch::kFloat32));
   Tensor dk_h = torch::empty({a.B, a.T, a.Hq, a.D}, q.options().dtype(torch::kFloat32));
   Tensor dv_h = torch::empty({a.B, a.T, a.Hq, a.D}, q.options().dtype(torch::kFloat32));
   a.q = q.data_ptr();
@@ -523,7 +522,6 @@ std::vector<Tensor> attention_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Ten
   a.dout = dout.data_ptr();
   a.lse = lse.data_ptr<float>();
   a.delta = delta.data_ptr<float>();
-  a.dq_acc = dq_acc.data_ptr<float>();
   a.dk_h = dk_h.data_ptr<float>();
   a.dv_h = dv_h.data_ptr<float>();
   a.dq = dq.data_ptr();
