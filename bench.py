@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--micro-bs", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32, help="debug only: fewer layers is not the named config")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="fsdp2",
+                    help="fsdp2: fully_shard everywhere; symm: block linears on symmetric memory with the "
+                         "fused all-gather GEMM / GEMM reduce-scatter kernels, the rest fully_shard")
     return ap.parse_args()
 
 
@@ -93,14 +96,23 @@ def build_ours(args, world, local):
     mesh = init_device_mesh("cuda", (world,))
     with torch.device("meta"):
         model = Llama(cfg).to(torch.bfloat16)
-    apply_fsdp(model, mesh)
-    model.to_empty(device=torch.device("cuda", local))
+    ctl = None
+    if args.fsdp == "symm" and world > 1:
+        from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+        ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local))
+    else:
+        apply_fsdp(model, mesh)
+        model.to_empty(device=torch.device("cuda", local))
     model.init_weights(seed=0)
     muon_names = set(model.muon_param_names())
     muon_p = [p for n, p in model.named_parameters() if n in muon_names]
     adam_p = [p for n, p in model.named_parameters() if n not in muon_names]
     opts = [MuonOptimizer(muon_p, lr=0.02, momentum=0.95, weight_decay=0.01, nesterov=False, ns_steps=5),
             FusedAdamW(adam_p, lr=1e-3, weight_decay=0.01)]
+    if ctl is not None:
+        for o in opts:
+            ctl.attach_optimizer(o)
     return model, opts, cfg.vocab_size
 
 
@@ -265,6 +277,7 @@ def main():
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",
+                       "fsdp_impl": (args.fsdp if (args.impl == "ours" and world > 1) else "fully_shard"),
                        "tokens_per_step": tokens_per_step,
                        "l2": "no flush: per-step working set (16 GB bf16 weights + activations) >> 126 MB L2",
                        "optimizers": "Muon(attn+FFN matrices, lr .02, mom .95, wd .01, ns 5) + AdamW(rest, lr 1e-3)"},

@@ -1,0 +1,122 @@
+"""FSDP collectives of one Llama-3-8B block's linears, fused kernels vs NCCL + cuBLAS.
+
+For each weight W [N, K] (row-sharded over the ranks) and T tokens per rank:
+  * forward  : NCCL all_gather_into_tensor(W) + F.linear     vs  ag_gemm (one kernel)
+  * weight-gradient: dY^T X (cuBLAS) + NCCL reduce_scatter_tensor(avg)  vs
+                     wgrad_out (P2P stores from the epilogue) + bounded barrier + rs_reduce
+CUDA events on the launching stream, max over ranks, after warm-up; inputs are larger than L2
+for the big shapes (weights 32-117 MB bf16, activations 32-117 MB).
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench_fsdp_comm.py [--tokens 4096]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+SHAPES = {"wq/wo": (4096, 4096), "wk/wv": (1024, 4096), "w1/w3": (14336, 4096), "w2": (4096, 14336)}
+
+
+def timed(fn, iters, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / iters], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args()
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    from my_muon_fsdp2_b200._ext import check_device_error, ext
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmFSDP
+
+    T = args.tokens
+    lins = {k: nn.Linear(kk, n, bias=False, device="meta") for k, (n, kk) in SHAPES.items()}
+    for m in lins.values():
+        m.to_empty(device=dev)
+        m.to(torch.bfloat16)
+        with torch.no_grad():
+            m.weight.normal_(0, 0.02)
+    names = list(lins)
+    ctl = SymmFSDP([lins[k] for k in names], device=dev)
+    rows = []
+    for i, name in enumerate(names):
+        n, k = SHAPES[name]
+        x = torch.randn(T, k, device=dev, dtype=torch.bfloat16)
+        dy = torch.randn(T, n, device=dev, dtype=torch.bfloat16)
+        shard = ctl.params[i].to_local()
+        full = torch.empty(n, k, device=dev, dtype=torch.bfloat16)
+
+        def nccl_fwd():
+            dist.all_gather_into_tensor(full, shard)
+            return F.linear(x, full)
+
+        def fused_fwd():
+            ctl.valid[i] = False
+            return ctl.linear_forward(i, x)
+
+        rs_out = torch.empty(n // world, k, device=dev, dtype=torch.bfloat16)
+
+        def nccl_wgrad():
+            dw = dy.t() @ x
+            dist.reduce_scatter_tensor(rs_out, dw, op=dist.ReduceOp.AVG)
+
+        def fused_wgrad():
+            ctl.params[i].grad = None
+            ctl._accumulate_grad(i, dy, x)
+
+        r = {"weight": name, "N": n, "K": k, "tokens": T}
+        r["fwd_nccl_ms"] = timed(nccl_fwd, args.iters, args.warmup)
+        r["fwd_fused_ms"] = timed(fused_fwd, args.iters, args.warmup)
+        r["gemm_only_ms"] = timed(lambda: F.linear(x, full), args.iters, args.warmup)
+        r["wgrad_nccl_ms"] = timed(nccl_wgrad, args.iters, args.warmup)
+        r["wgrad_fused_ms"] = timed(fused_wgrad, args.iters, args.warmup)
+        r["wgrad_gemm_only_ms"] = timed(lambda: dy.t() @ x, args.iters, args.warmup)
+        loc = torch.empty(n, k, device=dev, dtype=torch.bfloat16)
+        loc_ptrs = torch.tensor([loc.data_ptr()], dtype=torch.int64, device=dev)
+        loc_meta = torch.tensor([k, 0, n], dtype=torch.int64, device=dev)
+        r["wgrad_own_gemm_ms"] = timed(lambda: ext().wgrad_out(dy, x, loc_ptrs, 1, loc_meta, False, 0.0, None, 0.0),
+                                       args.iters, args.warmup)
+        ref_dw = (dy.t() @ x).float()
+        r["wgrad_own_rel_err"] = float((loc.float() - ref_dw).norm() / ref_dw.norm())
+        # correctness spot check of the fused forward
+        with torch.no_grad():
+            y = fused_fwd()
+            ref = F.linear(x, full)
+        r["fwd_rel_err"] = float((y.float() - ref.float()).norm() / ref.float().norm())
+        rows.append(r)
+    torch.cuda.synchronize()
+    check_device_error(local)
+    if rank == 0:
+        for r in rows:
+            print(json.dumps({"metric": "fsdp collective + GEMM ms", "n_gpus": world, **r}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -142,6 +142,88 @@ void tc_gemm_out(Tensor A, Tensor B, bool b_mn_major, c10::optional<Tensor> C, c
   mmf::tc_gemm_out(a, cur_stream());
 }
 
+// Weight gradient of a linear layer, scattered by rows: dW = dY^T X ([N, K] from dY [T, N] and
+// X [T, K]), row r of dW goes to segment r / seg_rows (out_ptrs[seg], leading dimension and
+// seg_rows from out_meta = [ld, 0, seg_rows] on the device); T = p_scale * T + dW + beta * C.
+void wgrad_out(Tensor dY, Tensor X, Tensor out_ptrs, int64_t nseg, Tensor out_meta, bool out_f32, double p_scale,
+               c10::optional<Tensor> C, double beta) {
+  check_bf16_contig(dY, "dY");
+  check_bf16_contig(X, "X");
+  TORCH_CHECK(dY.dim() == 2 && X.dim() == 2 && dY.size(0) == X.size(0), "mmf: wgrad_out needs dY [T, N], X [T, K]");
+  check_cuda(out_ptrs, "out_ptrs");
+  TORCH_CHECK(out_ptrs.scalar_type() == torch::kInt64 && out_ptrs.numel() == nseg, "mmf: out_ptrs must be int64[nseg]");
+  TORCH_CHECK(out_meta.is_cuda() && out_meta.scalar_type() == torch::kInt64 && out_meta.numel() == 3,
+              "mmf: out_meta must be a CUDA int64[3]");
+  const c10::cuda::CUDAGuard guard(dY.device());
+  mmf::GemmOutArgs a{};
+  a.A = dY.data_ptr();
+  a.a_mn_major = true;
+  a.B = X.data_ptr();
+  a.b_mn_major = true;
+  a.batch = 1;
+  a.M = static_cast<int>(dY.size(1));
+  a.N = static_cast<int>(X.size(1));
+  a.K = static_cast<int>(dY.size(0));
+  a.alpha = 1.f;
+  a.beta = 0.f;
+  if (C.has_value()) {  // + beta * C, C [N, K] bf16 (an unsharded gradient accumulator)
+    check_bf16_contig(*C, "C");
+    TORCH_CHECK(C->dim() == 2 && C->size(0) == a.M && C->size(1) == a.N, "mmf: wgrad_out: C must be [N, K]");
+    a.C = C->data_ptr();
+    a.beta = static_cast<float>(beta);
+  }
+  a.out_ptrs = out_ptrs.data_ptr<int64_t>();
+  a.nseg = static_cast<int>(nseg);
+  a.out_meta = out_meta.data_ptr<int64_t>();
+  a.out_ld = 0;
+  a.out_f32 = out_f32;
+  a.m_true = a.M;
+  a.n_true = a.N;
+  a.p_scale = static_cast<float>(p_scale);
+  a.v_scale = 1.f;
+  mmf::tc_gemm_out(a, cur_stream());
+}
+
+// Y = X @ W^T with W row-sharded over the group (shard_ptrs: every rank's shard address in this
+// process's address space); also assembles the full W into G.  ready: int32 [N / 128] scratch.
+Tensor ag_gemm(Tensor X, std::vector<int64_t> shard_ptrs, int64_t rank, Tensor G, Tensor ready, double wait_s) {
+  check_bf16_contig(X, "X");
+  check_bf16_contig(G, "G");
+  check_cuda(ready, "ready");
+  TORCH_CHECK(X.dim() == 2 && G.dim() == 2 && X.size(1) == G.size(1), "mmf: ag_gemm needs X [M, K], G [N, K]");
+  TORCH_CHECK(ready.scalar_type() == torch::kInt32 && ready.numel() >= G.size(0) / 128, "mmf: ready must be int32[N/128]");
+  const int ws = static_cast<int>(shard_ptrs.size());
+  TORCH_CHECK(ws >= 1 && ws <= 8, "mmf: ag_gemm supports 1..8 ranks");
+  const c10::cuda::CUDAGuard guard(X.device());
+  Tensor Y = torch::empty({X.size(0), G.size(0)}, X.options());
+  mmf::AgGemmArgs a{};
+  a.X = X.data_ptr();
+  a.M = static_cast<int>(X.size(0));
+  a.N = static_cast<int>(G.size(0));
+  a.K = static_cast<int>(X.size(1));
+  a.rank = static_cast<int>(rank);
+  a.ws = ws;
+  for (int s = 0; s < ws; ++s) a.shard_ptrs[s] = shard_ptrs[s];
+  a.G = G.data_ptr();
+  a.Y = Y.data_ptr();
+  a.ready = reinterpret_cast<uint32_t*>(ready.data_ptr<int32_t>());
+  a.wait_ns = static_cast<uint64_t>(wait_s * 1e9);
+  mmf::ag_gemm(a, cur_stream());
+  return Y;
+}
+
+// out (bf16, n elements) = (accumulate ? out : 0) + scale * sum over ranks s of
+// slots[s * slot_stride : s * slot_stride + n] (rank order, fp32)
+void rs_reduce(Tensor slots, int64_t ws, int64_t slot_stride, Tensor out, bool accumulate, double scale) {
+  check_bf16_contig(slots, "slots");
+  check_bf16_contig(out, "out");
+  TORCH_CHECK(slot_stride >= out.numel() && slots.numel() >= (ws - 1) * slot_stride + out.numel(),
+              "mmf: rs_reduce: slots too small");
+  const c10::cuda::CUDAGuard guard(out.device());
+  mmf::rs_reduce(slots.data_ptr(), static_cast<int>(ws), slot_stride, out.numel(), out.data_ptr(), accumulate,
+                 static_cast<float>(scale), cur_stream());
+}
+
 // grads/bufs/params: per-matrix tensors (bufs/params may be empty lists).  dst: optional bf16
 // workspace; per-matrix destination = dst_base_offsets[i] elements into dst.
 void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<Tensor> params,
@@ -546,6 +628,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ptr_table", &ptr_table);
   m.def("tc_gemm_ws", &tc_gemm_ws);
   m.def("tc_gemm_out", &tc_gemm_out);
+  m.def("wgrad_out", &wgrad_out);
+  m.def("ag_gemm", &ag_gemm);
+  m.def("rs_reduce", &rs_reduce);
   m.def("muon_prep", &muon_prep);
   m.def("ns_scale", &ns_scale);
   m.def("ws_to_out", &ws_to_out);

@@ -61,6 +61,7 @@ struct GemmOutArgs {
   const void* A;
   const void* B;
   bool b_mn_major;
+  bool a_mn_major;  // true: A is [batch, K, M] row-major (the product uses A^T); single-CTA kernel
   const void* C;
   int batch, M, N, K;
   const float* alpha_vec;
@@ -80,6 +81,34 @@ struct GemmOutArgs {
   float v_scale;
 };
 void tc_gemm_out(const GemmOutArgs& args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------------
+// FSDP all-gather fused with the consuming GEMM:  Y[M, N] = X[M, K] @ W^T, where W [N, K] is
+// row-sharded over `ws` ranks (rank s holds rows [s*N/ws, (s+1)*N/ws) at shard_ptrs[s], a
+// peer-mapped address for s != rank).  The same launch assembles the full W into the local
+// buffer G [N, K]: one extra warp per CTA pulls 128x64 pieces of the peers' shards (ring
+// order starting at rank+1) with TMA loads and writes them into G with TMA stores, publishing
+// a per-128-row-panel counter in `ready` [N/128] (zeroed by the launcher).  The GEMM visits
+// its own shard's columns first, then the other shards in ring order, and reads a remote panel
+// from G once it is complete; a panel that is not complete within `wait_ns` is read from the
+// owner directly (never a wait without a bound, never a multicast load).
+// Requirements: M % 128 == 0, K % 64 == 0, N % 256 == 0, (N / ws) % 128 == 0, ws <= 8.
+struct AgGemmArgs {
+  const void* X;
+  int M, N, K;
+  int rank, ws;
+  int64_t shard_ptrs[8];
+  void* G;
+  void* Y;
+  uint32_t* ready;
+  uint64_t wait_ns;
+};
+void ag_gemm(const AgGemmArgs& args, cudaStream_t stream);
+
+// Deterministic reduction of reduce-scatter slots: out[i] = bf16((accumulate ? out[i] : 0) +
+// scale * sum_{s = 0..ws-1} slots[s * slot_stride + i]) with the sum taken in fp32 in rank order.
+void rs_reduce(const void* slots, int ws, int64_t slot_stride, int64_t n, void* out, bool accumulate, float scale,
+               cudaStream_t stream);
 
 // ----------------------------------------------------------------------------------------
 // Muon pre-NS multi-tensor kernel.  For matrix b (a row block of rows_b x cols_b elements):

@@ -67,6 +67,53 @@ __global__ void symm_barrier_kernel(const int64_t* __restrict__ pad_ptrs, int ra
   __syncthreads();
 }
 
+// out = bf16((acc ? out : 0) + scale * sum_s slots[s]) in fp32, ranks in order (deterministic);
+// 8 bf16 per thread when n % 8 == 0 and the bases are 16-byte aligned.
+template <bool VEC>
+__global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, int ws, int64_t stride_s, int64_t n,
+                                 __nv_bfloat16* __restrict__ out, int accumulate, float scale) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (VEC) {
+    const int64_t nv = n / 8;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += stride) {
+      float acc[8], base[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = base[e] = 0.f;
+      if (accumulate) {
+        const uint4 w = reinterpret_cast<const uint4*>(out)[i];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          base[2 * e] = f.x;
+          base[2 * e + 1] = f.y;
+        }
+      }
+      for (int s = 0; s < ws; ++s) {
+        const uint4 w = reinterpret_cast<const uint4*>(slots + static_cast<int64_t>(s) * stride_s)[i];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          acc[2 * e] += f.x;
+          acc[2 * e + 1] += f.y;
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) oh[e] = __floats2bfloat162_rn(base[2 * e] + scale * acc[2 * e], base[2 * e + 1] + scale * acc[2 * e + 1]);
+      reinterpret_cast<uint4*>(out)[i] = o;
+    }
+  } else {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+      float acc = 0.f;
+      for (int s = 0; s < ws; ++s) acc += __bfloat162float(slots[static_cast<int64_t>(s) * stride_s + i]);
+      out[i] = __float2bfloat16_rn((accumulate ? __bfloat162float(out[i]) : 0.f) + scale * acc);
+    }
+  }
+}
+
 }  // namespace
 
 void symm_barrier(const int64_t* pad_ptrs, int rank, int ws, uint32_t epoch, int slot_base, const float* payload,
@@ -79,6 +126,29 @@ void symm_barrier(const int64_t* pad_ptrs, int rank, int ws, uint32_t epoch, int
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: symm_barrier launch failed: ") + cudaGetErrorString(e));
+}
+
+void rs_reduce(const void* slots, int ws, int64_t slot_stride, int64_t n, void* out, bool accumulate, float scale,
+               cudaStream_t stream) {
+  if (ws < 1 || n < 0) throw std::runtime_error("mmf: rs_reduce: bad arguments");
+  if (n == 0) return;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool vec = (n % 8 == 0) && (slot_stride % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(slots) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const int64_t work = vec ? n / 8 : n;
+  const int64_t want = (work + 255) / 256;
+  const unsigned grid = static_cast<unsigned>(want < sms * 8 ? (want < 1 ? 1 : want) : sms * 8);
+  if (vec)
+    rs_reduce_kernel<true><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(slots), ws, slot_stride, n,
+                                                     static_cast<__nv_bfloat16*>(out), accumulate ? 1 : 0, scale);
+  else
+    rs_reduce_kernel<false><<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(slots), ws, slot_stride, n,
+                                                      static_cast<__nv_bfloat16*>(out), accumulate ? 1 : 0, scale);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: rs_reduce launch failed: ") + cudaGetErrorString(e));
 }
 
 }  // namespace mmf

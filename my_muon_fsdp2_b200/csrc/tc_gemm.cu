@@ -237,7 +237,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int b, int ro
       }
 }
 
-template <bool B_MN>
+template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmParams p) {
@@ -297,7 +297,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_3d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, tm * BM, b);
+          if (A_MN) {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_3d(sA + stage * A_BYTES + c * (BK * 64 * 2), &tmA, &full[stage], tm * BM + c * 64, kb * BK,
+                          b);
+          } else {
+            tma_load_3d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, tm * BM, b);
+          }
           if (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
@@ -325,7 +332,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ---------------------------------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, B_MN);
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -348,7 +355,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = sdesc_kmajor(a_addr + kk * 32);
+            const uint64_t ad = A_MN ? sdesc_mnmajor(a_addr + kk * 16 * 128, BK * 64 * 2) : sdesc_kmajor(a_addr + kk * 32);
             const uint64_t bd = B_MN ? sdesc_mnmajor(b_addr + kk * 16 * 128, BK * 64 * 2) : sdesc_kmajor(b_addr + kk * 32);
             umma_bf16(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
           }
@@ -600,6 +607,260 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ======================================================================================
+// FSDP all-gather fused with the consuming GEMM (Y = X W^T, W row-sharded over the ranks).
+//   warp 0      : TMA producer; B tiles are two 128-row panels, each read from this rank's
+//                 shard (own panels), from the local gather buffer G (remote panels already
+//                 pulled) or, if a panel is not complete within wait_ns, from its owner directly
+//   warp 1      : MMA issuer (as tc_gemm_kernel)
+//   warps 2..5  : epilogue (bf16 Y)
+//   warp 6      : puller: 128x64 pieces of every shard, peer -> smem (TMA load) -> G (TMA
+//                 store); per-panel counters published with release semantics
+// Output columns are visited starting at this rank's own shard, then ring order, which is
+// also the order in which the pullers fetch: the NVLink transfer of shard r+s overlaps the
+// tensor-core work on shards r .. r+s-1.  No CTA ever waits without a bound, so the kernel
+// cannot deadlock even if some CTAs are not co-resident.  No multicast loads.
+// ======================================================================================
+constexpr int AG_MAX_WS = 8;
+constexpr int AG_PANEL = 128;
+constexpr int AG_PIECE_BYTES = AG_PANEL * BK * 2;  // 16 KB
+constexpr int AG_THREADS = 224;
+constexpr int AG_SMEM_BYTES = STAGES * STAGE_BYTES + 2 * AG_PIECE_BYTES + 1024 + 256;
+
+struct AgMaps {
+  CUtensorMap shard[AG_MAX_WS];
+};
+
+struct AgParams {
+  GemmParams g;  // M, N, K, tiling, epilogue (mode 0, D = Y)
+  int rot;       // tile-column rotation that puts this rank's shard first
+  int rank, ws, rows_per_shard, pps, ppp;
+  uint32_t* ready;
+  uint64_t wait_ns;
+};
+
+__device__ __forceinline__ void ag_tile(const AgParams& p, int t, int& tm, int& tn) {
+  int b;
+  tile_coords(p.g, t, b, tm, tn);
+  tn += p.rot;
+  if (tn >= p.g.tiles_n) tn -= p.g.tiles_n;
+}
+
+__global__ void __launch_bounds__(AG_THREADS, 1)
+    ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
+                   const __grid_constant__ AgMaps maps, const AgParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sP = sB + STAGES * B_BYTES;  // 2 pull buffers
+  uint64_t* full = reinterpret_cast<uint64_t*>(sP + 2 * AG_PIECE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* pfull = drain + 1;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pfull + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* err = p.g.err;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&tfull[j], 1);
+      mbar_init(&tempty[j], 4);
+      mbar_init(&pfull[j], 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmG);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int k_blocks = p.g.K / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued = 0;
+      for (int t = blockIdx.x; t < p.g.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        ag_tile(p, t, tm, tn);
+        // source of each 128-row half of the B tile: -1 = local G, else a shard map index
+        int src[2], row[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int panel = 2 * tn + h;
+          const int owner = panel / p.pps;
+          const int lrow = (panel - owner * p.pps) * AG_PANEL;
+          src[h] = owner;
+          row[h] = lrow;
+          if (owner != p.rank) {
+            const uint32_t* flag = p.ready + panel;
+            bool ready = ld_acquire_gpu(flag) >= static_cast<uint32_t>(p.ppp);
+            if (!ready) {
+              const uint64_t t0 = globaltimer_ns();
+              while (!(ready = ld_acquire_gpu(flag) >= static_cast<uint32_t>(p.ppp))) {
+                if (globaltimer_ns() - t0 > p.wait_ns) break;  // fall back to the owner's memory
+                __nanosleep(64);
+              }
+            }
+            if (ready) {
+              fence_proxy_async_global();
+              src[h] = -1;
+              row[h] = panel * AG_PANEL;
+            }
+          }
+        }
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err, ERR_TMA_EMPTY_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_3d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, tm * BM, 0);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const CUtensorMap* m = src[h] < 0 ? &tmG : &maps.shard[src[h]];
+            tma_load_3d(sB + stage * B_BYTES + h * AG_PIECE_BYTES, m, &full[stage], kb * BK, row[h], 0);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < STAGES && s < issued; ++s) {
+          int st = (stage + STAGES - 1 - s) % STAGES;
+          uint32_t ph = (st < stage) ? phase : (phase ^ 1u);
+          mbar_wait(&full[st], ph, err, ERR_TMA_EMPTY_TIMEOUT, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.g.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, ERR_MMA_FULL_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(d_tmem, sdesc_kmajor(a_addr + kk * 32), sdesc_kmajor(b_addr + kk * 32), idesc,
+                      (kb | kk) ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else if (warp < 6) {
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.g.num_tiles; t += gridDim.x) {
+      int tm, tn;
+      ag_tile(p, t, tm, tn);
+      if (!mbar_wait(&tfull[acc], acc_phase, err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
+      tc_fence_after();
+      epilogue_tile(p.g, 0, tm * BM + q * 32 + lane, tn,
+                    tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ------------------------------ puller -------------------------------------------
+    if (lane == 0) {
+      const int per_shard = p.pps * p.ppp;
+      const int total = p.ws * per_shard;
+      int i = 0, prev_panel = -1;
+      for (int gi = blockIdx.x; gi < total; gi += gridDim.x, ++i) {
+        const int step = gi / per_shard;  // 0 -> shard rank+1, ..., ws-1 -> own shard
+        int src = p.rank + 1 + step;
+        src -= (src >= p.ws) ? p.ws : 0;
+        src -= (src >= p.ws) ? p.ws : 0;
+        const int rem = gi - step * per_shard;
+        const int lp = rem / p.ppp;
+        const int kb = rem - lp * p.ppp;
+        const int buf = i & 1;
+        uint8_t* dst = sP + buf * AG_PIECE_BYTES;
+        mbar_arrive_expect_tx(&pfull[buf], AG_PIECE_BYTES);
+        tma_load_3d(dst, &maps.shard[src], &pfull[buf], kb * BK, lp * AG_PANEL, 0);
+        if (!mbar_wait(&pfull[buf], (i >> 1) & 1, err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        tma_store_3d(&tmG, dst, kb * BK, src * p.rows_per_shard + lp * AG_PANEL, 0);
+        bulk_commit_group();
+        bulk_wait_group<1>();  // every store but the newest has completed
+        if (prev_panel >= 0) {
+          fence_proxy_async_global();
+          red_release_gpu_add(p.ready + prev_panel, 1u);
+        }
+        prev_panel = src * p.pps + lp;
+      }
+      bulk_wait_group<0>();
+      if (prev_panel >= 0) {
+        fence_proxy_async_global();
+        red_release_gpu_add(p.ready + prev_panel, 1u);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
 // ------------------------------------ host side ------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -631,7 +892,7 @@ CUtensorMap make_map_bf16_3d(const void* base, uint64_t inner, uint64_t outer, u
 
 struct DeviceInfo {
   int sms = 0;
-  bool attr_set[4] = {false, false, false, false};
+  bool attr_set[8] = {false, false, false, false, false, false, false, false};
 };
 DeviceInfo& dev_info(int dev) {
   static DeviceInfo infos[64];
@@ -656,7 +917,7 @@ int pair_tiles(const GemmParams& p) {
   return (p.symmetric ? tm * (tm + 1) / 2 : tm * tn) * p.batch;
 }
 
-void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t stream) {
+void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t stream, bool a_mn = false) {
   int dev = 0;
   cudaGetDevice(&dev);
   DeviceInfo& di = dev_info(dev);
@@ -666,7 +927,7 @@ void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t
     // the CTA pair needs 256-row blocks and enough tiles to keep most SMs busy
     variant = (p.M % P_BM == 0 && pair_tiles(p) >= di.sms / 2) ? 2 : 1;
   }
-  if (variant == 2 && p.M % P_BM != 0) variant = 1;
+  if (variant == 2 && (p.M % P_BM != 0 || a_mn)) variant = 1;  // the pair kernel reads A K-major only
   const bool pair = variant == 2;
   const int bm = pair ? P_BM : BM;
   p.tiles_m = p.M / bm;
@@ -687,22 +948,24 @@ void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t
   }
   const int a_rows = pair ? 128 : BM;
   const int b_rows = pair ? 128 : BN;
-  CUtensorMap ma = make_map_bf16_3d(A, p.K, p.M, p.batch, BK, a_rows);
+  CUtensorMap ma = a_mn ? make_map_bf16_3d(A, p.M, p.K, p.batch, 64, BK) : make_map_bf16_3d(A, p.K, p.M, p.batch, BK, a_rows);
   CUtensorMap mb = b_mn ? make_map_bf16_3d(B, p.N, p.K, p.batch, 64, BK) : make_map_bf16_3d(B, p.K, p.N, p.batch, BK, b_rows);
   if (!pair) {
     const int grid = p.num_tiles < di.sms ? p.num_tiles : di.sms;
-    if (b_mn) {
-      if (!di.attr_set[1]) {
-        cudaFuncSetAttribute(tc_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        di.attr_set[1] = true;
+    auto go = [&](auto kern, int slot) {
+      if (!di.attr_set[slot]) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        di.attr_set[slot] = true;
       }
-      tc_gemm_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+      kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+    };
+    if (a_mn) {
+      if (b_mn) go(tc_gemm_kernel<true, true>, 4);
+      else go(tc_gemm_kernel<true, false>, 5);
+    } else if (b_mn) {
+      go(tc_gemm_kernel<false, true>, 1);
     } else {
-      if (!di.attr_set[0]) {
-        cudaFuncSetAttribute(tc_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        di.attr_set[0] = true;
-      }
-      tc_gemm_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ma, mb, p);
+      go(tc_gemm_kernel<false, false>, 0);
     }
   } else {
     const int clusters = p.num_tiles < di.sms / 2 ? p.num_tiles : di.sms / 2;
@@ -827,7 +1090,63 @@ void tc_gemm_out(const GemmOutArgs& a, cudaStream_t stream) {
   p.p_scale = a.p_scale;
   p.v_scale_vec = a.v_scale_vec;
   p.v_scale = a.v_scale;
-  launch(p, a.A, a.B, a.b_mn_major, stream);
+  launch(p, a.A, a.B, a.b_mn_major, stream, a.a_mn_major);
+}
+
+void ag_gemm(const AgGemmArgs& a, cudaStream_t stream) {
+  if (a.ws < 1 || a.ws > AG_MAX_WS || a.rank < 0 || a.rank >= a.ws) throw std::runtime_error("mmf: ag_gemm: bad rank/world");
+  check_shape(1, a.M, a.N, a.K);
+  if (a.N % (AG_PANEL * a.ws) != 0)
+    throw std::runtime_error("mmf: ag_gemm needs (N / world) % 128 == 0 (N=" + std::to_string(a.N) + ")");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceInfo& di = dev_info(dev);
+  AgParams p{};
+  GemmParams& g = p.g;
+  g.M = a.M;
+  g.N = a.N;
+  g.K = a.K;
+  g.batch = 1;
+  g.mode = 0;
+  g.symmetric = 0;
+  g.D = static_cast<__nv_bfloat16*>(a.Y);
+  g.C = nullptr;
+  g.alpha = 1.f;
+  g.beta = 0.f;
+  g.err = device_error_word(dev);
+  g.tiles_m = a.M / BM;
+  g.tiles_n = a.N / BN;
+  g.tiles_per_batch = g.tiles_m * g.tiles_n;
+  g.num_tiles = g.tiles_per_batch;
+  const int band = (di.sms + g.tiles_m - 1) / g.tiles_m;
+  g.band = band < 1 ? 1 : (band > g.tiles_n ? g.tiles_n : band);
+  p.rank = a.rank;
+  p.ws = a.ws;
+  p.rows_per_shard = a.N / a.ws;
+  p.pps = p.rows_per_shard / AG_PANEL;
+  p.ppp = a.K / BK;
+  p.rot = (a.rank * p.rows_per_shard) / BN;
+  p.ready = a.ready;
+  p.wait_ns = a.wait_ns;
+  if ((reinterpret_cast<uintptr_t>(a.Y) & 15) || (reinterpret_cast<uintptr_t>(a.G) & 15))
+    throw std::runtime_error("mmf: ag_gemm: Y/G must be 16-byte aligned");
+  AgMaps maps;
+  for (int s = 0; s < AG_MAX_WS; ++s) {
+    const void* base = reinterpret_cast<const void*>(a.shard_ptrs[s < a.ws ? s : a.rank]);
+    maps.shard[s] = make_map_bf16_3d(base, a.K, p.rows_per_shard, 1, BK, AG_PANEL);
+  }
+  CUtensorMap ma = make_map_bf16_3d(a.X, a.K, a.M, 1, BK, BM);
+  CUtensorMap mg = make_map_bf16_3d(a.G, a.K, a.N, 1, BK, AG_PANEL);
+  cudaMemsetAsync(a.ready, 0, sizeof(uint32_t) * (a.N / AG_PANEL), stream);
+  if (!di.attr_set[6]) {
+    cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AG_SMEM_BYTES);
+    di.attr_set[6] = true;
+  }
+  const int grid = g.num_tiles < di.sms ? g.num_tiles : di.sms;
+  ag_gemm_kernel<<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(ma, mg, maps, p);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: ag_gemm launch failed: ") + cudaGetErrorString(e));
 }
 
 }  // namespace mmf

@@ -32,12 +32,6 @@ class SymmWorkspace:
         self.payload: Optional[torch.Tensor] = None
         self.payload_handle = None
         self.epoch = 0
-        name = getattr(group, "group_name", None)
-        if name is not None and hasattr(symm_mem, "enable_symm_mem_for_group"):
-            try:
-                symm_mem.enable_symm_mem_for_group(name)
-            except Exception:
-                pass
 
     def _rdv(self, t: torch.Tensor):
         try:

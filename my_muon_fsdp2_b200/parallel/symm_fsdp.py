@@ -1,0 +1,348 @@
+"""FSDP for the linear layers on symmetric memory, with the collectives fused into the GEMMs.
+
+The reference delegates FSDP to PyTorch's ``fully_shard`` (examples/train_gpt.py:265-268,
+examples/fsdp_distributed.py:108-120): every forward and backward all-gathers each block's
+parameters with NCCL and the backward reduce-scatters the gradients.  This module keeps the same
+data layout (each linear weight is a ``DTensor`` with ``Shard(0)`` placement, ``torch.chunk``
+row blocks, so the Muon/AdamW optimizers and checkpoints see exactly what FSDP2 produces) but
+moves the two collectives into this library's kernels:
+
+* **all-gather -> GEMM** (``ext.ag_gemm``): the rank-local shards live in one symmetric-memory
+  buffer that every peer has mapped.  The first forward of a step computes ``Y = X W^T`` while
+  the same kernel pulls the peers' shards over NVLink into a local copy of the full weight
+  (ring order, overlapped with the tensor-core work on the panels already present).  The full
+  weight then stays resident for the rest of the step: later micro-batches and every backward
+  ``dX = dY W`` are plain local GEMMs, so a step gathers each weight once instead of twice per
+  micro-batch.  With 180 GB of HBM per GPU the resident copy of an 8B model's linears (16 GB)
+  is cheap.
+* **GEMM -> reduce-scatter** (``ext.wgrad_out`` + ``ext.rs_reduce``): the weight-gradient GEMM
+  ``dW = dY^T X`` writes each rank's row block of its partial product straight into that rank's
+  receive slot (P2P stores from the epilogue); after a bounded barrier each rank sums its slots
+  in rank order (deterministic) and accumulates ``1/world`` of the sum into its gradient shard,
+  which is what FSDP2's averaging reduce-scatter produces.
+
+The remaining parameters (embeddings, norms, LM head) stay under ``fully_shard`` with the fused
+linears passed as ``ignored_params``.  Without CUDA (gloo tests) the same module runs its
+collectives with ``torch.distributed`` (all_gather + all_reduce), which is the oracle for the
+semantics.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+PANEL = 128
+
+
+def _ext():
+    from .._ext import ext
+
+    return ext()
+
+
+def fusable_shape(n: int, k: int, world: int) -> bool:
+    """Shapes the fused kernels take: N split into 128-row panels per rank, 256-wide tiles."""
+    return n % 256 == 0 and n % (PANEL * world) == 0 and k % 256 == 0
+
+
+def _pad_rows(x: torch.Tensor, mult: int) -> torch.Tensor:
+    """Zero rows appended up to a multiple of ``mult`` (zero rows add nothing to X^T Y)."""
+    t = x.shape[0]
+    if t % mult == 0:
+        return x
+    out = x.new_zeros((t + mult - 1) // mult * mult, x.shape[1])
+    out[:t] = x
+    return out
+
+
+class _SymmLinearFn(torch.autograd.Function):
+    """y2 = x2 @ W^T on 2-D activations (the caller reshapes, so that views of the output are
+    ordinary autograd views and may be modified in place, e.g. by RoPE)."""
+
+    @staticmethod
+    def forward(ctx, x2, weight, ctl, idx):
+        y = ctl.linear_forward(idx, x2)
+        ctx.save_for_backward(x2)
+        ctx.ctl = ctl
+        ctx.idx = idx
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x2,) = ctx.saved_tensors
+        if not dy.is_contiguous():
+            dy = dy.contiguous()
+        return ctx.ctl.linear_backward(ctx.idx, dy, x2), None, None, None
+
+
+class SymmLinear(nn.Linear):
+    """``nn.Linear`` (no bias) whose weight is a row shard in symmetric memory."""
+
+    _symm_ctl: "SymmFSDP"
+    _symm_idx: int
+
+    def forward(self, x):
+        x2 = x.reshape(-1, x.shape[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        y = _SymmLinearFn.apply(x2, self.weight, self._symm_ctl, self._symm_idx)
+        return y.view(*x.shape[:-1], y.shape[-1])
+
+
+class SymmFSDP:
+    """Owns the shard buffer, the resident full weights and the reduce-scatter slots of a set of
+    bias-free linear layers, all sharded over one process group."""
+
+    def __init__(self, linears: Sequence[nn.Linear], mesh=None, group: Optional[dist.ProcessGroup] = None,
+                 device: Optional[torch.device] = None, wait_s: float = 2e-3, barrier_timeout_s: float = 60.0):
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.tensor import DTensor, Shard
+
+        if group is None:
+            group = mesh.get_group() if mesh is not None else dist.group.WORLD
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device(device) if device is not None else linears[0].weight.device
+        if mesh is None:
+            mesh = init_device_mesh(self.device.type, (self.world,))
+        self.mesh = mesh
+        self.wait_s = float(wait_s)
+        self.barrier_timeout_s = float(barrier_timeout_s)
+        self.fused = self.device.type == "cuda" and dist.get_backend(group) == "nccl"
+        self.modules: List[nn.Linear] = list(linears)
+        self.shapes: List[Tuple[int, int]] = []
+        for m in self.modules:
+            if m.bias is not None:
+                raise ValueError("SymmFSDP: linear layers with a bias are not supported")
+            n, k = m.weight.shape
+            if n % self.world:
+                raise ValueError(f"SymmFSDP: out_features {n} is not divisible by the world size {self.world}")
+            if self.fused and not fusable_shape(n, k, self.world):
+                raise ValueError(f"SymmFSDP: weight {n}x{k} does not fit the fused kernels at world size "
+                                 f"{self.world} (need N % 256 == 0, (N/world) % 128 == 0, K % 256 == 0)")
+            self.shapes.append((n, k))
+        self.rows = [n // self.world for n, _ in self.shapes]
+        sizes = [r * k for r, (_, k) in zip(self.rows, self.shapes)]
+        offsets, off = [], 0
+        for s in sizes:
+            offsets.append(off)
+            off += (s + 7) // 8 * 8  # 16-byte aligned shards
+        total = max(off, 8)
+        dtype = self.modules[0].weight.dtype
+        if self.fused:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            self._sm = symm_mem
+            self.shard_buf = symm_mem.empty(total, dtype=dtype, device=self.device)
+            self.shard_handle = self._rendezvous(self.shard_buf)
+            slot_elems = max(sizes) * self.world
+            self.slot_elems = slot_elems
+            self.slot_buf = symm_mem.empty(2 * slot_elems, dtype=dtype, device=self.device)
+            self.slot_handle = self._rendezvous(self.slot_buf)
+            self.pad_ptrs = torch.tensor(list(self.slot_handle.signal_pad_ptrs), dtype=torch.int64,
+                                         device=self.device)
+            self.ready = torch.zeros(max(n for n, _ in self.shapes) // PANEL + 1, dtype=torch.int32,
+                                     device=self.device)
+            self._slot_ptrs = [
+                torch.tensor([int(self.slot_handle.buffer_ptrs[s]) + 2 * (b * slot_elems + self.rank * (slot_elems // self.world))
+                              for s in range(self.world)], dtype=torch.int64, device=self.device)
+                for b in range(2)
+            ]
+            self._meta: Dict[int, torch.Tensor] = {}
+        else:
+            self.shard_buf = torch.empty(total, dtype=dtype, device=self.device)
+        self.epoch = 0
+        self.parity = 0
+        self.sync_grads = True
+        self.acc: List[Optional[torch.Tensor]] = [None] * len(self.modules)  # unsharded dW (no-sync)
+        self.acc_live = [False] * len(self.modules)
+        self.params: List[nn.Parameter] = []
+        self.full: List[Optional[torch.Tensor]] = [None] * len(self.modules)
+        self.valid = [False] * len(self.modules)
+        self._step_synced = False
+        for i, m in enumerate(self.modules):
+            n, k = self.shapes[i]
+            r = self.rows[i]
+            local = self.shard_buf[offsets[i]:offsets[i] + r * k].view(r, k)
+            w = m.weight
+            if w.device.type != "meta":
+                src = w.detach()
+                if isinstance(src, DTensor):
+                    src = src.full_tensor()
+                local.copy_(src[self.rank * r:(self.rank + 1) * r])
+            p = nn.Parameter(DTensor.from_local(local, self.mesh, [Shard(0)], run_check=False, shape=(n, k),
+                                                stride=(k, 1)), requires_grad=w.requires_grad)
+            del m._parameters["weight"]
+            m.weight = p
+            m.__class__ = SymmLinear
+            m._symm_ctl = self
+            m._symm_idx = i
+            self.params.append(p)
+        self.shard_offsets = offsets
+
+    # ------------------------------------------------------------------ plumbing
+    def _rendezvous(self, t):
+        try:
+            return self._sm.rendezvous(t, self.group)
+        except TypeError:
+            return self._sm.rendezvous(t, self.group.group_name)
+
+    def _barrier(self) -> None:
+        self.epoch += 1
+        _ext().symm_barrier(self.pad_ptrs, self.rank, self.world, self.epoch, 0, None, None, self.barrier_timeout_s)
+
+    def invalidate(self) -> None:
+        """The shards changed (optimizer step, checkpoint load): gather again on next use."""
+        self.valid = [False] * len(self.modules)
+        self._step_synced = False
+
+    def set_requires_gradient_sync(self, flag: bool) -> None:
+        """As FSDP2's: with False, weight gradients accumulate unsharded on each rank (one local
+        GEMM per micro-batch) and the next synchronising backward reduce-scatters the sum."""
+        self.sync_grads = bool(flag)
+
+    def attach_optimizer(self, opt) -> None:
+        opt.register_step_post_hook(lambda *a, **k: self.invalidate())
+
+    def shard_ptrs(self, i: int) -> List[int]:
+        return [int(self.shard_handle.buffer_ptrs[s]) + 2 * self.shard_offsets[i] for s in range(self.world)]
+
+    def _local(self, i: int) -> torch.Tensor:
+        return self.params[i].to_local()
+
+    # ------------------------------------------------------------------ forward
+    def linear_forward(self, i: int, x2: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return F.linear(x2, self._local(i))
+        if self.valid[i]:
+            return F.linear(x2, self.full[i])
+        n, k = self.shapes[i]
+        if self.full[i] is None:
+            self.full[i] = torch.empty(n, k, dtype=x2.dtype, device=x2.device)
+        if self.fused:
+            if not self._step_synced:
+                # every rank has finished writing its shards (optimizer step) before any reads them
+                self._barrier()
+                self._step_synced = True
+            t = x2.shape[0]
+            xp = _pad_rows(x2, 128)
+            y = _ext().ag_gemm(xp, self.shard_ptrs(i), self.rank, self.full[i], self.ready, self.wait_s)
+            if xp is not x2:
+                y = y[:t]
+        else:
+            parts = [torch.empty_like(self._local(i)) for _ in range(self.world)]
+            dist.all_gather(parts, self._local(i).contiguous(), group=self.group)
+            torch.cat(parts, 0, out=self.full[i])
+            y = F.linear(x2, self.full[i])
+        self.valid[i] = True
+        return y
+
+    # ------------------------------------------------------------------ backward
+    def linear_backward(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> torch.Tensor:
+        w = self._local(i) if self.world == 1 else self.full[i]
+        dx = dy2 @ w
+        p = self.params[i]
+        if not p.requires_grad:
+            return dx
+        self._accumulate_grad(i, dy2, x2)
+        return dx
+
+    def _grad_local(self, i: int) -> Tuple[torch.Tensor, bool]:
+        from torch.distributed.tensor import DTensor, Shard
+
+        p = self.params[i]
+        if p.grad is None:
+            n, k = self.shapes[i]
+            local = torch.empty(self.rows[i], k, dtype=p.dtype, device=self.device)
+            p.grad = DTensor.from_local(local, self.mesh, [Shard(0)], run_check=False, shape=(n, k), stride=(k, 1))
+            return local, False
+        return p.grad.to_local(), True
+
+    def _accumulate_grad(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
+        n, k = self.shapes[i]
+        r = self.rows[i]
+        if self.world > 1 and not self.sync_grads:
+            # no-sync micro-batch: accumulate this rank's unsharded partial dW locally
+            if self.acc[i] is None:
+                self.acc[i] = torch.empty(n, k, dtype=dy2.dtype, device=dy2.device)
+            if self.acc_live[i]:
+                self.acc[i].addmm_(dy2.t(), x2)
+            else:
+                torch.mm(dy2.t(), x2, out=self.acc[i])
+                self.acc_live[i] = True
+            return
+        carry = self.acc[i] if self.acc_live[i] else None
+        self.acc_live[i] = False
+        g, acc = self._grad_local(i)
+        if self.world == 1:
+            dw = dy2.t() @ x2
+            if acc:
+                g.add_(dw)
+            else:
+                g.copy_(dw)
+            return
+        if not self.fused:
+            dw = (dy2.t().float() @ x2.float())
+            if carry is not None:
+                dw += carry.float()
+            dist.all_reduce(dw, group=self.group)
+            dw = dw[self.rank * r:(self.rank + 1) * r].div_(self.world).to(g.dtype)
+            if acc:
+                g.add_(dw)
+            else:
+                g.copy_(dw)
+            return
+        ext = _ext()
+        meta = self._meta.get(i)
+        if meta is None:
+            meta = torch.tensor([k, 0, r], dtype=torch.int64, device=self.device)
+            self._meta[i] = meta
+        b = self.parity
+        self.parity ^= 1
+        # rank s's rows of this rank's partial dW (+ the no-sync accumulation) -> slot [b][rank]
+        # of rank s, by P2P stores from the GEMM epilogue
+        ext.wgrad_out(_pad_rows(dy2, 64), _pad_rows(x2, 64), self._slot_ptrs[b], self.world, meta, False, 0.0,
+                      carry, 1.0)
+        self._barrier()
+        slots = self.slot_buf[b * self.slot_elems:(b + 1) * self.slot_elems]
+        ext.rs_reduce(slots, self.world, self.slot_elems // self.world, g, acc, 1.0 / self.world)
+
+
+def block_linears(model: nn.Module, blocks_attr: str = "layers") -> List[nn.Linear]:
+    out = []
+    for blk in getattr(model, blocks_attr):
+        for m in blk.modules():
+            if isinstance(m, nn.Linear) and m.bias is None:
+                out.append(m)
+    return out
+
+
+def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str = "layers",
+                    reshard_after_forward: Optional[bool] = None) -> SymmFSDP:
+    """Shard every bias-free linear of the transformer blocks on symmetric memory (fused
+    all-gather/reduce-scatter kernels) and ``fully_shard`` the rest of the model (embeddings,
+    norms, LM head) with FSDP2, the linears passed as ``ignored_params``.  A model on the meta
+    device is materialised on ``device``.  Returns the controller (``model._symm_fsdp``)."""
+    from torch.distributed.fsdp import fully_shard
+
+    lin = block_linears(model, blocks_attr)
+    fully_shard(model, mesh=mesh, reshard_after_forward=reshard_after_forward,
+                ignored_params={m.weight for m in lin})
+    if device is not None and any(p.device.type == "meta" for p in model.parameters()):
+        model.to_empty(device=torch.device(device))
+    dev = torch.device(device) if device is not None else next(model.parameters()).device
+    ctl = SymmFSDP(lin, mesh=mesh, device=dev)
+    model._symm_fsdp = ctl
+    fsdp_sync = model.set_requires_gradient_sync
+
+    def set_requires_gradient_sync(flag: bool, *a, **kw):
+        fsdp_sync(flag, *a, **kw)
+        ctl.set_requires_gradient_sync(flag)
+
+    model.set_requires_gradient_sync = set_requires_gradient_sync
+    return ctl

@@ -1,0 +1,124 @@
+"""Worker for the multi-GPU SymmFSDP tests (launched with torchrun by tests/test_gpu_symm_fsdp.py).
+
+``--mode kernels``: fused all-gather GEMM and GEMM -> reduce-scatter on single linears, checked
+against fp32 references built from all ranks' inputs.  ``--mode train``: a small Llama trained
+for a few steps with SymmFSDP linears and with plain FSDP2; rank 0 saves both trajectories."""
+import argparse
+import datetime
+import os
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+
+def _gather(t):
+    parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t.contiguous())
+    return parts
+
+
+def run_kernels(rank, world, dev):
+    from my_muon_fsdp2_b200._ext import check_device_error
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmFSDP
+
+    shapes = [(1024, 512), (512, 1024), (256 * world, 256), (768 * world, 512)]
+    torch.manual_seed(0)
+    lins = [nn.Linear(k, n, bias=False).to(dev, torch.bfloat16) for n, k in shapes]
+    fulls = [m.weight.detach().clone() for m in lins]
+    ctl = SymmFSDP(lins, device=dev)
+    assert ctl.fused
+    res = {}
+    for i, (m, w) in enumerate(zip(lins, fulls)):
+        for t in (256, 200):  # 200: token count padded to the tile size inside
+            g = torch.Generator(device="cpu").manual_seed(1000 * i + 10 * rank + t)
+            x = torch.randn(t, w.shape[1], generator=g).to(dev, torch.bfloat16).requires_grad_(True)
+            ctl.invalidate()
+            m.weight.grad = None
+            y = m(x)  # fused all-gather GEMM
+            y2 = m(x)  # resident full weight
+            ref = x.detach().float() @ w.float().t()
+            res[f"y{i}_{t}"] = ((y.float() - ref).norm() / ref.norm()).item()
+            res[f"y2{i}_{t}"] = ((y2.float() - ref).norm() / ref.norm()).item()
+            res[f"g{i}_{t}"] = bool(torch.equal(ctl.full[i], w))
+            dy = torch.randn(t, w.shape[0], generator=g).to(dev, torch.bfloat16)
+            y.backward(dy)
+            xs, dys = _gather(x.detach()), _gather(dy)
+            dw = sum(d.float().t() @ a.float() for d, a in zip(dys, xs)) / world
+            r = w.shape[0] // world
+            dw_loc = dw[rank * r:(rank + 1) * r]
+            got = m.weight.grad.to_local().float()
+            res[f"dw{i}_{t}"] = ((got - dw_loc).norm() / dw_loc.norm()).item()
+            dx_ref = dy.float() @ w.float()
+            res[f"dx{i}_{t}"] = ((x.grad.float() - dx_ref).norm() / dx_ref.norm()).item()
+    torch.cuda.synchronize()
+    check_device_error(dev.index)
+    return res
+
+
+def run_train(rank, world, dev, steps=3):
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from my_muon_fsdp2_b200 import FusedAdamW, MuonOptimizer
+    from my_muon_fsdp2_b200.models.llama import Llama, LlamaConfig, apply_fsdp
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    out = {}
+    for mode in ("symm", "fsdp2"):
+        torch.manual_seed(0)
+        cfg = LlamaConfig.tiny(dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab_size=1024, n_layers=2)
+        model = Llama(cfg).to(dev, torch.bfloat16)
+        mesh = init_device_mesh("cuda", (world,))
+        if mode == "symm":
+            ctl = apply_symm_fsdp(model, mesh)
+        else:
+            apply_fsdp(model, mesh)
+        names = set(model.muon_param_names())
+        opts = [MuonOptimizer([p for n, p in model.named_parameters() if n in names], lr=0.02, weight_decay=0.01),
+                FusedAdamW([p for n, p in model.named_parameters() if n not in names], lr=1e-3)]
+        if mode == "symm":
+            for o in opts:
+                ctl.attach_optimizer(o)
+        losses = []
+        for s in range(steps):
+            g = torch.Generator().manual_seed(100 * s + rank)
+            tok = torch.randint(0, cfg.vocab_size, (2, 2, 129), generator=g).to(dev)
+            tot = 0.0
+            for mb in range(2):
+                model.set_requires_gradient_sync(mb == 1)
+                loss = model(tok[mb, :, :-1], tok[mb, :, 1:]) / 2
+                loss.backward()
+                tot += loss.item()
+            for o in opts:
+                o.step()
+                o.zero_grad(set_to_none=True)
+            losses.append(tot)
+        params = {n: (p.full_tensor() if hasattr(p, "full_tensor") else p).detach().float().cpu()
+                  for n, p in model.named_parameters()}
+        out[mode] = {"losses": losses, "params": params}
+        del model, opts
+        torch.cuda.synchronize()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", choices=["kernels", "train"], required=True)
+    ap.add_argument("--out", required=True)
+    a = ap.parse_args()
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    try:
+        res = run_kernels(rank, world, dev) if a.mode == "kernels" else run_train(rank, world, dev)
+        if rank == 0:
+            torch.save(res, a.out)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

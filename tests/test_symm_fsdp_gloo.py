@@ -1,0 +1,122 @@
+"""SymmFSDP semantics on CPU gloo ranks: the linears sharded by ``apply_symm_fsdp`` (collectives
+through torch.distributed here; fused kernels on CUDA) must give the gradients and the training
+trajectory of a single-process model trained on the union of the ranks' data."""
+import copy
+
+import pytest
+import torch
+import torch.nn as nn
+
+from tests.conftest import rel_err
+from tests.dist_util import run_ranks
+
+pytestmark = pytest.mark.distributed
+
+D, H = 256, 512
+
+
+class Block(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.norm = nn.LayerNorm(D)
+        self.up = nn.Linear(D, H, bias=False)
+        self.down = nn.Linear(H, D, bias=False)
+
+    def forward(self, x):
+        return x + self.down(torch.nn.functional.gelu(self.up(self.norm(x))))
+
+
+class Net(nn.Module):
+    def __init__(self):
+        super().__init__()
+        torch.manual_seed(0)
+        self.inp = nn.Linear(32, D)
+        self.layers = nn.ModuleList([Block() for _ in range(2)])
+        self.out = nn.Linear(D, 8)
+
+    def forward(self, x):
+        x = self.inp(x)
+        for b in self.layers:
+            x = b(x)
+        return self.out(x)
+
+
+def _data(step, rank, batch=16):
+    g = torch.Generator().manual_seed(100 * step + rank)
+    return torch.randn(batch, 32, generator=g), torch.randn(batch, 8, generator=g)
+
+
+def _full(t):
+    return t.full_tensor() if hasattr(t, "full_tensor") else t
+
+
+def _symm_grads(rank, world, no_sync):
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmLinear, apply_symm_fsdp
+
+    model = Net()
+    ctl = apply_symm_fsdp(model)
+    assert ctl.world == world and not ctl.fused
+    assert sum(isinstance(m, SymmLinear) for m in model.modules()) == 4
+    for step in range(2):  # two micro-batches: gradients accumulate
+        if no_sync:
+            model.set_requires_gradient_sync(step == 1)
+        x, y = _data(step, rank)
+        loss = ((model(x) - y) ** 2).mean() / 2
+        loss.backward()
+    return {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+
+
+@pytest.mark.parametrize("no_sync", [False, True])
+def test_symm_fsdp_grads_match_single_process(no_sync):
+    world = 2
+    got = run_ranks(_symm_grads, world, no_sync)
+    ref = Net()
+    for step in range(2):
+        xs, ys = zip(*[_data(step, r) for r in range(world)])
+        loss = ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean() / 2
+        loss.backward()
+    for n, p in ref.named_parameters():
+        assert rel_err(got[n], p.grad) < 1e-5, n
+
+
+def _symm_train(rank, world, steps):
+    from my_muon_fsdp2_b200 import MuonOptimizer
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    model = Net()
+    ctl = apply_symm_fsdp(model)
+    mats = [p for p in ctl.params]
+    rest = [p for p in model.parameters() if all(p is not q for q in mats)]
+    opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95, weight_decay=0.01), torch.optim.AdamW(rest, lr=1e-3)]
+    for o in opts:
+        ctl.attach_optimizer(o)
+    losses = []
+    for step in range(steps):
+        x, y = _data(step, rank)
+        loss = ((model(x) - y) ** 2).mean()
+        loss.backward()
+        for o in opts:
+            o.step()
+            o.zero_grad(set_to_none=True)
+        losses.append(loss.item())
+    return {"params": {n: _full(p.detach()).clone() for n, p in model.named_parameters()}, "losses": losses}
+
+
+def test_symm_fsdp_training_matches_single_process():
+    from my_muon_fsdp2_b200 import MuonOptimizer
+
+    world, steps = 2, 3
+    got = run_ranks(_symm_train, world, steps)
+    ref = Net()
+    mats = [m.weight for b in ref.layers for m in (b.up, b.down)]
+    rest = [p for p in ref.parameters() if all(p is not q for q in mats)]
+    opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95, weight_decay=0.01), torch.optim.AdamW(rest, lr=1e-3)]
+    for step in range(steps):
+        xs, ys = zip(*[_data(step, r) for r in range(world)])
+        loss = ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean()
+        loss.backward()
+        for o in opts:
+            o.step()
+            o.zero_grad(set_to_none=True)
+    for n, p in ref.named_parameters():
+        assert rel_err(got["params"][n], p.detach()) < 1e-4, n
