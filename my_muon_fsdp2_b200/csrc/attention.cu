@@ -469,7 +469,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + (tid & 127);
     float stat_next = stat_src[stat_base + j * QB] * stat_mul;
     for (int n = 0; n < n_iter && ok; ++n) {
-      const int h = hq;
       const int i = j + n;
       // publish this iteration's statistics (the previous iteration's readers are past the barrier)
       asm volatile("bar.sync 1, 256;" ::: "memory");
