@@ -4,7 +4,9 @@ Inputs: row-sharded (torch.chunk / FSDP2 Shard(0)) bf16 momentum matrices ~N(0,1
 shapes 4096x4096, 1024x4096, 4096x14336, 14336x4096, 8192x28672 (``--shapes`` to override).
 
 * ``--impl ours``: the library's MuonEngine on DTensor shards (owner-computes schedule, fused
-  momentum/NS/update kernels, ``--comm nccl|p2p`` exchange), one launch group per shape.
+  momentum/NS/update kernels, ``--comm nccl|p2p`` exchange), one launch group per shape; the
+  matrices that dominate the per-rank load (8192x28672) take the cooperative all-rank chain
+  (``--schedule auto``; ``never``/``always`` force a schedule).
 * ``--impl reference``: the reference's own path per matrix — ``muon_fsdp.distributed
   .all_gather_grads`` (NCCL all_gather_into_tensor) -> ``muon_fsdp.utils
   .zeropower_via_newtonschulz5`` (fp32, larger-side Gram) -> row slice -> ``add_``.
@@ -40,6 +42,8 @@ def parse():
     ap.add_argument("--comm", choices=["auto", "nccl", "p2p"], default="auto")
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--gemm-variant", type=int, default=0, help="0 auto, 1 single-CTA, 2 CTA pair")
+    ap.add_argument("--schedule", choices=["auto", "never", "always"], default="auto",
+                    help="cooperative all-rank NS chain per shape: auto (cost model), never, always")
     return ap.parse_args()
 
 
@@ -94,7 +98,7 @@ def main():
 
         ext().set_gemm_variant(args.gemm_variant)
 
-        engine = MuonEngine(comm=args.comm)
+        engine = MuonEngine(comm=args.comm, split=args.schedule)
         hp = MuonHyper(mode=MODE_COPY, ns_steps=args.ns_steps)
 
         def step():
@@ -137,7 +141,9 @@ def main():
                           "shapes": args.shapes, "iters": args.iters, "warmup": args.warmup,
                           "tflops_effective": flops / (ms / 1e3) / 1e12,
                           "roofline_ms": roof_ms, "roofline_fraction": roof_ms / ms, "peak_source": src,
-                          "comm": args.comm if args.impl == "ours" else "nccl all_gather"}))
+                          "comm": args.comm if args.impl == "ours" else "nccl all_gather",
+                          "schedule": args.schedule if args.impl == "ours" else "replicated",
+                          "cooperative_matrices": (engine.split_count if args.impl == "ours" else 0)}))
     dist.destroy_process_group()
 
 

@@ -207,8 +207,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (diag && (j * KB + e > qi)) sv[e] = -INFINITY;
         mx = fmaxf(mx, sv[e]);
       }
-      const float m_new = fmaxf(m2, mx);
-      const float alpha = (m2 == -INFINITY) ? 0.f : fast_exp2(m2 - m_new);
+      // The reference max only moves when the row max grows by more than 2^8: probabilities stay
+      // below 256 and O / l is unchanged (both use the same reference), while O rarely needs a
+      // rescale in TMEM.
+      const bool grow = (m2 == -INFINITY) || (mx > m2 + 8.f);
+      const float m_new = grow ? mx : m2;
+      const float alpha = (m2 == -INFINITY) ? 0.f : (grow ? fast_exp2(m2 - m_new) : 1.f);
       // P_{j-1} V_{j-1} must be done before O is rescaled and P is overwritten
       if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
         ok = false;

@@ -450,7 +450,7 @@ __device__ __forceinline__ void tile_coords_pair(const GemmParams& p, int t, int
   }
 }
 
-template <bool B_MN>
+template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmParams p) {
@@ -514,7 +514,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
-          tma_load_3d_pair(sA + stage * P_A_BYTES, &tmA, fb, kb * BK, tm * P_BM + rank * 128, b);
+          if (A_MN) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+              tma_load_3d_pair(sA + stage * P_A_BYTES + c * (BK * 64 * 2), &tmA, fb, tm * P_BM + rank * 128 + c * 64,
+                               kb * BK, b);
+          } else {
+            tma_load_3d_pair(sA + stage * P_A_BYTES, &tmA, fb, kb * BK, tm * P_BM + rank * 128, b);
+          }
           if (B_MN) {
 #pragma unroll
             for (int c = 0; c < 2; ++c)
@@ -533,7 +540,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer (leader CTA only) ---------------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, BN, false, B_MN);
+      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -556,7 +563,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t b_addr = smem_u32(sB + stage * P_B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = sdesc_kmajor(a_addr + kk * 32);
+            const uint64_t ad = A_MN ? sdesc_mnmajor(a_addr + kk * 16 * 128, BK * 64 * 2) : sdesc_kmajor(a_addr + kk * 32);
             const uint64_t bd = B_MN ? sdesc_mnmajor(b_addr + kk * 16 * 128, BK * 64 * 2) : sdesc_kmajor(b_addr + kk * 32);
             umma_bf16_pair(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
           }
@@ -892,7 +899,7 @@ CUtensorMap make_map_bf16_3d(const void* base, uint64_t inner, uint64_t outer, u
 
 struct DeviceInfo {
   int sms = 0;
-  bool attr_set[8] = {false, false, false, false, false, false, false, false};
+  bool attr_set[12] = {};
 };
 DeviceInfo& dev_info(int dev) {
   static DeviceInfo infos[64];
@@ -927,7 +934,7 @@ void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t
     // the CTA pair needs 256-row blocks and enough tiles to keep most SMs busy
     variant = (p.M % P_BM == 0 && pair_tiles(p) >= di.sms / 2) ? 2 : 1;
   }
-  if (variant == 2 && (p.M % P_BM != 0 || a_mn)) variant = 1;  // the pair kernel reads A K-major only
+  if (variant == 2 && p.M % P_BM != 0) variant = 1;
   const bool pair = variant == 2;
   const int bm = pair ? P_BM : BM;
   p.tiles_m = p.M / bm;
@@ -982,19 +989,17 @@ void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t le;
-    if (b_mn) {
-      if (!di.attr_set[3]) {
-        cudaFuncSetAttribute(tc_gemm_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
-        di.attr_set[3] = true;
+    auto go = [&](auto kern, int slot) {
+      if (!di.attr_set[slot]) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+        di.attr_set[slot] = true;
       }
-      le = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<true>, ma, mb, p);
-    } else {
-      if (!di.attr_set[2]) {
-        cudaFuncSetAttribute(tc_gemm_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
-        di.attr_set[2] = true;
-      }
-      le = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<false>, ma, mb, p);
-    }
+      return cudaLaunchKernelEx(&cfg, kern, ma, mb, p);
+    };
+    if (a_mn)
+      le = b_mn ? go(tc_gemm_pair_kernel<true, true>, 7) : go(tc_gemm_pair_kernel<true, false>, 8);
+    else
+      le = b_mn ? go(tc_gemm_pair_kernel<false, true>, 3) : go(tc_gemm_pair_kernel<false, false>, 2);
     if (le != cudaSuccess) throw std::runtime_error(std::string("mmf: tc_gemm pair launch failed: ") + cudaGetErrorString(le));
   }
   count_launch();

@@ -37,11 +37,11 @@ def local_of(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
 _ENGINES: Dict[Any, MuonEngine] = {}
 
 
-def default_engine(group=None, comm: str = "auto") -> MuonEngine:
-    key = (id(group), comm)
+def default_engine(group=None, comm: str = "auto", split: str = "auto") -> MuonEngine:
+    key = (id(group), comm, split)
     eng = _ENGINES.get(key)
     if eng is None:
-        eng = MuonEngine(process_group=group, comm=comm)
+        eng = MuonEngine(process_group=group, comm=comm, split=split)
         _ENGINES[key] = eng
     return eng
 

@@ -48,14 +48,17 @@ class MuonOptimizer(Optimizer):
         weight_decay: decoupled weight decay (0).  nesterov: Nesterov form (False).
         ns_steps: Newton–Schulz iterations (5).
         process_group / comm: optional overrides for the sharded engine.
+        schedule: "auto" picks owner-computes or the cooperative all-rank chain per matrix shape
+            (``select_split``); "never" / "always" force one of them (eligible shapes only).
     """
 
     def __init__(self, params, lr: float = 0.02, momentum: float = 0.95, weight_decay: float = 0.0,
-                 nesterov: bool = False, ns_steps: int = 5, *, process_group=None, comm: str = "auto") -> None:
+                 nesterov: bool = False, ns_steps: int = 5, *, process_group=None, comm: str = "auto",
+                 schedule: str = "auto") -> None:
         _validate(lr, momentum, weight_decay, ns_steps, nesterov)
         defaults = dict(lr=lr, momentum=momentum, weight_decay=weight_decay, nesterov=nesterov, ns_steps=ns_steps)
         super().__init__(params, defaults)
-        self._engine = default_engine(process_group, comm)
+        self._engine = default_engine(process_group, comm, schedule)
 
     def __setstate__(self, state: dict) -> None:
         super().__setstate__(state)

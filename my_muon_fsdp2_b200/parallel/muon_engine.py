@@ -83,6 +83,55 @@ def assign_owners(costs: Sequence[float], world: int) -> List[int]:
     return owners
 
 
+# Relative throughputs of the schedule cost model (only their ratio matters).
+_GEMM_FLOPS = 1.4e15   # sustained bf16 tensor-core rate
+_LINK_BPS = 7.0e11     # NVLink bytes/s per direction per GPU
+
+
+def split_eligible(rows: int, cols: int, world: int) -> bool:
+    """The cooperative schedule takes wide matrices whose row shards are whole GEMM tiles."""
+    return world > 1 and rows <= cols and rows % (128 * world) == 0 and rows % 256 == 0 and cols % 256 == 0
+
+
+def select_split(shapes: Sequence[Tuple[int, int]], world: int, steps: int) -> List[int]:
+    """Per-shape schedule choice.  Owner-computes runs each matrix's whole chain on one rank
+    (makespan = LPT load of the busiest rank); the cooperative schedule splits one matrix's
+    chain over all ranks (FLOPs / world, plus two all-gathers per iteration).  Matrices move to
+    the cooperative schedule, largest first, while that lowers the predicted step time — in
+    practice the ones bigger than the average per-rank load, e.g. 8192 x 28672 among
+    4096-wide layers."""
+    costs = [ns_flops(r, c, steps) / _GEMM_FLOPS for r, c in shapes]
+
+    def makespan(idx):
+        if not idx:
+            return 0.0
+        owners = assign_owners([costs[i] for i in idx], world)
+        load = [0.0] * world
+        for i, o in zip(idx, owners):
+            load[o] += costs[i]
+        return max(load)
+
+    def split_time(i):
+        r, c = shapes[i]
+        comm = steps * 2.0 * (r * c + r * r) * (world - 1) / world / _LINK_BPS
+        return costs[i] / world + comm
+
+    rest = list(range(len(shapes)))
+    chosen: List[int] = []
+    best = makespan(rest)
+    for i in sorted(rest, key=lambda k: -costs[k]):
+        if not split_eligible(shapes[i][0], shapes[i][1], world):
+            continue
+        cand = [k for k in rest if k != i]
+        t = makespan(cand) + sum(split_time(k) for k in chosen + [i])
+        if t < best:
+            best, rest = t, cand
+            chosen.append(i)
+        else:
+            break
+    return sorted(chosen)
+
+
 def _local(t: torch.Tensor) -> torch.Tensor:
     return t.to_local() if is_dtensor(t) else t
 
@@ -99,11 +148,15 @@ class MuonEngine:
     """Executes Muon steps for lists of :class:`MuonTask` (see module docstring)."""
 
     def __init__(self, process_group: Optional[dist.ProcessGroup] = None, comm: str = "auto",
-                 max_workspace_bytes: int = 8 << 30):
+                 max_workspace_bytes: int = 8 << 30, split: str = "auto"):
         if comm not in ("auto", "nccl", "p2p"):
             raise ValueError(f"comm must be 'auto', 'nccl' or 'p2p', got {comm!r}")
+        if split not in ("auto", "never", "always"):
+            raise ValueError(f"split must be 'auto', 'never' or 'always', got {split!r}")
         self.group = process_group
         self.comm = comm
+        self.split = split
+        self.split_count = 0  # matrices of the last step that took the cooperative schedule
         self.max_workspace_bytes = int(max_workspace_bytes)
         self._p2p = None
         self.last_stats: Dict[str, float] = {}
@@ -148,6 +201,16 @@ class MuonEngine:
                 self._local_cuda(local, hp)
             else:
                 self._local_cpu(local, hp)
+        if sharded and world > 1 and self.split != "never":
+            shp = [tuple(t.param.shape) for t in sharded]
+            if self.split == "always":
+                pick = [i for i, (r, c) in enumerate(shp) if split_eligible(r, c, world)]
+            else:
+                pick = select_split(shp, world, hp.ns_steps)
+            for i in pick:
+                self._split_chain(sharded[i], hp, world, rank, group, is_cuda)
+            self.split_count = len(pick)
+            sharded = [t for i, t in enumerate(sharded) if i not in set(pick)]
         if sharded:
             if is_cuda and self._use_p2p(group):
                 self._sharded_p2p(sharded, hp, world, rank, group)
@@ -225,6 +288,82 @@ class MuonEngine:
                 vvec = torch.tensor([-t.lr_eff for t in sub], dtype=torch.float32).to(dev, non_blocking=True)
                 run_ns_group(X0, s, s2, hp.ns_steps, ptrs, cols, pdt == torch.float32, tall, mw, nw,
                              p_scale=1.0, v_scale=1.0, p_scale_vec=pvec, v_scale_vec=vvec)
+
+    # ------------------------------------------------------------------ cooperative schedule
+    def _split_chain(self, t: MuonTask, hp: MuonHyper, world: int, rank: int, group: dist.ProcessGroup,
+                     is_cuda: bool) -> None:
+        """One wide matrix X (m x n, m <= n, row-sharded) orthogonalised by all ranks together.
+        Rank r owns rows R_r of every iterate; per quintic iteration:
+
+            all-gather X               (every rank needs all of X for its Gram rows)
+            A_r = X_r X^T              rows R_r of the Gram matrix (x s^2 on iteration 0)
+            all-gather A
+            B_r = c A_r A + b A_r      rows R_r of b A + c A^2
+            X'_r = B_r X + a X_r       (x s on iteration 0); the last one is written straight
+                                       into the parameter shard as p = decay p - lr X'_r
+
+        Each rank does 1/world of the chain's FLOPs; the all-gathers move m n + m^2 elements
+        per iteration.  Same algebra as ``newton_schulz_reference`` (fp64 oracle)."""
+        a, b, c = NS_COEFFICIENTS
+        m, n = t.param.shape
+        mr = m // world
+        p = t.local_param
+        dev = p.device
+        if not is_cuda:
+            u = _momentum_torch(t, hp).float()
+            ss = (u * u).sum().reshape(1)
+            dist.all_reduce(ss, group=group)
+            X = torch.cat(_gather_list(u.contiguous(), world, group)) / (ss.sqrt() + NS_EPS)
+            for it in range(hp.ns_steps):
+                if it:
+                    X = torch.cat(_gather_list(Xr.contiguous(), world, group))
+                Xr = X[rank * mr:(rank + 1) * mr]
+                Ar = Xr @ X.t()
+                A = torch.cat(_gather_list(Ar.contiguous(), world, group))
+                Br = b * Ar + c * (Ar @ A)
+                Xr = a * Xr + Br @ X
+            _decay_(p, t.decay)
+            p.add_(Xr.to(p.dtype), alpha=-t.lr_eff)
+            return
+        from .._ext import ext
+
+        E = ext()
+        Xa = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        Xb = torch.empty_like(Xa)
+        Ar = torch.empty(mr, m, dtype=torch.bfloat16, device=dev)
+        Af = torch.empty(m, m, dtype=torch.bfloat16, device=dev)
+        Br = torch.empty_like(Ar)
+        sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
+        E.muon_prep([t.local_grad.contiguous()], [t.buf] if hp.mode != MODE_COPY else [],
+                    [p] if hp.wd_coupled != 0 else [], Xa, [rank * mr * n], [0], [0], [n], [], [], hp.mode,
+                    hp.nesterov, hp.momentum, hp.wd_coupled, sumsq)
+        parts = torch.empty(world, 1, dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(parts, sumsq, group=group)
+        sc = torch.empty(1, dtype=torch.float32, device=dev)
+        sc2 = torch.empty_like(sc)
+        E.ns_scale(parts, 1, world, NS_EPS, sc, sc2)
+        X, Xn = Xa, Xb
+        for it in range(hp.ns_steps):
+            first = it == 0
+            Xr = X[rank * mr:(rank + 1) * mr]
+            dist.all_gather_into_tensor(X, Xr, group=group)
+            E.tc_gemm_ws(Xr.view(1, mr, n), X.view(1, m, n), False, Ar.view(1, mr, m), None, sc2 if first else None,
+                         1.0, None, 0.0, False)
+            dist.all_gather_into_tensor(Af, Ar, group=group)
+            E.tc_gemm_ws(Ar.view(1, mr, m), Af.view(1, m, m), False, Br.view(1, mr, m), Ar.view(1, mr, m), None, c,
+                         None, b, False)
+            if it == hp.ns_steps - 1:
+                if not p.is_contiguous():
+                    raise RuntimeError("MuonEngine: the cooperative schedule needs contiguous parameter shards")
+                E.tc_gemm_out(Br.view(1, mr, m), X.view(1, m, n), True, Xr.view(1, mr, n), sc if first else None, 1.0,
+                              sc if first else None, a, E.ptr_table([p]), 1, None, n, p.dtype == torch.float32,
+                              False, mr, n, _decay_vec([t.decay], dev), 1.0,
+                              torch.full((1,), -t.lr_eff, dtype=torch.float32, device=dev), 1.0)
+            else:
+                Xnr = Xn[rank * mr:(rank + 1) * mr]
+                E.tc_gemm_ws(Br.view(1, mr, m), X.view(1, m, n), True, Xnr.view(1, mr, n), Xr.view(1, mr, n),
+                             sc if first else None, 1.0, sc if first else None, a, False)
+                X, Xn = Xn, X
 
     # ------------------------------------------------------------------ sharded path
     def _sharded(self, tasks: List[MuonTask], hp: MuonHyper, world: int, rank: int,
@@ -504,6 +643,12 @@ class MuonEngine:
 
 
 # ---------------------------------------------------------------------- helpers
+def _gather_list(x: torch.Tensor, world: int, group) -> List[torch.Tensor]:
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x, group=group)
+    return parts
+
+
 def _group_by(items, key) -> "OrderedDict":
     out: "OrderedDict" = OrderedDict()
     for it in items:

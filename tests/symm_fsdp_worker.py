@@ -101,9 +101,44 @@ def run_train(rank, world, dev, steps=3):
     return out
 
 
+def run_split(rank, world, dev, steps=2):
+    """Muon with the cooperative all-rank chain vs owner-computes on the same FSDP2 model."""
+    from torch.distributed.fsdp import fully_shard
+
+    from my_muon_fsdp2_b200 import MuonOptimizer
+
+    out = {}
+    for schedule in ("always", "never"):
+        torch.manual_seed(0)
+        model = nn.Sequential(nn.Linear(2048, 512, bias=False), nn.Linear(1024, 1024, bias=False)).to(dev)
+        for m in model:
+            fully_shard(m)
+        fully_shard(model)
+        opt = MuonOptimizer(model.parameters(), lr=0.02, momentum=0.95, weight_decay=0.01, schedule=schedule)
+        for s in range(steps):
+            g = torch.Generator(device="cpu").manual_seed(s)
+            for p in model.parameters():
+                p.grad = None
+            w0, w1 = model[0].weight, model[1].weight
+            # synthetic gradients (the same full matrices on every rank, sharded like the params)
+            from torch.distributed.tensor import distribute_tensor
+
+            for w in (w0, w1):
+                full = torch.randn(w.shape, generator=g).to(dev)
+                w.grad = distribute_tensor(full, w.device_mesh, w.placements)
+            opt.step()
+            assert opt._engine.split_count == (2 if schedule == "always" else 0)
+        out[schedule] = {n: p.full_tensor().detach().float().cpu() for n, p in model.named_parameters()}
+    torch.cuda.synchronize()
+    from my_muon_fsdp2_b200._ext import check_device_error
+
+    check_device_error(dev.index)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["kernels", "train"], required=True)
+    ap.add_argument("--mode", choices=["kernels", "train", "split"], required=True)
     ap.add_argument("--out", required=True)
     a = ap.parse_args()
     local = int(os.environ["LOCAL_RANK"])
@@ -112,7 +147,7 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
     try:
-        res = run_kernels(rank, world, dev) if a.mode == "kernels" else run_train(rank, world, dev)
+        res = {"kernels": run_kernels, "train": run_train, "split": run_split}[a.mode](rank, world, dev)
         if rank == 0:
             torch.save(res, a.out)
         dist.barrier()

@@ -108,3 +108,24 @@ def test_out_mode_row_segments():
     V = (A.float() @ Bk.float())[:, :m_true, :n_true]
     assert rel_err(torch.cat(segs0), V[0]) < 1e-2
     assert rel_err(torch.cat(segs1), V[1].T) < 1e-2
+
+
+@pytest.mark.parametrize("T,N,K", [(64, 128, 256), (256, 512, 512), (4096, 1024, 4096), (320, 768, 256)])
+@pytest.mark.parametrize("with_c", [False, True])
+def test_wgrad_mnmajor_a_row_segments(T, N, K, with_c):
+    """Weight gradient dW = dY^T X (+ C) with both operands MN-major, rows scattered into two
+    segments (the reduce-scatter layout of two ranks)."""
+    dy, x = _bf(T, N), _bf(T, K)
+    C = _bf(N, K) if with_c else None
+    half = N // 2
+    segs = [torch.full((half, K), float("nan"), device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    ptrs = torch.tensor([s.data_ptr() for s in segs], dtype=torch.int64, device="cuda")
+    meta = torch.tensor([K, 0, half], dtype=torch.int64, device="cuda")
+    E().wgrad_out(dy, x, ptrs, 2, meta, False, 0.0, C, 1.0)
+    ref = dy.float().t() @ x.float()
+    if with_c:
+        ref = ref + C.float()
+    assert rel_err(torch.cat(segs), ref) < 1e-2
+    from my_muon_fsdp2_b200._ext import check_device_error
+
+    check_device_error(0)

@@ -46,3 +46,11 @@ def test_symm_fsdp_training_matches_fsdp2():
         assert abs(x - y) < 2e-2 * abs(y), (a["losses"], b["losses"])
     for n in b["params"]:
         assert rel_err(a["params"][n], b["params"][n]) < 2e-2, n
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_cooperative_ns_schedule_matches_owner_computes():
+    with tempfile.TemporaryDirectory() as d:
+        res = _run(2, "split", os.path.join(d, "s.pt"))
+    for n in res["never"]:
+        assert rel_err(res["always"][n], res["never"][n]) < 2e-2, n
