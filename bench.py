@@ -97,7 +97,7 @@ def build_ours(args, world, local):
     with torch.device("meta"):
         model = Llama(cfg).to(torch.bfloat16)
     ctl = None
-    if args.fsdp == "symm" and world > 1:
+    if args.fsdp == "symm":
         from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
 
         ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local))
@@ -277,7 +277,7 @@ def main():
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",
-                       "fsdp_impl": (args.fsdp if (args.impl == "ours" and world > 1) else "fully_shard"),
+                       "fsdp_impl": (args.fsdp if args.impl == "ours" else "fully_shard"),
                        "tokens_per_step": tokens_per_step,
                        "l2": "no flush: per-step working set (16 GB bf16 weights + activations) >> 126 MB L2",
                        "optimizers": "Muon(attn+FFN matrices, lr .02, mom .95, wd .01, ns 5) + AdamW(rest, lr 1e-3)"},

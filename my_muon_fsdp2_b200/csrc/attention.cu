@@ -45,8 +45,7 @@ struct AttnSmem {
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + TILE;        // 2 stages
   static constexpr int V_OFF = K_OFF + 2 * TILE;    // 2 stages
-  static constexpr int P_OFF = V_OFF + 2 * TILE;    // P: [128 q x 128 keys] bf16 = 32 KB
-  static constexpr int BAR_OFF = P_OFF + 128 * 128 * 2;
+  static constexpr int BAR_OFF = V_OFF + 2 * TILE;  // P_j lives in TMEM (over S_j), not in smem
   // >= 120 KB so that only one CTA (which holds all 512 TMEM columns) fits on an SM
   static constexpr int BYTES = (BAR_OFF + 256 + 1024) > 120 * 1024 ? (BAR_OFF + 256 + 1024) : 120 * 1024;
 };
@@ -70,17 +69,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint8_t* sQ = smem + L::Q_OFF;
   uint8_t* sK = smem + L::K_OFF;
   uint8_t* sV = smem + L::V_OFF;
-  uint8_t* sP = smem + L::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* s_full = bars + 5;    // [2] S_j in TMEM buffer j&1
+  uint64_t* p_full = bars + 7;    // [2] P_j (bf16, packed) written over S_j
+  uint64_t* pv_done = bars + 9;
+  uint64_t* drain = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = p.T / QB;
@@ -95,9 +92,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&p_full[i], 4);
     }
-    mbar_init(p_full, 4);
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -139,42 +135,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, KB, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
-      bool ok = mbar_wait(q_full, 0, p.err, ERR_MMA_FULL_TIMEOUT);
       const uint32_t q_addr = smem_u32(sQ);
-      for (int j = 0; ok && j <= nblk; ++j) {
-        if (j < nblk) {
-          const int st = j & 1;
-          ok = mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT) &&
-               mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + st * L::TILE);
+      // S_j = Q K_j^T into TMEM buffer j&1.  The buffer last held P_{j-2}, whose P V MMA was
+      // issued earlier by this thread, and tcgen05 MMAs of one thread execute in order.
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * L::TILE);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_bf16(tS[st], sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
-          }
-          umma_commit(&s_full[st]);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tS[st], sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
         }
-        if (j >= 1) {
-          // O += P_{j-1} V_{j-1} once the softmax warps have written P_{j-1}
-          const int pj = j - 1, st = pj & 1;
-          if (!mbar_wait(p_full, pj & 1, p.err, ERR_MMA_FULL_TIMEOUT)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t p_addr = smem_u32(sP);
-          const uint32_t v_addr = smem_u32(sV + st * L::TILE);
+        umma_commit(&s_full[st]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, ERR_MMA_FULL_TIMEOUT) && issue_s(0);
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int st = j & 1;
+        // S_{j+1} overlaps the softmax of block j
+        if (j + 1 < nblk && !(ok = issue_s(j + 1))) break;
+        // O += P_j V_j with P_j read from TMEM (bf16 pairs over S_j's first 64 columns)
+        if (!mbar_wait(&p_full[st], (j >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + st * L::TILE);
 #pragma unroll
-          for (int kk = 0; kk < KB / 16; ++kk) {
-            const uint64_t ad = sdesc_kmajor(p_addr + (kk >> 2) * 16384 + (kk & 3) * 32);
-            const uint64_t bd = sdesc_mnmajor(v_addr + kk * 16 * 128, 16384);
-            umma_bf16(tO, ad, bd, idesc_o, (pj | kk) ? 1u : 0u);
-          }
-          umma_commit(pv_done);
-          umma_commit(&kv_empty[st]);
-        }
+        for (int kk = 0; kk < KB / 16; ++kk)
+          umma_bf16_ts(tO, tS[st] + static_cast<uint32_t>(kk * 8), sdesc_mnmajor(v_addr + kk * 16 * 128, 16384),
+                       idesc_o, (j | kk) ? 1u : 0u);
+        umma_commit(pv_done);
+        umma_commit(&kv_empty[st]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
@@ -213,13 +207,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const bool grow = (m2 == -INFINITY) || (mx > m2 + 8.f);
       const float m_new = grow ? mx : m2;
       const float alpha = (m2 == -INFINITY) ? 0.f : (grow ? fast_exp2(m2 - m_new) : 1.f);
-      // P_{j-1} V_{j-1} must be done before O is rescaled and P is overwritten
-      if (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      // O may only be rescaled once P_{j-1} V_{j-1} has landed (rare: threshold above)
+      if (__any_sync(0xffffffffu, j >= 1 && alpha != 1.f)) {
+        if (!mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
         for (int hh = 0; hh < D / 64; ++hh) {
           float o[64];
@@ -231,33 +225,26 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           tmem_st_32cols_async(tO + lane_off + hh * 64, o);
           tmem_st_32cols_async(tO + lane_off + hh * 64 + 32, o + 32);
         }
-        tmem_st_wait();
       }
-      // probabilities -> swizzled bf16 P tile, row sum
+      // probabilities as bf16 pairs over the first 64 columns of S_j's TMEM buffer; row sum
       float sum = 0.f;
+      float pk[KB / 2];
 #pragma unroll
-      for (int g = 0; g < KB / 8; ++g) {
-        uint4 w;
-        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {
-          const float p0 = fast_exp2(sv[g * 8 + 2 * e2] - m_new);
-          const float p1 = fast_exp2(sv[g * 8 + 2 * e2 + 1] - m_new);
-          sum += p0 + p1;
-          hw[e2] = __floats2bfloat162_rn(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(sP + swz_offset(r, g * 8)) = w;
+      for (int e2 = 0; e2 < KB / 2; ++e2) {
+        const float p0 = fast_exp2(sv[2 * e2] - m_new);
+        const float p1 = fast_exp2(sv[2 * e2 + 1] - m_new);
+        sum += p0 + p1;
+        __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+        pk[e2] = *reinterpret_cast<float*>(&pb);
       }
+      tmem_st_32cols_async(tS[st] + lane_off, pk);
+      tmem_st_32cols_async(tS[st] + lane_off + 32, pk + 32);
+      tmem_st_wait();
       l = l * alpha + sum;
       m2 = m_new;
-      // S buffer free; P visible to the tensor core; O rescale stores complete
       tc_fence_before();
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_empty[st]);
-        mbar_arrive(p_full);
-      }
+      if (lane == 0) mbar_arrive(&p_full[st]);
     }
     // epilogue: wait for the last P V, then O / l
     if (ok && mbar_wait(pv_done, (nblk - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
@@ -291,12 +278,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
 // ======================================================================================
 // Backward, part 1 (dK, dV): one CTA per (128-key block j, query head, batch); loops over the
-// query blocks i >= j (causal).  K_j and V_j stay in smem; Q_i / dO_i are double-buffered.
-//   MMA      S^T = K_j Q_i^T  -> TMEM tS        dP^T = V_j dO_i^T -> TMEM tdP
-//   softmax  (one key row per TMEM lane) P^T = exp2(S^T*scale*log2e - lse_i*log2e) (causal mask
-//            on the diagonal block), packed back into TMEM as bf16; dS^T = P^T * (dP^T - delta_i)
+// query blocks i >= j (causal) in units of 64 queries.  K_j and V_j stay in smem; Q_i / dO_i are
+// double-buffered; S^T / dP^T / dS^T are double-buffered per 64-query half, so the tensor core
+// computes one half while the elementwise warps work on the other.
+//   MMA      S^T = K_j Q_u^T  -> TMEM tS[h]     dP^T = V_j dO_u^T -> TMEM tdP[h]     (N = 64)
+//   softmax  (one key row per TMEM lane) P^T = exp2(S^T*scale*log2e - lse*log2e) (causal mask
+//            on the diagonal block), packed back into TMEM as bf16; dS^T = P^T * (dP^T - delta)
 //            as bf16 into a swizzled smem tile
-//   MMA      dV += P^T dO_i (A from TMEM)      dK += dS^T Q_i   (dO_i, Q_i read MN-major)
+//   MMA      dV += P^T dO_u (A from TMEM)      dK += dS^T Q_u   (dO_u, Q_u read MN-major)
 // dK and dV of each query head are written once at the end as fp32 and summed over the GQA
 // group by gqa_reduce_kernel; no atomics.  dQ is computed by attn_bwd_dq_kernel (part 2).
 // ======================================================================================
@@ -318,7 +307,7 @@ struct BwdSmem {
   static constexpr int V_OFF = TILE;
   static constexpr int Q_OFF = 2 * TILE;            // 2 buffers (prefetch of the next query block)
   static constexpr int DO_OFF = 4 * TILE;           // 2 buffers
-  static constexpr int DST_OFF = 6 * TILE;          // dS^T [128 keys x 128 q] bf16 (P^T lives in TMEM)
+  static constexpr int DST_OFF = 6 * TILE;          // 2 x dS^T [128 keys x 64 q] bf16 (P^T lives in TMEM)
   static constexpr int STAT_OFF = DST_OFF + 32768;  // lse*log2e [128], delta [128]
   static constexpr int BAR_OFF = STAT_OFF + 1024;
   static constexpr int BYTES0 = BAR_OFF + 256 + 1024;
@@ -337,27 +326,28 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint8_t* sV = smem + L::V_OFF;
   uint8_t* sQ = smem + L::Q_OFF;
   uint8_t* sDO = smem + L::DO_OFF;
-  uint8_t* sDSt = smem + L::DST_OFF;
+  uint8_t* sDSt = smem + L::DST_OFF;  // 2 buffers of dS^T [128 keys x 64 q] (16 KB each)
   float* sLse = reinterpret_cast<float*>(smem + L::STAT_OFF);
   float* sDelta = sLse + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;   // [2]
-  uint64_t* q_empty = bars + 3;  // [2]
+  uint64_t* q_full = bars + 1;    // [2]
+  uint64_t* q_empty = bars + 3;   // [2]
   uint64_t* do_full = bars + 5;   // [2]
   uint64_t* do_empty = bars + 7;  // [2]
-  uint64_t* sp_full = bars + 9;
-  uint64_t* ds_full = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* sp_full = bars + 9;   // [2] per query half
+  uint64_t* ds_full = bars + 11;  // [2]
+  uint64_t* ds_empty = bars + 13; // [2]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = p.T / QB;
   const int j = blockIdx.x;  // key block (small j = most work, scheduled first)
   const int hq = blockIdx.y, b = blockIdx.z;
   const int hk = hq / (p.Hq / p.Hkv);
-  const int per_head = nqb - j;
-  const int n_iter = per_head;
+  const int n_iter = nqb - j;   // query blocks i = j .. nqb-1
+  const int n_units = 2 * n_iter;  // each query block in two halves of 64 queries
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -366,9 +356,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&q_empty[t], 1);
       mbar_init(&do_full[t], 1);
       mbar_init(&do_empty[t], 1);
+      mbar_init(&sp_full[t], 1);
+      mbar_init(&ds_full[t], 8);
+      mbar_init(&ds_empty[t], 1);
     }
-    mbar_init(sp_full, 1);
-    mbar_init(ds_full, 8);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -386,8 +377,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
-
+  // S^T / dP^T of the two query halves (64 columns each), then the dV and dK accumulators
+  const uint32_t tS[2] = {tmem, tmem + 64};
+  const uint32_t tDP[2] = {tmem + 128, tmem + 192};
+  const uint32_t tDV = tmem + 256, tDK = tmem + 256 + D;
   if (warp == 0) {
     if (lane == 0) {
       mbar_arrive_expect_tx(kv_full, 2 * L::TILE);
@@ -397,142 +390,161 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tma_load_4d(sV + c * 16384, &tmV, kv_full, c * 64, hk, j * KB, b);
       }
       for (int n = 0; n < n_iter; ++n) {
-        const int h = hq;
         const int i = j + n;
         const int qs = n & 1;
         if (!mbar_wait(&q_empty[qs], ((n >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
         mbar_arrive_expect_tx(&q_full[qs], L::TILE);
 #pragma unroll
-        for (int c = 0; c < L::CH; ++c) tma_load_4d(sQ + qs * L::TILE + c * 16384, &tmQ, &q_full[qs], c * 64, h, i * QB, b);
+        for (int c = 0; c < L::CH; ++c)
+          tma_load_4d(sQ + qs * L::TILE + c * 16384, &tmQ, &q_full[qs], c * 64, hq, i * QB, b);
         if (!mbar_wait(&do_empty[qs], ((n >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
         mbar_arrive_expect_tx(&do_full[qs], L::TILE);
 #pragma unroll
         for (int c = 0; c < L::CH; ++c)
-          tma_load_4d(sDO + qs * L::TILE + c * 16384, &tmDO, &do_full[qs], c * 64, h, i * QB, b);
+          tma_load_4d(sDO + qs * L::TILE + c * 16384, &tmDO, &do_full[qs], c * 64, hq, i * QB, b);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_s = idesc_bf16_f32(128, 128, false, false);   // S^T, dP^T
-      constexpr uint32_t id_kv = idesc_bf16_f32(128, D, false, true);     // dV, dK (B MN-major)
+      constexpr uint32_t id_s = idesc_bf16_f32(128, 64, false, false);  // S^T, dP^T of one query half
+      constexpr uint32_t id_kv = idesc_bf16_f32(128, D, false, true);   // dV, dK (B MN-major)
       bool ok = mbar_wait(kv_full, 0, p.err, ERR_MMA_FULL_TIMEOUT);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_base = smem_u32(sQ), do_base = smem_u32(sDO);
-      const uint32_t dst_addr = smem_u32(sDSt);
-      for (int n = 0; ok && n < n_iter; ++n) {
-        // S^T into tS (free: the elementwise warps finished reading it before ds_full(n-1))
-        const int qs = n & 1;
+      const uint32_t ds_base = smem_u32(sDSt);
+      // S^T and dP^T of unit u = (query block n, half h) into the TMEM buffers of half h.  The
+      // buffers last held unit u-2, whose P^T was consumed by its dV MMA, issued earlier by this
+      // thread (tcgen05 MMAs of one thread execute in order).
+      auto issue_sdp = [&](int u) -> bool {
+        const int n = u >> 1, h = u & 1, qs = n & 1;
+        if (h == 0 && !(mbar_wait(&q_full[qs], (n >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT) &&
+                        mbar_wait(&do_full[qs], (n >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)))
+          return false;
+        tc_fence_after();
+        const uint32_t q_addr = q_base + qs * L::TILE + h * 8192;
+        const uint32_t do_addr = do_base + qs * L::TILE + h * 8192;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tS[h], sdesc_kmajor(k_addr + off), sdesc_kmajor(q_addr + off), id_s, kk ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tDP[h], sdesc_kmajor(v_addr + off), sdesc_kmajor(do_addr + off), id_s, kk ? 1u : 0u);
+        }
+        umma_commit(&sp_full[h]);
+        return true;
+      };
+      ok = ok && issue_sdp(0) && issue_sdp(1);
+      for (int u = 0; ok && u < n_units; ++u) {
+        const int n = u >> 1, h = u & 1, qs = n & 1;
+        if (!mbar_wait(&ds_full[h], (u >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
+        tc_fence_after();
         const uint32_t q_addr = q_base + qs * L::TILE;
         const uint32_t do_addr = do_base + qs * L::TILE;
-        if (!mbar_wait(&q_full[qs], (n >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
-        tc_fence_after();
+        const uint32_t ds_addr = ds_base + h * 16384;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tS, sdesc_kmajor(k_addr + off), sdesc_kmajor(q_addr + off), id_s, kk ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {  // K = the 64 queries of this half
+          const uint32_t row = static_cast<uint32_t>(h * 64 + kk * 16) * 128;
+          // P^T packed by the elementwise warps: queries [32w, 32w+32) in columns [32w, 32w+16)
+          const uint32_t a_tm = tS[h] + static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
+          umma_bf16_ts(tDV, a_tm, sdesc_mnmajor(do_addr + row, 16384), id_kv, (u | kk) ? 1u : 0u);
+          umma_bf16(tDK, sdesc_kmajor(ds_addr + kk * 32), sdesc_mnmajor(q_addr + row, 16384), id_kv,
+                    (u | kk) ? 1u : 0u);
         }
-        // dP^T into tDP (the elementwise warps read the previous one before ds_full)
-        if (!mbar_wait(&do_full[qs], (n >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tDP, sdesc_kmajor(v_addr + off), sdesc_kmajor(do_addr + off), id_s, kk ? 1u : 0u);
+        umma_commit(&ds_empty[h]);
+        if (h == 1) {
+          umma_commit(&q_empty[qs]);
+          umma_commit(&do_empty[qs]);
         }
-        umma_commit(sp_full);
-        if (!mbar_wait(ds_full, n & 1, p.err, ERR_MMA_FULL_TIMEOUT)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 128 / 16; ++kk) {  // K = 128 query rows
-          const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-          // P^T from TMEM: query columns [64h, 64h+64) were packed into columns [64h, 64h+32) of tS
-          const uint32_t a_tm = tS + static_cast<uint32_t>((kk >> 2) * 64 + (kk & 3) * 8);
-          umma_bf16_ts(tDV, a_tm, sdesc_mnmajor(do_addr + kk * 2048, 16384), id_kv, (n | kk) ? 1u : 0u);
-          umma_bf16(tDK, sdesc_kmajor(dst_addr + aoff), sdesc_mnmajor(q_addr + kk * 2048, 16384), id_kv,
-                    (n | kk) ? 1u : 0u);
-        }
-        umma_commit(&q_empty[qs]);
-        umma_commit(&do_empty[qs]);
+        if (u + 2 < n_units && !issue_sdp(u + 2)) break;
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
     }
   } else {
     const int q = warp & 3;
-    const int half = (warp - 2) >> 2;  // which 64 query columns (and D/2 output columns) this warp owns
-    const int kr = q * 32 + lane;      // key row (S^T / dP^T lane) and, for dQ, query row
+    const int half = (warp - 2) >> 2;  // which 32 queries of a 64-query unit (and D/2 output columns)
+    const int kr = q * 32 + lane;      // key row (S^T / dP^T lane)
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int tid = threadIdx.x - 64;  // 0..255
+    const int c0 = half * 32;
     // Every warp waits on the same mbarriers with waits that only give up on their own timeout: a
     // phase that completed is seen complete by all of them and one that never completes times
     // out in all of them, so every elementwise warp leaves the loop at the same point and the
     // named barriers stay matched.
     bool ok = true;
-    // row statistics are prefetched one iteration ahead into a register (one value per thread)
+    // row statistics of each query block, prefetched one block ahead (one value per thread)
     const float* stat_src = (tid < 128) ? p.lse : p.delta;
     const float stat_mul = (tid < 128) ? 1.4426950408889634f : 1.f;
     const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + (tid & 127);
     float stat_next = stat_src[stat_base + j * QB] * stat_mul;
-    for (int n = 0; n < n_iter && ok; ++n) {
+    for (int u = 0; u < n_units && ok; ++u) {
+      const int n = u >> 1, h = u & 1;
       const int i = j + n;
-      // publish this iteration's statistics (the previous iteration's readers are past the barrier)
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (tid < 128)
-        sLse[tid] = stat_next;
-      else
-        sDelta[tid - 128] = stat_next;
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
-      if (!mbar_wait(sp_full, n & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
+      if (h == 0) {
+        // publish this block's statistics (the previous block's readers are past the barrier)
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (tid < 128)
+          sLse[tid] = stat_next;
+        else
+          sDelta[tid - 128] = stat_next;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
+      }
+      if (!mbar_wait(&sp_full[h], (u >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const bool diag = (i == j);
-      {
-        const int c0 = half * 64;
-        float sv[64], dp[64];
-        tmem_ld_32cols_async(tS + lane_off + c0, sv);
-        tmem_ld_32cols_async(tS + lane_off + c0 + 32, sv + 32);
-        tmem_ld_32cols_async(tDP + lane_off + c0, dp);
-        tmem_ld_32cols_async(tDP + lane_off + c0 + 32, dp + 32);
-        tmem_ld_wait();
-        float ppk[32];  // P^T as bf16 pairs, reinterpreted as 32-bit TMEM words
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          uint4 wd;
-          __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            float pv[2], dv[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int e = g * 8 + e2 * 2 + t;
-              const int qc = c0 + e;
-              const bool masked = diag && (qc < kr);
-              const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - sLse[qc]);
-              pv[t] = pr;
-              dv[t] = pr * (dp[e] - sDelta[qc]);
-            }
-            __nv_bfloat162 pb = __floats2bfloat162_rn(pv[0], pv[1]);
-            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
-            hd[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
-          }
-          *reinterpret_cast<uint4*>(sDSt + swz_offset(kr, c0 + g * 8)) = wd;
-        }
-        // packed P^T over this warp's own (already consumed) S columns
-        tmem_st_32cols_async(tS + lane_off + c0, ppk);
-        tmem_st_wait();
+      float sv[32], dp[32];
+      tmem_ld_32cols_async(tS[h] + lane_off + c0, sv);
+      tmem_ld_32cols_async(tDP[h] + lane_off + c0, dp);
+      tmem_ld_wait();
+      // the dS^T buffer of this half was last read by the dK MMA of unit u-2
+      if (u >= 2 && !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
+                               MMF_WAIT_TIMEOUT_NS, false)) {
+        ok = false;
+        break;
       }
+      uint8_t* dst_tile = sDSt + h * 16384;
+      float ppk[16];  // P^T as bf16 pairs, reinterpreted as 32-bit TMEM words
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 wd;
+        __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int e = g * 8 + e2 * 2 + t;
+            const int qc = h * 64 + c0 + e;  // query column inside the block
+            const bool masked = diag && (qc < kr);
+            const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - sLse[qc]);
+            pv[t] = pr;
+            dv[t] = pr * (dp[e] - sDelta[qc]);
+          }
+          __nv_bfloat162 pb = __floats2bfloat162_rn(pv[0], pv[1]);
+          ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
+          hd[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
+        }
+        *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wd;
+      }
+      // packed P^T over this warp's own (already consumed) S^T columns [c0, c0 + 16)
+      tmem_st_16cols_async(tS[h] + lane_off + c0, ppk);
+      tmem_st_wait();
       tc_fence_before();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(ds_full);
+      if (lane == 0) mbar_arrive(&ds_full[h]);
     }
     // the last dV/dK MMAs: the drain commit of the MMA thread is not visible here, so wait for the
     // final Q/dO release (committed after them)
     if (ok) ok = mbar_wait(&q_empty[(n_iter - 1) & 1], ((n_iter - 1) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
                            MMF_WAIT_TIMEOUT_NS, false);
-    // dK_j (x scale) and dV_j
+    // dK_j (x scale) and dV_j of this query head
     if (ok) {
       tc_fence_after();
       const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hq + hq;
@@ -558,7 +570,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     tmem_dealloc(tmem, 512);
   }
 }
-
 
 // ======================================================================================
 // dQ kernel, one CTA per (128-query block i, query head, batch); loops over key blocks j <= i:

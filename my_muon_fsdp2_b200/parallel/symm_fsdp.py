@@ -207,6 +207,11 @@ class SymmFSDP:
         self.sync_grads = bool(flag)
 
     def attach_optimizer(self, opt) -> None:
+        """Invalidate the resident full weights after every ``opt.step()`` (idempotent)."""
+        attached = self.__dict__.setdefault("_attached", set())
+        if id(opt) in attached:
+            return
+        attached.add(id(opt))
         opt.register_step_post_hook(lambda *a, **k: self.invalidate())
 
     def shard_ptrs(self, i: int) -> List[int]:
@@ -280,11 +285,10 @@ class SymmFSDP:
         self.acc_live[i] = False
         g, acc = self._grad_local(i)
         if self.world == 1:
-            dw = dy2.t() @ x2
             if acc:
-                g.add_(dw)
+                g.addmm_(dy2.t(), x2)
             else:
-                g.copy_(dw)
+                torch.mm(dy2.t(), x2, out=g)
             return
         if not self.fused:
             dw = (dy2.t().float() @ x2.float())
@@ -345,4 +349,6 @@ def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str =
         ctl.set_requires_gradient_sync(flag)
 
     model.set_requires_gradient_sync = set_requires_gradient_sync
+    # loading a checkpoint rewrites the shards: gather again on the next forward
+    model.register_load_state_dict_post_hook(lambda *a, **k: ctl.invalidate())
     return ctl

@@ -24,6 +24,10 @@ class Trainer:
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
         self.step_timer = step_timer  # optional EventTimer around the optimizer steps
         self.fsdp = is_fsdp_module(model)
+        ctl = getattr(model, "_symm_fsdp", None)  # fused-collective linears: regather after each step
+        if ctl is not None:
+            for opt in self.optimizers:
+                ctl.attach_optimizer(opt)
 
     def _micro(self, tokens: torch.Tensor, i: int):
         last = i == self.grad_accum - 1
