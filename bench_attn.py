@@ -37,9 +37,11 @@ def main():
     ap.add_argument("--D", type=int, default=128)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", choices=["all", "ours_fwd", "ours_bwd"], default="all")
+    ap.add_argument("--fwd-variant", type=int, default=0, help="0: two query tiles per CTA, 1: one")
     a = ap.parse_args()
     from my_muon_fsdp2_b200._ext import ext
 
+    ext().set_attention_fwd_variant(a.fwd_variant)
     torch.manual_seed(0)
     q = torch.randn(a.B, a.T, a.Hq, a.D, device="cuda", dtype=torch.bfloat16)
     k = torch.randn(a.B, a.T, a.Hkv, a.D, device="cuda", dtype=torch.bfloat16)

@@ -13,6 +13,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -111,7 +112,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};
+  // S_j buffer of block j: tmem + (j & 1) * 128 (arithmetic, so no local-memory array)
+  auto ts_buf = [tmem](int st) { return tmem + static_cast<uint32_t>(st) * 128u; };
   const uint32_t tO = tmem + 256;
 
   if (warp == 0) {
@@ -146,7 +148,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tS[st], sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
+          umma_bf16(ts_buf(st), sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
         }
         umma_commit(&s_full[st]);
         return true;
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const uint32_t v_addr = smem_u32(sV + st * L::TILE);
 #pragma unroll
         for (int kk = 0; kk < KB / 16; ++kk)
-          umma_bf16_ts(tO, tS[st] + static_cast<uint32_t>(kk * 8), sdesc_mnmajor(v_addr + kk * 16 * 128, 16384),
+          umma_bf16_ts(tO, ts_buf(st) + static_cast<uint32_t>(kk * 8), sdesc_mnmajor(v_addr + kk * 16 * 128, 16384),
                        idesc_o, (j | kk) ? 1u : 0u);
         umma_commit(pv_done);
         umma_commit(&kv_empty[st]);
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       // the whole 128-column S row in registers: 4 loads, one wait
       float sv[KB];
 #pragma unroll
-      for (int c = 0; c < KB / 32; ++c) tmem_ld_32cols_async(tS[st] + lane_off + c * 32, sv + c * 32);
+      for (int c = 0; c < KB / 32; ++c) tmem_ld_32cols_async(ts_buf(st) + lane_off + c * 32, sv + c * 32);
       tmem_ld_wait();
       float mx = -INFINITY;
 #pragma unroll
@@ -237,8 +239,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
         pk[e2] = *reinterpret_cast<float*>(&pb);
       }
-      tmem_st_32cols_async(tS[st] + lane_off, pk);
-      tmem_st_32cols_async(tS[st] + lane_off + 32, pk + 32);
+      tmem_st_32cols_async(ts_buf(st) + lane_off, pk);
+      tmem_st_32cols_async(ts_buf(st) + lane_off + 32, pk + 32);
       tmem_st_wait();
       l = l * alpha + sum;
       m2 = m_new;
@@ -277,11 +279,290 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
 
 // ======================================================================================
+// Forward with two query tiles per CTA (query blocks 2x and 2x+1 of one head): two softmax
+// warpgroups, one per tile, so that the tensor core works on one tile's S / P V while the
+// other tile's softmax runs, and K_j / V_j are loaded once for both tiles.
+//   warp 0      TMA: Q_A, Q_B once; K_j / V_j per key block into a 2-stage ring
+//   warp 1      MMA: S_A(0), S_B(0); per j: P_A(j) V_j, S_A(j+1), P_B(j) V_j, S_B(j+1)
+//   warps 2..5  softmax + epilogue of tile A;  warps 6..9 of tile B
+// TMEM: S_A | S_B (128 columns each; P_t(j) is written as bf16 pairs over S_t(j)) | O_A | O_B.
+// ======================================================================================
+template <int D>
+struct Attn2Smem {
+  static constexpr int CH = D / 64;
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int Q_OFF = 0;                 // Q_A, Q_B
+  static constexpr int K_OFF = 2 * TILE;          // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * TILE;  // 2 stages
+  static constexpr int BAR_OFF = V_OFF + 2 * TILE;
+  static constexpr int BYTES = (BAR_OFF + 256 + 1024) > 120 * 1024 ? (BAR_OFF + 256 + 1024) : 120 * 1024;
+};
+constexpr int ATT2_THREADS = 320;
+
+// Online softmax of one query tile (128 rows, one per thread of the 4 calling warps) over key
+// blocks 0..nblk-1; P into TMEM over S; O rescale in TMEM when the reference max moves; epilogue.
+template <int D>
+__device__ __forceinline__ void fwd_softmax_tile(const AttnParams& p, uint32_t tS, uint32_t tO, uint64_t* s_full,
+                                                 uint64_t* p_full, uint64_t* pv_done, int qb, int nblk, int h, int b,
+                                                 int q, int lane) {
+  const int r = q * 32 + lane;
+  const int qi = qb * QB + r;
+  const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+  float m2 = -INFINITY, l = 0.f;
+  bool ok = true;
+  for (int j = 0; j < nblk && ok; ++j) {
+    if (!mbar_wait(s_full, j & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const bool diag = (j == qb);
+    // Two 64-column halves keep the register footprint at one half: the row max reads keys
+    // 64..127 then 0..63; the probabilities of keys 0..63 come from the registers, those of
+    // keys 64..127 from a second TMEM read (their S columns are not overwritten before that).
+    float sv[64];
+    auto load_half = [&](int hf) {
+      tmem_ld_32cols_async(tS + lane_off + hf * 64, sv);
+      tmem_ld_32cols_async(tS + lane_off + hf * 64 + 32, sv + 32);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        sv[e] *= p.scale_log2;
+        if (diag && (j * KB + hf * 64 + e > qi)) sv[e] = -INFINITY;
+      }
+    };
+    float mx = -INFINITY;
+    load_half(1);
+#pragma unroll
+    for (int e = 0; e < 64; ++e) mx = fmaxf(mx, sv[e]);
+    load_half(0);
+#pragma unroll
+    for (int e = 0; e < 64; ++e) mx = fmaxf(mx, sv[e]);
+    // the reference max moves only when the row max grows by more than 2^8 (see attn_fwd_kernel)
+    const bool grow = (m2 == -INFINITY) || (mx > m2 + 8.f);
+    const float m_new = grow ? mx : m2;
+    const float alpha = (m2 == -INFINITY) ? 0.f : (grow ? fast_exp2(m2 - m_new) : 1.f);
+    if (__any_sync(0xffffffffu, j >= 1 && alpha != 1.f)) {
+      if (!mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tmem_ld_32cols(tO + lane_off + c * 32, o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= alpha;
+        tmem_st_32cols_async(tO + lane_off + c * 32, o);
+      }
+    }
+    float sum = 0.f;
+#pragma unroll 1
+    for (int hf = 0; hf < 2; ++hf) {
+      if (hf == 1) {
+        tmem_st_wait();  // keys 0..63 stored over S columns 0..31, which were read already
+        load_half(1);
+      }
+      float pk[32];
+#pragma unroll
+      for (int e2 = 0; e2 < 32; ++e2) {
+        const float p0 = fast_exp2(sv[2 * e2] - m_new);
+        const float p1 = fast_exp2(sv[2 * e2 + 1] - m_new);
+        sum += p0 + p1;
+        __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+        pk[e2] = *reinterpret_cast<float*>(&pb);
+      }
+      tmem_st_32cols_async(tS + lane_off + hf * 32, pk);
+    }
+    tmem_st_wait();
+    l = l * alpha + sum;
+    m2 = m_new;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(p_full);
+  }
+  if (ok && nblk > 0 && mbar_wait(pv_done, (nblk - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+    tc_fence_after();
+    const float inv = (l > 0.f) ? 1.f / l : 0.f;
+    __nv_bfloat16* orow = p.o + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D;
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) {
+      float o[32];
+      tmem_ld_32cols(tO + lane_off + c * 32, o);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 w;
+        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(o[g * 8 + 2 * e2] * inv, o[g * 8 + 2 * e2 + 1] * inv);
+        *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = w;
+      }
+    }
+    p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + qi] = (m2 + log2f(l)) * 0.69314718055994531f;
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(ATT2_THREADS, 1)
+    attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using L = Attn2Smem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::Q_OFF;
+  uint8_t* sK = smem + L::K_OFF;
+  uint8_t* sV = smem + L::V_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2] per tile
+  uint64_t* p_full = bars + 7;    // [2] per tile
+  uint64_t* pv_done = bars + 9;   // [2] per tile
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = p.T / QB;
+  const int npair = (nqb + 1) / 2;
+  const int x = npair - 1 - static_cast<int>(blockIdx.x);  // heaviest pairs first
+  const int qa = 2 * x, qbb = 2 * x + 1;
+  const bool has_b = qbb < nqb;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int nblk_a = qa + 1, nblk_b = has_b ? qbb + 1 : 0;
+  const int nblk = has_b ? nblk_b : nblk_a;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // S of tile t at tmem + 128 t, O of tile t at tmem + 256 + D t (no runtime-indexed arrays)
+  auto ts_of = [tmem](int t) { return tmem + static_cast<uint32_t>(t) * 128u; };
+  auto to_of = [tmem](int t) { return tmem + 256u + static_cast<uint32_t>(t * D); };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      constexpr uint32_t TILE = L::TILE;
+      mbar_arrive_expect_tx(q_full, has_b ? 2 * TILE : TILE);
+#pragma unroll
+      for (int c = 0; c < L::CH; ++c) {
+        tma_load_4d(sQ + c * 16384, &tmQ, q_full, c * 64, h, qa * QB, b);
+        if (has_b) tma_load_4d(sQ + TILE + c * 16384, &tmQ, q_full, c * 64, h, qbb * QB, b);
+      }
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
+#pragma unroll
+        for (int c = 0; c < L::CH; ++c) {
+          tma_load_4d(sK + st * TILE + c * 16384, &tmK, &kv_full[st], c * 64, hk, j * KB, b);
+          tma_load_4d(sV + st * TILE + c * 16384, &tmV, &kv_full[st], c * 64, hk, j * KB, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, KB, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
+      const uint32_t q_addr0 = smem_u32(sQ);
+      // S_t(j) = Q_t K_j^T; its buffer last held P_t(j-1), consumed by P_t(j-1) V issued before
+      auto issue_s = [&](int t, int j) {
+        const uint32_t q_addr = q_addr0 + t * L::TILE;
+        const uint32_t k_addr = smem_u32(sK + (j & 1) * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(ts_of(t), sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait(&p_full[t], j & 1, p.err, ERR_MMA_FULL_TIMEOUT)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + (j & 1) * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < KB / 16; ++kk)
+          umma_bf16_ts(to_of(t), ts_of(t) + static_cast<uint32_t>(kk * 8), sdesc_mnmajor(v_addr + kk * 16 * 128, 16384),
+                       idesc_o, (j | kk) ? 1u : 0u);
+        umma_commit(&pv_done[t]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, ERR_MMA_FULL_TIMEOUT) &&
+                mbar_wait(&kv_full[0], 0, p.err, ERR_MMA_FULL_TIMEOUT);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (has_b) issue_s(1, 0);
+      }
+      // K/V of block j+1 (the other stage) before the S MMAs that read it
+      auto wait_kv = [&](int j1) {
+        const bool r = mbar_wait(&kv_full[j1 & 1], (j1 >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT);
+        tc_fence_after();
+        return r;
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        if (j < nblk_a) {
+          if (!(ok = issue_pv(0, j))) break;
+          if (j + 1 < nblk_a) {
+            if (!(ok = wait_kv(j + 1))) break;
+            issue_s(0, j + 1);
+          }
+        }
+        if (j < nblk_b) {
+          if (!(ok = issue_pv(1, j))) break;
+          if (j + 1 < nblk_b) {
+            if (!(ok = wait_kv(j + 1))) break;
+            issue_s(1, j + 1);
+          }
+        }
+        umma_commit(&kv_empty[j & 1]);  // K_j, V_j no longer read once these MMAs complete
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else {
+    const int t = (warp - 2) >> 2;  // tile of this warpgroup (one call site keeps the code small)
+    const int q = warp & 3;
+    if (t == 0 || has_b)
+      fwd_softmax_tile<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
+                          t ? nblk_b : nblk_a, h, b, q, lane);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+// ======================================================================================
 // Backward, part 1 (dK, dV): one CTA per (128-key block j, query head, batch); loops over the
 // query blocks i >= j (causal) in units of 64 queries.  K_j and V_j stay in smem; Q_i / dO_i are
 // double-buffered; S^T / dP^T / dS^T are double-buffered per 64-query half, so the tensor core
 // computes one half while the elementwise warps work on the other.
-//   MMA      S^T = K_j Q_u^T  -> TMEM tS[h]     dP^T = V_j dO_u^T -> TMEM tdP[h]     (N = 64)
+//   MMA      S^T = K_j Q_u^T  -> TMEM S(h)      dP^T = V_j dO_u^T -> TMEM dP(h)      (N = 64)
 //   softmax  (one key row per TMEM lane) P^T = exp2(S^T*scale*log2e - lse*log2e) (causal mask
 //            on the diagonal block), packed back into TMEM as bf16; dS^T = P^T * (dP^T - delta)
 //            as bf16 into a swizzled smem tile
@@ -378,8 +659,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // S^T / dP^T of the two query halves (64 columns each), then the dV and dK accumulators
-  const uint32_t tS[2] = {tmem, tmem + 64};
-  const uint32_t tDP[2] = {tmem + 128, tmem + 192};
+  // per-half buffers by arithmetic (a runtime-indexed array would live in local memory)
+  auto ts_h = [tmem](int h) { return tmem + static_cast<uint32_t>(h) * 64u; };
+  auto tdp_h = [tmem](int h) { return tmem + 128u + static_cast<uint32_t>(h) * 64u; };
   const uint32_t tDV = tmem + 256, tDK = tmem + 256 + D;
   if (warp == 0) {
     if (lane == 0) {
@@ -425,12 +707,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tS[h], sdesc_kmajor(k_addr + off), sdesc_kmajor(q_addr + off), id_s, kk ? 1u : 0u);
+          umma_bf16(ts_h(h), sdesc_kmajor(k_addr + off), sdesc_kmajor(q_addr + off), id_s, kk ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tDP[h], sdesc_kmajor(v_addr + off), sdesc_kmajor(do_addr + off), id_s, kk ? 1u : 0u);
+          umma_bf16(tdp_h(h), sdesc_kmajor(v_addr + off), sdesc_kmajor(do_addr + off), id_s, kk ? 1u : 0u);
         }
         umma_commit(&sp_full[h]);
         return true;
@@ -447,7 +729,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int kk = 0; kk < 4; ++kk) {  // K = the 64 queries of this half
           const uint32_t row = static_cast<uint32_t>(h * 64 + kk * 16) * 128;
           // P^T packed by the elementwise warps: queries [32w, 32w+32) in columns [32w, 32w+16)
-          const uint32_t a_tm = tS[h] + static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
+          const uint32_t a_tm = ts_h(h) + static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
           umma_bf16_ts(tDV, a_tm, sdesc_mnmajor(do_addr + row, 16384), id_kv, (u | kk) ? 1u : 0u);
           umma_bf16(tDK, sdesc_kmajor(ds_addr + kk * 32), sdesc_mnmajor(q_addr + row, 16384), id_kv,
                     (u | kk) ? 1u : 0u);
@@ -499,8 +781,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_after();
       const bool diag = (i == j);
       float sv[32], dp[32];
-      tmem_ld_32cols_async(tS[h] + lane_off + c0, sv);
-      tmem_ld_32cols_async(tDP[h] + lane_off + c0, dp);
+      tmem_ld_32cols_async(ts_h(h) + lane_off + c0, sv);
+      tmem_ld_32cols_async(tdp_h(h) + lane_off + c0, dp);
       tmem_ld_wait();
       // the dS^T buffer of this half was last read by the dK MMA of unit u-2
       if (u >= 2 && !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
@@ -533,7 +815,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wd;
       }
       // packed P^T over this warp's own (already consumed) S^T columns [c0, c0 + 16)
-      tmem_st_16cols_async(tS[h] + lane_off + c0, ppk);
+      tmem_st_16cols_async(ts_h(h) + lane_off + c0, ppk);
       tmem_st_wait();
       tc_fence_before();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -663,7 +945,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tSb[2] = {tmem, tmem + 128};
+  auto tsb = [tmem](int st) { return tmem + static_cast<uint32_t>(st) * 128u; };
   const uint32_t tDP = tmem + 256, tDQ = tmem + 384;
 
   if (warp == 0) {
@@ -701,7 +983,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tSb[st], sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), id_s, kk ? 1u : 0u);
+          umma_bf16(tsb(st), sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), id_s, kk ? 1u : 0u);
         }
         if (!mbar_wait(dp_empty, (j & 1) ^ 1u, p.err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) return false;
         tc_fence_after();
@@ -751,8 +1033,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const bool diag = (j == i);
       const int c0 = half * 64;
       float sv[64], dp[64];
-      tmem_ld_32cols_async(tSb[st] + lane_off + c0, sv);
-      tmem_ld_32cols_async(tSb[st] + lane_off + c0 + 32, sv + 32);
+      tmem_ld_32cols_async(tsb(st) + lane_off + c0, sv);
+      tmem_ld_32cols_async(tsb(st) + lane_off + c0 + 32, sv + 32);
       tmem_ld_32cols_async(tDP + lane_off + c0, dp);
       tmem_ld_32cols_async(tDP + lane_off + c0 + 32, dp + 32);
       tmem_ld_wait();
@@ -888,6 +1170,8 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
   return m;
 }
 
+std::atomic<int> g_fwd_variant{0};  // 0: two query tiles per CTA, 1: one tile per CTA
+
 template <int D>
 void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   static bool attr_set[64] = {false};
@@ -895,6 +1179,7 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
     cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
     attr_set[dev] = true;
   }
   AttnParams p{};
@@ -910,8 +1195,13 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap mq = map_bthd(a.q, a.B, a.T, a.Hq, D);
   CUtensorMap mk = map_bthd(a.k, a.B, a.T, a.Hkv, D);
   CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
-  dim3 grid(a.T / QB, a.Hq, a.B);
-  attn_fwd_kernel<D><<<grid, ATT_THREADS, AttnSmem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  if (g_fwd_variant.load() == 1) {
+    dim3 grid(a.T / QB, a.Hq, a.B);
+    attn_fwd_kernel<D><<<grid, ATT_THREADS, AttnSmem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  } else {
+    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+    attn_fwd2_kernel<D><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  }
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: attention launch failed: ") + cudaGetErrorString(e));
@@ -999,4 +1289,6 @@ void attention_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   else
     throw std::runtime_error("mmf: attention supports head_dim 64 or 128");
 }
+void set_attention_fwd_variant(int v) { g_fwd_variant.store(v); }
+
 }  // namespace mmf

@@ -23,11 +23,13 @@ def _ref(q, k, v):
     return o, lse
 
 
+@pytest.mark.parametrize("variant", [0, 1], ids=["two_tiles", "one_tile"])
 @pytest.mark.parametrize("B,T,Hq,Hkv,D", [(1, 128, 1, 1, 128), (2, 384, 4, 2, 128), (1, 512, 2, 2, 64),
-                                          (1, 1024, 8, 2, 128)])
-def test_attention_forward_matches_fp32(B, T, Hq, Hkv, D):
+                                          (1, 1024, 8, 2, 128), (1, 640, 2, 1, 64)])
+def test_attention_forward_matches_fp32(B, T, Hq, Hkv, D, variant):
     from my_muon_fsdp2_b200._ext import check_device_error, ext
 
+    ext().set_attention_fwd_variant(variant)
     torch.manual_seed(0)
     q = torch.randn(B, T, Hq, D, device="cuda").to(torch.bfloat16)
     k = torch.randn(B, T, Hkv, D, device="cuda").to(torch.bfloat16)
@@ -35,6 +37,7 @@ def test_attention_forward_matches_fp32(B, T, Hq, Hkv, D):
     o, lse = ext().attention_fwd(q, k, v, 1.0 / math.sqrt(D))
     torch.cuda.synchronize()
     check_device_error(0)
+    ext().set_attention_fwd_variant(0)
     ro, rlse = _ref(q, k, v)
     assert rel_err(o, ro) < 2e-2
     assert rel_err(lse, rlse) < 1e-3
