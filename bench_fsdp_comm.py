@@ -40,11 +40,38 @@ def timed(fn, iters, warmup):
     return float(t.item())
 
 
+def emulate(args, dev, ext, check_device_error, local):
+    ws = args.emulate_world
+    for name, (n, k) in SHAPES.items():
+        if n % (128 * ws):
+            continue
+        w = torch.randn(n, k, device=dev, dtype=torch.bfloat16)
+        x = torch.randn(args.tokens, k, device=dev, dtype=torch.bfloat16)
+        g = torch.empty_like(w)
+        ready = torch.zeros(n // 128 + 1, dtype=torch.int32, device=dev)
+        ns = n // ws
+        ptrs = [w.data_ptr() + 2 * s * ns * k for s in range(ws)]
+        y = ext().ag_gemm(x, ptrs, 0, g, ready, 2e-3)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(g, w))
+        ref = torch.nn.functional.linear(x, w)
+        err = float((y.float() - ref.float()).norm() / ref.float().norm())
+        t_ag = timed(lambda: ext().ag_gemm(x, ptrs, 0, g, ready, 2e-3), args.iters, args.warmup)
+        t_mm = timed(lambda: torch.nn.functional.linear(x, w), args.iters, args.warmup)
+        print(json.dumps({"metric": "ag_gemm emulated on one GPU (all shards local)", "weight": name, "N": n, "K": k,
+                          "tokens": args.tokens, "emulated_world": ws, "ag_gemm_ms": t_ag, "cublas_ms": t_mm,
+                          "gathered_equal": ok, "rel_err": err}))
+    check_device_error(local)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--emulate-world", type=int, default=0,
+                    help="one GPU: run ag_gemm as rank 0 of this many ranks whose shards are all local "
+                         "buffers (the kernel's pull / ready-flag / GEMM structure without NVLink, for ncu)")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
@@ -55,6 +82,10 @@ def main():
     from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmFSDP
 
     T = args.tokens
+    if args.emulate_world > 1:
+        emulate(args, dev, ext, check_device_error, local)
+        dist.destroy_process_group()
+        return
     lins = {k: nn.Linear(kk, n, bias=False, device="meta") for k, (n, kk) in SHAPES.items()}
     for m in lins.values():
         m.to_empty(device=dev)

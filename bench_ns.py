@@ -42,6 +42,7 @@ def parse():
     ap.add_argument("--comm", choices=["auto", "nccl", "p2p"], default="auto")
     ap.add_argument("--ns-steps", type=int, default=5)
     ap.add_argument("--gemm-variant", type=int, default=0, help="0 auto, 1 single-CTA, 2 CTA pair")
+    ap.add_argument("--repeat", type=int, default=1, help="every shape this many times (e.g. one per layer)")
     ap.add_argument("--schedule", choices=["auto", "never", "always"], default="auto",
                     help="cooperative all-rank NS chain per shape: auto (cost model), never, always")
     return ap.parse_args()
@@ -78,13 +79,17 @@ def main():
     args = parse()
     rank, world, local = init()
     dev = torch.device("cuda", local)
-    shapes = [tuple(int(x) for x in s.split("x")) for s in args.shapes.split(",") if s]
+    shapes = [tuple(int(x) for x in s.split("x")) for s in args.shapes.split(",") if s] * args.repeat
     from torch.distributed.device_mesh import init_device_mesh
     from torch.distributed.tensor import DTensor, Shard
 
     mesh = init_device_mesh("cuda", (world,))
     g = torch.Generator(device="cpu").manual_seed(1234)
-    fulls = [torch.randn(r, c, generator=g).to(torch.bfloat16) for r, c in shapes]
+    by_shape = {}
+    for r, c in shapes:  # one random matrix per distinct shape (repeats share values)
+        if (r, c) not in by_shape:
+            by_shape[(r, c)] = torch.randn(r, c, generator=g).to(torch.bfloat16)
+    fulls = [by_shape[sh] for sh in shapes]
 
     def shard(t):
         return DTensor.from_local(t.chunk(world, 0)[rank].contiguous().to(dev), mesh, [Shard(0)], run_check=False,
@@ -138,7 +143,7 @@ def main():
     if rank == 0:
         print(json.dumps({"metric": "isolated Muon step (gather+NS5+scatter-update) ms", "impl": args.impl,
                           "value": ms, "unit": "ms", "higher_is_better": False, "n_gpus": world,
-                          "shapes": args.shapes, "iters": args.iters, "warmup": args.warmup,
+                          "shapes": args.shapes, "repeat": args.repeat, "iters": args.iters, "warmup": args.warmup,
                           "tflops_effective": flops / (ms / 1e3) / 1e12,
                           "roofline_ms": roof_ms, "roofline_fraction": roof_ms / ms, "peak_source": src,
                           "comm": args.comm if args.impl == "ours" else "nccl all_gather",
