@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--micro-bs", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32, help="debug only: fewer layers is not the named config")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="fsdp2",
+    ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="symm",
                     help="fsdp2: fully_shard everywhere; symm: block linears on symmetric memory with the "
                          "fused all-gather GEMM / GEMM reduce-scatter kernels, the rest fully_shard")
     return ap.parse_args()

@@ -73,6 +73,13 @@ def main():
                     help="one GPU: run ag_gemm as rank 0 of this many ranks whose shards are all local "
                          "buffers (the kernel's pull / ready-flag / GEMM structure without NVLink, for ncu)")
     args = ap.parse_args()
+    if "RANK" not in os.environ:  # single process without torchrun
+        import socket
+
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        os.environ.update(RANK="0", WORLD_SIZE="1", LOCAL_RANK="0", MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     local = int(os.environ.get("LOCAL_RANK", 0))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)

@@ -201,8 +201,51 @@ __global__ void ns_scale_kernel(const float* sumsq, int n, int nparts, float eps
   if (s2) s2[b] = v * v;
 }
 
+// T[idx + e] = ps * T[idx + e] + vs * v[e] for e < n (n <= 8); 16-byte vectors when possible.
 template <bool OUT_F32>
-__global__ void ws_to_out_kernel(const WsOutArgs a) {
+__device__ __forceinline__ void apply_run8(void* T, int64_t idx, const float* v, int n, float ps, float vs) {
+  if (OUT_F32) {
+    float* p = reinterpret_cast<float*>(T) + idx;
+    if (n == 8 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+      float4* q = reinterpret_cast<float4*>(p);
+      float4 o0 = make_float4(0.f, 0.f, 0.f, 0.f), o1 = o0;
+      if (ps != 0.f) {
+        o0 = q[0];
+        o1 = q[1];
+      }
+      q[0] = make_float4(fmaf(ps, o0.x, vs * v[0]), fmaf(ps, o0.y, vs * v[1]), fmaf(ps, o0.z, vs * v[2]),
+                         fmaf(ps, o0.w, vs * v[3]));
+      q[1] = make_float4(fmaf(ps, o1.x, vs * v[4]), fmaf(ps, o1.y, vs * v[5]), fmaf(ps, o1.z, vs * v[6]),
+                         fmaf(ps, o1.w, vs * v[7]));
+      return;
+    }
+    for (int e = 0; e < n; ++e) p[e] = fmaf(ps, ps != 0.f ? p[e] : 0.f, vs * v[e]);
+  } else {
+    __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(T) + idx;
+    if (n == 8 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (ps != 0.f) w = *reinterpret_cast<const uint4*>(p);
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 o = __bfloat1622float2(h[e]);
+        h[e] = __floats2bfloat162_rn(fmaf(ps, o.x, vs * v[2 * e]), fmaf(ps, o.y, vs * v[2 * e + 1]));
+      }
+      *reinterpret_cast<uint4*>(p) = w;
+      return;
+    }
+    for (int e = 0; e < n; ++e)
+      p[e] = __float2bfloat16_rn(fmaf(ps, ps != 0.f ? __bfloat162float(p[e]) : 0.f, vs * v[e]));
+  }
+}
+
+// Workspace X [batch, Mp, Np] (bf16, the wide orientation) -> destinations, in 64 x 64 tiles.
+// A transposed destination goes through a shared-memory tile, so that both the workspace reads
+// and the destination read-modify-writes are 16-byte vectors along rows (a direct element-wise
+// transposed update would touch a different destination row per element).
+template <bool OUT_F32>
+__global__ void __launch_bounds__(256) ws_to_out_kernel(const WsOutArgs a) {
+  __shared__ float tile[64][65];
   const int b = blockIdx.y;
   const __nv_bfloat16* X = reinterpret_cast<const __nv_bfloat16*>(a.X) + static_cast<int64_t>(b) * a.Mp * a.Np;
   const float sc = a.s_vec ? a.s_vec[b] : 1.f;
@@ -216,17 +259,61 @@ __global__ void ws_to_out_kernel(const WsOutArgs a) {
     seg_rows = a.out_meta[3 * b + 2];
   }
   const int64_t* segp = a.out_ptrs + static_cast<int64_t>(b) * (a.nseg < 1 ? 1 : a.nseg);
-  const int64_t total = static_cast<int64_t>(a.m_true) * a.n_true;
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int i = static_cast<int>(e / a.n_true), j = static_cast<int>(e % a.n_true);
-    const float v = __bfloat162float(X[static_cast<int64_t>(i) * a.Np + j]);
-    const int64_t r = tr ? j : i, cc = tr ? i : j;
+  auto dest = [&](int64_t r, int64_t c, void*& T) -> int64_t {  // element (r, c) of the destination
     const int seg = (a.nseg > 1) ? static_cast<int>(r / seg_rows) : 0;
-    void* T = reinterpret_cast<void*>(segp[seg]);
-    const int64_t idx = (r - seg * seg_rows) * ld + cc;
-    const float old = (ps != 0.f) ? ld_val<OUT_F32>(T, idx) : 0.f;
-    st_val<OUT_F32>(T, idx, fmaf(ps, old, vs * v));
+    T = reinterpret_cast<void*>(segp[seg]);
+    return (r - seg * seg_rows) * ld + c;
+  };
+  const int tiles_n = (a.n_true + 63) / 64;
+  const int tiles = ((a.m_true + 63) / 64) * tiles_n;
+  const int tr8 = threadIdx.x >> 3, tc8 = (threadIdx.x & 7) * 8;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int i0 = (t / tiles_n) * 64, j0 = (t % tiles_n) * 64;
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      const int ii = tr8 + 32 * pass, i = i0 + ii, j = j0 + tc8;
+      float v[8];
+      if (i < a.m_true && j < a.n_true) {
+        const uint4 w = *reinterpret_cast<const uint4*>(X + static_cast<int64_t>(i) * a.Np + j);  // Np % 8 == 0
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          v[2 * e] = f.x;
+          v[2 * e + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
+      if (!tr) {
+        if (i < a.m_true && j < a.n_true) {
+          void* T;
+          const int64_t idx = dest(i, j, T);
+          apply_run8<OUT_F32>(T, idx, v, min(8, a.n_true - j), ps, vs);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tile[ii][tc8 + e] = v[e];
+      }
+    }
+    if (tr) {
+      __syncthreads();
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int rr = tr8 + 32 * pass;      // destination row j0 + rr = workspace column
+        const int R = j0 + rr, C = i0 + tc8;  // destination columns = workspace rows
+        if (R < a.n_true && C < a.m_true) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = tile[tc8 + e][rr];
+          void* T;
+          const int64_t idx = dest(R, C, T);
+          apply_run8<OUT_F32>(T, idx, v, min(8, a.m_true - C), ps, vs);
+        }
+      }
+      __syncthreads();
+    }
   }
 }
 
@@ -403,7 +490,9 @@ void ns_scale(const float* sumsq, int n, int nparts, float eps, float* s, float*
 
 void ws_to_out(const WsOutArgs& a, cudaStream_t stream) {
   if (a.batch <= 0) return;
-  dim3 grid(grid_for(static_cast<int64_t>(a.m_true) * a.n_true, 256, 2048), a.batch);
+  if (a.Np % 8 != 0) throw std::runtime_error("mmf: ws_to_out needs Np % 8 == 0");
+  const int64_t tiles = static_cast<int64_t>((a.m_true + 63) / 64) * ((a.n_true + 63) / 64);
+  dim3 grid(static_cast<unsigned>(tiles < 1184 ? tiles : 1184), a.batch);
   if (a.out_f32)
     ws_to_out_kernel<true><<<grid, 256, 0, stream>>>(a);
   else

@@ -212,26 +212,40 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int b, int ro
               }
             }
           }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          // Element-wise path (transposed destination, ragged edge, unaligned rows).  Lanes are
+          // consecutive rows, so with a transposed destination each element index i is one
+          // contiguous 64/128-byte access across the warp.  All old values are loaded before the
+          // first store: interleaving them would serialise every load behind the previous store
+          // (the compiler cannot prove the destinations distinct) at full DRAM latency each.
+          auto elem = [&](int i) -> char* {  // destination of element i, as a byte address base
             const int col = col0 + i;
-            if (col >= p.n_true) break;
-            float val = alpha_b * v[i];
-            if (beta_b != 0.f) val = fmaf(beta_b, c[i], val);
             const int64_t r = tr ? col : row;
             const int64_t cc = tr ? row : col;
             const int seg = (p.nseg > 1) ? static_cast<int>(r / seg_rows) : 0;
-            char* T = reinterpret_cast<char*>(segp[seg]);
-            const int64_t idx = (r - seg * seg_rows) * ld + cc;
-            if (p.out_f32) {
-              float* tp = reinterpret_cast<float*>(T) + idx;
-              const float old = (ps != 0.f) ? *tp : 0.f;
-              *tp = fmaf(ps, old, vs * val);
-            } else {
-              __nv_bfloat16* tp = reinterpret_cast<__nv_bfloat16*>(T) + idx;
-              const float old = (ps != 0.f) ? __bfloat162float(*tp) : 0.f;
-              *tp = __float2bfloat16_rn(fmaf(ps, old, vs * val));
+            return reinterpret_cast<char*>(segp[seg]) +
+                   ((r - seg * seg_rows) * ld + cc) * (p.out_f32 ? 4 : 2);
+          };
+          float olds[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            olds[i] = 0.f;
+            if (ps != 0.f && col0 + i < p.n_true) {
+              const char* a = elem(i);
+              olds[i] = p.out_f32 ? *reinterpret_cast<const float*>(a)
+                                  : __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(a));
             }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (col0 + i >= p.n_true) break;
+            float val = alpha_b * v[i];
+            if (beta_b != 0.f) val = fmaf(beta_b, c[i], val);
+            const float o = fmaf(ps, olds[i], vs * val);
+            char* a = elem(i);
+            if (p.out_f32)
+              *reinterpret_cast<float*>(a) = o;
+            else
+              *reinterpret_cast<__nv_bfloat16*>(a) = __float2bfloat16_rn(o);
           }
         }
       }

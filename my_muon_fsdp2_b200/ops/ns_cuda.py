@@ -56,6 +56,7 @@ def run_ns_group(
     workspace: Optional[Dict[str, torch.Tensor]] = None,
     nseg: int = 1,
     out_meta: Optional[torch.Tensor] = None,
+    transposed_dest: Optional[bool] = None,
 ) -> None:
     """Run ``steps`` quintic iterations on the stacked workspace and write the result out.
 
@@ -64,6 +65,11 @@ def run_ns_group(
     ``batch * nseg`` destination pointers; with ``nseg > 1`` each destination row block of
     ``seg_rows`` rows (from ``out_meta``, int64 [batch, 3] = ld, transposed, seg_rows) goes to
     its own pointer (the scatter of each rank's row shard).
+
+    ``transposed_dest`` (default ``out_transposed``) says whether the destinations hold the
+    transpose of the workspace (tall matrices).  Then the last iteration writes the workspace
+    and a tiled transpose kernel applies it: a GEMM epilogue that updates a transposed
+    destination touches a different destination row for every element.
     """
     E = ext()
     a, b, c = NS_COEFFICIENTS
@@ -79,15 +85,21 @@ def run_ns_group(
     Bm = ws.get("B")
     if Bm is None or Bm.shape != (batch, Mp, Mp):
         Bm = torch.empty_like(A)
+    if transposed_dest is None:
+        transposed_dest = out_transposed
     X1 = ws.get("X1")
-    if steps > 1 and (X1 is None or X1.shape != X0.shape):
+    if (steps > 1 or transposed_dest) and (X1 is None or X1.shape != X0.shape):
         X1 = torch.empty_like(X0)
     X = X0
     for it in range(steps):
         first = it == 0
         E.tc_gemm_ws(X, X, False, A, None, s2 if first else None, 1.0, None, 0.0, True)
         E.tc_gemm_ws(A, A, False, Bm, A, None, c, None, b, True)
-        if it == steps - 1:
+        if it == steps - 1 and transposed_dest:
+            E.tc_gemm_ws(Bm, X, True, X1, X, s if first else None, 1.0, s if first else None, a, False)
+            E.ws_to_out(X1, None, out_ptrs, nseg, out_meta, out_ld, out_f32, out_transposed, m_true, n_true,
+                        p_scale_vec, p_scale, v_scale_vec, v_scale)
+        elif it == steps - 1:
             E.tc_gemm_out(Bm, X, True, X, s if first else None, 1.0, s if first else None, a, out_ptrs, nseg,
                           out_meta, out_ld, out_f32, out_transposed, m_true, n_true, p_scale_vec, p_scale,
                           v_scale_vec, v_scale)

@@ -518,6 +518,7 @@ class MuonEngine:
             chunk = max(1, min(len(js), self.max_workspace_bytes // max(per, 1)))
             for c0 in range(0, len(js), chunk):
                 sub_js = js[c0:c0 + chunk]
+                tall_group = any(shapes[j][0] > shapes[j][1] for j in sub_js)
                 B = len(sub_js)
                 padded = (Mp != mw) or (Np != nw)
                 X0 = (torch.zeros if padded else torch.empty)(B, Mp, Np, dtype=torch.bfloat16, device=dev)
@@ -548,7 +549,7 @@ class MuonEngine:
                 ptrs = torch.tensor(addrs, dtype=torch.int64).to(dev, non_blocking=True)
                 meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
                 run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
-                             nseg=world, out_meta=meta_t)
+                             nseg=world, out_meta=meta_t, transposed_dest=tall_group)
         # 5. barrier: all owners' results have landed
         sw.barrier()
         # 6. local apply from the own buffer
@@ -596,6 +597,7 @@ class MuonEngine:
             chunk = max(1, min(len(js), self.max_workspace_bytes // max(per, 1)))
             for c0 in range(0, len(js), chunk):
                 sub = js[c0:c0 + chunk]
+                tall_group = any(shapes[j][0] > shapes[j][1] for j in sub)
                 B = len(sub)
                 padded = (Mp != mw) or (Np != nw)
                 X0 = (torch.zeros if padded else torch.empty)(B, Mp, Np, dtype=torch.bfloat16, device=dev)
@@ -628,7 +630,7 @@ class MuonEngine:
                 ptrs = E.ptr_table(seg_views)
                 meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
                 run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
-                             nseg=world, out_meta=meta_t)
+                             nseg=world, out_meta=meta_t, transposed_dest=tall_group)
 
     def _cuda_apply(self, tasks, ret, ret_at, cnt, rank) -> None:
         from .._ext import ext
