@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--micro-bs", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32, help="debug only: fewer layers is not the named config")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rs-mode", choices=["overlap", "fused"], default="overlap",
+                    help="symm: reduce-scatter on a side stream (overlap) or from the GEMM epilogue (fused)")
     ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="symm",
                     help="fsdp2: fully_shard everywhere; symm: block linears on symmetric memory with the "
                          "fused all-gather GEMM / GEMM reduce-scatter kernels, the rest fully_shard")
@@ -100,7 +102,7 @@ def build_ours(args, world, local):
     if args.fsdp == "symm":
         from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
 
-        ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local))
+        ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local), rs_mode=args.rs_mode)
     else:
         apply_fsdp(model, mesh)
         model.to_empty(device=torch.device("cuda", local))
@@ -277,7 +279,8 @@ def main():
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",
-                       "fsdp_impl": (args.fsdp if args.impl == "ours" else "fully_shard"),
+                       "fsdp_impl": ((args.fsdp + (f"/{args.rs_mode}" if args.fsdp == "symm" else ""))
+                                     if args.impl == "ours" else "fully_shard"),
                        "tokens_per_step": tokens_per_step,
                        "l2": "no flush: per-step working set (16 GB bf16 weights + activations) >> 126 MB L2",
                        "optimizers": "Muon(attn+FFN matrices, lr .02, mom .95, wd .01, ns 5) + AdamW(rest, lr 1e-3)"},

@@ -69,6 +69,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--rs-mode", choices=["overlap", "fused"], default="overlap")
     ap.add_argument("--emulate-world", type=int, default=0,
                     help="one GPU: run ag_gemm as rank 0 of this many ranks whose shards are all local "
                          "buffers (the kernel's pull / ready-flag / GEMM structure without NVLink, for ncu)")
@@ -100,7 +101,7 @@ def main():
         with torch.no_grad():
             m.weight.normal_(0, 0.02)
     names = list(lins)
-    ctl = SymmFSDP([lins[k] for k in names], device=dev)
+    ctl = SymmFSDP([lins[k] for k in names], device=dev, rs_mode=args.rs_mode)
     rows = []
     for i, name in enumerate(names):
         n, k = SHAPES[name]
@@ -127,7 +128,7 @@ def main():
             ctl.params[i].grad = None
             ctl._accumulate_grad(i, dy, x)
 
-        r = {"weight": name, "N": n, "K": k, "tokens": T}
+        r = {"weight": name, "N": n, "K": k, "tokens": T, "rs_mode": args.rs_mode}
         r["fwd_nccl_ms"] = timed(nccl_fwd, args.iters, args.warmup)
         r["fwd_fused_ms"] = timed(fused_fwd, args.iters, args.warmup)
         r["gemm_only_ms"] = timed(lambda: F.linear(x, full), args.iters, args.warmup)

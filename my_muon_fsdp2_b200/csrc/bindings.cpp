@@ -224,6 +224,17 @@ void rs_reduce(Tensor slots, int64_t ws, int64_t slot_stride, Tensor out, bool a
                  static_cast<float>(scale), cur_stream());
 }
 
+// out (bf16) = (accumulate ? out : 0) + scale * sum over ranks s of srcs[s][offset : offset + numel(out)]
+// (srcs: device int64 [ws] of every rank's partial buffer; P2P loads for the peers)
+void rs_pull_reduce(Tensor srcs, int64_t offset, Tensor out, bool accumulate, double scale) {
+  check_cuda(srcs, "srcs");
+  check_bf16_contig(out, "out");
+  TORCH_CHECK(srcs.scalar_type() == torch::kInt64, "mmf: srcs must be int64");
+  const c10::cuda::CUDAGuard guard(out.device());
+  mmf::rs_pull_reduce(srcs.data_ptr<int64_t>(), static_cast<int>(srcs.numel()), offset, out.numel(), out.data_ptr(),
+                      accumulate, static_cast<float>(scale), cur_stream());
+}
+
 // grads/bufs/params: per-matrix tensors (bufs/params may be empty lists).  dst: optional bf16
 // workspace; per-matrix destination = dst_base_offsets[i] elements into dst.
 void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<Tensor> params,
@@ -631,6 +642,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wgrad_out", &wgrad_out);
   m.def("ag_gemm", &ag_gemm);
   m.def("rs_reduce", &rs_reduce);
+  m.def("rs_pull_reduce", &rs_pull_reduce);
   m.def("muon_prep", &muon_prep);
   m.def("ns_scale", &ns_scale);
   m.def("ws_to_out", &ws_to_out);

@@ -110,6 +110,12 @@ void ag_gemm(const AgGemmArgs& args, cudaStream_t stream);
 void rs_reduce(const void* slots, int ws, int64_t slot_stride, int64_t n, void* out, bool accumulate, float scale,
                cudaStream_t stream);
 
+// Pull form of the same reduction: out[i] = bf16((accumulate ? out[i] : 0) + scale *
+// sum_{s = 0..ws-1} srcs[s][offset + i]) where srcs (device array) holds every rank's partial
+// buffer (peers through P2P mappings); fp32 sum in rank order.  n and offset multiples of 8.
+void rs_pull_reduce(const int64_t* srcs, int ws, int64_t offset, int64_t n, void* out, bool accumulate, float scale,
+                    cudaStream_t stream);
+
 // ----------------------------------------------------------------------------------------
 // Muon pre-NS multi-tensor kernel.  For matrix b (a row block of rows_b x cols_b elements):
 //   mode 0 (copy):      u = g

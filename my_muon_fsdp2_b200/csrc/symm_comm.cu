@@ -114,6 +114,50 @@ __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, int ws
   }
 }
 
+// out[i] = bf16((acc ? out[i] : 0) + scale * sum_s src_s[offset + i]) with src_s = srcs[s] (one
+// pointer per rank, P2P-mapped for peers), fp32 sum in rank order.  8 bf16 per thread (16-byte
+// loads over NVLink).
+__global__ void rs_pull_reduce_kernel(const int64_t* __restrict__ srcs, int ws, int64_t offset, int64_t n,
+                                      __nv_bfloat16* __restrict__ out, int accumulate, float scale) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t nv = n / 8;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += stride) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int s = 0; s < ws; ++s) {
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(srcs[s]) + offset;
+      const uint4 w = reinterpret_cast<const uint4*>(src)[i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
+      }
+    }
+    float base[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) base[e] = 0.f;
+    if (accumulate) {
+      const uint4 w = reinterpret_cast<const uint4*>(out)[i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        base[2 * e] = f.x;
+        base[2 * e + 1] = f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      oh[e] = __floats2bfloat162_rn(base[2 * e] + scale * acc[2 * e], base[2 * e + 1] + scale * acc[2 * e + 1]);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
 }  // namespace
 
 void symm_barrier(const int64_t* pad_ptrs, int rank, int ws, uint32_t epoch, int slot_base, const float* payload,
@@ -149,6 +193,25 @@ void rs_reduce(const void* slots, int ws, int64_t slot_stride, int64_t n, void* 
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: rs_reduce launch failed: ") + cudaGetErrorString(e));
+}
+
+void rs_pull_reduce(const int64_t* srcs, int ws, int64_t offset, int64_t n, void* out, bool accumulate, float scale,
+                    cudaStream_t stream) {
+  if (ws < 1 || n < 0 || offset < 0) throw std::runtime_error("mmf: rs_pull_reduce: bad arguments");
+  if (n % 8 != 0 || offset % 8 != 0 || (reinterpret_cast<uintptr_t>(out) & 15) != 0)
+    throw std::runtime_error("mmf: rs_pull_reduce needs n % 8 == 0, offset % 8 == 0 and a 16-byte aligned output");
+  if (n == 0) return;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n / 8 + 255) / 256;
+  // a few blocks per SM: enough loads in flight over NVLink while the compute stream keeps running
+  const unsigned grid = static_cast<unsigned>(want < sms * 2 ? (want < 1 ? 1 : want) : sms * 2);
+  rs_pull_reduce_kernel<<<grid, 256, 0, stream>>>(srcs, ws, offset, n, static_cast<__nv_bfloat16*>(out),
+                                                  accumulate ? 1 : 0, scale);
+  count_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: rs_pull_reduce launch failed: ") + cudaGetErrorString(e));
 }
 
 }  // namespace mmf

@@ -15,11 +15,14 @@ moves the two collectives into this library's kernels:
   ``dX = dY W`` are plain local GEMMs, so a step gathers each weight once instead of twice per
   micro-batch.  With 180 GB of HBM per GPU the resident copy of an 8B model's linears (16 GB)
   is cheap.
-* **GEMM -> reduce-scatter** (``ext.wgrad_out`` + ``ext.rs_reduce``): the weight-gradient GEMM
-  ``dW = dY^T X`` writes each rank's row block of its partial product straight into that rank's
-  receive slot (P2P stores from the epilogue); after a bounded barrier each rank sums its slots
-  in rank order (deterministic) and accumulates ``1/world`` of the sum into its gradient shard,
-  which is what FSDP2's averaging reduce-scatter produces.
+* **GEMM -> reduce-scatter**, two modes.  ``rs_mode="overlap"`` (default): the weight-gradient
+  GEMM writes this rank's unsharded partial ``dW`` into a peer-readable buffer, then a side
+  stream runs a bounded barrier and ``ext.rs_pull_reduce`` (each rank pulls its rows from every
+  rank with P2P loads and sums them in rank order) while the backward continues on the compute
+  stream.  ``rs_mode="fused"``: the GEMM epilogue itself stores each rank's row block into that
+  rank's receive slot (``ext.wgrad_out``), then barrier + ``ext.rs_reduce`` on the compute
+  stream.  Both accumulate ``1/world`` of the rank-order sum into the gradient shard, which is
+  what FSDP2's averaging reduce-scatter produces, deterministically.
 
 The remaining parameters (embeddings, norms, LM head) stay under ``fully_shard`` with the fused
 linears passed as ``ignored_params``.  Without CUDA (gloo tests) the same module runs its
@@ -98,7 +101,8 @@ class SymmFSDP:
     bias-free linear layers, all sharded over one process group."""
 
     def __init__(self, linears: Sequence[nn.Linear], mesh=None, group: Optional[dist.ProcessGroup] = None,
-                 device: Optional[torch.device] = None, wait_s: float = 2e-3, barrier_timeout_s: float = 60.0):
+                 device: Optional[torch.device] = None, wait_s: float = 2e-3, barrier_timeout_s: float = 60.0,
+                 rs_mode: str = "overlap"):
         from torch.distributed.device_mesh import init_device_mesh
         from torch.distributed.tensor import DTensor, Shard
 
@@ -113,6 +117,9 @@ class SymmFSDP:
         self.mesh = mesh
         self.wait_s = float(wait_s)
         self.barrier_timeout_s = float(barrier_timeout_s)
+        if rs_mode not in ("overlap", "fused"):
+            raise ValueError(f"rs_mode must be 'overlap' or 'fused', got {rs_mode!r}")
+        self.rs_mode = rs_mode
         self.fused = self.device.type == "cuda" and dist.get_backend(group) == "nccl"
         self.modules: List[nn.Linear] = list(linears)
         self.shapes: List[Tuple[int, int]] = []
@@ -154,6 +161,21 @@ class SymmFSDP:
                 for b in range(2)
             ]
             self._meta: Dict[int, torch.Tensor] = {}
+            if rs_mode == "overlap" and self.world > 1:
+                # unsharded partial dW of every weight, peer-readable: the reduce-scatter pulls
+                # each rank's rows from all ranks on a side stream while backward continues
+                full_sizes = [n * k for n, k in self.shapes]
+                self.acc_offsets, o = [], 0
+                for fs in full_sizes:
+                    self.acc_offsets.append(o)
+                    o += (fs + 7) // 8 * 8
+                self.acc_buf = symm_mem.empty(max(o, 8), dtype=dtype, device=self.device)
+                self.acc_handle = self._rendezvous(self.acc_buf)
+                self._acc_ptrs = torch.tensor([int(self.acc_handle.buffer_ptrs[s_]) for s_ in range(self.world)],
+                                              dtype=torch.int64, device=self.device)
+                self.comm = torch.cuda.Stream(device=self.device)
+                self.comm_epoch = 0
+                self._join_queued = False
         else:
             self.shard_buf = torch.empty(total, dtype=dtype, device=self.device)
         self.epoch = 0
@@ -195,6 +217,17 @@ class SymmFSDP:
     def _barrier(self) -> None:
         self.epoch += 1
         _ext().symm_barrier(self.pad_ptrs, self.rank, self.world, self.epoch, 0, None, None, self.barrier_timeout_s)
+
+    def _comm_barrier(self) -> None:
+        """Barrier on the side stream, over its own signal slots (slot_base 64)."""
+        self.comm_epoch += 1
+        _ext().symm_barrier(self.pad_ptrs, self.rank, self.world, self.comm_epoch, 64, None, None,
+                            self.barrier_timeout_s)
+
+    def _join(self) -> None:
+        """End of backward: later work on the compute stream (optimizer) sees the gradients."""
+        self._join_queued = False
+        torch.cuda.current_stream(self.device).wait_stream(self.comm)
 
     def invalidate(self) -> None:
         """The shards changed (optimizer step, checkpoint load): gather again on next use."""
@@ -271,6 +304,13 @@ class SymmFSDP:
     def _accumulate_grad(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         n, k = self.shapes[i]
         r = self.rows[i]
+        overlap = self.fused and self.world > 1 and self.rs_mode == "overlap"
+        if overlap and self.acc[i] is None:
+            o = self.acc_offsets[i]
+            self.acc[i] = self.acc_buf[o:o + n * k].view(n, k)
+        if overlap and self.sync_grads:
+            self._overlapped_reduce_scatter(i, dy2, x2)
+            return
         if self.world > 1 and not self.sync_grads:
             # no-sync micro-batch: accumulate this rank's unsharded partial dW locally
             if self.acc[i] is None:
@@ -316,6 +356,35 @@ class SymmFSDP:
         slots = self.slot_buf[b * self.slot_elems:(b + 1) * self.slot_elems]
         ext.rs_reduce(slots, self.world, self.slot_elems // self.world, g, acc, 1.0 / self.world)
 
+    def _overlapped_reduce_scatter(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
+        """Synchronising backward of weight i (overlap mode): local partial GEMM, then the
+        reduce-scatter on the side stream, overlapped with the rest of the backward."""
+        n, k = self.shapes[i]
+        r = self.rows[i]
+        acc_i = self.acc[i]
+        # 1. this rank's complete partial dW (+ the no-sync accumulation), local GEMM
+        if self.acc_live[i]:
+            acc_i.addmm_(dy2.t(), x2)
+        else:
+            torch.mm(dy2.t(), x2, out=acc_i)
+        self.acc_live[i] = False
+        g, acc = self._grad_local(i)
+        cur = torch.cuda.current_stream(self.device)
+        self.comm.wait_stream(cur)
+        g.record_stream(self.comm)
+        # 2. side stream: every rank's partial is complete -> pull and sum my rows from all ranks
+        #    (P2P loads, rank order) -> every rank is done reading -> the buffers may be rewritten
+        with torch.cuda.stream(self.comm):
+            self._comm_barrier()
+            _ext().rs_pull_reduce(self._acc_ptrs, self.acc_offsets[i] + self.rank * r * k, g, acc, 1.0 / self.world)
+            self._comm_barrier()
+        if not self._join_queued:
+            self._join_queued = True
+            try:
+                torch.autograd.Variable._execution_engine.queue_callback(self._join)
+            except RuntimeError:  # called outside a backward pass
+                self._join()
+
 
 def block_linears(model: nn.Module, blocks_attr: str = "layers") -> List[nn.Linear]:
     out = []
@@ -327,7 +396,7 @@ def block_linears(model: nn.Module, blocks_attr: str = "layers") -> List[nn.Line
 
 
 def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str = "layers",
-                    reshard_after_forward: Optional[bool] = None) -> SymmFSDP:
+                    reshard_after_forward: Optional[bool] = None, rs_mode: str = "overlap") -> SymmFSDP:
     """Shard every bias-free linear of the transformer blocks on symmetric memory (fused
     all-gather/reduce-scatter kernels) and ``fully_shard`` the rest of the model (embeddings,
     norms, LM head) with FSDP2, the linears passed as ``ignored_params``.  A model on the meta
@@ -340,7 +409,7 @@ def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str =
     if device is not None and any(p.device.type == "meta" for p in model.parameters()):
         model.to_empty(device=torch.device(device))
     dev = torch.device(device) if device is not None else next(model.parameters()).device
-    ctl = SymmFSDP(lin, mesh=mesh, device=dev)
+    ctl = SymmFSDP(lin, mesh=mesh, device=dev, rs_mode=rs_mode)
     model._symm_fsdp = ctl
     fsdp_sync = model.set_requires_gradient_sync
 

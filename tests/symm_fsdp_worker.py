@@ -23,12 +23,20 @@ def run_kernels(rank, world, dev):
     from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmFSDP
 
     shapes = [(1024, 512), (512, 1024), (256 * world, 256), (768 * world, 512)]
-    torch.manual_seed(0)
-    lins = [nn.Linear(k, n, bias=False).to(dev, torch.bfloat16) for n, k in shapes]
-    fulls = [m.weight.detach().clone() for m in lins]
-    ctl = SymmFSDP(lins, device=dev)
-    assert ctl.fused
     res = {}
+    for mode in ("overlap", "fused"):
+        torch.manual_seed(0)
+        lins = [nn.Linear(k, n, bias=False).to(dev, torch.bfloat16) for n, k in shapes]
+        fulls = [m.weight.detach().clone() for m in lins]
+        ctl = SymmFSDP(lins, device=dev, rs_mode=mode)
+        assert ctl.fused
+        _check_linears(ctl, lins, fulls, rank, world, dev, res, mode)
+    torch.cuda.synchronize()
+    check_device_error(dev.index)
+    return res
+
+
+def _check_linears(ctl, lins, fulls, rank, world, dev, res, mode):
     for i, (m, w) in enumerate(zip(lins, fulls)):
         for t in (256, 200):  # 200: token count padded to the tile size inside
             g = torch.Generator(device="cpu").manual_seed(1000 * i + 10 * rank + t)
@@ -38,9 +46,9 @@ def run_kernels(rank, world, dev):
             y = m(x)  # fused all-gather GEMM
             y2 = m(x)  # resident full weight
             ref = x.detach().float() @ w.float().t()
-            res[f"y{i}_{t}"] = ((y.float() - ref).norm() / ref.norm()).item()
-            res[f"y2{i}_{t}"] = ((y2.float() - ref).norm() / ref.norm()).item()
-            res[f"g{i}_{t}"] = bool(torch.equal(ctl.full[i], w))
+            res[f"y{i}_{t}_{mode}"] = ((y.float() - ref).norm() / ref.norm()).item()
+            res[f"y2{i}_{t}_{mode}"] = ((y2.float() - ref).norm() / ref.norm()).item()
+            res[f"g{i}_{t}_{mode}"] = bool(torch.equal(ctl.full[i], w))
             dy = torch.randn(t, w.shape[0], generator=g).to(dev, torch.bfloat16)
             y.backward(dy)
             xs, dys = _gather(x.detach()), _gather(dy)
@@ -48,12 +56,9 @@ def run_kernels(rank, world, dev):
             r = w.shape[0] // world
             dw_loc = dw[rank * r:(rank + 1) * r]
             got = m.weight.grad.to_local().float()
-            res[f"dw{i}_{t}"] = ((got - dw_loc).norm() / dw_loc.norm()).item()
+            res[f"dw{i}_{t}_{mode}"] = ((got - dw_loc).norm() / dw_loc.norm()).item()
             dx_ref = dy.float() @ w.float()
-            res[f"dx{i}_{t}"] = ((x.grad.float() - dx_ref).norm() / dx_ref.norm()).item()
-    torch.cuda.synchronize()
-    check_device_error(dev.index)
-    return res
+            res[f"dx{i}_{t}_{mode}"] = ((x.grad.float() - dx_ref).norm() / dx_ref.norm()).item()
 
 
 def run_train(rank, world, dev, steps=3):
