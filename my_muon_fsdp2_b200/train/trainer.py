@@ -17,8 +17,12 @@ from ..parallel.fsdp_utils import is_fsdp_module
 
 class Trainer:
     def __init__(self, model: nn.Module, optimizers: Sequence, grad_accum: int = 1, device=None,
-                 step_timer=None):
+                 step_timer=None, max_grad_norm: Optional[float] = None):
+        """``max_grad_norm``: clip the global gradient norm before the optimizer steps, as the
+        reference trainers do with 1.0 (examples/train_gpt.py:367-371); None disables it."""
         self.model = model
+        self.max_grad_norm = max_grad_norm
+        self.last_grad_norm: Optional[torch.Tensor] = None
         self.optimizers = list(optimizers)
         self.grad_accum = int(grad_accum)
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
@@ -45,6 +49,9 @@ class Trainer:
         for i in range(self.grad_accum):
             l = self._micro(tokens, i).detach()
             total = l if total is None else total + l
+        if self.max_grad_norm is not None:
+            params = [p for p in self.model.parameters() if p.grad is not None]
+            self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.max_grad_norm)
         if self.step_timer is not None:
             self.step_timer.start()
         for opt in self.optimizers:

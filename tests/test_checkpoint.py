@@ -53,3 +53,35 @@ def test_two_optimizers(tmp_path):
     m2 = _setup()
     opts2 = [MuonOptimizer([m2[0].weight, m2[2].weight]), torch.optim.AdamW([m2[0].bias, m2[2].bias])]
     load_checkpoint(path, m2, opts2)
+
+
+def test_trainer_clips_gradient_norm():
+    """max_grad_norm (the reference trainers clip at 1.0): gradients leave the step with global
+    norm <= the bound, and the pre-clip norm is reported."""
+    import torch.nn as nn
+
+    from my_muon_fsdp2_b200.train import Trainer
+
+    class Toy(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.emb = nn.Embedding(16, 8)
+            self.out = nn.Linear(8, 16)
+
+        def forward(self, x, y):
+            return 100.0 * nn.functional.cross_entropy(self.out(self.emb(x)).flatten(0, 1), y.flatten())
+
+    torch.manual_seed(0)
+    model = Toy()
+    seen = {}
+
+    class Probe(torch.optim.SGD):
+        def step(self, closure=None):
+            seen["norm"] = torch.sqrt(sum((p.grad.float() ** 2).sum() for p in model.parameters()))
+            return super().step(closure)
+
+    trainer = Trainer(model, [Probe(model.parameters(), lr=0.0)], grad_accum=2, device="cpu", max_grad_norm=1.0)
+    batch = torch.randint(0, 16, (2, 3, 9))
+    trainer.train_step(batch)
+    assert float(trainer.last_grad_norm) > 1.0
+    assert float(seen["norm"]) <= 1.0 + 1e-4
