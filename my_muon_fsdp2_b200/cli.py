@@ -19,6 +19,7 @@ def muon_fsdp_main(argv=None) -> int:
     info.add_argument("--verbose", "-v", action="store_true")
     check = sub.add_parser("check", help="check installation and dependencies")
     check.add_argument("--full", action="store_true", help="also run a small optimizer step")
+    sub.add_parser("configs", help="list the benchmark workloads and the commands that measure them")
     args = parser.parse_args(argv)
     import torch
 
@@ -32,6 +33,13 @@ def muon_fsdp_main(argv=None) -> int:
                          "HybridMuonAdamW", "Newton-Schulz (tcgen05 chain on sm_100a)",
                          "distributed primitives (NCCL / symmetric-memory P2P)"):
                 print(f"  - {line}")
+        return 0
+    if args.command == "configs":
+        from .configs import WORKLOADS
+
+        for w in WORKLOADS.values():
+            print(f"{w.name}: {w.model}\n  gpus: {w.gpus}; dtype: {w.dtype}; batch/GPU: {w.batch_per_gpu}\n"
+                  f"  optimizer: {w.optimizer}\n  run: {w.command}")
         return 0
     if args.command == "check":
         print(f"OK PyTorch {torch.__version__}")

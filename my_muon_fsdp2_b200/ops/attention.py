@@ -15,6 +15,7 @@ import torch
 import torch.nn.functional as F
 
 from .._ext import ext
+from ..utils.tracing import nvtx_range
 
 
 def _pad_t(x: torch.Tensor, tp: int) -> torch.Tensor:
@@ -30,7 +31,8 @@ class _FlashAttnFn(torch.autograd.Function):
         tp = (T + 127) // 128 * 128
         qp, kp, vp = _pad_t(q, tp), _pad_t(k, tp), _pad_t(v, tp)
         scale = 1.0 / math.sqrt(q.shape[-1])
-        o, lse = ext().attention_fwd(qp, kp, vp, scale)
+        with nvtx_range("attention/forward"):
+            o, lse = ext().attention_fwd(qp, kp, vp, scale)
         ctx.save_for_backward(qp, kp, vp, o, lse)
         ctx.T, ctx.scale = T, scale
         return o[:, :T] if tp != T else o
@@ -40,7 +42,8 @@ class _FlashAttnFn(torch.autograd.Function):
         qp, kp, vp, o, lse = ctx.saved_tensors
         T = ctx.T
         dop = _pad_t(do, qp.shape[1])
-        dq, dk, dv = ext().attention_bwd(dop, qp, kp, vp, o, lse, ctx.scale)
+        with nvtx_range("attention/backward"):
+            dq, dk, dv = ext().attention_bwd(dop, qp, kp, vp, o, lse, ctx.scale)
         if qp.shape[1] != T:
             dq, dk, dv = dq[:, :T], dk[:, :T], dv[:, :T]
         return dq, dk, dv

@@ -37,6 +37,7 @@ import torch.distributed as dist
 from ..ops.newton_schulz import NS_COEFFICIENTS, NS_EPS, _ns_torch
 from .comm import chunk_offset, chunk_rows
 from .dtensor import is_dtensor
+from ..utils.tracing import nvtx_range
 
 MODE_COPY, MODE_EMA, MODE_HEAVYBALL = 0, 1, 2
 
@@ -188,7 +189,8 @@ class MuonEngine:
         elementwise = [t for t in tasks if not (t.orthogonalize and t.param.dim() == 2)]
         matrices = [t for t in tasks if t.orthogonalize and t.param.dim() == 2]
         if elementwise:
-            self._elementwise(elementwise, hp, is_cuda)
+            with nvtx_range("muon/elementwise"):
+                self._elementwise(elementwise, hp, is_cuda)
         if not matrices:
             return
         sharded = [t for t in matrices if is_dtensor(t.param)]
@@ -197,10 +199,11 @@ class MuonEngine:
             local = local + sharded
             sharded = []
         if local:
-            if is_cuda:
-                self._local_cuda(local, hp)
-            else:
-                self._local_cpu(local, hp)
+            with nvtx_range("muon/local"):
+                if is_cuda:
+                    self._local_cuda(local, hp)
+                else:
+                    self._local_cpu(local, hp)
         if sharded and world > 1 and self.split != "never":
             shp = [tuple(t.param.shape) for t in sharded]
             if self.split == "always":
@@ -208,14 +211,17 @@ class MuonEngine:
             else:
                 pick = select_split(shp, world, hp.ns_steps)
             for i in pick:
-                self._split_chain(sharded[i], hp, world, rank, group, is_cuda)
+                with nvtx_range("muon/cooperative_chain"):
+                    self._split_chain(sharded[i], hp, world, rank, group, is_cuda)
             self.split_count = len(pick)
             sharded = [t for i, t in enumerate(sharded) if i not in set(pick)]
         if sharded:
             if is_cuda and self._use_p2p(group):
-                self._sharded_p2p(sharded, hp, world, rank, group)
+                with nvtx_range("muon/owner_computes_p2p"):
+                    self._sharded_p2p(sharded, hp, world, rank, group)
             else:
-                self._sharded(sharded, hp, world, rank, group, is_cuda)
+                with nvtx_range("muon/owner_computes_nccl"):
+                    self._sharded(sharded, hp, world, rank, group, is_cuda)
 
     def _use_p2p(self, group) -> bool:
         if self.comm == "nccl":

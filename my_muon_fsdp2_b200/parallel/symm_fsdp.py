@@ -38,6 +38,8 @@ import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..utils.tracing import nvtx_range
+
 PANEL = 128
 
 
@@ -269,7 +271,8 @@ class SymmFSDP:
                 self._step_synced = True
             t = x2.shape[0]
             xp = _pad_rows(x2, 128)
-            y = _ext().ag_gemm(xp, self.shard_ptrs(i), self.rank, self.full[i], self.ready, self.wait_s)
+            with nvtx_range("symm_fsdp/ag_gemm"):
+                y = _ext().ag_gemm(xp, self.shard_ptrs(i), self.rank, self.full[i], self.ready, self.wait_s)
             if xp is not x2:
                 y = y[:t]
         else:
@@ -309,7 +312,8 @@ class SymmFSDP:
             o = self.acc_offsets[i]
             self.acc[i] = self.acc_buf[o:o + n * k].view(n, k)
         if overlap and self.sync_grads:
-            self._overlapped_reduce_scatter(i, dy2, x2)
+            with nvtx_range("symm_fsdp/reduce_scatter_overlap"):
+                self._overlapped_reduce_scatter(i, dy2, x2)
             return
         if self.world > 1 and not self.sync_grads:
             # no-sync micro-batch: accumulate this rank's unsharded partial dW locally

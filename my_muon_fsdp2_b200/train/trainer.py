@@ -13,6 +13,7 @@ import torch
 import torch.nn as nn
 
 from ..parallel.fsdp_utils import is_fsdp_module
+from ..utils.tracing import nvtx_range
 
 
 class Trainer:
@@ -23,6 +24,8 @@ class Trainer:
         self.model = model
         self.max_grad_norm = max_grad_norm
         self.last_grad_norm: Optional[torch.Tensor] = None
+        self.steps = 0
+        self.last_metrics: dict = {}
         self.optimizers = list(optimizers)
         self.grad_accum = int(grad_accum)
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
@@ -38,8 +41,10 @@ class Trainer:
         if self.fsdp:
             self.model.set_requires_gradient_sync(last)
         t = tokens[i]
-        loss = self.model(t[:, :-1], t[:, 1:]) / self.grad_accum
-        loss.backward()
+        with nvtx_range(f"trainer/micro_batch_{i}/forward"):
+            loss = self.model(t[:, :-1], t[:, 1:]) / self.grad_accum
+        with nvtx_range(f"trainer/micro_batch_{i}/backward"):
+            loss.backward()
         return loss
 
     def step_on_device(self, tokens: torch.Tensor) -> torch.Tensor:
@@ -54,13 +59,38 @@ class Trainer:
             self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.max_grad_norm)
         if self.step_timer is not None:
             self.step_timer.start()
-        for opt in self.optimizers:
-            opt.step()
+        with nvtx_range("trainer/optimizer_step"):
+            for opt in self.optimizers:
+                opt.step()
         if self.step_timer is not None:
             self.step_timer.stop()
         for opt in self.optimizers:
             opt.zero_grad(set_to_none=True)
+        self.steps += 1
+        self.last_metrics = self._metrics(tokens, total)
         return total
+
+    def _metrics(self, tokens: torch.Tensor, loss: torch.Tensor) -> dict:
+        """Per-step observability without a device sync: loss / grad norm stay device tensors;
+        the Muon engine's exchange statistics and the fused-FSDP state are host values."""
+        m = {"step": self.steps, "micro_batches": self.grad_accum,
+             "tokens": int(tokens[:, :, 1:].numel()), "loss": loss}
+        if self.last_grad_norm is not None:
+            m["grad_norm"] = self.last_grad_norm
+        if self.step_timer is not None and getattr(self.step_timer, "pairs", None):
+            m["optimizer_step_timer"] = self.step_timer
+        for k, opt in enumerate(self.optimizers):
+            eng = getattr(opt, "_engine", None)
+            if eng is not None:
+                for key, val in getattr(eng, "last_stats", {}).items():
+                    m[f"opt{k}/{key}"] = val
+                m[f"opt{k}/cooperative_matrices"] = getattr(eng, "split_count", 0)
+        ctl = getattr(self.model, "_symm_fsdp", None)
+        if ctl is not None:
+            m["symm_fsdp/world"] = ctl.world
+            m["symm_fsdp/rs_mode"] = ctl.rs_mode
+            m["symm_fsdp/resident_weights"] = sum(1 for f in ctl.full if f is not None)
+        return m
 
     def train_step(self, batch: torch.Tensor) -> float:
         """End-to-end step from a host batch [grad_accum, micro_bs, seq+1] (int64)."""

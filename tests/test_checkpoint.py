@@ -85,3 +85,6 @@ def test_trainer_clips_gradient_norm():
     trainer.train_step(batch)
     assert float(trainer.last_grad_norm) > 1.0
     assert float(seen["norm"]) <= 1.0 + 1e-4
+    m = trainer.last_metrics
+    assert m["step"] == 1 and m["micro_batches"] == 2 and m["tokens"] == 2 * 3 * 8
+    assert float(m["grad_norm"]) == float(trainer.last_grad_norm)

@@ -312,3 +312,21 @@ class TestHDSP:
         c = HSDPConfig(dp_size=2, fsdp_size=4)
         assert c.to_dict()["fsdp_size"] == 4
         assert c.create_device_mesh() is None  # no process group
+
+
+def test_workload_registry_and_cli():
+    from my_muon_fsdp2_b200.cli import muon_fsdp_main
+    from my_muon_fsdp2_b200.configs import WORKLOADS, describe
+
+    assert set(WORKLOADS) == {"mlp_gloo", "encoder", "gpt2_small", "llama3_8b", "muon_sweep"}
+    assert all("command" in v for v in describe().values())
+    assert muon_fsdp_main(["configs"]) == 0
+
+
+def test_nvtx_ranges_are_noops_when_disabled():
+    from my_muon_fsdp2_b200.utils import tracing
+
+    tracing.enable(False)
+    with tracing.nvtx_range("x"):
+        pass
+    assert not tracing.enabled()
