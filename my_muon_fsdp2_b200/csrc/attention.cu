@@ -796,17 +796,24 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       for (int g = 0; g < 4; ++g) {
         uint4 wd;
         __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
+        // the 8 query columns' statistics: same address in every lane (broadcast), 16-byte reads
+        const int q0 = h * 64 + c0 + g * 8;
+        float st_l[8], st_d[8];
+        *reinterpret_cast<float4*>(st_l) = *reinterpret_cast<const float4*>(sLse + q0);
+        *reinterpret_cast<float4*>(st_l + 4) = *reinterpret_cast<const float4*>(sLse + q0 + 4);
+        *reinterpret_cast<float4*>(st_d) = *reinterpret_cast<const float4*>(sDelta + q0);
+        *reinterpret_cast<float4*>(st_d + 4) = *reinterpret_cast<const float4*>(sDelta + q0 + 4);
 #pragma unroll
         for (int e2 = 0; e2 < 4; ++e2) {
           float pv[2], dv[2];
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             const int e = g * 8 + e2 * 2 + t;
-            const int qc = h * 64 + c0 + e;  // query column inside the block
+            const int qc = q0 + e2 * 2 + t;  // query column inside the block
             const bool masked = diag && (qc < kr);
-            const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - sLse[qc]);
+            const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - st_l[e2 * 2 + t]);
             pv[t] = pr;
-            dv[t] = pr * (dp[e] - sDelta[qc]);
+            dv[t] = pr * (dp[e] - st_d[e2 * 2 + t]);
           }
           __nv_bfloat162 pb = __floats2bfloat162_rn(pv[0], pv[1]);
           ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
