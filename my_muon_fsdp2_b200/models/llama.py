@@ -16,6 +16,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..ops.model_ops import apply_rope, causal_attention, fused_linear_cross_entropy, rms_norm, swiglu
+from ..parallel.symm_fsdp import multi_linear
 
 
 @dataclass
@@ -75,9 +76,10 @@ class Attention(nn.Module):
     def forward(self, x):
         B, T, _ = x.shape
         c = self.cfg
-        q = self.wq(x).view(B, T, c.n_heads, c.head_dim)
-        k = self.wk(x).view(B, T, c.n_kv_heads, c.head_dim)
-        v = self.wv(x).view(B, T, c.n_kv_heads, c.head_dim)
+        q, k, v = multi_linear(x, (self.wq, self.wk, self.wv))
+        q = q.view(B, T, c.n_heads, c.head_dim)
+        k = k.view(B, T, c.n_kv_heads, c.head_dim)
+        v = v.view(B, T, c.n_kv_heads, c.head_dim)
         q = apply_rope(q, c.rope_theta)
         k = apply_rope(k, c.rope_theta)
         o = causal_attention(q, k, v)
@@ -92,7 +94,8 @@ class FeedForward(nn.Module):
         self.w2 = nn.Linear(cfg.ffn_dim, cfg.dim, bias=False)
 
     def forward(self, x):
-        return self.w2(swiglu(self.w1(x), self.w3(x)))
+        gate, up = multi_linear(x, (self.w1, self.w3))
+        return self.w2(swiglu(gate, up))
 
 
 class TransformerBlock(nn.Module):

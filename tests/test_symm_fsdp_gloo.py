@@ -120,3 +120,56 @@ def test_symm_fsdp_training_matches_single_process():
             o.zero_grad(set_to_none=True)
     for n, p in ref.named_parameters():
         assert rel_err(got["params"][n], p.detach()) < 1e-4, n
+
+
+class GatedBlock(nn.Module):
+    """Two projections of the same input (as q/k/v or gate/up) through multi_linear."""
+
+    def __init__(self):
+        super().__init__()
+        self.gate = nn.Linear(D, H, bias=False)
+        self.up = nn.Linear(D, H, bias=False)
+        self.down = nn.Linear(H, D, bias=False)
+
+    def forward(self, x):
+        from my_muon_fsdp2_b200.parallel.symm_fsdp import multi_linear
+
+        g, u = multi_linear(x, (self.gate, self.up))
+        return x + self.down(torch.nn.functional.silu(g) * u)
+
+
+class GatedNet(nn.Module):
+    def __init__(self):
+        super().__init__()
+        torch.manual_seed(1)
+        self.inp = nn.Linear(32, D)
+        self.layers = nn.ModuleList([GatedBlock() for _ in range(2)])
+        self.out = nn.Linear(D, 8)
+
+    def forward(self, x):
+        x = self.inp(x)
+        for b in self.layers:
+            x = b(x)
+        return self.out(x)
+
+
+def _gated_grads(rank, world):
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    model = GatedNet()
+    apply_symm_fsdp(model)
+    for step in range(2):
+        model.set_requires_gradient_sync(step == 1)
+        x, y = _data(step, rank)
+        ((model(x) - y) ** 2).mean().div(2).backward()
+    return {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+
+
+def test_symm_fsdp_multi_linear_grads_match_single_process():
+    got = run_ranks(_gated_grads, 2)
+    ref = GatedNet()
+    for step in range(2):
+        xs, ys = zip(*[_data(step, r) for r in range(2)])
+        ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
+    for n, p in ref.named_parameters():
+        assert rel_err(got[n], p.grad) < 1e-5, n
