@@ -184,41 +184,44 @@ class SymmFSDP:
             off += (s + 7) // 8 * 8  # 16-byte aligned shards
         total = max(off, 8)
         dtype = self.modules[0].weight.dtype
-        if self.fused:
+        # peer-mapped (symmetric) buffers only when there are peers; one rank keeps plain memory
+        self.peer = self.fused and self.world > 1
+        if self.peer:
             import torch.distributed._symmetric_memory as symm_mem
 
             self._sm = symm_mem
             self.shard_buf = symm_mem.empty(total, dtype=dtype, device=self.device)
             self.shard_handle = self._rendezvous(self.shard_buf)
-            slot_elems = max(sizes) * self.world
-            self.slot_elems = slot_elems
-            self.slot_buf = symm_mem.empty(2 * slot_elems, dtype=dtype, device=self.device)
-            self.slot_handle = self._rendezvous(self.slot_buf)
-            self.pad_ptrs = torch.tensor(list(self.slot_handle.signal_pad_ptrs), dtype=torch.int64,
-                                         device=self.device)
             self.ready = torch.zeros(max(n for n, _ in self.shapes) // PANEL + 1, dtype=torch.int32,
                                      device=self.device)
-            self._slot_ptrs = [
-                torch.tensor([int(self.slot_handle.buffer_ptrs[s]) + 2 * (b * slot_elems + self.rank * (slot_elems // self.world))
-                              for s in range(self.world)], dtype=torch.int64, device=self.device)
-                for b in range(2)
-            ]
-            self._meta: Dict[int, torch.Tensor] = {}
-            if rs_mode == "overlap" and self.world > 1:
+            if rs_mode == "fused":
+                # receive slots, double-buffered: [2][world][largest shard] (epilogue P2P stores)
+                slot_elems = max(sizes) * self.world
+                self.slot_elems = slot_elems
+                self.slot_buf = symm_mem.empty(2 * slot_elems, dtype=dtype, device=self.device)
+                sync_handle = self._rendezvous(self.slot_buf)
+                self._slot_ptrs = [
+                    torch.tensor([int(sync_handle.buffer_ptrs[s_]) + 2 * (b * slot_elems + self.rank * (slot_elems // self.world))
+                                  for s_ in range(self.world)], dtype=torch.int64, device=self.device)
+                    for b in range(2)
+                ]
+                self._meta: Dict[int, torch.Tensor] = {}
+            else:
                 # unsharded partial dW of every weight, peer-readable: the reduce-scatter pulls
                 # each rank's rows from all ranks on a side stream while backward continues
-                full_sizes = [n * k for n, k in self.shapes]
                 self.acc_offsets, o = [], 0
-                for fs in full_sizes:
+                for n, k in self.shapes:
                     self.acc_offsets.append(o)
-                    o += (fs + 7) // 8 * 8
+                    o += (n * k + 7) // 8 * 8
                 self.acc_buf = symm_mem.empty(max(o, 8), dtype=dtype, device=self.device)
-                self.acc_handle = self._rendezvous(self.acc_buf)
-                self._acc_ptrs = torch.tensor([int(self.acc_handle.buffer_ptrs[s_]) for s_ in range(self.world)],
+                sync_handle = self._rendezvous(self.acc_buf)
+                self._acc_ptrs = torch.tensor([int(sync_handle.buffer_ptrs[s_]) for s_ in range(self.world)],
                                               dtype=torch.int64, device=self.device)
                 self.comm = torch.cuda.Stream(device=self.device)
                 self.comm_epoch = 0
                 self._join_queued = False
+            # barriers use the signal pads of the synchronisation buffer's allocation
+            self.pad_ptrs = torch.tensor(list(sync_handle.signal_pad_ptrs), dtype=torch.int64, device=self.device)
         else:
             self.shard_buf = torch.empty(total, dtype=dtype, device=self.device)
         self.epoch = 0
@@ -305,7 +308,7 @@ class SymmFSDP:
         n, k = self.shapes[i]
         if self.full[i] is None:
             self.full[i] = torch.empty(n, k, dtype=x2.dtype, device=x2.device)
-        if self.fused:
+        if self.peer:
             if not self._step_synced:
                 # every rank has finished writing its shards (optimizer step) before any reads them
                 self._barrier()
@@ -353,7 +356,7 @@ class SymmFSDP:
     def _accumulate_grad(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         n, k = self.shapes[i]
         r = self.rows[i]
-        overlap = self.fused and self.world > 1 and self.rs_mode == "overlap"
+        overlap = self.peer and self.rs_mode == "overlap"
         if overlap and self.acc[i] is None:
             o = self.acc_offsets[i]
             self.acc[i] = self.acc_buf[o:o + n * k].view(n, k)
@@ -380,7 +383,7 @@ class SymmFSDP:
             else:
                 torch.mm(dy2.t(), x2, out=g)
             return
-        if not self.fused:
+        if not self.peer:
             dw = (dy2.t().float() @ x2.float())
             if carry is not None:
                 dw += carry.float()
