@@ -173,3 +173,37 @@ def test_symm_fsdp_multi_linear_grads_match_single_process():
         ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
     for n, p in ref.named_parameters():
         assert rel_err(got[n], p.grad) < 1e-5, n
+
+
+def _ckpt_roundtrip(rank, world, path):
+    from my_muon_fsdp2_b200 import MuonOptimizer
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+    from my_muon_fsdp2_b200.train import load_checkpoint, save_checkpoint
+
+    model = Net()
+    ctl = apply_symm_fsdp(model)
+    opt = MuonOptimizer(list(ctl.params), lr=0.02, momentum=0.95)
+    ctl.attach_optimizer(opt)
+    x, y = _data(0, rank)
+    ((model(x) - y) ** 2).mean().backward()
+    opt.step()
+    opt.zero_grad(set_to_none=True)
+    save_checkpoint(path, "net", model, opt, epoch=1, loss=0.0)
+    ref_out = model(x).detach()
+
+    torch.manual_seed(123)  # different init: the checkpoint must overwrite it
+    fresh = Net()
+    for p in fresh.parameters():
+        torch.nn.init.normal_(p)
+    ctl2 = apply_symm_fsdp(fresh)
+    opt2 = MuonOptimizer(list(ctl2.params), lr=0.02, momentum=0.95)
+    fresh(x)  # gathers the pre-load weights, which the load must invalidate
+    meta = load_checkpoint(f"{path}/muon_net.pt", fresh, opt2)
+    out = fresh(x).detach()
+    return {"ref": ref_out, "out": out, "epoch": meta["epoch"]}
+
+
+def test_symm_fsdp_checkpoint_roundtrip(tmp_path):
+    got = run_ranks(_ckpt_roundtrip, 2, str(tmp_path))
+    assert got["epoch"] == 1
+    assert rel_err(got["out"], got["ref"]) < 1e-6
