@@ -66,7 +66,7 @@ def _sharded_worker(rank, world, kind, steps, dims):
 
 @pytest.mark.parametrize("kind", ["fsdp", "muon", "model_muon"])
 def test_sharded_equals_single_process(kind):
-    """BASELINE config-1 shape (MLP 512->2048->512, ws=2, gloo), shortened to 6 steps."""
+    """The CPU/gloo MLP workload (512->2048->512, world size 2), shortened to 6 steps."""
     dims, steps = (512, 2048, 512), 6
     res = run_ranks(_sharded_worker, 2, kind, steps, dims)
     model = _mlp(0, *dims)
