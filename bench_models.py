@@ -39,6 +39,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="fsdp2",
+                    help="gpt2 (ours): fully_shard everywhere, or the block linears on the fused collectives")
     return ap.parse_args()
 
 
@@ -66,7 +68,7 @@ def ref_muon():
     return MuonOptimizer
 
 
-def build_encoder(impl, dev):
+def build_encoder(impl, dev, fsdp="fsdp2"):
     from torch.distributed.fsdp import fully_shard
 
     torch.manual_seed(0)
@@ -92,7 +94,7 @@ def build_encoder(impl, dev):
     return model, mats, rest, batch, loss_fn, B * T
 
 
-def build_gpt2(impl, dev):
+def build_gpt2(impl, dev, fsdp="fsdp2"):
     from torch.distributed.fsdp import fully_shard
 
     torch.manual_seed(0)
@@ -101,7 +103,12 @@ def build_gpt2(impl, dev):
         from my_muon_fsdp2_b200.models.gpt2 import GPT2SmallConfig, GPTModel
 
         model = GPTModel(GPT2SmallConfig()).to(dev, torch.bfloat16)
-        model.configure_fsdp()
+        if fsdp == "symm":
+            from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+            apply_symm_fsdp(model, blocks_attr="h")
+        else:
+            model.configure_fsdp()
         names = set(model.muon_param_names())
 
         def loss_fn(x, y):
@@ -136,12 +143,15 @@ def main():
     dev = torch.device("cuda", local)
     try:
         build = build_encoder if args.model == "encoder" else build_gpt2
-        model, mats, rest, batch, loss_fn, tokens_per_gpu = build(args.impl, dev)
+        model, mats, rest, batch, loss_fn, tokens_per_gpu = build(args.impl, dev, args.fsdp)
         if args.impl == "ours":
             from my_muon_fsdp2_b200 import FusedAdamW, MuonOptimizer
 
             opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95, weight_decay=0.01),
                     FusedAdamW(rest, lr=1e-3, weight_decay=0.01)]
+            ctl = getattr(model, "_symm_fsdp", None)
+            for o in opts if ctl is not None else []:
+                ctl.attach_optimizer(o)
         else:
             Muon = ref_muon()
             opts = [Muon(mats, lr=0.02, momentum=0.95, weight_decay=0.01),
@@ -185,7 +195,7 @@ def main():
                           "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
                           "data": "synthetic; random-init weights", "final_loss": float(loss.item()),
                           "config": {"model": args.model, "tokens_per_gpu": tokens_per_gpu,
-                                     "parallelism": f"fsdp{world}"}}))
+                                     "parallelism": f"fsdp{world}", "fsdp_impl": args.fsdp}}))
     dist.barrier()
     dist.destroy_process_group()
 

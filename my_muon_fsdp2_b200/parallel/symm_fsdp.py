@@ -122,11 +122,13 @@ def multi_linear(x: torch.Tensor, modules: Sequence[nn.Module]) -> Tuple[torch.T
         x2 = x2.contiguous()
     idxs = tuple(m._symm_idx for m in modules)
     ys = _SymmMultiLinearFn.apply(x2, ctl, idxs, *[m.weight for m in modules])
-    return tuple(y.view(*x.shape[:-1], y.shape[-1]) for y in ys)
+    ys = tuple(y.view(*x.shape[:-1], y.shape[-1]) for y in ys)
+    return tuple(y if m.bias is None else y + m.bias for y, m in zip(ys, modules))
 
 
 class SymmLinear(nn.Linear):
-    """``nn.Linear`` (no bias) whose weight is a row shard in symmetric memory."""
+    """``nn.Linear`` whose weight is a row shard in symmetric memory (a bias stays an ordinary
+    parameter, added after the product)."""
 
     _symm_ctl: "SymmFSDP"
     _symm_idx: int
@@ -136,12 +138,13 @@ class SymmLinear(nn.Linear):
         if not x2.is_contiguous():
             x2 = x2.contiguous()
         y = _SymmLinearFn.apply(x2, self.weight, self._symm_ctl, self._symm_idx)
-        return y.view(*x.shape[:-1], y.shape[-1])
+        y = y.view(*x.shape[:-1], y.shape[-1])
+        return y if self.bias is None else y + self.bias
 
 
 class SymmFSDP:
-    """Owns the shard buffer, the resident full weights and the reduce-scatter slots of a set of
-    bias-free linear layers, all sharded over one process group."""
+    """Owns the shard buffer, the resident full weights and the reduce-scatter buffers of a set of
+    linear layers (weights only; biases stay with the module), all sharded over one group."""
 
     def __init__(self, linears: Sequence[nn.Linear], mesh=None, group: Optional[dist.ProcessGroup] = None,
                  device: Optional[torch.device] = None, wait_s: float = 2e-3, barrier_timeout_s: float = 60.0,
@@ -167,14 +170,9 @@ class SymmFSDP:
         self.modules: List[nn.Linear] = list(linears)
         self.shapes: List[Tuple[int, int]] = []
         for m in self.modules:
-            if m.bias is not None:
-                raise ValueError("SymmFSDP: linear layers with a bias are not supported")
             n, k = m.weight.shape
             if n % self.world:
                 raise ValueError(f"SymmFSDP: out_features {n} is not divisible by the world size {self.world}")
-            if self.fused and not fusable_shape(n, k, self.world):
-                raise ValueError(f"SymmFSDP: weight {n}x{k} does not fit the fused kernels at world size "
-                                 f"{self.world} (need N % 256 == 0, (N/world) % 128 == 0, K % 256 == 0)")
             self.shapes.append((n, k))
         self.rows = [n // self.world for n, _ in self.shapes]
         sizes = [r * k for r, (_, k) in zip(self.rows, self.shapes)]
@@ -186,6 +184,9 @@ class SymmFSDP:
         dtype = self.modules[0].weight.dtype
         # peer-mapped (symmetric) buffers only when there are peers; one rank keeps plain memory
         self.peer = self.fused and self.world > 1
+        # weights whose shapes the fused kernels take (N % 256, (N/world) % 128, K % 256); the
+        # others gather / reduce-scatter through NCCL, still once per step for the gather
+        self.fused_ok = [self.peer and fusable_shape(n, k, self.world) for n, k in self.shapes]
         if self.peer:
             import torch.distributed._symmetric_memory as symm_mem
 
@@ -194,6 +195,8 @@ class SymmFSDP:
             self.shard_handle = self._rendezvous(self.shard_buf)
             self.ready = torch.zeros(max(n for n, _ in self.shapes) // PANEL + 1, dtype=torch.int32,
                                      device=self.device)
+            if not any(self.fused_ok):
+                self.ready = None
             if rs_mode == "fused":
                 # receive slots, double-buffered: [2][world][largest shard] (epilogue P2P stores)
                 slot_elems = max(sizes) * self.world
@@ -308,7 +311,10 @@ class SymmFSDP:
         n, k = self.shapes[i]
         if self.full[i] is None:
             self.full[i] = torch.empty(n, k, dtype=x2.dtype, device=x2.device)
-        if self.peer:
+        if self.peer and not self.fused_ok[i]:
+            dist.all_gather_into_tensor(self.full[i], self._local(i).contiguous(), group=self.group)
+            y = F.linear(x2, self.full[i])
+        elif self.peer:
             if not self._step_synced:
                 # every rank has finished writing its shards (optimizer step) before any reads them
                 self._barrier()
@@ -356,7 +362,10 @@ class SymmFSDP:
     def _accumulate_grad(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         n, k = self.shapes[i]
         r = self.rows[i]
-        overlap = self.peer and self.rs_mode == "overlap"
+        overlap = self.peer and self.rs_mode == "overlap" and self.fused_ok[i]
+        if self.peer and not self.fused_ok[i] and self.sync_grads:
+            self._nccl_reduce_scatter(i, dy2, x2)
+            return
         if overlap and self.acc[i] is None:
             o = self.acc_offsets[i]
             self.acc[i] = self.acc_buf[o:o + n * k].view(n, k)
@@ -409,6 +418,23 @@ class SymmFSDP:
         slots = self.slot_buf[b * self.slot_elems:(b + 1) * self.slot_elems]
         ext.rs_reduce(slots, self.world, self.slot_elems // self.world, g, acc, 1.0 / self.world)
 
+    def _nccl_reduce_scatter(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
+        """Weights the fused kernels do not take: partial dW (+ the no-sync accumulation), then
+        NCCL's averaging reduce-scatter into the gradient shard."""
+        n, k = self.shapes[i]
+        if self.acc_live[i]:
+            part = self.acc[i].addmm_(dy2.t(), x2)
+        else:
+            part = dy2.t() @ x2
+        self.acc_live[i] = False
+        g, acc = self._grad_local(i)
+        if acc:
+            tmp = torch.empty_like(g)
+            dist.reduce_scatter_tensor(tmp, part, op=dist.ReduceOp.AVG, group=self.group)
+            g.add_(tmp)
+        else:
+            dist.reduce_scatter_tensor(g, part, op=dist.ReduceOp.AVG, group=self.group)
+
     def _overlapped_reduce_scatter(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         """Synchronising backward of weight i (overlap mode): local partial GEMM, then the
         reduce-scatter on the side stream, overlapped with the rest of the backward."""
@@ -440,19 +466,23 @@ class SymmFSDP:
 
 
 def block_linears(model: nn.Module, blocks_attr: str = "layers") -> List[nn.Linear]:
+    """The ``nn.Linear`` modules of the blocks that run through their own ``forward`` (the
+    projections inside ``nn.MultiheadAttention`` are read as raw weights, so they stay out)."""
     out = []
     for blk in getattr(model, blocks_attr):
+        inside_mha = {id(c) for m in blk.modules() if isinstance(m, nn.MultiheadAttention) for c in m.modules()}
         for m in blk.modules():
-            if isinstance(m, nn.Linear) and m.bias is None:
+            if isinstance(m, nn.Linear) and id(m) not in inside_mha:
                 out.append(m)
     return out
 
 
 def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str = "layers",
                     reshard_after_forward: Optional[bool] = None, rs_mode: str = "overlap") -> SymmFSDP:
-    """Shard every bias-free linear of the transformer blocks on symmetric memory (fused
-    all-gather/reduce-scatter kernels) and ``fully_shard`` the rest of the model (embeddings,
-    norms, LM head) with FSDP2, the linears passed as ``ignored_params``.  A model on the meta
+    """Shard the weights of the transformer blocks' linears on symmetric memory (fused
+    all-gather/reduce-scatter kernels where the shapes allow, NCCL otherwise; gathered once per
+    step either way) and ``fully_shard`` the rest of the model (embeddings, norms, biases, LM
+    head) with FSDP2, the linear weights passed as ``ignored_params``.  A model on the meta
     device is materialised on ``device``.  Returns the controller (``model._symm_fsdp``)."""
     from torch.distributed.fsdp import fully_shard
 

@@ -207,3 +207,55 @@ def test_symm_fsdp_checkpoint_roundtrip(tmp_path):
     got = run_ranks(_ckpt_roundtrip, 2, str(tmp_path))
     assert got["epoch"] == 1
     assert rel_err(got["out"], got["ref"]) < 1e-6
+
+
+class BiasBlock(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.norm = nn.LayerNorm(D)
+        self.up = nn.Linear(D, H)       # with bias
+        self.down = nn.Linear(H, D)
+        self.attn = nn.MultiheadAttention(D, 4, batch_first=True)  # its projections stay out
+
+    def forward(self, x):
+        h = self.norm(x)
+        a, _ = self.attn(h[:, None], h[:, None], h[:, None])
+        return x + a[:, 0] + self.down(torch.nn.functional.gelu(self.up(h)))
+
+
+class BiasNet(nn.Module):
+    def __init__(self):
+        super().__init__()
+        torch.manual_seed(2)
+        self.inp = nn.Linear(32, D)
+        self.layers = nn.ModuleList([BiasBlock() for _ in range(2)])
+        self.out = nn.Linear(D, 8)
+
+    def forward(self, x):
+        x = self.inp(x)
+        for b in self.layers:
+            x = b(x)
+        return self.out(x)
+
+
+def _bias_grads(rank, world):
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmLinear, apply_symm_fsdp
+
+    model = BiasNet()
+    ctl = apply_symm_fsdp(model)
+    assert len(ctl.params) == 4  # up/down of two blocks; the attention projections stay out
+    assert not isinstance(model.layers[0].attn.out_proj, SymmLinear)
+    for step in range(2):
+        x, y = _data(step, rank)
+        ((model(x) - y) ** 2).mean().div(2).backward()
+    return {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+
+
+def test_symm_fsdp_biased_linears_match_single_process():
+    got = run_ranks(_bias_grads, 2)
+    ref = BiasNet()
+    for step in range(2):
+        xs, ys = zip(*[_data(step, r) for r in range(2)])
+        ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
+    for n, p in ref.named_parameters():
+        assert rel_err(got[n], p.grad) < 1e-5, n
