@@ -36,6 +36,23 @@ def run_kernels(rank, world, dev):
     return res
 
 
+def run_mixed(rank, world, dev):
+    """A weight the fused kernels take next to one they do not (NCCL path), both with biases."""
+    from my_muon_fsdp2_b200._ext import check_device_error
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmFSDP
+
+    res = {}
+    torch.manual_seed(0)
+    lins = [nn.Linear(512, 256 * world).to(dev, torch.bfloat16), nn.Linear(512, 192 * world).to(dev, torch.bfloat16)]
+    fulls = [m.weight.detach().clone() for m in lins]
+    ctl = SymmFSDP(lins, device=dev)
+    res["fused_ok"] = list(ctl.fused_ok)
+    _check_linears(ctl, lins, fulls, rank, world, dev, res, "mixed")
+    torch.cuda.synchronize()
+    check_device_error(dev.index)
+    return res
+
+
 def _check_linears(ctl, lins, fulls, rank, world, dev, res, mode):
     for i, (m, w) in enumerate(zip(lins, fulls)):
         for t in (256, 200):  # 200: token count padded to the tile size inside
@@ -46,6 +63,8 @@ def _check_linears(ctl, lins, fulls, rank, world, dev, res, mode):
             y = m(x)  # fused all-gather GEMM
             y2 = m(x)  # resident full weight
             ref = x.detach().float() @ w.float().t()
+            if m.bias is not None:
+                ref = ref + m.bias.detach().float()
             res[f"y{i}_{t}_{mode}"] = ((y.float() - ref).norm() / ref.norm()).item()
             res[f"y2{i}_{t}_{mode}"] = ((y2.float() - ref).norm() / ref.norm()).item()
             res[f"g{i}_{t}_{mode}"] = bool(torch.equal(ctl.full[i], w))
@@ -143,7 +162,7 @@ def run_split(rank, world, dev, steps=2):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["kernels", "train", "split"], required=True)
+    ap.add_argument("--mode", choices=["kernels", "train", "split", "mixed"], required=True)
     ap.add_argument("--out", required=True)
     a = ap.parse_args()
     local = int(os.environ["LOCAL_RANK"])
@@ -152,7 +171,8 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
     try:
-        res = {"kernels": run_kernels, "train": run_train, "split": run_split}[a.mode](rank, world, dev)
+        res = {"kernels": run_kernels, "train": run_train, "split": run_split, "mixed": run_mixed}[a.mode](
+            rank, world, dev)
         if rank == 0:
             torch.save(res, a.out)
         dist.barrier()

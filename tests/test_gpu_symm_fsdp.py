@@ -54,3 +54,15 @@ def test_cooperative_ns_schedule_matches_owner_computes():
         res = _run(2, "split", os.path.join(d, "s.pt"))
     for n in res["never"]:
         assert rel_err(res["always"][n], res["never"][n]) < 2e-2, n
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_mixed_fused_and_nccl_weights_with_bias():
+    with tempfile.TemporaryDirectory() as d:
+        res = _run(2, "mixed", os.path.join(d, "m.pt"))
+    assert res.pop("fused_ok") == [True, False]
+    for k, v in res.items():
+        if k.startswith("g"):
+            assert v, f"{k}: gathered weight differs from the full weight"
+        else:
+            assert v < 1e-2, f"{k}: relative error {v}"
