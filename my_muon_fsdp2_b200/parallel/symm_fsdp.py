@@ -150,17 +150,29 @@ class SymmFSDP:
                  device: Optional[torch.device] = None, wait_s: float = 2e-3, barrier_timeout_s: float = 60.0,
                  rs_mode: str = "overlap"):
         from torch.distributed.device_mesh import init_device_mesh
-        from torch.distributed.tensor import DTensor, Shard
+        from torch.distributed.tensor import DTensor, Replicate, Shard
 
+        # A 2-D mesh (dp_replicate, fsdp_shard) is HSDP: weights are sharded over the last mesh
+        # dimension and replicated over the first; gradients are reduce-scattered inside the
+        # shard group, then averaged over the replicas.
+        self.rgroup: Optional[dist.ProcessGroup] = None
+        if mesh is not None and mesh.ndim == 2:
+            if group is None:
+                group = mesh.get_group(1)
+            self.rgroup = mesh.get_group(0)
+        elif mesh is not None and mesh.ndim != 1:
+            raise ValueError("SymmFSDP: the mesh must be 1-D (shard) or 2-D (replicate, shard)")
         if group is None:
             group = mesh.get_group() if mesh is not None else dist.group.WORLD
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self.replicas = dist.get_world_size(self.rgroup) if self.rgroup is not None else 1
         self.device = torch.device(device) if device is not None else linears[0].weight.device
         if mesh is None:
             mesh = init_device_mesh(self.device.type, (self.world,))
         self.mesh = mesh
+        self.placements = [Replicate(), Shard(0)] if mesh.ndim == 2 else [Shard(0)]
         self.wait_s = float(wait_s)
         self.barrier_timeout_s = float(barrier_timeout_s)
         if rs_mode not in ("overlap", "fused"):
@@ -246,7 +258,7 @@ class SymmFSDP:
                 if isinstance(src, DTensor):
                     src = src.full_tensor()
                 local.copy_(src[self.rank * r:(self.rank + 1) * r])
-            p = nn.Parameter(DTensor.from_local(local, self.mesh, [Shard(0)], run_check=False, shape=(n, k),
+            p = nn.Parameter(DTensor.from_local(local, self.mesh, self.placements, run_check=False, shape=(n, k),
                                                 stride=(k, 1)), requires_grad=w.requires_grad)
             del m._parameters["weight"]
             m.weight = p
@@ -348,6 +360,16 @@ class SymmFSDP:
         self._accumulate_grad(i, dy2, x2)
         return dx
 
+    def _replica_average(self, g: torch.Tensor) -> None:
+        """HSDP: average a gradient shard over the replicas (no-op on a 1-D mesh)."""
+        if self.rgroup is None or self.replicas == 1:
+            return
+        if g.is_cuda:
+            dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.rgroup)
+        else:
+            dist.all_reduce(g, group=self.rgroup)
+            g.div_(self.replicas)
+
     def _grad_local(self, i: int) -> Tuple[torch.Tensor, bool]:
         from torch.distributed.tensor import DTensor, Shard
 
@@ -355,7 +377,8 @@ class SymmFSDP:
         if p.grad is None:
             n, k = self.shapes[i]
             local = torch.empty(self.rows[i], k, dtype=p.dtype, device=self.device)
-            p.grad = DTensor.from_local(local, self.mesh, [Shard(0)], run_check=False, shape=(n, k), stride=(k, 1))
+            p.grad = DTensor.from_local(local, self.mesh, self.placements, run_check=False, shape=(n, k),
+                                        stride=(k, 1))
             return local, False
         return p.grad.to_local(), True
 
@@ -391,6 +414,8 @@ class SymmFSDP:
                 g.addmm_(dy2.t(), x2)
             else:
                 torch.mm(dy2.t(), x2, out=g)
+            if self.sync_grads:
+                self._replica_average(g)
             return
         if not self.peer:
             dw = (dy2.t().float() @ x2.float())
@@ -402,6 +427,7 @@ class SymmFSDP:
                 g.add_(dw)
             else:
                 g.copy_(dw)
+            self._replica_average(g)
             return
         ext = _ext()
         meta = self._meta.get(i)
@@ -417,6 +443,7 @@ class SymmFSDP:
         self._barrier()
         slots = self.slot_buf[b * self.slot_elems:(b + 1) * self.slot_elems]
         ext.rs_reduce(slots, self.world, self.slot_elems // self.world, g, acc, 1.0 / self.world)
+        self._replica_average(g)
 
     def _nccl_reduce_scatter(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         """Weights the fused kernels do not take: partial dW (+ the no-sync accumulation), then
@@ -434,6 +461,7 @@ class SymmFSDP:
             g.add_(tmp)
         else:
             dist.reduce_scatter_tensor(g, part, op=dist.ReduceOp.AVG, group=self.group)
+        self._replica_average(g)
 
     def _overlapped_reduce_scatter(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         """Synchronising backward of weight i (overlap mode): local partial GEMM, then the
@@ -457,6 +485,7 @@ class SymmFSDP:
             self._comm_barrier()
             _ext().rs_pull_reduce(self._acc_ptrs, self.acc_offsets[i] + self.rank * r * k, g, acc, 1.0 / self.world)
             self._comm_barrier()
+            self._replica_average(g)
         if not self._join_queued:
             self._join_queued = True
             try:

@@ -259,3 +259,64 @@ def test_symm_fsdp_biased_linears_match_single_process():
         ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
     for n, p in ref.named_parameters():
         assert rel_err(got[n], p.grad) < 1e-5, n
+
+
+def _hsdp_run(rank, world, steps):
+    """2 x 2 mesh (replicate, shard): weights sharded over pairs of ranks, replicated across
+    the pairs; gradients reduce-scattered in the shard group, then averaged over replicas."""
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from my_muon_fsdp2_b200 import MuonOptimizer
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    mesh = init_device_mesh("cpu", (2, 2), mesh_dim_names=("replicate", "shard"))
+    model = Net()
+    ctl = apply_symm_fsdp(model, mesh=mesh)
+    assert ctl.world == 2 and ctl.replicas == 2
+    assert ctl.rank == rank % 2
+    assert [p.placements for p in ctl.params][0][0].is_replicate()
+    # gradients of two micro-batches (the first without sync)
+    for mb in range(2):
+        model.set_requires_gradient_sync(mb == 1)
+        x, y = _data(mb, rank)
+        ((model(x) - y) ** 2).mean().div(2).backward()
+    grads = {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+    for p in model.parameters():
+        p.grad = None
+    mats = list(ctl.params)
+    rest = [p for p in model.parameters() if all(p is not q for q in mats)]
+    opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95, weight_decay=0.01), torch.optim.AdamW(rest, lr=1e-3)]
+    for o in opts:
+        ctl.attach_optimizer(o)
+    for step in range(steps):
+        x, y = _data(10 + step, rank)
+        ((model(x) - y) ** 2).mean().backward()
+        for o in opts:
+            o.step()
+            o.zero_grad(set_to_none=True)
+    return {"grads": grads, "params": {n: _full(p.detach()).clone() for n, p in model.named_parameters()}}
+
+
+def test_symm_fsdp_hsdp_mesh_matches_single_process():
+    from my_muon_fsdp2_b200 import MuonOptimizer
+
+    world, steps = 4, 2
+    got = run_ranks(_hsdp_run, world, steps)
+    ref = Net()
+    for mb in range(2):
+        xs, ys = zip(*[_data(mb, r) for r in range(world)])
+        ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
+    for n, p in ref.named_parameters():
+        assert rel_err(got["grads"][n], p.grad) < 1e-5, n
+    ref.zero_grad(set_to_none=True)
+    mats = [m.weight for b in ref.layers for m in (b.up, b.down)]
+    rest = [p for p in ref.parameters() if all(p is not q for q in mats)]
+    opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95, weight_decay=0.01), torch.optim.AdamW(rest, lr=1e-3)]
+    for step in range(steps):
+        xs, ys = zip(*[_data(10 + step, r) for r in range(world)])
+        ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().backward()
+        for o in opts:
+            o.step()
+            o.zero_grad(set_to_none=True)
+    for n, p in ref.named_parameters():
+        assert rel_err(got["params"][n], p.detach()) < 1e-4, n
