@@ -242,6 +242,11 @@ class SymmFSDP:
         self.epoch = 0
         self.parity = 0
         self.sync_grads = True
+        # cumulative bytes this rank received from its peers (algorithmic counts): weight
+        # all-gathers, gradient reduce-scatters, and the replica all-reduces of HSDP
+        self.bytes_gathered = 0
+        self.bytes_reduced = 0
+        self.bytes_replica = 0
         self.acc: List[Optional[torch.Tensor]] = [None] * len(self.modules)  # unsharded dW (no-sync)
         self.acc_live = [False] * len(self.modules)
         self.params: List[nn.Parameter] = []
@@ -323,6 +328,7 @@ class SymmFSDP:
         n, k = self.shapes[i]
         if self.full[i] is None:
             self.full[i] = torch.empty(n, k, dtype=x2.dtype, device=x2.device)
+        self.bytes_gathered += self._shard_bytes(i, self.full[i].element_size())
         if self.peer and not self.fused_ok[i]:
             dist.all_gather_into_tensor(self.full[i], self._local(i).contiguous(), group=self.group)
             y = F.linear(x2, self.full[i])
@@ -360,10 +366,20 @@ class SymmFSDP:
         self._accumulate_grad(i, dy2, x2)
         return dx
 
+    def _shard_bytes(self, i: int, elem: int) -> int:
+        """Bytes of the other ranks' shards of weight i (what one gather or reduce moves in)."""
+        return (self.world - 1) * self.rows[i] * self.shapes[i][1] * elem
+
+    def stats(self) -> Dict[str, int]:
+        """Cumulative traffic counters (bytes received by this rank)."""
+        return {"bytes_gathered": self.bytes_gathered, "bytes_reduced": self.bytes_reduced,
+                "bytes_replica": self.bytes_replica}
+
     def _replica_average(self, g: torch.Tensor) -> None:
         """HSDP: average a gradient shard over the replicas (no-op on a 1-D mesh)."""
         if self.rgroup is None or self.replicas == 1:
             return
+        self.bytes_replica += 2 * (self.replicas - 1) * g.numel() * g.element_size() // self.replicas
         if g.is_cuda:
             dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.rgroup)
         else:
@@ -409,6 +425,7 @@ class SymmFSDP:
         carry = self.acc[i] if self.acc_live[i] else None
         self.acc_live[i] = False
         g, acc = self._grad_local(i)
+        self.bytes_reduced += self._shard_bytes(i, g.element_size())
         if self.world == 1:
             if acc:
                 g.addmm_(dy2.t(), x2)
@@ -455,6 +472,7 @@ class SymmFSDP:
             part = dy2.t() @ x2
         self.acc_live[i] = False
         g, acc = self._grad_local(i)
+        self.bytes_reduced += self._shard_bytes(i, part.element_size())
         if acc:
             tmp = torch.empty_like(g)
             dist.reduce_scatter_tensor(tmp, part, op=dist.ReduceOp.AVG, group=self.group)
@@ -476,6 +494,7 @@ class SymmFSDP:
             torch.mm(dy2.t(), x2, out=acc_i)
         self.acc_live[i] = False
         g, acc = self._grad_local(i)
+        self.bytes_reduced += self._shard_bytes(i, acc_i.element_size())
         cur = torch.cuda.current_stream(self.device)
         self.comm.wait_stream(cur)
         g.record_stream(self.comm)

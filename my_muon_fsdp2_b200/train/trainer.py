@@ -18,9 +18,11 @@ from ..utils.tracing import nvtx_range
 
 class Trainer:
     def __init__(self, model: nn.Module, optimizers: Sequence, grad_accum: int = 1, device=None,
-                 step_timer=None, max_grad_norm: Optional[float] = None):
+                 step_timer=None, max_grad_norm: Optional[float] = None, time_steps: bool = False):
         """``max_grad_norm``: clip the global gradient norm before the optimizer steps, as the
-        reference trainers do with 1.0 (examples/train_gpt.py:367-371); None disables it."""
+        reference trainers do with 1.0 (examples/train_gpt.py:367-371); None disables it.
+        ``time_steps``: bracket every step with CUDA events (read by ``last_step_ms`` and
+        ``metrics_summary``; no synchronisation inside the step)."""
         self.model = model
         self.max_grad_norm = max_grad_norm
         self.last_grad_norm: Optional[torch.Tensor] = None
@@ -31,6 +33,9 @@ class Trainer:
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
         self.step_timer = step_timer  # optional EventTimer around the optimizer steps
         self.fsdp = is_fsdp_module(model)
+        self.time_steps = bool(time_steps) and self.device.type == "cuda"
+        self._step_events = None
+        self._prev_comm: Optional[dict] = None
         ctl = getattr(model, "_symm_fsdp", None)  # fused-collective linears: regather after each step
         if ctl is not None:
             for opt in self.optimizers:
@@ -50,6 +55,9 @@ class Trainer:
     def step_on_device(self, tokens: torch.Tensor) -> torch.Tensor:
         """One optimizer step on a device batch [grad_accum, micro_bs, seq+1]; returns the loss
         (device tensor, no synchronisation)."""
+        if self.time_steps:
+            t0 = torch.cuda.Event(enable_timing=True)
+            t0.record()
         total = None
         for i in range(self.grad_accum):
             l = self._micro(tokens, i).detach()
@@ -66,6 +74,10 @@ class Trainer:
             self.step_timer.stop()
         for opt in self.optimizers:
             opt.zero_grad(set_to_none=True)
+        if self.time_steps:
+            t1 = torch.cuda.Event(enable_timing=True)
+            t1.record()
+            self._step_events = (t0, t1)
         self.steps += 1
         self.last_metrics = self._metrics(tokens, total)
         return total
@@ -90,7 +102,41 @@ class Trainer:
             m["symm_fsdp/world"] = ctl.world
             m["symm_fsdp/rs_mode"] = ctl.rs_mode
             m["symm_fsdp/resident_weights"] = sum(1 for f in ctl.full if f is not None)
+            cur = ctl.stats()
+            prev = self._prev_comm or {k: 0 for k in cur}
+            for k, v in cur.items():  # this step's traffic
+                m[f"symm_fsdp/{k}"] = v - prev[k]
+            self._prev_comm = cur
         return m
+
+    def last_step_ms(self) -> Optional[float]:
+        """Device time of the last step (waits for it); None unless ``time_steps``."""
+        if self._step_events is None:
+            return None
+        t0, t1 = self._step_events
+        t1.synchronize()
+        return t0.elapsed_time(t1)
+
+    def metrics_summary(self) -> dict:
+        """``last_metrics`` with device values read back (synchronises), plus the step time,
+        tokens/s and the achieved bandwidth of the step's collectives when they are known."""
+        out = {}
+        for k, v in self.last_metrics.items():
+            if isinstance(v, torch.Tensor):
+                out[k] = float(v.detach().float().item())
+            elif hasattr(v, "mean_ms"):
+                out[k.replace("timer", "ms")] = v.mean_ms()
+            else:
+                out[k] = v
+        ms = self.last_step_ms()
+        if ms:
+            out["step_ms"] = ms
+            out["tokens_per_s"] = out["tokens"] / (ms / 1e3)
+            comm = sum(v for k, v in out.items()
+                       if isinstance(v, (int, float)) and (k.endswith("exchange_bytes") or k.startswith("symm_fsdp/bytes")))
+            out["comm_bytes"] = comm
+            out["comm_gbps"] = comm / (ms / 1e3) / 1e9
+        return out
 
     def train_step(self, batch: torch.Tensor) -> float:
         """End-to-end step from a host batch [grad_accum, micro_bs, seq+1] (int64)."""

@@ -88,3 +88,6 @@ def test_trainer_clips_gradient_norm():
     m = trainer.last_metrics
     assert m["step"] == 1 and m["micro_batches"] == 2 and m["tokens"] == 2 * 3 * 8
     assert float(m["grad_norm"]) == float(trainer.last_grad_norm)
+    s = trainer.metrics_summary()  # device values read back; no step timing on CPU
+    assert isinstance(s["loss"], float) and s["grad_norm"] == float(trainer.last_grad_norm)
+    assert "step_ms" not in s and trainer.last_step_ms() is None

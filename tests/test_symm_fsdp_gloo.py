@@ -320,3 +320,23 @@ def test_symm_fsdp_hsdp_mesh_matches_single_process():
             o.zero_grad(set_to_none=True)
     for n, p in ref.named_parameters():
         assert rel_err(got["params"][n], p.detach()) < 1e-4, n
+
+
+def _traffic(rank, world):
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    model = Net()
+    ctl = apply_symm_fsdp(model)
+    x, y = _data(0, rank)
+    for mb in range(2):
+        model.set_requires_gradient_sync(mb == 1)
+        ((model(x) - y) ** 2).mean().backward()
+    return ctl.stats()
+
+
+def test_symm_fsdp_traffic_counters():
+    """One step of two micro-batches: each weight is gathered once and reduce-scattered once
+    (the no-sync micro-batch moves nothing); counts are the other rank's shard bytes."""
+    got = run_ranks(_traffic, 2)
+    shard = sum((H // 2) * D + (D // 2) * H for _ in range(2)) * 4  # fp32, the other rank's rows
+    assert got == {"bytes_gathered": shard, "bytes_reduced": shard, "bytes_replica": 0}
