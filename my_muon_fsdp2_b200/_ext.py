@@ -44,8 +44,27 @@ def launch_count() -> int:
     return int(ext().launch_count()) if available() else 0
 
 
+_ERROR_TEXT = {
+    1: "a TMA producer's wait for a free stage timed out",
+    2: "the MMA issuer's wait for loaded operands timed out",
+    3: "the MMA issuer's wait for a free accumulator timed out",
+    4: "the epilogue's wait for a finished accumulator timed out",
+    5: "a wait on a peer's flag or barrier timed out",
+    6: "a kernel rejected its arguments",
+    7: "debug check: a TMA innermost coordinate is not on a 16-byte boundary",
+    8: "debug check: an index is outside its buffer or segment table",
+}
+
+
+def device_checks() -> bool:
+    """True when the extension was built with the device-side debug checks (MMF_DEVICE_CHECKS=1)."""
+    return bool(ext().device_checks())
+
+
 def check_device_error(device: int = 0) -> None:
-    """Raise if a bounded wait inside one of our kernels timed out (reads and clears the flag)."""
+    """Raise if one of our kernels recorded an error: a bounded wait that timed out, or (debug
+    builds) a failed device-side check.  Reads and clears the error word."""
     code = int(ext().device_error(device))
     if code != 0:
-        raise RuntimeError(f"my_muon_fsdp2_b200: device-side wait timed out (error code {code}) on cuda:{device}")
+        what = _ERROR_TEXT.get(code, "unknown error")
+        raise RuntimeError(f"my_muon_fsdp2_b200: device error code {code} on cuda:{device}: {what}")

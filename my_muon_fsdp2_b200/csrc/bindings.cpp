@@ -632,6 +632,14 @@ int64_t device_error(int64_t device) {
 
 int64_t launch_count() { return static_cast<int64_t>(mmf::launch_count()); }
 
+bool device_checks() {
+#ifdef MMF_DEVICE_CHECKS
+  return true;
+#else
+  return false;
+#endif
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -666,4 +674,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_variant", []() { return static_cast<int64_t>(mmf::gemm_variant()); });
   m.def("device_error", &device_error);
   m.def("launch_count", &launch_count);
+  m.def("device_checks", &device_checks);
 }

@@ -27,7 +27,27 @@ enum ErrCode : int {
   ERR_EPI_TMEM_FULL_TIMEOUT = 4,
   ERR_PEER_FLAG_TIMEOUT = 5,
   ERR_BAD_ARGUMENT = 6,
+  ERR_CHECK_TMA_X = 7,   // debug builds: a TMA innermost coordinate off its 16-byte boundary
+  ERR_CHECK_BOUNDS = 8,  // debug builds: an index outside its buffer or segment table
 };
+
+// Debug-build device checks.  With MMF_DEVICE_CHECKS defined (set MMF_DEVICE_CHECKS=1 when
+// building the extension), MMF_DCHECK(cond, err, code) records `code` in the error word when
+// `cond` is false and yields false, so the caller skips the access.  It never traps: a skipped
+// TMA load leaves its mbarrier short of bytes, and the bounded wait on it unwinds the kernel.
+// Without the macro MMF_DCHECK is the constant true and compiles away.
+#ifdef MMF_DEVICE_CHECKS
+__device__ __forceinline__ bool dcheck_fail(int* err, int code) {
+  atomicCAS(err, 0, code);
+  return false;
+}
+#define MMF_DCHECK(cond, err, code) ((cond) ? true : ::mmf::dcheck_fail((err), (code)))
+#else
+#define MMF_DCHECK(cond, err, code) true
+#endif
+// The TMA rule: the innermost coordinate times the element size is a multiple of 16 bytes.
+#define MMF_DCHECK_TMA_X(x, elem_bytes, err) \
+  MMF_DCHECK((static_cast<long long>(x) * (elem_bytes)) % 16 == 0, (err), ::mmf::ERR_CHECK_TMA_X)
 
 #ifndef MMF_WAIT_TIMEOUT_NS
 #define MMF_WAIT_TIMEOUT_NS 4000000000ull  // 4 s: far above any legitimate single wait

@@ -177,6 +177,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int b, int ro
           if (!tr && col0 + 32 <= p.n_true && (ld & 7) == 0) {
             // contiguous 32-element run of one destination row: 16-byte vector accesses
             const int seg = (p.nseg > 1) ? static_cast<int>(row / seg_rows) : 0;
+            if (!MMF_DCHECK(seg < p.nseg, p.err, ERR_CHECK_BOUNDS)) continue;
             char* T = reinterpret_cast<char*>(segp[seg]);
             const int64_t idx = (static_cast<int64_t>(row) - seg * seg_rows) * ld + col0;
             float val[32];
@@ -222,6 +223,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int b, int ro
             const int64_t r = tr ? col : row;
             const int64_t cc = tr ? row : col;
             const int seg = (p.nseg > 1) ? static_cast<int>(r / seg_rows) : 0;
+#ifdef MMF_DEVICE_CHECKS
+            if (!MMF_DCHECK(seg < p.nseg, p.err, ERR_CHECK_BOUNDS)) return nullptr;
+#endif
             return reinterpret_cast<char*>(segp[seg]) +
                    ((r - seg * seg_rows) * ld + cc) * (p.out_f32 ? 4 : 2);
           };
@@ -231,6 +235,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int b, int ro
             olds[i] = 0.f;
             if (ps != 0.f && col0 + i < p.n_true) {
               const char* a = elem(i);
+#ifdef MMF_DEVICE_CHECKS
+              if (a == nullptr) continue;
+#endif
               olds[i] = p.out_f32 ? *reinterpret_cast<const float*>(a)
                                   : __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(a));
             }
@@ -242,6 +249,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int b, int ro
             if (beta_b != 0.f) val = fmaf(beta_b, c[i], val);
             const float o = fmaf(ps, olds[i], vs * val);
             char* a = elem(i);
+#ifdef MMF_DEVICE_CHECKS
+            if (a == nullptr) continue;
+#endif
             if (p.out_f32)
               *reinterpret_cast<float*>(a) = o;
             else
@@ -730,6 +740,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
           const int panel = 2 * tn + h;
           const int owner = panel / p.pps;
           const int lrow = (panel - owner * p.pps) * AG_PANEL;
+          if (!MMF_DCHECK(owner >= 0 && owner < p.ws && owner < 8, err, ERR_CHECK_BOUNDS)) ok = false;
           src[h] = owner;
           row[h] = lrow;
           if (owner != p.rank) {
@@ -749,6 +760,9 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
             }
           }
         }
+#ifdef MMF_DEVICE_CHECKS
+        if (!ok) break;
+#endif
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, ERR_TMA_EMPTY_TIMEOUT)) {
             ok = false;
@@ -854,6 +868,7 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
         const int kb = rem - lp * p.ppp;
         const int buf = i & 1;
         uint8_t* dst = sP + buf * AG_PIECE_BYTES;
+        if (!MMF_DCHECK(src >= 0 && src < p.ws && src < 8, err, ERR_CHECK_BOUNDS)) break;
         mbar_arrive_expect_tx(&pfull[buf], AG_PIECE_BYTES);
         tma_load_3d(dst, &maps.shard[src], &pfull[buf], kb * BK, lp * AG_PANEL, 0);
         if (!mbar_wait(&pfull[buf], (i >> 1) & 1, err, ERR_TMA_EMPTY_TIMEOUT)) break;

@@ -1,6 +1,7 @@
 """Build script for my_muon_fsdp2_b200 and its sm_100a extension.
 
     python setup.py build_ext --inplace     # builds my_muon_fsdp2_b200/_C*.so in the tree
+    MMF_DEVICE_CHECKS=1 python setup.py build_ext --inplace --force   # debug build with device checks
 
 The extension is compiled for Blackwell only (``-gencode arch=compute_100a,code=sm_100a``);
 passing the arch flag explicitly bypasses torch's own TORCH_CUDA_ARCH_LIST handling.
@@ -20,6 +21,10 @@ NVCC_FLAGS = [
     "-Xptxas", "-warn-spills",
 ]
 CXX_FLAGS = ["-O3", "-std=c++17"]
+if os.environ.get("MMF_DEVICE_CHECKS", "0") == "1":
+    # debug build: device-side index / segment checks that record an error code and skip
+    NVCC_FLAGS.append("-DMMF_DEVICE_CHECKS")
+    CXX_FLAGS.append("-DMMF_DEVICE_CHECKS")
 
 SOURCES = [
     "bindings.cpp",
