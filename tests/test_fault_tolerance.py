@@ -76,7 +76,10 @@ def test_raising_rank_detected_before_next_collective():
 def _delayed_rank(rank, world):
     from my_muon_fsdp2_b200.parallel.fault import FaultInjector, RankFailure, guarded_barrier
 
-    inj = FaultInjector(rank, delay_at=(1, 0, 2.0))
+    import torch.distributed as dist
+
+    inj = FaultInjector(rank, delay_at=(1, 0, 3.0))
+    dist.barrier()  # both ranks start the step together, however late either process came up
     try:
         inj.on_step(0)
         guarded_barrier(timeout_s=0.5)
