@@ -17,7 +17,10 @@ chain runs once per matrix and the ranks split the FLOPs:
    epilogue scatters every rank's row shard of the orthogonalised update into that rank's
    return segment (local buffer for NCCL, the peer's symmetric buffer for P2P);
 5. after the return exchange each rank applies ``p = (1 - lr*wd) * p - lr_eff * O`` to its shard
-   (``muon_prep`` in direct-apply mode).
+   (``muon_prep`` in direct-apply mode).  With ``comm="p2p"`` and parameters that live in
+   peer-mapped storage (the shards of the fused FSDP linears), the owner's final epilogue
+   applies this update straight into every rank's parameter shard instead, and there is no
+   return buffer or local apply for them.
 
 Unsharded (plain) parameters, or a world of one, take the local path: the momentum kernel
 writes directly into the NS workspace and the last GEMM epilogue updates the parameters.
@@ -149,7 +152,7 @@ class MuonEngine:
     """Executes Muon steps for lists of :class:`MuonTask` (see module docstring)."""
 
     def __init__(self, process_group: Optional[dist.ProcessGroup] = None, comm: str = "auto",
-                 max_workspace_bytes: int = 8 << 30, split: str = "auto"):
+                 max_workspace_bytes: int = 8 << 30, split: str = "auto", direct_update: bool = True):
         if comm not in ("auto", "nccl", "p2p"):
             raise ValueError(f"comm must be 'auto', 'nccl' or 'p2p', got {comm!r}")
         if split not in ("auto", "never", "always"):
@@ -159,6 +162,9 @@ class MuonEngine:
         self.split = split
         self.split_count = 0  # matrices of the last step that took the cooperative schedule
         self.max_workspace_bytes = int(max_workspace_bytes)
+        # comm="p2p": write updates straight into parameters that live in peer-mapped storage
+        self.direct_update = bool(direct_update)
+        self._direct_agreed: Dict[tuple, List[bool]] = {}
         self._p2p = None
         self.last_stats: Dict[str, float] = {}
 
@@ -477,7 +483,8 @@ class MuonEngine:
         """Same schedule as :meth:`_sharded`, with the exchange done by our kernels over NVLink:
         momentum -> own symmetric buffer; barrier (+ partial norms to every peer); owner assembly
         reads peer shards (P2P loads); final NS epilogue stores each rank's rows into that rank's
-        buffer (P2P stores); barrier; local apply."""
+        buffer, or for parameters in peer-mapped storage applies the update straight into that
+        rank's parameter shard (P2P loads and stores); barrier; local apply of the rest."""
         from .._ext import ext
         from ..ops.ns_cuda import round_up, run_ns_group, wide_shape
         from .symm import workspace_for
@@ -513,12 +520,16 @@ class MuonEngine:
                         [0] * len(js), [0] * len(js), [shapes[j][1] for j in js], [], [], hp.mode, hp.nesterov,
                         hp.momentum, hp.wd_coupled, sub)
             part.index_copy_(0, torch.tensor(js, device=dev), sub)
+        # parameters in peer-mapped storage (the fused FSDP shards): the owner's final epilogue
+        # applies p <- decay p - lr_eff O straight into every rank's shard of them
+        direct = self._direct_targets(tasks, rows_of, group, dev)
         # 2. barrier: every rank's shards are in place; all partial norms delivered to all ranks
         sw.barrier(payload=part)
         rows_ssq = sw.payload_rows()  # [world, n]
         mine = [j for j in range(n) if owners[j] == rank]
-        groups = _group_by(mine, lambda j: wide_shape(*shapes[j])[:2])
-        for (mw, nw), js in groups.items():
+        groups = _group_by(mine, lambda j: (wide_shape(*shapes[j])[:2],
+                                            tasks[j].local_param.dtype if direct[j] is not None else None))
+        for ((mw, nw), direct_dtype), js in groups.items():
             Mp, Np = round_up(mw), round_up(nw)
             per = 2 * Mp * Np * 2 + 2 * Mp * Mp * 2
             chunk = max(1, min(len(js), self.max_workspace_bytes // max(per, 1)))
@@ -549,23 +560,56 @@ class MuonEngine:
                 for j in sub_js:
                     rws, cls = shapes[j]
                     for d in range(world):
-                        # 4. P2P stores: rows of rank d go straight into rank d's buffer
-                        addrs.append(sw.peer_addr(d, off[d][j]))
+                        # 4. P2P stores: rows of rank d go straight into rank d's parameter shard
+                        #    (direct) or into rank d's buffer
+                        addrs.append(direct[j][d] if direct_dtype is not None else sw.peer_addr(d, off[d][j]))
                     meta += [cls, int(rws > cls), (rws + world - 1) // world]
                 ptrs = torch.tensor(addrs, dtype=torch.int64).to(dev, non_blocking=True)
                 meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
-                run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
-                             nseg=world, out_meta=meta_t, transposed_dest=tall_group)
-        # 5. barrier: all owners' results have landed
+                if direct_dtype is not None:
+                    pvec = _decay_vec([tasks[j].decay for j in sub_js], dev)
+                    vvec = torch.tensor([-tasks[j].lr_eff for j in sub_js], dtype=torch.float32).to(
+                        dev, non_blocking=True)
+                    run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, direct_dtype == torch.float32, False, mw, nw,
+                                 p_scale=1.0, v_scale=1.0, p_scale_vec=pvec, v_scale_vec=vvec, nseg=world,
+                                 out_meta=meta_t, transposed_dest=tall_group)
+                else:
+                    run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
+                                 nseg=world, out_meta=meta_t, transposed_dest=tall_group)
+        # 5. barrier: all owners' results have landed (parameters and buffers)
         sw.barrier()
-        # 6. local apply from the own buffer
+        # 6. local apply from the own buffer (matrices not updated in place by their owner)
+        idx = [j for j in idx if direct[j] is None]
         for key, js in _group_by(idx, lambda j: tasks[j].local_param.dtype).items():
             srcs = [sw.peer_view(rank, off[rank][j], tuple(tasks[j].local_param.shape)) for j in js]
             params = [tasks[j].local_param for j in js]
             E.muon_prep(srcs, [], params, None, [], [], [], [0], [_decay_float(tasks[j].decay) for j in js],
                         [-tasks[j].lr_eff for j in js], MODE_COPY, False, 0.0, 0.0, None)
         self.last_stats = {"matrices": float(n), "owned": float(len(mine)), "exchange_bytes": float(2 * 2 * total),
-                           "comm": "p2p"}
+                           "comm": "p2p", "direct_updates": float(sum(d is not None for d in direct))}
+
+    def _direct_targets(self, tasks: List[MuonTask], rows_of, group: dist.ProcessGroup,
+                        dev: torch.device) -> List[Optional[List[int]]]:
+        """Per matrix, the address of every rank's parameter shard when the parameters live in
+        peer-mapped storage of ``group`` with equal shards (else None).  All ranks must agree:
+        the decision is checked with one collective the first time a parameter layout is seen."""
+        from .symm import peer_param_addrs
+
+        out: List[Optional[List[int]]] = []
+        for j, t in enumerate(tasks):
+            lp = t.local_param
+            addrs = None
+            if self.direct_update and lp.dtype in (torch.bfloat16, torch.float32) and len(set(rows_of[j])) == 1:
+                addrs = peer_param_addrs(lp, group)
+            out.append(addrs)
+        key = tuple((t.local_param.data_ptr(), a is not None) for t, a in zip(tasks, out))
+        agreed = self._direct_agreed.get(key)
+        if agreed is None:
+            flags = torch.tensor([int(a is not None) for a in out], dtype=torch.int32, device=dev)
+            dist.all_reduce(flags, op=dist.ReduceOp.MIN, group=group)
+            agreed = [bool(f) for f in flags.tolist()]
+            self._direct_agreed[key] = agreed
+        return [a if ok else None for a, ok in zip(out, agreed)]
 
     # ---- CUDA pieces of the sharded path
     def _cuda_local_momentum(self, tasks, hp, send, send_off, sumsq) -> None:

@@ -11,7 +11,8 @@ peer (the per-matrix partial sums of squares).
 """
 from __future__ import annotations
 
-from typing import Dict, Optional
+import weakref
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -86,6 +87,42 @@ class SymmWorkspace:
 
 
 _WORKSPACES: Dict[int, SymmWorkspace] = {}
+
+# Peer-mapped storage that holds parameters (the shard buffers of the fused FSDP linears):
+# (weak reference to the buffer, ranks of its group, each rank's base address).  The Muon
+# engine's final epilogue writes a parameter's update straight into every rank's shard of it
+# when the parameter lives here.
+_PEER_STORES: List[Tuple["weakref.ref", Tuple[int, ...], List[int]]] = []
+
+
+def register_peer_storage(buf: torch.Tensor, group: dist.ProcessGroup, buffer_ptrs: Sequence[int]) -> None:
+    """Record a symmetric buffer (same layout on every rank of ``group``) whose views are
+    parameters; ``buffer_ptrs[r]`` is rank r's copy as mapped into this process."""
+    ranks = tuple(dist.get_process_group_ranks(group))
+    _PEER_STORES[:] = [e for e in _PEER_STORES if e[0]() is not None]
+    _PEER_STORES.append((weakref.ref(buf), ranks, [int(x) for x in buffer_ptrs]))
+
+
+def peer_param_addrs(t: torch.Tensor, group: dist.ProcessGroup) -> Optional[List[int]]:
+    """Address of ``t``'s first element in every rank's copy of the registered symmetric
+    buffer that holds it (the same offset on every rank), or None when ``t`` is not in
+    peer-mapped storage of ``group``'s ranks."""
+    if not t.is_contiguous():
+        return None
+    ptr = t.data_ptr()
+    ranks = None
+    for ref, rk, bases in _PEER_STORES:
+        buf = ref()
+        if buf is None or buf.device != t.device:
+            continue
+        lo = buf.data_ptr()
+        if lo <= ptr and ptr + t.numel() * t.element_size() <= lo + buf.numel() * buf.element_size():
+            if ranks is None:
+                ranks = tuple(dist.get_process_group_ranks(group))
+            if rk != ranks:
+                return None
+            return [b + (ptr - lo) for b in bases]
+    return None
 
 
 def workspace_for(group: dist.ProcessGroup, device: torch.device) -> SymmWorkspace:

@@ -205,6 +205,10 @@ class SymmFSDP:
             self._sm = symm_mem
             self.shard_buf = symm_mem.empty(total, dtype=dtype, device=self.device)
             self.shard_handle = self._rendezvous(self.shard_buf)
+            # the Muon engine may write updates straight into every rank's shards
+            from .symm import register_peer_storage
+
+            register_peer_storage(self.shard_buf, group, self.shard_handle.buffer_ptrs)
             self.ready = torch.zeros(max(n for n, _ in self.shapes) // PANEL + 1, dtype=torch.int32,
                                      device=self.device)
             if not any(self.fused_ok):

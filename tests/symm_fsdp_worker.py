@@ -119,7 +119,9 @@ def run_train(rank, world, dev, steps=3):
             losses.append(tot)
         params = {n: (p.full_tensor() if hasattr(p, "full_tensor") else p).detach().float().cpu()
                   for n, p in model.named_parameters()}
-        out[mode] = {"losses": losses, "params": params}
+        # matrices whose owner wrote the update straight into every rank's parameter shard
+        direct = float(opts[0]._engine.last_stats.get("direct_updates", 0.0))
+        out[mode] = {"losses": losses, "params": params, "direct_updates": direct}
         del model, opts
         torch.cuda.synchronize()
     return out

@@ -42,6 +42,7 @@ def test_symm_fsdp_training_matches_fsdp2():
     with tempfile.TemporaryDirectory() as d:
         res = _run(2, "train", os.path.join(d, "t.pt"))
     a, b = res["symm"], res["fsdp2"]
+    assert a["direct_updates"] > 0 and b["direct_updates"] == 0  # in-place peer updates on symm shards only
     for x, y in zip(a["losses"], b["losses"]):
         assert abs(x - y) < 2e-2 * abs(y), (a["losses"], b["losses"])
     for n in b["params"]:

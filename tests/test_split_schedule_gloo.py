@@ -67,3 +67,34 @@ def test_cooperative_schedule_matches_single_process():
         opt.step()
     for n, p in ref.named_parameters():
         assert rel_err(got[n], p.detach()) < 1e-4, n
+
+
+def _peer_storage(rank, world):
+    import torch.distributed as dist
+
+    from my_muon_fsdp2_b200.parallel.symm import peer_param_addrs, register_peer_storage
+
+    buf = torch.zeros(100)  # stands in for a symmetric buffer; the bases below are never dereferenced
+    register_peer_storage(buf, dist.group.WORLD, [10_000, 20_000])
+    out = {
+        "inside": peer_param_addrs(buf[40:60].view(4, 5), dist.group.WORLD),
+        "outside": peer_param_addrs(torch.zeros(4), dist.group.WORLD),
+        "strided": peer_param_addrs(buf[:40].view(8, 5)[:, :2], dist.group.WORLD),
+    }
+    buf2 = torch.zeros(50, dtype=torch.bfloat16)  # a second store with its own bases
+    register_peer_storage(buf2, dist.group.WORLD, [50_000, 60_000])
+    out["second"] = peer_param_addrs(buf2[10:], dist.group.WORLD)
+    sub = dist.new_group([0])
+    if rank == 0:
+        out["other_group"] = peer_param_addrs(buf[40:60], sub)
+    return out
+
+
+def test_peer_parameter_storage_addresses():
+    """The Muon engine's in-place peer update finds every rank's copy of a parameter shard at
+    the same offset of the registered symmetric buffer, and only for that buffer's group."""
+    got = run_ranks(_peer_storage, 2)
+    assert got["inside"] == [10_000 + 40 * 4, 20_000 + 40 * 4]
+    assert got["outside"] is None and got["strided"] is None
+    assert got["second"] == [50_000 + 10 * 2, 60_000 + 10 * 2]
+    assert got["other_group"] is None
