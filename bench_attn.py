@@ -37,7 +37,8 @@ def main():
     ap.add_argument("--D", type=int, default=128)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", choices=["all", "ours_fwd", "ours_bwd"], default="all")
-    ap.add_argument("--fwd-variant", type=int, default=0, help="0: two query tiles per CTA, 1: one")
+    ap.add_argument("--fwd-variant", type=int, default=0,
+                    help="0: two query tiles per CTA (packed-arithmetic softmax), 1: one, 2: two (plain softmax)")
     a = ap.parse_args()
     from my_muon_fsdp2_b200._ext import ext
 

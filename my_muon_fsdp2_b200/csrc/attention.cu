@@ -403,7 +403,115 @@ __device__ __forceinline__ void fwd_softmax_tile(const AttnParams& p, uint32_t t
   }
 }
 
+// Same contract as fwd_softmax_tile, with fewer instructions per score: the row max is taken
+// on the raw scores (the scale is positive), three at a time; the exponent argument is one
+// packed fma s*scale - m per pair of scores; the row sum is a packed add; the causal mask is
+// applied only on the diagonal block.
 template <int D>
+__device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_t tS, uint32_t tO, uint64_t* s_full,
+                                                    uint64_t* p_full, uint64_t* pv_done, int qb, int nblk, int h,
+                                                    int b, int q, int lane) {
+  const int r = q * 32 + lane;
+  const int qi = qb * QB + r;
+  const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+  const float c = p.scale_log2;
+  float m2 = -INFINITY, l = 0.f;  // running max in the scaled log2 domain, running sum
+  bool ok = true;
+  for (int j = 0; j < nblk && ok; ++j) {
+    if (!mbar_wait(s_full, j & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const bool diag = (j == qb);
+    float sv[64];
+    auto load_half = [&](int hf) {  // raw scores of keys j*KB + hf*64 + 0..63
+      tmem_ld_32cols_async(tS + lane_off + hf * 64, sv);
+      tmem_ld_32cols_async(tS + lane_off + hf * 64 + 32, sv + 32);
+      tmem_ld_wait();
+      if (diag) {
+        const int lim = qi - (j * KB + hf * 64);  // keys past the query row are masked
+#pragma unroll
+        for (int e = 0; e < 64; ++e)
+          if (e > lim) sv[e] = -INFINITY;
+      }
+    };
+    float mx = -INFINITY;
+    load_half(1);
+#pragma unroll
+    for (int e = 0; e < 64; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
+    load_half(0);
+#pragma unroll
+    for (int e = 0; e < 64; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
+    const float mxs = mx * c;
+    // the reference max moves only when the row max grows by more than 2^8 (see attn_fwd_kernel)
+    const bool grow = (m2 == -INFINITY) || (mxs > m2 + 8.f);
+    const float m_new = grow ? mxs : m2;
+    const float alpha = (m2 == -INFINITY) ? 0.f : (grow ? fast_exp2(m2 - m_new) : 1.f);
+    if (__any_sync(0xffffffffu, j >= 1 && alpha != 1.f)) {
+      if (!mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        float o[32];
+        tmem_ld_32cols(tO + lane_off + cc * 32, o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= alpha;
+        tmem_st_32cols_async(tO + lane_off + cc * 32, o);
+      }
+    }
+    const float2 c2 = make_float2(c, c);
+    const float2 nm = make_float2(-m_new, -m_new);
+    float2 sum2 = make_float2(0.f, 0.f);
+#pragma unroll 1
+    for (int hf = 0; hf < 2; ++hf) {
+      if (hf == 1) {
+        tmem_st_wait();  // keys 0..63 stored over S columns 0..31, which were read already
+        load_half(1);
+      }
+      float pk[32];
+#pragma unroll
+      for (int e2 = 0; e2 < 32; ++e2) {
+        const float2 x = ffma2(make_float2(sv[2 * e2], sv[2 * e2 + 1]), c2, nm);
+        const float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        sum2 = fadd2(sum2, pp);
+        __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
+        pk[e2] = *reinterpret_cast<float*>(&pb);
+      }
+      tmem_st_32cols_async(tS + lane_off + hf * 32, pk);
+    }
+    tmem_st_wait();
+    l = l * alpha + (sum2.x + sum2.y);
+    m2 = m_new;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(p_full);
+  }
+  if (ok && nblk > 0 && mbar_wait(pv_done, (nblk - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+    tc_fence_after();
+    const float inv = (l > 0.f) ? 1.f / l : 0.f;
+    __nv_bfloat16* orow = p.o + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D;
+#pragma unroll
+    for (int cc = 0; cc < D / 32; ++cc) {
+      float o[32];
+      tmem_ld_32cols(tO + lane_off + cc * 32, o);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 w;
+        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(o[g * 8 + 2 * e2] * inv, o[g * 8 + 2 * e2 + 1] * inv);
+        *reinterpret_cast<uint4*>(orow + cc * 32 + g * 8) = w;
+      }
+    }
+    p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + qi] = (m2 + log2f(l)) * 0.69314718055994531f;
+  }
+}
+
+template <int D, bool V2>
 __global__ void __launch_bounds__(ATT2_THREADS, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -546,9 +654,14 @@ __global__ void __launch_bounds__(ATT2_THREADS, 1)
   } else {
     const int t = (warp - 2) >> 2;  // tile of this warpgroup (one call site keeps the code small)
     const int q = warp & 3;
-    if (t == 0 || has_b)
-      fwd_softmax_tile<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
-                          t ? nblk_b : nblk_a, h, b, q, lane);
+    if (t == 0 || has_b) {
+      if constexpr (V2)
+        fwd_softmax_tile_v2<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
+                               t ? nblk_b : nblk_a, h, b, q, lane);
+      else
+        fwd_softmax_tile<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
+                            t ? nblk_b : nblk_a, h, b, q, lane);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1177,7 +1290,9 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
   return m;
 }
 
-std::atomic<int> g_fwd_variant{0};  // 0: two query tiles per CTA, 1: one tile per CTA
+// 0: two query tiles per CTA with the packed-arithmetic softmax (fwd_softmax_tile_v2),
+// 1: one tile per CTA, 2: two tiles with the plain softmax (fwd_softmax_tile)
+std::atomic<int> g_fwd_variant{0};
 
 template <int D>
 void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
@@ -1186,7 +1301,8 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
     cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_fwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd2_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd2_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
     attr_set[dev] = true;
   }
   AttnParams p{};
@@ -1205,9 +1321,12 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   if (g_fwd_variant.load() == 1) {
     dim3 grid(a.T / QB, a.Hq, a.B);
     attn_fwd_kernel<D><<<grid, ATT_THREADS, AttnSmem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  } else if (g_fwd_variant.load() == 2) {
+    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+    attn_fwd2_kernel<D, false><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
   } else {
     dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
-    attn_fwd2_kernel<D><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
+    attn_fwd2_kernel<D, true><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
   }
   count_launch();
   cudaError_t e = cudaGetLastError();

@@ -15,7 +15,8 @@ struct AttnArgs {
   float scale;
 };
 void attention_fwd(const AttnArgs& a, cudaStream_t stream);
-// Forward kernel choice: 0 = two query tiles per CTA (default), 1 = one query tile per CTA.
+// Forward kernel choice: 0 = two query tiles per CTA with the packed-arithmetic softmax
+// (default), 1 = one query tile per CTA, 2 = two query tiles with the plain softmax.
 void set_attention_fwd_variant(int v);
 
 struct AttnBwdArgs {

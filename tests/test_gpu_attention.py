@@ -23,7 +23,7 @@ def _ref(q, k, v):
     return o, lse
 
 
-@pytest.mark.parametrize("variant", [0, 1], ids=["two_tiles", "one_tile"])
+@pytest.mark.parametrize("variant", [0, 1, 2], ids=["two_tiles_packed", "one_tile", "two_tiles_plain"])
 @pytest.mark.parametrize("B,T,Hq,Hkv,D", [(1, 128, 1, 1, 128), (2, 384, 4, 2, 128), (1, 512, 2, 2, 64),
                                           (1, 1024, 8, 2, 128), (1, 640, 2, 1, 64)])
 def test_attention_forward_matches_fp32(B, T, Hq, Hkv, D, variant):
