@@ -39,10 +39,12 @@ def main():
     ap.add_argument("--only", choices=["all", "ours_fwd", "ours_bwd"], default="all")
     ap.add_argument("--fwd-variant", type=int, default=0,
                     help="0: two query tiles per CTA (packed-arithmetic softmax), 1: one, 2: two (plain softmax)")
+    ap.add_argument("--bwd-variant", type=int, default=0, help="0: plain elementwise, 1: packed f32x2 arithmetic")
     a = ap.parse_args()
     from my_muon_fsdp2_b200._ext import ext
 
     ext().set_attention_fwd_variant(a.fwd_variant)
+    ext().set_attention_bwd_variant(a.bwd_variant)
     torch.manual_seed(0)
     q = torch.randn(a.B, a.T, a.Hq, a.D, device="cuda", dtype=torch.bfloat16)
     k = torch.randn(a.B, a.T, a.Hkv, a.D, device="cuda", dtype=torch.bfloat16)

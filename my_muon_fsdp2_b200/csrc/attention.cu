@@ -708,7 +708,7 @@ struct BwdSmem {
   static constexpr int BYTES = BYTES0 > 120 * 1024 ? BYTES0 : 120 * 1024;
 };
 
-template <int D>
+template <int D, bool V2>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -871,7 +871,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     bool ok = true;
     // row statistics of each query block, prefetched one block ahead (one value per thread)
     const float* stat_src = (tid < 128) ? p.lse : p.delta;
-    const float stat_mul = (tid < 128) ? 1.4426950408889634f : 1.f;
+    // V2 keeps the statistics negated (-lse*log2e, -delta) so that both enter as addends
+    const float stat_mul = ((tid < 128) ? 1.4426950408889634f : 1.f) * (V2 ? -1.f : 1.f);
     const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + (tid & 127);
     float stat_next = stat_src[stat_base + j * QB] * stat_mul;
     for (int u = 0; u < n_units && ok; ++u) {
@@ -916,21 +917,43 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         *reinterpret_cast<float4*>(st_l + 4) = *reinterpret_cast<const float4*>(sLse + q0 + 4);
         *reinterpret_cast<float4*>(st_d) = *reinterpret_cast<const float4*>(sDelta + q0);
         *reinterpret_cast<float4*>(st_d + 4) = *reinterpret_cast<const float4*>(sDelta + q0 + 4);
+        if constexpr (V2) {
+          // one packed fma per pair for the exponent argument, packed add + mul for dS; the
+          // causal mask only on the diagonal block
+          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
 #pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int e = g * 8 + e2 * 2 + t;
-            const int qc = q0 + e2 * 2 + t;  // query column inside the block
-            const bool masked = diag && (qc < kr);
-            const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - st_l[e2 * 2 + t]);
-            pv[t] = pr;
-            dv[t] = pr * (dp[e] - st_d[e2 * 2 + t]);
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int e = g * 8 + e2 * 2;
+            const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, make_float2(st_l[e2 * 2], st_l[e2 * 2 + 1]));
+            float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            if (diag) {
+              const int qc = q0 + e2 * 2;  // query column inside the block
+              if (qc < kr) pr.x = 0.f;
+              if (qc + 1 < kr) pr.y = 0.f;
+            }
+            const float2 dd =
+                fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), make_float2(st_d[e2 * 2], st_d[e2 * 2 + 1])));
+            __nv_bfloat162 pb = __floats2bfloat162_rn(pr.x, pr.y);
+            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
+            hd[e2] = __floats2bfloat162_rn(dd.x, dd.y);
           }
-          __nv_bfloat162 pb = __floats2bfloat162_rn(pv[0], pv[1]);
-          ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
-          hd[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
+        } else {
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            float pv[2], dv[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int e = g * 8 + e2 * 2 + t;
+              const int qc = q0 + e2 * 2 + t;  // query column inside the block
+              const bool masked = diag && (qc < kr);
+              const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - st_l[e2 * 2 + t]);
+              pv[t] = pr;
+              dv[t] = pr * (dp[e] - st_d[e2 * 2 + t]);
+            }
+            __nv_bfloat162 pb = __floats2bfloat162_rn(pv[0], pv[1]);
+            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
+            hd[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
+          }
         }
         *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wd;
       }
@@ -1005,7 +1028,7 @@ struct AttnDqParams {
   int* err;
 };
 
-template <int D>
+template <int D, bool V2>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1173,17 +1196,35 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       for (int g = 0; g < 8; ++g) {
         uint4 w;
         __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+        if constexpr (V2) {
+          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+          const float2 nl = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
 #pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {
-          float dv[2];
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int e = g * 8 + e2 * 2 + t;
-            const bool masked = diag && (j * KB + c0 + e > qi);
-            const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - lse2);
-            dv[t] = pr * (dp[e] - dlt);
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int e = g * 8 + e2 * 2;
+            const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nl);
+            float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            if (diag) {
+              const int key = j * KB + c0 + e;
+              if (key > qi) pr.x = 0.f;
+              if (key + 1 > qi) pr.y = 0.f;
+            }
+            const float2 dd = fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), nd));
+            hw[e2] = __floats2bfloat162_rn(dd.x, dd.y);
           }
-          hw[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
+        } else {
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            float dv[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int e = g * 8 + e2 * 2 + t;
+              const bool masked = diag && (j * KB + c0 + e > qi);
+              const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - lse2);
+              dv[t] = pr * (dp[e] - dlt);
+            }
+            hw[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
+          }
         }
         *reinterpret_cast<uint4*>(sDS + swz_offset(r, c0 + g * 8)) = w;
       }
@@ -1293,6 +1334,8 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
 // 0: two query tiles per CTA with the packed-arithmetic softmax (fwd_softmax_tile_v2),
 // 1: one tile per CTA, 2: two tiles with the plain softmax (fwd_softmax_tile)
 std::atomic<int> g_fwd_variant{0};
+// backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask)
+std::atomic<int> g_bwd_variant{0};
 
 template <int D>
 void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
@@ -1340,8 +1383,10 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     attr_set[dev] = true;
   }
   const int64_t rows = static_cast<int64_t>(a.B) * a.T * a.Hq;
@@ -1366,7 +1411,11 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
   CUtensorMap mdo = map_bthd(a.dout, a.B, a.T, a.Hq, D);
   dim3 grid(a.T / KB, a.Hq, a.B);
-  attn_bwd_kernel<D><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  const bool v2 = g_bwd_variant.load() == 1;
+  if (v2)
+    attn_bwd_kernel<D, true><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  else
+    attn_bwd_kernel<D, false><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
   count_launch();
   AttnDqParams pq{};
   pq.B = a.B;
@@ -1379,7 +1428,11 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   pq.delta = a.delta;
   pq.dq = static_cast<__nv_bfloat16*>(a.dq);
   pq.err = p.err;
-  attn_bwd_dq_kernel<D><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, pq);
+  if (v2)
+    attn_bwd_dq_kernel<D, true><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, pq);
+  else
+    attn_bwd_dq_kernel<D, false><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo,
+                                                                                                       pq);
   count_launch();
   const int64_t rows_kv = static_cast<int64_t>(a.B) * a.T * a.Hkv;
   gqa_reduce_kernel<<<static_cast<unsigned>(std::min<int64_t>((rows_kv * D + 255) / 256, 148 * 16)), 256, 0, stream>>>(
@@ -1416,5 +1469,6 @@ void attention_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
     throw std::runtime_error("mmf: attention supports head_dim 64 or 128");
 }
 void set_attention_fwd_variant(int v) { g_fwd_variant.store(v); }
+void set_attention_bwd_variant(int v) { g_bwd_variant.store(v); }
 
 }  // namespace mmf

@@ -43,10 +43,11 @@ def test_attention_forward_matches_fp32(B, T, Hq, Hkv, D, variant):
     assert rel_err(lse, rlse) < 1e-3
 
 
+@pytest.mark.parametrize("bwd_variant", [0, 1], ids=["plain", "packed"])
 @pytest.mark.parametrize("B,T,Hq,Hkv,D", [(1, 128, 1, 1, 128), (2, 256, 4, 2, 128), (1, 384, 2, 1, 64),
                                           (1, 200, 4, 2, 128)])
-def test_attention_backward_matches_fp32(B, T, Hq, Hkv, D):
-    from my_muon_fsdp2_b200._ext import check_device_error
+def test_attention_backward_matches_fp32(B, T, Hq, Hkv, D, bwd_variant):
+    from my_muon_fsdp2_b200._ext import check_device_error, ext
     from my_muon_fsdp2_b200.ops.attention import flash_attention
 
     torch.manual_seed(1)
@@ -55,8 +56,12 @@ def test_attention_backward_matches_fp32(B, T, Hq, Hkv, D):
     v = torch.randn(B, T, Hkv, D, device="cuda").to(torch.bfloat16).requires_grad_()
     o = flash_attention(q, k, v)
     do = torch.randn_like(o)
-    gq, gk, gv = torch.autograd.grad(o, (q, k, v), do)
-    torch.cuda.synchronize()
+    ext().set_attention_bwd_variant(bwd_variant)
+    try:
+        gq, gk, gv = torch.autograd.grad(o, (q, k, v), do)
+        torch.cuda.synchronize()
+    finally:
+        ext().set_attention_bwd_variant(0)
     check_device_error(0)
     qf, kf, vf = (t.detach().float().requires_grad_() for t in (q, k, v))
     ro, _ = _ref(qf, kf, vf)
