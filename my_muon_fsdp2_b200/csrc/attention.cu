@@ -407,7 +407,7 @@ __device__ __forceinline__ void fwd_softmax_tile(const AttnParams& p, uint32_t t
 // on the raw scores (the scale is positive), three at a time; the exponent argument is one
 // packed fma s*scale - m per pair of scores; the row sum is a packed add; the causal mask is
 // applied only on the diagonal block.
-template <int D>
+template <int D, bool FULL_ROW>
 __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_t tS, uint32_t tO, uint64_t* s_full,
                                                     uint64_t* p_full, uint64_t* pv_done, int qb, int nblk, int h,
                                                     int b, int q, int lane) {
@@ -424,25 +424,40 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
     }
     tc_fence_after();
     const bool diag = (j == qb);
-    float sv[64];
+    constexpr int NV = FULL_ROW ? 128 : 64;
+    float sv[NV];
+    auto mask = [&](float* v, int k0) {  // keys past the query row are masked (diagonal block only)
+      const int lim = qi - k0;
+#pragma unroll
+      for (int e = 0; e < 64; ++e)
+        if (e > lim) v[e] = -INFINITY;
+    };
     auto load_half = [&](int hf) {  // raw scores of keys j*KB + hf*64 + 0..63
       tmem_ld_32cols_async(tS + lane_off + hf * 64, sv);
       tmem_ld_32cols_async(tS + lane_off + hf * 64 + 32, sv + 32);
       tmem_ld_wait();
-      if (diag) {
-        const int lim = qi - (j * KB + hf * 64);  // keys past the query row are masked
-#pragma unroll
-        for (int e = 0; e < 64; ++e)
-          if (e > lim) sv[e] = -INFINITY;
-      }
+      if (diag) mask(sv, j * KB + hf * 64);
     };
     float mx = -INFINITY;
-    load_half(1);
+    if constexpr (FULL_ROW) {
+      // the whole row in one TMEM read: keys 0..127 -> sv[0..127]
 #pragma unroll
-    for (int e = 0; e < 64; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
-    load_half(0);
+      for (int cc = 0; cc < 4; ++cc) tmem_ld_32cols_async(tS + lane_off + cc * 32, sv + cc * 32);
+      tmem_ld_wait();
+      if (diag) {
+        mask(sv, j * KB);
+        mask(sv + 64, j * KB + 64);
+      }
 #pragma unroll
-    for (int e = 0; e < 64; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
+      for (int e = 0; e < 128; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
+    } else {
+      load_half(1);
+#pragma unroll
+      for (int e = 0; e < 64; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
+      load_half(0);
+#pragma unroll
+      for (int e = 0; e < 64; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
+    }
     const float mxs = mx * c;
     // the reference max moves only when the row max grows by more than 2^8 (see attn_fwd_kernel)
     const bool grow = (m2 == -INFINITY) || (mxs > m2 + 8.f);
@@ -466,22 +481,31 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
     const float2 c2 = make_float2(c, c);
     const float2 nm = make_float2(-m_new, -m_new);
     float2 sum2 = make_float2(0.f, 0.f);
-#pragma unroll 1
-    for (int hf = 0; hf < 2; ++hf) {
-      if (hf == 1) {
-        tmem_st_wait();  // keys 0..63 stored over S columns 0..31, which were read already
-        load_half(1);
-      }
+    // P of keys hf*64 .. hf*64+63 as bf16 pairs over S columns hf*32 .. hf*32+31
+    auto exp_store = [&](const float* v, int hf) {
       float pk[32];
 #pragma unroll
       for (int e2 = 0; e2 < 32; ++e2) {
-        const float2 x = ffma2(make_float2(sv[2 * e2], sv[2 * e2 + 1]), c2, nm);
+        const float2 x = ffma2(make_float2(v[2 * e2], v[2 * e2 + 1]), c2, nm);
         const float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         sum2 = fadd2(sum2, pp);
         __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
         pk[e2] = *reinterpret_cast<float*>(&pb);
       }
       tmem_st_32cols_async(tS + lane_off + hf * 32, pk);
+    };
+    if constexpr (FULL_ROW) {
+      exp_store(sv, 0);
+      exp_store(sv + 64, 1);
+    } else {
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        if (hf == 1) {
+          tmem_st_wait();  // keys 0..63 stored over S columns 0..31, which were read already
+          load_half(1);
+        }
+        exp_store(sv, hf);
+      }
     }
     tmem_st_wait();
     l = l * alpha + (sum2.x + sum2.y);
@@ -511,7 +535,7 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
   }
 }
 
-template <int D, bool V2>
+template <int D, bool V2, bool FULL_ROW = false>
 __global__ void __launch_bounds__(ATT2_THREADS, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -656,12 +680,177 @@ __global__ void __launch_bounds__(ATT2_THREADS, 1)
     const int q = warp & 3;
     if (t == 0 || has_b) {
       if constexpr (V2)
-        fwd_softmax_tile_v2<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
+        fwd_softmax_tile_v2<D, FULL_ROW>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
                                t ? nblk_b : nblk_a, h, b, q, lane);
       else
         fwd_softmax_tile<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
                             t ? nblk_b : nblk_a, h, b, q, lane);
     }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+// ======================================================================================
+// Forward, 3 warpgroups (384 threads) so that the softmax threads can hold a whole row of 128
+// scores: WG0 = warp 0 TMA, warp 1 MMA, warps 2-3 idle, with its registers cut to 56 per thread;
+// WG1 / WG2 = softmax + epilogue of query tile A / B with 224 per thread.  Launch allocation:
+// 384 x 168 = 64512 registers; after the reallocation 128 x 56 + 256 x 224 = 64512, and each
+// SM sub-partition holds one WG0 warp and two softmax warps: (56 + 2 x 224) x 32 = 16128 of
+// its 16384.  Same barriers, TMEM layout and MMA schedule as attn_fwd2_kernel.
+// ======================================================================================
+constexpr int ATT3_THREADS = 384;
+constexpr uint32_t ATT3_REGS_CTRL = 56, ATT3_REGS_SOFTMAX = 224, ATT3_REGS_LAUNCH = 168;
+static_assert(128 * ATT3_REGS_CTRL + 256 * ATT3_REGS_SOFTMAX <= ATT3_THREADS * ATT3_REGS_LAUNCH,
+              "register split exceeds the launch allocation");
+static_assert((ATT3_REGS_CTRL + 2 * ATT3_REGS_SOFTMAX) * 32 <= 16384, "register split exceeds a sub-partition");
+
+template <int D>
+__global__ void __launch_bounds__(ATT3_THREADS, 1)
+    attn_fwd3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using L = Attn2Smem<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + L::Q_OFF;
+  uint8_t* sK = smem + L::K_OFF;
+  uint8_t* sV = smem + L::V_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2] per tile
+  uint64_t* p_full = bars + 7;    // [2] per tile
+  uint64_t* pv_done = bars + 9;   // [2] per tile
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = p.T / QB;
+  const int npair = (nqb + 1) / 2;
+  const int x = npair - 1 - static_cast<int>(blockIdx.x);  // heaviest pairs first
+  const int qa = 2 * x, qbb = 2 * x + 1;
+  const bool has_b = qbb < nqb;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int nblk_a = qa + 1, nblk_b = has_b ? qbb + 1 : 0;
+  const int nblk = has_b ? nblk_b : nblk_a;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto ts_of = [tmem](int t) { return tmem + static_cast<uint32_t>(t) * 128u; };
+  auto to_of = [tmem](int t) { return tmem + 256u + static_cast<uint32_t>(t * D); };
+
+  if (warp < 4) {
+    reg_dealloc<ATT3_REGS_CTRL>();  // unconditionally: the softmax warpgroups wait for these
+    if (warp == 0 && lane == 0) {
+      constexpr uint32_t TILE = L::TILE;
+      mbar_arrive_expect_tx(q_full, has_b ? 2 * TILE : TILE);
+#pragma unroll
+      for (int c = 0; c < L::CH; ++c) {
+        tma_load_4d(sQ + c * 16384, &tmQ, q_full, c * 64, h, qa * QB, b);
+        if (has_b) tma_load_4d(sQ + TILE + c * 16384, &tmQ, q_full, c * 64, h, qbb * QB, b);
+      }
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
+#pragma unroll
+        for (int c = 0; c < L::CH; ++c) {
+          tma_load_4d(sK + st * TILE + c * 16384, &tmK, &kv_full[st], c * 64, hk, j * KB, b);
+          tma_load_4d(sV + st * TILE + c * 16384, &tmV, &kv_full[st], c * 64, hk, j * KB, b);
+        }
+      }
+    } else if (warp == 1 && lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, KB, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
+      const uint32_t q_addr0 = smem_u32(sQ);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t q_addr = q_addr0 + t * L::TILE;
+        const uint32_t k_addr = smem_u32(sK + (j & 1) * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(ts_of(t), sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
+        }
+        umma_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait(&p_full[t], j & 1, p.err, ERR_MMA_FULL_TIMEOUT)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + (j & 1) * L::TILE);
+#pragma unroll
+        for (int kk = 0; kk < KB / 16; ++kk)
+          umma_bf16_ts(to_of(t), ts_of(t) + static_cast<uint32_t>(kk * 8), sdesc_mnmajor(v_addr + kk * 16 * 128, 16384),
+                       idesc_o, (j | kk) ? 1u : 0u);
+        umma_commit(&pv_done[t]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, ERR_MMA_FULL_TIMEOUT) &&
+                mbar_wait(&kv_full[0], 0, p.err, ERR_MMA_FULL_TIMEOUT);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (has_b) issue_s(1, 0);
+      }
+      auto wait_kv = [&](int j1) {
+        const bool r = mbar_wait(&kv_full[j1 & 1], (j1 >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT);
+        tc_fence_after();
+        return r;
+      };
+      for (int j = 0; ok && j < nblk; ++j) {
+        if (j < nblk_a) {
+          if (!(ok = issue_pv(0, j))) break;
+          if (j + 1 < nblk_a) {
+            if (!(ok = wait_kv(j + 1))) break;
+            issue_s(0, j + 1);
+          }
+        }
+        if (j < nblk_b) {
+          if (!(ok = issue_pv(1, j))) break;
+          if (j + 1 < nblk_b) {
+            if (!(ok = wait_kv(j + 1))) break;
+            issue_s(1, j + 1);
+          }
+        }
+        umma_commit(&kv_empty[j & 1]);
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else {
+    reg_alloc<ATT3_REGS_SOFTMAX>();
+    const int t = (warp - 4) >> 2;
+    const int q = warp & 3;
+    if (t == 0 || has_b)
+      fwd_softmax_tile_v2<D, true>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
+                                   t ? nblk_b : nblk_a, h, b, q, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -1332,7 +1521,9 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
 }
 
 // 0: two query tiles per CTA with the packed-arithmetic softmax (fwd_softmax_tile_v2),
-// 1: one tile per CTA, 2: two tiles with the plain softmax (fwd_softmax_tile)
+// 1: one tile per CTA, 2: two tiles with the plain softmax (fwd_softmax_tile),
+// 3: as 0 with the whole score row held in registers (one TMEM read per key block),
+// 4: as 3 in 3 warpgroups with the registers moved to the softmax warps (attn_fwd3_kernel)
 std::atomic<int> g_fwd_variant{0};
 // backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask)
 std::atomic<int> g_bwd_variant{0};
@@ -1346,6 +1537,9 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
     cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_fwd2_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
     cudaFuncSetAttribute(attn_fwd2_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd2_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Attn2Smem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd3_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
     attr_set[dev] = true;
   }
   AttnParams p{};
@@ -1367,6 +1561,23 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   } else if (g_fwd_variant.load() == 2) {
     dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
     attn_fwd2_kernel<D, false><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  } else if (g_fwd_variant.load() == 4) {
+    // the register split assumes the launch allocation; an increase beyond the block's pool
+    // would wait forever, so refuse to launch if the compiled kernel differs
+    static int regs[64] = {0};
+    if (!regs[dev]) {
+      cudaFuncAttributes fa{};
+      cudaFuncGetAttributes(&fa, attn_fwd3_kernel<D>);
+      regs[dev] = fa.numRegs;
+    }
+    if (regs[dev] != static_cast<int>(ATT3_REGS_LAUNCH))
+      throw std::runtime_error("mmf: attn_fwd3_kernel compiled with " + std::to_string(regs[dev]) +
+                               " registers per thread; its register split needs " + std::to_string(ATT3_REGS_LAUNCH));
+    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+    attn_fwd3_kernel<D><<<grid, ATT3_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  } else if (g_fwd_variant.load() == 3) {
+    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+    attn_fwd2_kernel<D, true, true><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
   } else {
     dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
     attn_fwd2_kernel<D, true><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);

@@ -317,6 +317,19 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Warpgroup register reallocation.  Every warp of a warpgroup executes the same instruction.
+// An increase waits until registers are free, so the warpgroups that decrease must do so
+// unconditionally, and the per-thread counts summed over the block must not exceed the
+// block's launch allocation (threads x registers per thread at launch).
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for both halves) and the
 // three-input max.  Pairs are packed and unpacked in the same order, so the lane-wise ops
 // are order-agnostic.
