@@ -80,7 +80,12 @@ def _check_linears(ctl, lins, fulls, rank, world, dev, res, mode):
             res[f"dx{i}_{t}_{mode}"] = ((x.grad.float() - dx_ref).norm() / dx_ref.norm()).item()
 
 
-def run_train(rank, world, dev, steps=3):
+def run_hsdp(rank, world, dev):
+    """2 x (world / 2) mesh (replicate, shard): SymmFSDP HSDP against FSDP2 HSDP."""
+    return run_train(rank, world, dev, mesh_shape=(2, world // 2))
+
+
+def run_train(rank, world, dev, steps=3, mesh_shape=None):
     from torch.distributed.device_mesh import init_device_mesh
 
     from my_muon_fsdp2_b200 import FusedAdamW, MuonOptimizer
@@ -92,7 +97,7 @@ def run_train(rank, world, dev, steps=3):
         torch.manual_seed(0)
         cfg = LlamaConfig.tiny(dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab_size=1024, n_layers=2)
         model = Llama(cfg).to(dev, torch.bfloat16)
-        mesh = init_device_mesh("cuda", (world,))
+        mesh = init_device_mesh("cuda", mesh_shape or (world,))
         if mode == "symm":
             ctl = apply_symm_fsdp(model, mesh)
         else:
@@ -164,7 +169,7 @@ def run_split(rank, world, dev, steps=2):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["kernels", "train", "split", "mixed"], required=True)
+    ap.add_argument("--mode", choices=["kernels", "train", "split", "mixed", "hsdp"], required=True)
     ap.add_argument("--out", required=True)
     a = ap.parse_args()
     local = int(os.environ["LOCAL_RANK"])
@@ -173,7 +178,8 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
     try:
-        res = {"kernels": run_kernels, "train": run_train, "split": run_split, "mixed": run_mixed}[a.mode](
+        res = {"kernels": run_kernels, "train": run_train, "split": run_split, "mixed": run_mixed,
+               "hsdp": run_hsdp}[a.mode](
             rank, world, dev)
         if rank == 0:
             torch.save(res, a.out)

@@ -67,3 +67,15 @@ def test_mixed_fused_and_nccl_weights_with_bias():
             assert v, f"{k}: gathered weight differs from the full weight"
         else:
             assert v < 1e-2, f"{k}: relative error {v}"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_symm_fsdp_hsdp_training_matches_fsdp2_hsdp():
+    """2 x 2 mesh: fused collectives inside each shard pair, replica averaging across pairs."""
+    with tempfile.TemporaryDirectory() as d:
+        res = _run(4, "hsdp", os.path.join(d, "h.pt"))
+    a, b = res["symm"], res["fsdp2"]
+    for x, y in zip(a["losses"], b["losses"]):
+        assert abs(x - y) < 2e-2 * abs(y), (a["losses"], b["losses"])
+    for n in b["params"]:
+        assert rel_err(a["params"][n], b["params"][n]) < 2e-2, n
