@@ -5,6 +5,7 @@ gradient accumulation with a synchronising last micro-batch, gradient clipping, 
 
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 examples/llama_symm_fsdp.py      # B200s
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 examples/llama_symm_fsdp.py      # CPU/gloo too
+    torchrun --nproc-per-node 4 --master-addr 127.0.0.1 examples/llama_symm_fsdp.py --replicas 2   # HSDP
 
 On CPU (gloo) the same module runs its collectives through torch.distributed.
 """
@@ -29,6 +30,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--seq", type=int, default=256)
     ap.add_argument("--grad-accum", type=int, default=2)
+    ap.add_argument("--replicas", type=int, default=1,
+                    help="HSDP: a (replicas, world / replicas) mesh; the linears are sharded over the second dim")
     a = ap.parse_args()
     cuda = torch.cuda.is_available()
     dist.init_process_group("nccl" if cuda else "gloo")
@@ -39,7 +42,13 @@ def main():
     torch.manual_seed(0)
     cfg = LlamaConfig.tiny(dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab_size=2048, n_layers=2)
     model = Llama(cfg).to(dev, torch.bfloat16 if cuda else torch.float32)
-    ctl = apply_symm_fsdp(model)
+    mesh = None
+    if a.replicas > 1:
+        from torch.distributed.device_mesh import init_device_mesh
+
+        world = dist.get_world_size()
+        mesh = init_device_mesh(dev.type, (a.replicas, world // a.replicas), mesh_dim_names=("replicate", "shard"))
+    ctl = apply_symm_fsdp(model, mesh=mesh)
     names = set(model.muon_param_names())
     opts = [MuonOptimizer([p for n, p in model.named_parameters() if n in names], lr=0.02, weight_decay=0.01),
             FusedAdamW([p for n, p in model.named_parameters() if n not in names], lr=1e-3)]
