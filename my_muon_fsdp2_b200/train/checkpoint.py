@@ -105,22 +105,65 @@ def load_checkpoint(path: str, model: nn.Module, optimizer: Optional[Opts] = Non
     return {"epoch": ckpt.get("epoch"), "loss": ckpt.get("loss")}
 
 
+def _encode_extra(extra: Optional[Dict[str, Any]]) -> str:
+    # one string leaf: DCP loads only the leaves its template has, and an empty dict has none
+    import base64
+    import pickle
+
+    return base64.b64encode(pickle.dumps(dict(extra or {}))).decode("ascii")
+
+
+def _decode_extra(blob: str) -> Dict[str, Any]:
+    import base64
+    import pickle
+
+    return pickle.loads(base64.b64decode(blob)) if blob else {}
+
+
+@torch.no_grad()
+def _init_optimizer_state(opt: torch.optim.Optimizer) -> None:
+    """Create the optimizer's lazily-built state (one step on zero gradients at lr 0), so that
+    the load template has every entry the checkpoint holds."""
+    if opt.state:
+        return
+    params = [p for g in opt.param_groups for p in g["params"] if p.requires_grad]
+    if any(p.grad is not None for p in params):
+        return
+    for p in params:
+        p.grad = torch.zeros_like(p)
+    lrs = [g.get("lr") for g in opt.param_groups]
+    for g in opt.param_groups:
+        if "lr" in g:
+            g["lr"] = 0.0
+    opt.step()
+    for g, lr in zip(opt.param_groups, lrs):
+        if lr is not None:
+            g["lr"] = lr
+    for p in params:
+        p.grad = None
+
+
 def save_sharded(path: str, model: nn.Module, optimizer: Opts, extra: Optional[Dict[str, Any]] = None) -> None:
-    """DCP checkpoint: each rank writes its shards of the model and optimizer state."""
+    """DCP checkpoint: each rank writes its shards of the model and optimizer state; ``extra``
+    (picklable metadata: epoch, step, ...) is stored alongside."""
     import torch.distributed.checkpoint as dcp
 
     state = {"model": model.state_dict(), "optim": [o.state_dict() for o in _opts(optimizer)],
-             "extra": extra or {}}
+             "extra": _encode_extra(extra)}
     dcp.save(state, checkpoint_id=path)
 
 
 def load_sharded(path: str, model: nn.Module, optimizer: Opts) -> Dict[str, Any]:
+    """Load a :func:`save_sharded` checkpoint into ``model`` / ``optimizer`` (re-sharded to the
+    current layout by DCP) and return its ``extra`` metadata."""
     import torch.distributed.checkpoint as dcp
 
     opts = _opts(optimizer)
-    state = {"model": model.state_dict(), "optim": [o.state_dict() for o in opts], "extra": {}}
+    for o in opts:
+        _init_optimizer_state(o)
+    state = {"model": model.state_dict(), "optim": [o.state_dict() for o in opts], "extra": ""}
     dcp.load(state, checkpoint_id=path)
     model.load_state_dict(state["model"])
     for o, sd in zip(opts, state["optim"]):
         o.load_state_dict(sd)
-    return state["extra"]
+    return _decode_extra(state["extra"])

@@ -340,3 +340,51 @@ def test_symm_fsdp_traffic_counters():
     got = run_ranks(_traffic, 2)
     shard = sum((H // 2) * D + (D // 2) * H for _ in range(2)) * 4  # fp32, the other rank's rows
     assert got == {"bytes_gathered": shard, "bytes_reduced": shard, "bytes_replica": 0}
+
+
+def _dcp_roundtrip(rank, world, path):
+    """DCP sharded save / load with the fused-FSDP linears and FSDP2 for the rest: the resumed
+    run's next step equals the uninterrupted run's."""
+    from my_muon_fsdp2_b200 import MuonOptimizer
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+    from my_muon_fsdp2_b200.train.checkpoint import load_sharded, save_sharded
+
+    def build(seed_override=None):
+        model = Net()
+        if seed_override is not None:
+            torch.manual_seed(seed_override)
+            for p in model.parameters():
+                torch.nn.init.normal_(p)
+        ctl = apply_symm_fsdp(model)
+        mats = list(ctl.params)
+        rest = [p for p in model.parameters() if all(p is not q for q in mats)]
+        opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95), torch.optim.AdamW(rest, lr=1e-3)]
+        for o in opts:
+            ctl.attach_optimizer(o)
+        return model, opts
+
+    def step(model, opts, s):
+        x, y = _data(s, rank)
+        ((model(x) - y) ** 2).mean().backward()
+        for o in opts:
+            o.step()
+            o.zero_grad(set_to_none=True)
+
+    model, opts = build()
+    step(model, opts, 0)
+    save_sharded(path, model, opts, extra={"step": 1})
+    step(model, opts, 1)
+    want = {n: _full(p.detach()).clone() for n, p in model.named_parameters()}
+
+    model2, opts2 = build(seed_override=7)
+    extra = load_sharded(path, model2, opts2)
+    step(model2, opts2, 1)
+    got = {n: _full(p.detach()).clone() for n, p in model2.named_parameters()}
+    return {"extra": extra, "want": want, "got": got}
+
+
+def test_symm_fsdp_dcp_checkpoint_resume(tmp_path):
+    res = run_ranks(_dcp_roundtrip, 2, str(tmp_path / "ckpt"))
+    assert res["extra"] == {"step": 1}
+    for n in res["want"]:
+        assert torch.equal(res["got"][n], res["want"][n]), n
