@@ -1,0 +1,82 @@
+"""The Trainer end to end on 2 gloo ranks: a tiny Llama under FSDP2 or the fused-FSDP linears,
+Muon + AdamW, gradient accumulation with a synchronising last micro-batch, gradient clipping.
+Each rank's loss and the trained weights must match one process that trains on the union of
+the ranks' micro-batches."""
+import pytest
+import torch
+
+from tests.conftest import rel_err
+from tests.dist_util import run_ranks
+
+pytestmark = pytest.mark.distributed
+
+ACCUM, MB, SEQ, STEPS = 2, 2, 16, 2
+
+
+def _cfg():
+    from my_muon_fsdp2_b200.models.llama import LlamaConfig
+
+    return LlamaConfig.tiny(dim=64, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab_size=96, n_layers=2)
+
+
+def _batch(step, rank):
+    g = torch.Generator().manual_seed(1000 * step + rank)
+    return torch.randint(0, 96, (ACCUM, MB, SEQ + 1), generator=g)
+
+
+def _opts(model):
+    from my_muon_fsdp2_b200 import FusedAdamW, MuonOptimizer
+
+    names = set(model.muon_param_names())
+    return [MuonOptimizer([p for n, p in model.named_parameters() if n in names], lr=0.02, weight_decay=0.01),
+            FusedAdamW([p for n, p in model.named_parameters() if n not in names], lr=1e-3)]
+
+
+def _full(t):
+    return t.full_tensor() if hasattr(t, "full_tensor") else t
+
+
+def _ranked(rank, world, mode):
+    from my_muon_fsdp2_b200.models.llama import Llama, apply_fsdp
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+    from my_muon_fsdp2_b200.train import Trainer
+
+    torch.manual_seed(0)
+    model = Llama(_cfg())
+    if mode == "symm":
+        apply_symm_fsdp(model)
+    else:
+        apply_fsdp(model)
+    trainer = Trainer(model, _opts(model), grad_accum=ACCUM, device="cpu", max_grad_norm=1.0)
+    losses, norms = [], []
+    for s in range(STEPS):
+        losses.append(trainer.train_step(_batch(s, rank)))
+        norms.append(float(trainer.last_grad_norm))
+    params = {n: _full(p.detach()).clone() for n, p in model.named_parameters()}
+    return {"losses": losses, "norms": norms, "params": params, "metrics": trainer.metrics_summary()}
+
+
+@pytest.mark.parametrize("mode", ["fsdp2", "symm"])
+def test_trainer_matches_single_process(mode):
+    from my_muon_fsdp2_b200.models.llama import Llama
+    from my_muon_fsdp2_b200.train import Trainer
+
+    world = 2
+    got = run_ranks(_ranked, world, mode)
+    torch.manual_seed(0)
+    ref = Llama(_cfg())
+    # one process, micro-batch i = the ranks' micro-batches i side by side (the same mean loss)
+    trainer = Trainer(ref, _opts(ref), grad_accum=ACCUM, device="cpu", max_grad_norm=1.0)
+    norms = []
+    for s in range(STEPS):
+        both = torch.cat([_batch(s, r) for r in range(world)], dim=1)
+        trainer.train_step(both)
+        norms.append(float(trainer.last_grad_norm))
+    for a, b in zip(got["norms"], norms):
+        assert abs(a - b) < 1e-4 * max(1.0, b), (got["norms"], norms)
+    for n, p in ref.named_parameters():
+        assert rel_err(got["params"][n], p.detach()) < 1e-4, n
+    m = got["metrics"]
+    assert m["step"] == STEPS and m["micro_batches"] == ACCUM and isinstance(m["loss"], float)
+    if mode == "symm":
+        assert m["symm_fsdp/world"] == world and m["symm_fsdp/bytes_gathered"] > 0
