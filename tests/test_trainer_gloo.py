@@ -1,4 +1,4 @@
-"""The Trainer end to end on 2 gloo ranks: a tiny Llama under FSDP2 or the fused-FSDP linears,
+"""The Trainer end to end on 2 gloo ranks: a tiny Llama or GPT-2 under FSDP2 or the fused-FSDP linears,
 Muon + AdamW, gradient accumulation with a synchronising last micro-batch, gradient clipping.
 Each rank's loss and the trained weights must match one process that trains on the union of
 the ranks' micro-batches."""
@@ -13,10 +13,26 @@ pytestmark = pytest.mark.distributed
 ACCUM, MB, SEQ, STEPS = 2, 2, 16, 2
 
 
-def _cfg():
-    from my_muon_fsdp2_b200.models.llama import LlamaConfig
+def _build(arch):
+    torch.manual_seed(0)
+    if arch == "gpt2":
+        from my_muon_fsdp2_b200.models.gpt2 import GPTConfig, GPTModel
 
-    return LlamaConfig.tiny(dim=64, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab_size=96, n_layers=2)
+        return GPTModel(GPTConfig(vocab_size=96, n_positions=64, n_embd=64, n_layer=2, n_head=4))
+    from my_muon_fsdp2_b200.models.llama import Llama, LlamaConfig
+
+    return Llama(LlamaConfig.tiny(dim=64, n_heads=4, n_kv_heads=2, ffn_dim=128, vocab_size=96, n_layers=2))
+
+
+def _shard(model, arch, mode):
+    from my_muon_fsdp2_b200.models.llama import apply_fsdp
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    blocks = "h" if arch == "gpt2" else "layers"
+    if mode == "symm":
+        apply_symm_fsdp(model, blocks_attr=blocks)
+    else:
+        apply_fsdp(model, blocks_attr=blocks)
 
 
 def _batch(step, rank):
@@ -36,17 +52,11 @@ def _full(t):
     return t.full_tensor() if hasattr(t, "full_tensor") else t
 
 
-def _ranked(rank, world, mode):
-    from my_muon_fsdp2_b200.models.llama import Llama, apply_fsdp
-    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+def _ranked(rank, world, arch, mode):
     from my_muon_fsdp2_b200.train import Trainer
 
-    torch.manual_seed(0)
-    model = Llama(_cfg())
-    if mode == "symm":
-        apply_symm_fsdp(model)
-    else:
-        apply_fsdp(model)
+    model = _build(arch)
+    _shard(model, arch, mode)
     trainer = Trainer(model, _opts(model), grad_accum=ACCUM, device="cpu", max_grad_norm=1.0)
     losses, norms = [], []
     for s in range(STEPS):
@@ -56,15 +66,14 @@ def _ranked(rank, world, mode):
     return {"losses": losses, "norms": norms, "params": params, "metrics": trainer.metrics_summary()}
 
 
+@pytest.mark.parametrize("arch", ["llama", "gpt2"])
 @pytest.mark.parametrize("mode", ["fsdp2", "symm"])
-def test_trainer_matches_single_process(mode):
-    from my_muon_fsdp2_b200.models.llama import Llama
+def test_trainer_matches_single_process(arch, mode):
     from my_muon_fsdp2_b200.train import Trainer
 
     world = 2
-    got = run_ranks(_ranked, world, mode)
-    torch.manual_seed(0)
-    ref = Llama(_cfg())
+    got = run_ranks(_ranked, world, arch, mode)
+    ref = _build(arch)
     # one process, micro-batch i = the ranks' micro-batches i side by side (the same mean loss)
     trainer = Trainer(ref, _opts(ref), grad_accum=ACCUM, device="cpu", max_grad_norm=1.0)
     norms = []
@@ -74,8 +83,11 @@ def test_trainer_matches_single_process(mode):
         norms.append(float(trainer.last_grad_norm))
     for a, b in zip(got["norms"], norms):
         assert abs(a - b) < 1e-4 * max(1.0, b), (got["norms"], norms)
+    # GPT-2's key bias has a zero gradient in exact arithmetic (softmax is shift invariant), so
+    # AdamW turns summation-order noise into +-lr steps there: a looser bound for that model
+    tol = 1e-3 if arch == "gpt2" else 1e-4
     for n, p in ref.named_parameters():
-        assert rel_err(got["params"][n], p.detach()) < 1e-4, n
+        assert rel_err(got["params"][n], p.detach()) < tol, n
     m = got["metrics"]
     assert m["step"] == STEPS and m["micro_batches"] == ACCUM and isinstance(m["loss"], float)
     if mode == "symm":
