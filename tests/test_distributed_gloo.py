@@ -44,6 +44,15 @@ def _make_opt(kind, model):
         return MuonOptimizer(model.parameters(), lr=0.02, momentum=0.95, weight_decay=0.01, nesterov=True)
     if kind == "model_muon":
         return ModelMuon(model, lr=0.02, momentum=0.95, weight_decay=0.01, nesterov=True)
+    if kind == "sso":
+        from my_muon_fsdp2_b200 import SpectralSphereOptimizer
+
+        torch.manual_seed(11)  # the power iteration's start vector: the same on every rank
+        return SpectralSphereOptimizer(model.parameters(), lr=0.02, momentum=0.95, power_iteration_steps=20)
+    if kind == "hybrid":
+        from my_muon_fsdp2_b200 import create_hybrid_optimizer
+
+        return create_hybrid_optimizer(model, muon_lr=0.02, adamw_lr=1e-3, muon_weight_decay=0.01)
     raise ValueError(kind)
 
 
@@ -64,7 +73,7 @@ def _sharded_worker(rank, world, kind, steps, dims):
     return {"losses": losses, "params": full}
 
 
-@pytest.mark.parametrize("kind", ["fsdp", "muon", "model_muon"])
+@pytest.mark.parametrize("kind", ["fsdp", "muon", "model_muon", "sso", "hybrid"])
 def test_sharded_equals_single_process(kind):
     """The CPU/gloo MLP workload (512->2048->512, world size 2), shortened to 6 steps."""
     dims, steps = (512, 2048, 512), 6
