@@ -897,7 +897,7 @@ struct BwdSmem {
   static constexpr int BYTES = BYTES0 > 120 * 1024 ? BYTES0 : 120 * 1024;
 };
 
-template <int D, bool V2>
+template <int D, bool V2, bool PING = false>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -940,7 +940,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&do_full[t], 1);
       mbar_init(&do_empty[t], 1);
       mbar_init(&sp_full[t], 1);
-      mbar_init(&ds_full[t], 8);
+      mbar_init(&ds_full[t], PING ? 4 : 8);
       mbar_init(&ds_empty[t], 1);
     }
     mbar_init(drain, 1);
@@ -1045,6 +1045,117 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
+    }
+  } else if constexpr (PING) {
+    // Ping-pong: warpgroup wg (warps 2-5 / 6-9) owns the units of query half wg, i.e. queries
+    // wg*64 .. wg*64+63 of every query block, all 64 of them per warp (two 32-query passes), so
+    // the two warpgroups work on consecutive units at the same time.  Packed arithmetic as V2.
+    const int q = warp & 3;
+    const int wg = (warp - 2) >> 2;
+    const int kr = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const int wt = threadIdx.x - 64 - wg * 128;  // 0..127 inside the warpgroup
+    // this warpgroup's statistics of the current block: [0, 64) = -lse*log2e, [64, 128) = -delta
+    float* sStat = sLse + wg * 128;
+    const float* stat_src = (wt < 64) ? p.lse : p.delta;
+    const float stat_mul = (wt < 64) ? -1.4426950408889634f : -1.f;
+    const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + wg * 64 + (wt & 63);
+    float stat_next = stat_src[stat_base + j * QB] * stat_mul;
+    const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+    bool ok = true;
+    for (int u = wg; u < n_units && ok; u += 2) {
+      const int n = u >> 1, h = u & 1;  // h == wg
+      const int i = j + n;
+      // publish this block's statistics (the previous block's readers are past the barrier)
+      if (wg == 0)
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      else
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+      sStat[wt] = stat_next;
+      if (wg == 0)
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      else
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
+      if (!mbar_wait(&sp_full[h], (u >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (i == j);
+      uint8_t* dst_tile = sDSt + h * 16384;
+#pragma unroll 1
+      for (int pass = 0; pass < 2; ++pass) {
+        const int c0 = pass * 32;  // queries c0 .. c0+31 of this unit
+        float sv[32], dp[32];
+        tmem_ld_32cols_async(ts_h(h) + lane_off + c0, sv);
+        tmem_ld_32cols_async(tdp_h(h) + lane_off + c0, dp);
+        tmem_ld_wait();
+        // the dS^T buffer of this half was last read by the dK MMA of unit u-2
+        if (pass == 0 && u >= 2 &&
+            !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS,
+                       false)) {
+          ok = false;
+          break;
+        }
+        float ppk[16];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 wd;
+          __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
+          const int qu = c0 + g * 8;  // query column inside the unit
+          float st_l[8], st_d[8];
+          *reinterpret_cast<float4*>(st_l) = *reinterpret_cast<const float4*>(sStat + qu);
+          *reinterpret_cast<float4*>(st_l + 4) = *reinterpret_cast<const float4*>(sStat + qu + 4);
+          *reinterpret_cast<float4*>(st_d) = *reinterpret_cast<const float4*>(sStat + 64 + qu);
+          *reinterpret_cast<float4*>(st_d + 4) = *reinterpret_cast<const float4*>(sStat + 64 + qu + 4);
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int e = g * 8 + e2 * 2;
+            const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, make_float2(st_l[e2 * 2], st_l[e2 * 2 + 1]));
+            float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            if (diag) {
+              const int qc = h * 64 + qu + e2 * 2;  // query column inside the block
+              if (qc < kr) pr.x = 0.f;
+              if (qc + 1 < kr) pr.y = 0.f;
+            }
+            const float2 dd =
+                fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), make_float2(st_d[e2 * 2], st_d[e2 * 2 + 1])));
+            __nv_bfloat162 pb = __floats2bfloat162_rn(pr.x, pr.y);
+            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
+            hd[e2] = __floats2bfloat162_rn(dd.x, dd.y);
+          }
+          *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, qu)) = wd;
+        }
+        // packed P^T of queries c0 .. c0+31 over their own (consumed) S^T columns [c0, c0 + 16)
+        tmem_st_16cols_async(ts_h(h) + lane_off + c0, ppk);
+      }
+      if (!ok) break;
+      tmem_st_wait();
+      tc_fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ds_full[h]);
+    }
+    // the last dV/dK MMAs: wait for the final Q/dO release (committed after them)
+    if (ok) ok = mbar_wait(&q_empty[(n_iter - 1) & 1], ((n_iter - 1) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
+                           MMF_WAIT_TIMEOUT_NS, false);
+    if (ok) {
+      tc_fence_after();
+      const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hq + hq;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        float* dst = (which == 0 ? p.dv_h : p.dk_h) + row * D + wg * (D / 2);
+        const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off + wg * (D / 2);
+        const float f = which == 0 ? 1.f : p.scale;
+        float v[D / 2];
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tb + c * 32, v + c * 32);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < D / 8; ++g)
+          *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4] * f, v[g * 4 + 1] * f, v[g * 4 + 2] * f, v[g * 4 + 3] * f);
+      }
     }
   } else {
     const int q = warp & 3;
@@ -1525,7 +1636,8 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
 // 3: as 0 with the whole score row held in registers (one TMEM read per key block),
 // 4: as 3 in 3 warpgroups with the registers moved to the softmax warps (attn_fwd3_kernel)
 std::atomic<int> g_fwd_variant{0};
-// backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask)
+// backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask),
+// 2 as 1 with the dK/dV kernel's two warpgroups on alternate 64-query units (ping-pong)
 std::atomic<int> g_bwd_variant{0};
 
 template <int D>
@@ -1596,6 +1708,8 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   if (!attr_set[dev]) {
     cudaFuncSetAttribute(attn_bwd_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         BwdSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_dq_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     attr_set[dev] = true;
@@ -1622,8 +1736,11 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
   CUtensorMap mdo = map_bthd(a.dout, a.B, a.T, a.Hq, D);
   dim3 grid(a.T / KB, a.Hq, a.B);
-  const bool v2 = g_bwd_variant.load() == 1;
-  if (v2)
+  const int bv = g_bwd_variant.load();
+  const bool v2 = bv >= 1;
+  if (bv == 2)
+    attn_bwd_kernel<D, true, true><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  else if (v2)
     attn_bwd_kernel<D, true><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
   else
     attn_bwd_kernel<D, false><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
