@@ -110,3 +110,109 @@ def test_weight_gradient_segments(N, ws):
     for r in range(N):
         seg = r // seg_rows
         assert 0 <= seg < ws and 0 <= r - seg * seg_rows < seg_rows
+
+
+# ----------------------------------------------------------------- attention (csrc/attention.cu)
+QB = KB = 128
+
+
+def swz_offset(row, col):
+    chunk, c = col >> 6, col & 63
+    unit = (c >> 3) ^ (row & 7)
+    return chunk * (128 * 128) + row * 128 + unit * 16 + (c & 7) * 2
+
+
+def _bwd_unit_elements(ping):
+    """(warp, lane) -> the (key row, query column, dS^T byte offset, P^T TMEM column) each thread
+    handles for one 64-query unit of half h, as the plain (8 warps x 32 queries) and the ping-pong
+    (one warpgroup x 64 queries in two passes) elementwise code computes them."""
+    out = {}
+    for h in range(2):
+        items = []
+        warps = range(2, 6) if (ping and h == 0) else range(6, 10) if ping else range(2, 10)
+        for warp in warps:
+            q = warp & 3
+            for lane in range(32):
+                kr = q * 32 + lane
+                passes = [0, 32] if ping else [((warp - 2) >> 2) * 32]
+                for c0 in passes:
+                    for g in range(4):
+                        for e in range(8):
+                            qu = c0 + g * 8 + e                       # query column in the unit
+                            items.append((kr, h * 64 + qu, swz_offset(kr, c0 + g * 8) + 2 * e, c0 + g * 4 + e // 2))
+        out[h] = items
+    return out
+
+
+def test_attention_bwd_ping_pong_covers_each_unit_like_the_plain_layout():
+    """Each (key, query) element of a unit is produced exactly once, at the same dS^T smem byte
+    and the same packed-P^T TMEM column in both layouts, so the MMA side needs no change."""
+    plain, ping = _bwd_unit_elements(False), _bwd_unit_elements(True)
+    for h in range(2):
+        assert sorted(plain[h]) == sorted(ping[h])
+        keys = {(kr, qc) for kr, qc, _, _ in ping[h]}
+        assert len(keys) == len(ping[h]) == 128 * 64
+        offs = [o for _, _, o, _ in ping[h]]
+        assert len(set(offs)) == len(offs) and max(offs) < 16384  # one 16 KB dS^T buffer per half
+        # the dV MMA reads query k-step kk (16 queries) from TMEM column (kk >> 1) * 32 + (kk & 1) * 8
+        for kr, qc, _, col in ping[h]:
+            qu = qc - h * 64
+            kk = qu // 16
+            assert col == (kk >> 1) * 32 + (kk & 1) * 8 + (qu % 16) // 2
+
+
+def test_attention_bwd_ping_pong_statistics_and_mask():
+    """Warpgroup wg stages -lse*log2e / -delta of queries wg*64 .. wg*64+63 at [0, 64) / [64, 128)
+    of its own 128 floats; the packed mask (qc < kr per pair) equals the plain one."""
+    for wg in range(2):
+        staged = {}
+        for wt in range(128):
+            src = "lse" if wt < 64 else "delta"
+            staged[wt] = (src, wg * 64 + (wt & 63))
+        for qu in range(64):
+            assert staged[qu] == ("lse", wg * 64 + qu) and staged[64 + qu] == ("delta", wg * 64 + qu)
+        assert 0 <= wg * 128 and wg * 128 + 127 < 256  # inside the 1 KB statistics region
+    for h in range(2):
+        for kr in range(128):
+            for qu in range(0, 64, 2):
+                qc = h * 64 + qu
+                plain = [qc + t < kr for t in range(2)]
+                packed = [qc < kr, qc + 1 < kr]
+                assert plain == packed
+
+
+def test_attention_forward_packed_mask_and_exponent():
+    """Forward v2: keys past the query row are masked with e > qi - k0, and exp2(s*c - m) with m the
+    scaled max equals exp2(s*c - max(s*c)) because c > 0."""
+    import math
+    import random
+
+    for qb in range(3):
+        for j in range(qb + 1):
+            for r in range(0, 128, 7):
+                qi = qb * QB + r
+                for hf in range(2):
+                    k0 = j * KB + hf * 64
+                    for e in range(64):
+                        assert (e > qi - k0) == (j * KB + hf * 64 + e > qi)
+    rnd = random.Random(0)
+    c = 0.088 * 1.4426950408889634
+    s = [rnd.uniform(-30, 30) for _ in range(128)]
+    m_scaled = max(s) * c
+    assert abs(m_scaled - max(x * c for x in s)) < 1e-12
+    ref = [2 ** (x * c - max(y * c for y in s)) for x in s]
+    got = [2 ** (math.fma(x, c, -m_scaled) if hasattr(math, "fma") else x * c - m_scaled) for x in s]
+    assert max(abs(a - b) for a, b in zip(ref, got)) < 1e-12
+
+
+def test_attention_fwd3_register_split():
+    """attn_fwd3_kernel: 384 threads launched at 168 registers; WG0 drops to 56, the two softmax
+    warpgroups rise to 224.  The block's pool and each sub-partition's 16384 registers suffice."""
+    launch, ctrl, soft = 168, 56, 224
+    assert 128 * ctrl + 256 * soft <= 384 * launch
+    # warp w runs on sub-partition w % 4: one WG0 warp and two softmax warps each
+    for sp in range(4):
+        warps = [w for w in range(12) if w % 4 == sp]
+        regs = sum((ctrl if w < 4 else soft) * 32 for w in warps)
+        assert regs <= 16384
+    assert all(r % 8 == 0 for r in (launch, ctrl, soft)) and 24 <= ctrl and soft <= 256
