@@ -19,6 +19,7 @@
 #include <string>
 
 #include "attention.h"
+#include "exp2_poly.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
 
@@ -407,7 +408,7 @@ __device__ __forceinline__ void fwd_softmax_tile(const AttnParams& p, uint32_t t
 // on the raw scores (the scale is positive), three at a time; the exponent argument is one
 // packed fma s*scale - m per pair of scores; the row sum is a packed add; the causal mask is
 // applied only on the diagonal block.
-template <int D, bool FULL_ROW>
+template <int D, bool FULL_ROW, int EMU = 0>
 __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_t tS, uint32_t tO, uint64_t* s_full,
                                                     uint64_t* p_full, uint64_t* pv_done, int qb, int nblk, int h,
                                                     int b, int q, int lane) {
@@ -487,7 +488,11 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
 #pragma unroll
       for (int e2 = 0; e2 < 32; ++e2) {
         const float2 x = ffma2(make_float2(v[2 * e2], v[2 * e2 + 1]), c2, nm);
-        const float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        // with EMU > 0, every EMU-th pair takes the FMA-pipe exponential (exp2_poly.cuh) so that
+        // the MUFU unit is not the only one computing exponentials
+        const bool emu = (EMU > 0) && (e2 % (EMU > 0 ? EMU : 1) == (EMU > 0 ? EMU : 1) - 1);
+        const float2 pp = emu ? make_float2(exp2_poly(x.x), exp2_poly(x.y))
+                              : make_float2(fast_exp2(x.x), fast_exp2(x.y));
         sum2 = fadd2(sum2, pp);
         __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
         pk[e2] = *reinterpret_cast<float*>(&pb);
@@ -535,7 +540,7 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
   }
 }
 
-template <int D, bool V2, bool FULL_ROW = false>
+template <int D, bool V2, bool FULL_ROW = false, int EMU = 0>
 __global__ void __launch_bounds__(ATT2_THREADS, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -680,7 +685,7 @@ __global__ void __launch_bounds__(ATT2_THREADS, 1)
     const int q = warp & 3;
     if (t == 0 || has_b) {
       if constexpr (V2)
-        fwd_softmax_tile_v2<D, FULL_ROW>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
+        fwd_softmax_tile_v2<D, FULL_ROW, EMU>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
                                t ? nblk_b : nblk_a, h, b, q, lane);
       else
         fwd_softmax_tile<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
@@ -1634,7 +1639,8 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
 // 0: two query tiles per CTA with the packed-arithmetic softmax (fwd_softmax_tile_v2),
 // 1: one tile per CTA, 2: two tiles with the plain softmax (fwd_softmax_tile),
 // 3: as 0 with the whole score row held in registers (one TMEM read per key block),
-// 4: as 3 in 3 warpgroups with the registers moved to the softmax warps (attn_fwd3_kernel)
+// 4: as 3 in 3 warpgroups with the registers moved to the softmax warps (attn_fwd3_kernel),
+// 5 / 6: as 0 with every 4th / 2nd pair of exponentials on the FMA pipe (exp2_poly.cuh)
 std::atomic<int> g_fwd_variant{0};
 // backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask),
 // 2 as 1 with the dK/dV kernel's two warpgroups on alternate 64-query units (ping-pong)
@@ -1652,6 +1658,10 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
     cudaFuncSetAttribute(attn_fwd2_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          Attn2Smem<D>::BYTES);
     cudaFuncSetAttribute(attn_fwd3_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd2_kernel<D, true, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Attn2Smem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd2_kernel<D, true, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Attn2Smem<D>::BYTES);
     attr_set[dev] = true;
   }
   AttnParams p{};
@@ -1687,6 +1697,12 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
                                " registers per thread; its register split needs " + std::to_string(ATT3_REGS_LAUNCH));
     dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
     attn_fwd3_kernel<D><<<grid, ATT3_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  } else if (g_fwd_variant.load() == 5) {
+    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+    attn_fwd2_kernel<D, true, false, 4><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
+  } else if (g_fwd_variant.load() == 6) {
+    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+    attn_fwd2_kernel<D, true, false, 2><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
   } else if (g_fwd_variant.load() == 3) {
     dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
     attn_fwd2_kernel<D, true, true><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);

@@ -29,8 +29,9 @@ _EXPERIMENTAL = pytest.mark.skipif(os.environ.get("MMF_TEST_EXPERIMENTAL") != "1
                                    reason="experimental kernel, enabled by MMF_TEST_EXPERIMENTAL=1")
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, pytest.param(3, marks=_EXPERIMENTAL), pytest.param(4, marks=_EXPERIMENTAL)],
-                         ids=["two_tiles_packed", "one_tile", "two_tiles_plain", "full_row", "three_warpgroups"])
+@pytest.mark.parametrize("variant", [0, 1, 2] + [pytest.param(v, marks=_EXPERIMENTAL) for v in (3, 4, 5, 6)],
+                         ids=["two_tiles_packed", "one_tile", "two_tiles_plain", "full_row", "three_warpgroups",
+                              "fma_exp_quarter", "fma_exp_half"])
 @pytest.mark.parametrize("B,T,Hq,Hkv,D", [(1, 128, 1, 1, 128), (2, 384, 4, 2, 128), (1, 512, 2, 2, 64),
                                           (1, 1024, 8, 2, 128), (1, 640, 2, 1, 64)])
 def test_attention_forward_matches_fp32(B, T, Hq, Hkv, D, variant):
