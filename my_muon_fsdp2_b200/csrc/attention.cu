@@ -1333,7 +1333,7 @@ struct AttnDqParams {
   int* err;
 };
 
-template <int D, bool V2>
+template <int D, bool V2, bool EARLY = false>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1492,6 +1492,39 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         mbar_arrive(&s_empty[st]);
         mbar_arrive(dp_empty);
       }
+      if constexpr (EARLY) {
+        // dS of this block into registers first (packed bf16 pairs), so that the math overlaps
+        // the previous block's dQ MMA; then wait for it to release the dS buffer and store
+        uint32_t packed[32];
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nl = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
+#pragma unroll
+        for (int e2 = 0; e2 < 32; ++e2) {
+          const int e = e2 * 2;
+          const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nl);
+          float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          if (diag) {
+            const int key = j * KB + c0 + e;
+            if (key > qi) pr.x = 0.f;
+            if (key + 1 > qi) pr.y = 0.f;
+          }
+          const float2 dd = fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), nd));
+          __nv_bfloat162 hb = __floats2bfloat162_rn(dd.x, dd.y);
+          packed[e2] = *reinterpret_cast<uint32_t*>(&hb);
+        }
+        if (j >= 1 && !mbar_wait(ds_empty, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          *reinterpret_cast<uint4*>(sDS + swz_offset(r, c0 + g * 8)) =
+              make_uint4(packed[g * 4], packed[g * 4 + 1], packed[g * 4 + 2], packed[g * 4 + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ds_full);
+        continue;
+      }
       // the dS buffer must have been consumed by the previous dQ MMA
       if (j >= 1 && !mbar_wait(ds_empty, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
         ok = false;
@@ -1643,7 +1676,8 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
 // 5 / 6: as 0 with every 4th / 2nd pair of exponentials on the FMA pipe (exp2_poly.cuh)
 std::atomic<int> g_fwd_variant{0};
 // backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask),
-// 2 as 1 with the dK/dV kernel's two warpgroups on alternate 64-query units (ping-pong)
+// 2 as 1 with the dK/dV kernel's two warpgroups on alternate 64-query units (ping-pong) and
+// the dQ kernel computing dS before it waits for the dS buffer
 std::atomic<int> g_bwd_variant{0};
 
 template <int D>
@@ -1728,6 +1762,8 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
                          BwdSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_dq_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         DqSmem<D>::BYTES);
     attr_set[dev] = true;
   }
   const int64_t rows = static_cast<int64_t>(a.B) * a.T * a.Hq;
@@ -1772,7 +1808,10 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   pq.delta = a.delta;
   pq.dq = static_cast<__nv_bfloat16*>(a.dq);
   pq.err = p.err;
-  if (v2)
+  if (bv == 2)
+    attn_bwd_dq_kernel<D, true, true><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(
+        mq, mk, mv, mdo, pq);
+  else if (v2)
     attn_bwd_dq_kernel<D, true><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, pq);
   else
     attn_bwd_dq_kernel<D, false><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo,
