@@ -1096,17 +1096,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tmem_ld_32cols_async(ts_h(h) + lane_off + c0, sv);
         tmem_ld_32cols_async(tdp_h(h) + lane_off + c0, dp);
         tmem_ld_wait();
-        // the dS^T buffer of this half was last read by the dK MMA of unit u-2
-        if (pass == 0 && u >= 2 &&
-            !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS,
-                       false)) {
-          ok = false;
-          break;
-        }
         float ppk[16];
+        uint4 wds[4];  // dS^T of this pass, stored once the buffer is free
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          uint4 wd;
+          uint4& wd = wds[g];
           __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
           const int qu = c0 + g * 8;  // query column inside the unit
           float st_l[8], st_d[8];
@@ -1130,10 +1124,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
             hd[e2] = __floats2bfloat162_rn(dd.x, dd.y);
           }
-          *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, qu)) = wd;
         }
-        // packed P^T of queries c0 .. c0+31 over their own (consumed) S^T columns [c0, c0 + 16)
+        // packed P^T of queries c0 .. c0+31 over their own (consumed) S^T columns [c0, c0 + 16);
+        // the dV MMA that read this half's previous P^T completed before S^T of this unit
         tmem_st_16cols_async(ts_h(h) + lane_off + c0, ppk);
+        // the dS^T buffer of this half was last read by the dK MMA of unit u-2
+        if (pass == 0 && u >= 2 &&
+            !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS,
+                       false)) {
+          tmem_st_wait();  // leave no TMEM store in flight on the way out
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wds[g];
       }
       if (!ok) break;
       tmem_st_wait();
