@@ -1,4 +1,4 @@
-"""``fsdp2_utils.comm``."""
+"""``fsdp2_utils.comm`` (the reference's public names of src/fsdp2_utils/comm.py:18-267)."""
 from ..parallel.comm import (  # noqa: F401
     all_gather,
     all_gather_grads,

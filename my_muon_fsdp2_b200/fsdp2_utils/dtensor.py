@@ -1,4 +1,4 @@
-"""``fsdp2_utils.dtensor``."""
+"""``fsdp2_utils.dtensor`` (the reference's public names of src/fsdp2_utils/dtensor.py:17-193)."""
 from ..parallel.dtensor import (  # noqa: F401
     HAS_DTENSOR,
     create_dtensor,

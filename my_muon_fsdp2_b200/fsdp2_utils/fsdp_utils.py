@@ -1,4 +1,4 @@
-"""``fsdp2_utils.fsdp_utils``."""
+"""``fsdp2_utils.fsdp_utils`` (the reference's public names of src/fsdp2_utils/fsdp_utils.py:19-119)."""
 from ..parallel.fsdp_utils import (  # noqa: F401
     HAS_FSDP2,
     apply_local_updates,

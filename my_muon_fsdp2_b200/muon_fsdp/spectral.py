@@ -1,4 +1,4 @@
-"""``muon_fsdp.spectral``: spectral operations for SSO."""
+"""``muon_fsdp.spectral``: spectral operations for SSO (the reference's public names of src/muon_fsdp/spectral.py:18-282)."""
 from ..ops.spectral import (
     apply_spectral_retraction,
     bisect_spectral_radius,
