@@ -18,11 +18,16 @@ from ..utils.tracing import nvtx_range
 
 class Trainer:
     def __init__(self, model: nn.Module, optimizers: Sequence, grad_accum: int = 1, device=None,
-                 step_timer=None, max_grad_norm: Optional[float] = None, time_steps: bool = False):
+                 step_timer=None, max_grad_norm: Optional[float] = None, time_steps: bool = False,
+                 keep_gathered: bool = True):
         """``max_grad_norm``: clip the global gradient norm before the optimizer steps, as the
         reference trainers do with 1.0 (examples/train_gpt.py:367-371); None disables it.
         ``time_steps``: bracket every step with CUDA events (read by ``last_step_ms`` and
-        ``metrics_summary``; no synchronisation inside the step)."""
+        ``metrics_summary``; no synchronisation inside the step).
+        ``keep_gathered``: FSDP2 modules do not reshard after the backward of a non-final
+        micro-batch, so the next micro-batch's forward needs no all-gather (FSDP2's
+        ``set_reshard_after_backward``; the root module then gathers once per step); the last
+        micro-batch reshards as usual."""
         self.model = model
         self.max_grad_norm = max_grad_norm
         self.last_grad_norm: Optional[torch.Tensor] = None
@@ -33,6 +38,7 @@ class Trainer:
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
         self.step_timer = step_timer  # optional EventTimer around the optimizer steps
         self.fsdp = is_fsdp_module(model)
+        self.keep_gathered = bool(keep_gathered) and self.fsdp and self.grad_accum > 1
         self.time_steps = bool(time_steps) and self.device.type == "cuda"
         self._step_events = None
         self._prev_comm: Optional[dict] = None
@@ -45,6 +51,10 @@ class Trainer:
         last = i == self.grad_accum - 1
         if self.fsdp:
             self.model.set_requires_gradient_sync(last)
+            if self.keep_gathered and i in (0, self.grad_accum - 1):
+                # no resharding after the backward of a non-final micro-batch: the next forward
+                # finds the parameters still gathered
+                self.model.set_reshard_after_backward(last)
         t = tokens[i]
         with nvtx_range(f"trainer/micro_batch_{i}/forward"):
             loss = self.model(t[:, :-1], t[:, 1:]) / self.grad_accum
