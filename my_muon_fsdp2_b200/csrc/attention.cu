@@ -902,7 +902,7 @@ struct BwdSmem {
   static constexpr int BYTES = BYTES0 > 120 * 1024 ? BYTES0 : 120 * 1024;
 };
 
-template <int D, bool V2, bool PING = false>
+template <int D, bool V2, bool PING = false, int EMU = 0>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1112,7 +1112,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           for (int e2 = 0; e2 < 4; ++e2) {
             const int e = g * 8 + e2 * 2;
             const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, make_float2(st_l[e2 * 2], st_l[e2 * 2 + 1]));
-            float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            // with EMU > 0, every EMU-th pair of exponentials on the FMA pipe (exp2_poly.cuh)
+            const bool emu = (EMU > 0) && ((g * 4 + e2) % (EMU > 0 ? EMU : 1) == (EMU > 0 ? EMU : 1) - 1);
+            float2 pr = emu ? make_float2(exp2_poly(x.x), exp2_poly(x.y)) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
             if (diag) {
               const int qc = h * 64 + qu + e2 * 2;  // query column inside the block
               if (qc < kr) pr.x = 0.f;
@@ -1337,7 +1339,7 @@ struct AttnDqParams {
   int* err;
 };
 
-template <int D, bool V2, bool EARLY = false>
+template <int D, bool V2, bool EARLY = false, int EMU = 0>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1506,7 +1508,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int e2 = 0; e2 < 32; ++e2) {
           const int e = e2 * 2;
           const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nl);
-          float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          const bool emu = (EMU > 0) && (e2 % (EMU > 0 ? EMU : 1) == (EMU > 0 ? EMU : 1) - 1);
+          float2 pr = emu ? make_float2(exp2_poly(x.x), exp2_poly(x.y)) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
           if (diag) {
             const int key = j * KB + c0 + e;
             if (key > qi) pr.x = 0.f;
@@ -1681,7 +1684,8 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
 std::atomic<int> g_fwd_variant{0};
 // backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask),
 // 2 as 1 with the dK/dV kernel's two warpgroups on alternate 64-query units (ping-pong) and
-// the dQ kernel computing dS before it waits for the dS buffer
+// the dQ kernel computing dS before it waits for the dS buffer, 3 as 2 with every 4th pair of
+// exponentials on the FMA pipe (exp2_poly.cuh)
 std::atomic<int> g_bwd_variant{0};
 
 template <int D>
@@ -1764,6 +1768,10 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
     cudaFuncSetAttribute(attn_bwd_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          BwdSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_kernel<D, true, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         BwdSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         DqSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_dq_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1794,7 +1802,9 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   dim3 grid(a.T / KB, a.Hq, a.B);
   const int bv = g_bwd_variant.load();
   const bool v2 = bv >= 1;
-  if (bv == 2)
+  if (bv == 3)
+    attn_bwd_kernel<D, true, true, 4><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  else if (bv == 2)
     attn_bwd_kernel<D, true, true><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
   else if (v2)
     attn_bwd_kernel<D, true><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
@@ -1812,7 +1822,10 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   pq.delta = a.delta;
   pq.dq = static_cast<__nv_bfloat16*>(a.dq);
   pq.err = p.err;
-  if (bv == 2)
+  if (bv == 3)
+    attn_bwd_dq_kernel<D, true, true, 4><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(
+        mq, mk, mv, mdo, pq);
+  else if (bv == 2)
     attn_bwd_dq_kernel<D, true, true><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(
         mq, mk, mv, mdo, pq);
   else if (v2)

@@ -51,7 +51,8 @@ def test_attention_forward_matches_fp32(B, T, Hq, Hkv, D, variant):
     assert rel_err(lse, rlse) < 1e-3
 
 
-@pytest.mark.parametrize("bwd_variant", [0, 1, pytest.param(2, marks=_EXPERIMENTAL)], ids=["plain", "packed", "ping_pong"])
+@pytest.mark.parametrize("bwd_variant", [0, 1] + [pytest.param(v, marks=_EXPERIMENTAL) for v in (2, 3)],
+                         ids=["plain", "packed", "ping_pong", "ping_pong_fma_exp"])
 @pytest.mark.parametrize("B,T,Hq,Hkv,D", [(1, 128, 1, 1, 128), (2, 256, 4, 2, 128), (1, 384, 2, 1, 64),
                                           (1, 200, 4, 2, 128)])
 def test_attention_backward_matches_fp32(B, T, Hq, Hkv, D, bwd_variant):
