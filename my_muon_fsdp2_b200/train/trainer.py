@@ -19,15 +19,16 @@ from ..utils.tracing import nvtx_range
 class Trainer:
     def __init__(self, model: nn.Module, optimizers: Sequence, grad_accum: int = 1, device=None,
                  step_timer=None, max_grad_norm: Optional[float] = None, time_steps: bool = False,
-                 keep_gathered: bool = True):
+                 keep_gathered: bool = False):
         """``max_grad_norm``: clip the global gradient norm before the optimizer steps, as the
         reference trainers do with 1.0 (examples/train_gpt.py:367-371); None disables it.
         ``time_steps``: bracket every step with CUDA events (read by ``last_step_ms`` and
         ``metrics_summary``; no synchronisation inside the step).
         ``keep_gathered``: FSDP2 modules do not reshard after the backward of a non-final
         micro-batch, so the next micro-batch's forward needs no all-gather (FSDP2's
-        ``set_reshard_after_backward``; the root module then gathers once per step); the last
-        micro-batch reshards as usual."""
+        ``set_reshard_after_backward``; the root module then gathers once per step) at the cost
+        of holding the gathered parameters through the accumulation; the last micro-batch
+        reshards as usual."""
         self.model = model
         self.max_grad_norm = max_grad_norm
         self.last_grad_norm: Optional[torch.Tensor] = None

@@ -57,7 +57,7 @@ def _ranked(rank, world, arch, mode):
 
     model = _build(arch)
     _shard(model, arch, mode)
-    trainer = Trainer(model, _opts(model), grad_accum=ACCUM, device="cpu", max_grad_norm=1.0)
+    trainer = Trainer(model, _opts(model), grad_accum=ACCUM, device="cpu", max_grad_norm=1.0, keep_gathered=True)
     losses, norms = [], []
     for s in range(STEPS):
         losses.append(trainer.train_step(_batch(s, rank)))
