@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--rs-mode", choices=["overlap", "fused"], default="overlap",
                     help="symm: reduce-scatter on a side stream (overlap) or from the GEMM epilogue (fused)")
+    ap.add_argument("--keep-gathered", action="store_true",
+                    help="FSDP2 modules stay gathered between the micro-batches of a step (Trainer keep_gathered)")
     ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="symm",
                     help="fsdp2: fully_shard everywhere; symm: block linears on symmetric memory with the "
                          "fused all-gather GEMM / GEMM reduce-scatter kernels, the rest fully_shard")
@@ -218,7 +220,7 @@ def main():
     else:
         from my_muon_fsdp2_b200.train import Trainer
 
-        trainer = Trainer(model, opts, grad_accum=ga, step_timer=opt_timer)
+        trainer = Trainer(model, opts, grad_accum=ga, step_timer=opt_timer, keep_gathered=args.keep_gathered)
 
     dev_batches = [synthetic_tokens(s, ga, mbs, seq, vocab, rank, device="cuda") for s in range(2)]
     for s in range(args.warmup):
@@ -281,7 +283,8 @@ def main():
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",
-                       "fsdp_impl": ((args.fsdp + (f"/{args.rs_mode}" if args.fsdp == "symm" else ""))
+                       "fsdp_impl": ((args.fsdp + (f"/{args.rs_mode}" if args.fsdp == "symm" else "")
+                                      + ("/keep_gathered" if args.keep_gathered else ""))
                                      if args.impl == "ours" else "fully_shard"),
                        "tokens_per_step": tokens_per_step,
                        "l2": "no flush: per-step working set (16 GB bf16 weights + activations) >> 126 MB L2",
