@@ -388,3 +388,39 @@ def test_symm_fsdp_dcp_checkpoint_resume(tmp_path):
     assert res["extra"] == {"step": 1}
     for n in res["want"]:
         assert torch.equal(res["got"][n], res["want"][n]), n
+
+
+class CkptNet(Net):
+    """Net with each block under non-reentrant activation checkpointing."""
+
+    def forward(self, x):
+        from torch.utils.checkpoint import checkpoint
+
+        x = self.inp(x)
+        for b in self.layers:
+            x = checkpoint(b, x, use_reentrant=False)
+        return self.out(x)
+
+
+def _ckpt_grads(rank, world):
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    model = CkptNet()
+    apply_symm_fsdp(model)
+    for mb in range(2):
+        model.set_requires_gradient_sync(mb == 1)
+        x, y = _data(mb, rank)
+        ((model(x) - y) ** 2).mean().div(2).backward()
+    return {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+
+
+def test_symm_fsdp_with_activation_checkpointing():
+    """Recomputing a block in backward runs its SymmLinears' forward again (on the resident
+    weights) and their gradient path once: gradients equal the single-process ones."""
+    got = run_ranks(_ckpt_grads, 2)
+    ref = Net()
+    for mb in range(2):
+        xs, ys = zip(*[_data(mb, r) for r in range(2)])
+        ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
+    for n, p in ref.named_parameters():
+        assert rel_err(got[n], p.grad) < 1e-5, n
