@@ -424,3 +424,35 @@ def test_symm_fsdp_with_activation_checkpointing():
         ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
     for n, p in ref.named_parameters():
         assert rel_err(got[n], p.grad) < 1e-5, n
+
+
+def _frozen(rank, world):
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    model = Net()
+    model.layers[0].up.weight.requires_grad_(False)  # frozen before sharding
+    ctl = apply_symm_fsdp(model)
+    x, y = _data(0, rank)
+    ((model(x) - y) ** 2).mean().div(2).backward()
+    frozen = model.layers[0].up.weight
+    return {"frozen_grad": frozen.grad is None, "frozen_rg": frozen.requires_grad,
+            "grads": {n: _full(p.grad).clone() for n, p in model.named_parameters() if p.grad is not None},
+            "reduced": ctl.stats()["bytes_reduced"]}
+
+
+def test_symm_fsdp_frozen_weight():
+    """A frozen linear keeps no gradient and moves no reduce-scatter traffic; the input gradient
+    still flows through it to the layers below."""
+    got = run_ranks(_frozen, 2)
+    assert got["frozen_grad"] and not got["frozen_rg"]
+    ref = Net()
+    ref.layers[0].up.weight.requires_grad_(False)
+    xs, ys = zip(*[_data(0, r) for r in range(2)])
+    ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
+    names = {n for n, p in ref.named_parameters() if p.grad is not None}
+    assert set(got["grads"]) == names
+    for n, p in ref.named_parameters():
+        if p.grad is not None:
+            assert rel_err(got["grads"][n], p.grad) < 1e-5, n
+    shard = ((H // 2) * D + (D // 2) * H) * 4  # one up and one down weight: the other rank's rows
+    assert got["reduced"] == 2 * shard - (H // 2) * D * 4
