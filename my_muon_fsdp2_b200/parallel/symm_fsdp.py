@@ -194,8 +194,11 @@ class SymmFSDP:
             off += (s + 7) // 8 * 8  # 16-byte aligned shards
         total = max(off, 8)
         dtype = self.modules[0].weight.dtype
-        # peer-mapped (symmetric) buffers only when there are peers; one rank keeps plain memory
-        self.peer = self.fused and self.world > 1
+        if any(m.weight.dtype != dtype for m in self.modules):
+            raise ValueError("SymmFSDP: all weights must have one dtype (they share one shard buffer)")
+        # peer-mapped (symmetric) buffers only when there are peers; one rank keeps plain memory.
+        # The fused kernels take bf16; other dtypes gather and reduce through torch.distributed.
+        self.peer = self.fused and self.world > 1 and dtype == torch.bfloat16
         # weights whose shapes the fused kernels take (N % 256, (N/world) % 128, K % 256); the
         # others gather / reduce-scatter through NCCL, still once per step for the gather
         self.fused_ok = [self.peer and fusable_shape(n, k, self.world) for n, k in self.shapes]
