@@ -13,7 +13,6 @@ from typing import Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from ..ops.model_ops import causal_attention, fused_linear_cross_entropy, gelu, layer_norm
 

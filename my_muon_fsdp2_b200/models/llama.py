@@ -7,13 +7,11 @@ LM-head cross entropy are this library's sm_100a kernels (``ops.model_ops``).
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 from typing import Optional
 
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from ..ops.model_ops import apply_rope, causal_attention, fused_linear_cross_entropy, rms_norm, swiglu
 from ..parallel.symm_fsdp import multi_linear

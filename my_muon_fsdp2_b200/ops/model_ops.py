@@ -5,8 +5,6 @@ plain PyTorch with the same math.  Every forward saves only what its backward ne
 """
 from __future__ import annotations
 
-import math
-
 import torch
 import torch.nn.functional as F
 

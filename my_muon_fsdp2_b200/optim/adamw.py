@@ -9,7 +9,6 @@ from __future__ import annotations
 
 import math
 from collections import OrderedDict
-from typing import Optional
 
 import torch
 from torch.optim import Optimizer

@@ -12,7 +12,6 @@ from __future__ import annotations
 
 from typing import List, Optional
 
-import torch
 import torch.nn as nn
 
 from ..ops.newton_schulz import muon_lr_scale

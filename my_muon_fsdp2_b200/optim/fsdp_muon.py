@@ -29,7 +29,7 @@ import torch
 import torch.nn as nn
 from torch.optim import Optimizer
 
-from ..ops.newton_schulz import _ns_torch, muon_lr_scale, zeropower_via_newtonschulz5
+from ..ops.newton_schulz import muon_lr_scale, zeropower_via_newtonschulz5
 from ..parallel.dtensor import get_local_tensor, is_dtensor
 from ..parallel.fsdp_utils import collect_fsdp_modules
 from ..parallel.muon_engine import MODE_EMA, MuonHyper, MuonTask

@@ -29,7 +29,6 @@ CPU tensors (gloo process groups, tests) run the same schedule with PyTorch math
 """
 from __future__ import annotations
 
-import math
 from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence, Tuple

@@ -7,7 +7,7 @@ gradients and returns the loss as a Python float (one device->host read).
 """
 from __future__ import annotations
 
-from typing import Iterable, List, Optional, Sequence
+from typing import Optional, Sequence
 
 import torch
 import torch.nn as nn
