@@ -23,8 +23,17 @@ def _entry(rank, world, port, fn, result_path, args):
 
 
 def run_ranks(fn, world, *args):
-    """Run fn(rank, world, *args) on `world` gloo ranks; return rank 0's return value."""
-    with tempfile.TemporaryDirectory() as d:
-        path = os.path.join(d, "result.pt")
-        mp.spawn(_entry, args=(world, free_port(), fn, path, args), nprocs=world, join=True)
-        return torch.load(path, weights_only=False)
+    """Run fn(rank, world, *args) on `world` gloo ranks; return rank 0's return value.  A start-up
+    that lost its rendezvous port to another process (tests run in parallel) is retried on a new
+    port; any other failure propagates."""
+    for attempt in range(3):
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "result.pt")
+            try:
+                mp.spawn(_entry, args=(world, free_port(), fn, path, args), nprocs=world, join=True)
+            except mp.ProcessRaisedException as e:
+                msg = str(e).lower()
+                if attempt < 2 and ("address already in use" in msg or "eaddrinuse" in msg):
+                    continue
+                raise
+            return torch.load(path, weights_only=False)

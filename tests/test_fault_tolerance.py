@@ -52,6 +52,7 @@ def _raising_rank(rank, world):
     hb = Heartbeat(store, rank, world, interval_s=0.05).start()
     inj = FaultInjector(rank, raise_at=(1, 1))
     out = None
+    dist.barrier()  # both ranks start together, however late either process came up
     for step in range(3):
         try:
             inj.on_step(step, hb)
@@ -60,7 +61,8 @@ def _raising_rank(rank, world):
             time.sleep(2.5)
             return None
         try:
-            guarded_barrier(timeout_s=1.0, heartbeat=hb if step > 0 else None)
+            # step 0 is fault-free: a generous limit keeps a loaded machine from tripping it
+            guarded_barrier(timeout_s=1.0 if step > 0 else 10.0, heartbeat=hb if step > 0 else None)
         except RankFailure as e:
             out = {"step": step, "ranks": e.ranks}
             break
