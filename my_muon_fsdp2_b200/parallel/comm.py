@@ -71,10 +71,19 @@ def chunk_offset(rows: int, world: int, rank: int) -> int:
 
 
 def all_gather(tensors: Sequence[torch.Tensor], group: Optional[dist.ProcessGroup] = None) -> List[torch.Tensor]:
-    """All-gather each tensor along dim 0 (equal local sizes), one bucketed collective per dtype."""
+    """All-gather each tensor along dim 0 (equal local sizes), one bucketed collective per dtype.
+    A DTensor (e.g. an FSDP2 gradient) is gathered to its full tensor over its own mesh."""
     tensors = list(tensors)
     if not is_available() or get_world_size(group) == 1 or not tensors:
         return tensors
+    from .dtensor import is_dtensor
+
+    if any(is_dtensor(t) for t in tensors):
+        plain = [i for i, t in enumerate(tensors) if not is_dtensor(t)]
+        out = [t.full_tensor() if is_dtensor(t) else None for t in tensors]
+        for i, g in zip(plain, all_gather([tensors[i] for i in plain], group=group)):
+            out[i] = g
+        return out
     ws = get_world_size(group)
     out: List[Optional[torch.Tensor]] = [None] * len(tensors)
     buckets: "OrderedDict[tuple, List[int]]" = OrderedDict()

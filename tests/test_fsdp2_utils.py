@@ -193,3 +193,28 @@ class TestCommandLines:
             fsdp2_utils_main(["--version"])
         assert e.value.code == 0
         assert __version__ in capsys.readouterr().out
+
+
+def _gather_dtensor(rank, world):
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import distribute_tensor
+    from torch.distributed.tensor.placement_types import Shard
+
+    from my_muon_fsdp2_b200 import all_gather_grads
+
+    torch.manual_seed(0)
+    full = torch.randn(6, 3)
+    mesh = init_device_mesh("cpu", (world,))
+    d = distribute_tensor(full, mesh, [Shard(0)])
+    plain = torch.full((2, 2), float(rank))
+    g_d, g_p = all_gather_grads([d, plain])
+    return {"dtensor_full": bool(torch.equal(g_d, full)) and not hasattr(g_d, "to_local"),
+            "plain": g_p}
+
+
+def test_all_gather_grads_accepts_fsdp2_gradients():
+    """FSDP2 gradients are DTensors: they gather to their full plain tensors (the reference's
+    helper fails on them with a missing sharding strategy); plain tensors concatenate along dim 0."""
+    got = run_ranks(_gather_dtensor, 2)
+    assert got["dtensor_full"]
+    assert torch.equal(got["plain"], torch.tensor([[0.0, 0.0], [0.0, 0.0], [1.0, 1.0], [1.0, 1.0]]))
