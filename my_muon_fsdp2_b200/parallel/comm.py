@@ -147,30 +147,45 @@ def scatter_updates(updates: Sequence[torch.Tensor], src_rank: int = 0,
     return out
 
 
-def all_reduce(tensor: torch.Tensor, op=None, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+def _each(tensors):
+    """A list of tensors (the reference's form) or one tensor (accepted as well)."""
+    return [tensors] if isinstance(tensors, torch.Tensor) else list(tensors)
+
+
+def all_reduce(tensors, op=None, group: Optional[dist.ProcessGroup] = None):
+    """In-place all-reduce of each tensor (``op`` defaults to SUM); returns ``tensors``
+    (``src/fsdp2_utils/comm.py:180-201``: a list of tensors; a single tensor also works)."""
     if not is_available() or get_world_size(group) == 1:
-        return tensor
-    dist.all_reduce(tensor, op=op if op is not None else dist.ReduceOp.SUM, group=group)
-    return tensor
+        return tensors
+    for t in _each(tensors):
+        dist.all_reduce(t, op=op if op is not None else dist.ReduceOp.SUM, group=group)
+    return tensors
 
 
-def all_reduce_sum(tensor: torch.Tensor, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
-    return all_reduce(tensor, dist.ReduceOp.SUM if is_available() else None, group)
+def all_reduce_sum(tensors, group: Optional[dist.ProcessGroup] = None):
+    return all_reduce(tensors, dist.ReduceOp.SUM if is_available() else None, group)
 
 
-def all_reduce_avg(tensor: torch.Tensor, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+def all_reduce_avg(tensors, group: Optional[dist.ProcessGroup] = None):
+    """Sum, then divide by the group size (as the reference does, for every backend)."""
     if not is_available() or get_world_size(group) == 1:
-        return tensor
-    all_reduce(tensor, dist.ReduceOp.SUM, group)
-    tensor.div_(get_world_size(group))
-    return tensor
+        return tensors
+    all_reduce(tensors, dist.ReduceOp.SUM, group)
+    ws = get_world_size(group)
+    for t in _each(tensors):
+        t.div_(ws)
+    return tensors
 
 
-def broadcast(tensor: torch.Tensor, src: int = 0, group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
+def broadcast(tensors, src_rank: int = 0, group: Optional[dist.ProcessGroup] = None, *, src: Optional[int] = None):
+    """In-place broadcast of each tensor from ``src_rank`` (``src`` is accepted as an alias)."""
+    if src is not None:
+        src_rank = src
     if not is_available() or get_world_size(group) == 1:
-        return tensor
-    dist.broadcast(tensor, src=src, group=group)
-    return tensor
+        return tensors
+    for t in _each(tensors):
+        dist.broadcast(t, src=src_rank, group=group)
+    return tensors
 
 
 def barrier(group: Optional[dist.ProcessGroup] = None) -> None:

@@ -218,3 +218,25 @@ def test_all_gather_grads_accepts_fsdp2_gradients():
     got = run_ranks(_gather_dtensor, 2)
     assert got["dtensor_full"]
     assert torch.equal(got["plain"], torch.tensor([[0.0, 0.0], [0.0, 0.0], [1.0, 1.0], [1.0, 1.0]]))
+
+
+def _list_collectives(rank, world):
+    import torch.distributed as dist
+
+    from my_muon_fsdp2_b200 import fsdp2_utils as fu
+
+    a, b = torch.tensor([1.0 + rank]), torch.tensor([10.0 * (rank + 1)])
+    out = {"sum": [t.clone() for t in fu.all_reduce_sum([a.clone(), b.clone()])],
+           "avg": [t.clone() for t in fu.all_reduce_avg([a.clone(), b.clone()])],
+           "max": fu.all_reduce([a.clone()], op=dist.ReduceOp.MAX)[0],
+           "bcast": fu.broadcast([torch.tensor([float(rank)]), torch.tensor([rank + 5.0])], src_rank=1)}
+    return out
+
+
+def test_collectives_take_lists_like_the_reference():
+    """fsdp2_utils.comm takes lists of tensors and ``src_rank`` (src/fsdp2_utils/comm.py:180-244)."""
+    got = run_ranks(_list_collectives, 2)
+    assert [float(t) for t in got["sum"]] == [3.0, 30.0]
+    assert [float(t) for t in got["avg"]] == [1.5, 15.0]
+    assert float(got["max"]) == 2.0
+    assert [float(t) for t in got["bcast"]] == [1.0, 6.0]
