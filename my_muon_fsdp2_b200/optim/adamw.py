@@ -14,6 +14,7 @@ import torch
 from torch.optim import Optimizer
 
 from ._common import load_index_state_dict, local_of, zeros_state_like
+from .errors import InvalidParameterError, SparseGradientError
 
 
 def adamw_update_(params, grads, exp_avgs, exp_avg_sqs, step: int, lr: float, beta1: float, beta2: float,
@@ -47,13 +48,13 @@ def adamw_update_(params, grads, exp_avgs, exp_avg_sqs, step: int, lr: float, be
 class FusedAdamW(Optimizer):
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.01):
         if lr < 0:
-            raise ValueError(f"Invalid learning rate: {lr}")
+            raise InvalidParameterError(f"Invalid learning rate: {lr}")
         if not 0.0 <= betas[0] < 1.0 or not 0.0 <= betas[1] < 1.0:
-            raise ValueError(f"Invalid betas: {betas}")
+            raise InvalidParameterError(f"Invalid betas: {betas}")
         if eps < 0:
-            raise ValueError(f"Invalid epsilon value: {eps}")
+            raise InvalidParameterError(f"Invalid epsilon value: {eps}")
         if weight_decay < 0:
-            raise ValueError(f"Invalid weight_decay value: {weight_decay}")
+            raise InvalidParameterError(f"Invalid weight_decay value: {weight_decay}")
         super().__init__(params, dict(lr=lr, betas=tuple(betas), eps=eps, weight_decay=weight_decay))
 
     @torch.no_grad()
@@ -69,7 +70,7 @@ class FusedAdamW(Optimizer):
                 if p.grad is None:
                     continue
                 if p.grad.is_sparse:
-                    raise RuntimeError("FusedAdamW does not support sparse gradients")
+                    raise SparseGradientError("FusedAdamW does not support sparse gradients")
                 st = self.state[p]
                 if not st:
                     st["step"] = 0

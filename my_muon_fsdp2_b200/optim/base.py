@@ -18,6 +18,7 @@ from ..parallel.comm import all_gather_grads, get_world_size, is_distributed, sc
 from ..parallel.dtensor import get_local_tensor, is_dtensor
 from ..parallel.fsdp_utils import collect_fsdp_modules
 from ._common import index_state_dict, load_index_state_dict
+from .errors import InvalidParameterError
 
 logger = logging.getLogger(__name__)
 
@@ -26,7 +27,7 @@ class FSDPCompatibleOptimizer(Optimizer):
     def __init__(self, model: nn.Module, params: Optional[List[nn.Parameter]] = None,
                  defaults: Optional[Dict[str, Any]] = None, gradient_accumulation_steps: int = 1) -> None:
         if gradient_accumulation_steps < 1:
-            raise ValueError(f"Invalid gradient_accumulation_steps: {gradient_accumulation_steps}")
+            raise InvalidParameterError(f"Invalid gradient_accumulation_steps: {gradient_accumulation_steps}")
         self.model = model
         self.gradient_accumulation_steps = gradient_accumulation_steps
         self._step_count = 0

@@ -34,6 +34,7 @@ from ..parallel.dtensor import get_local_tensor, is_dtensor
 from ..parallel.fsdp_utils import collect_fsdp_modules
 from ..parallel.muon_engine import MODE_EMA, MuonHyper, MuonTask
 from ._common import default_engine, index_state_dict, load_index_state_dict, local_of, zeros_state_like
+from .errors import InvalidParameterError
 
 logger = logging.getLogger(__name__)
 
@@ -60,7 +61,7 @@ class FSDPMuonOptimizer(Optimizer):
         if update_rule not in ("muon", "reference"):
             raise ValueError(f"update_rule must be 'muon' or 'reference', got {update_rule!r}")
         if gradient_accumulation_steps < 1:
-            raise ValueError(f"Invalid gradient_accumulation_steps: {gradient_accumulation_steps}")
+            raise InvalidParameterError(f"Invalid gradient_accumulation_steps: {gradient_accumulation_steps}")
         self.model = model
         self.gradient_accumulation_steps = gradient_accumulation_steps
         self.update_rule = update_rule

@@ -26,6 +26,7 @@ from ..ops.newton_schulz import muon_lr_scale
 from ..parallel.muon_engine import MODE_EMA, MuonHyper, MuonTask
 from ._common import default_engine, load_index_state_dict, local_of, zeros_state_like
 from .adamw import adamw_update_
+from .errors import SparseGradientError
 
 
 class HybridMuonAdamW(optim.Optimizer):
@@ -57,7 +58,7 @@ class HybridMuonAdamW(optim.Optimizer):
                 if p.grad is None:
                     continue
                 if p.grad.is_sparse:
-                    raise RuntimeError("HybridMuonAdamW does not support sparse gradients")
+                    raise SparseGradientError("HybridMuonAdamW does not support sparse gradients")
                 (muon if self._is_muon(group, p) else adam).append(p)
             if muon:
                 self._muon_step(group, muon)

@@ -24,19 +24,20 @@ from torch.optim.optimizer import Optimizer
 from ..ops.newton_schulz import muon_lr_scale
 from ..parallel.muon_engine import MODE_EMA, MuonHyper, MuonTask
 from ._common import default_engine, load_index_state_dict, local_of, zeros_state_like
+from .errors import InvalidParameterError, SparseGradientError
 
 
 def _validate(lr, momentum, weight_decay, ns_steps, nesterov):
     if lr < 0.0:
-        raise ValueError(f"Invalid learning rate: {lr}")
+        raise InvalidParameterError(f"Invalid learning rate: {lr}")
     if momentum < 0.0 or momentum > 1.0:
-        raise ValueError(f"Invalid momentum value: {momentum}")
+        raise InvalidParameterError(f"Invalid momentum value: {momentum}")
     if weight_decay < 0.0:
-        raise ValueError(f"Invalid weight_decay value: {weight_decay}")
+        raise InvalidParameterError(f"Invalid weight_decay value: {weight_decay}")
     if ns_steps < 0:
-        raise ValueError(f"Invalid ns_steps value: {ns_steps}")
+        raise InvalidParameterError(f"Invalid ns_steps value: {ns_steps}")
     if nesterov and momentum <= 0:
-        raise ValueError("Nesterov momentum requires a positive momentum")
+        raise InvalidParameterError("Nesterov momentum requires a positive momentum")
 
 
 class MuonOptimizer(Optimizer):
@@ -80,7 +81,7 @@ class MuonOptimizer(Optimizer):
                 if p.grad is None:
                     continue
                 if p.grad.is_sparse:
-                    raise RuntimeError("MuonOptimizer does not support sparse gradients")
+                    raise SparseGradientError("MuonOptimizer does not support sparse gradients")
                 st = self.state[p]
                 if "momentum_buffer" not in st:
                     st["momentum_buffer"] = zeros_state_like(p)

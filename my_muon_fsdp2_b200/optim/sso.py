@@ -22,6 +22,7 @@ from ..ops.spectral import compute_target_radius, power_iteration, retraction_sc
 from ..parallel.dtensor import is_dtensor
 from ..parallel.muon_engine import MODE_EMA, MuonHyper, MuonTask
 from ._common import default_engine, load_index_state_dict, local_of, zeros_state_like
+from .errors import InvalidParameterError, SparseGradientError
 
 
 class SpectralSphereOptimizer(Optimizer):
@@ -29,21 +30,21 @@ class SpectralSphereOptimizer(Optimizer):
                  nesterov: bool = False, ns_steps: int = 5, power_iteration_steps: int = 10,
                  radius_mode: str = "spectral_mup", radius_scaler: float = 1.0, retract_mode: str = "hard") -> None:
         if lr < 0.0:
-            raise ValueError(f"Invalid learning rate: {lr}")
+            raise InvalidParameterError(f"Invalid learning rate: {lr}")
         if momentum < 0.0 or momentum > 1.0:
-            raise ValueError(f"Invalid momentum value: {momentum}")
+            raise InvalidParameterError(f"Invalid momentum value: {momentum}")
         if weight_decay < 0.0:
-            raise ValueError(f"Invalid weight_decay value: {weight_decay}")
+            raise InvalidParameterError(f"Invalid weight_decay value: {weight_decay}")
         if ns_steps < 0:
-            raise ValueError(f"Invalid ns_steps value: {ns_steps}")
+            raise InvalidParameterError(f"Invalid ns_steps value: {ns_steps}")
         if power_iteration_steps < 1:
-            raise ValueError(f"Invalid power_iteration_steps value: {power_iteration_steps}")
+            raise InvalidParameterError(f"Invalid power_iteration_steps value: {power_iteration_steps}")
         if nesterov and momentum <= 0:
-            raise ValueError("Nesterov momentum requires positive momentum")
+            raise InvalidParameterError("Nesterov momentum requires positive momentum")
         if radius_mode not in ("spectral_mup", "identity"):
-            raise ValueError(f"Invalid radius_mode: {radius_mode}")
+            raise InvalidParameterError(f"Invalid radius_mode: {radius_mode}")
         if retract_mode not in ("hard", "dynamic"):
-            raise ValueError(f"Invalid retract_mode: {retract_mode}")
+            raise InvalidParameterError(f"Invalid retract_mode: {retract_mode}")
         defaults = dict(lr=lr, momentum=momentum, weight_decay=weight_decay, nesterov=nesterov, ns_steps=ns_steps,
                         power_iteration_steps=power_iteration_steps, radius_mode=radius_mode,
                         radius_scaler=radius_scaler, retract_mode=retract_mode)
@@ -81,7 +82,7 @@ class SpectralSphereOptimizer(Optimizer):
                 if p.grad is None:
                     continue
                 if p.grad.is_sparse:
-                    raise RuntimeError("SpectralSphereOptimizer does not support sparse gradients")
+                    raise SparseGradientError("SpectralSphereOptimizer does not support sparse gradients")
                 st = self.state[p]
                 if len(st) == 0:
                     st["momentum_buffer"] = zeros_state_like(p)

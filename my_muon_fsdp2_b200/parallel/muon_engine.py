@@ -40,6 +40,7 @@ from ..ops.newton_schulz import NS_COEFFICIENTS, NS_EPS, _ns_torch
 from .comm import chunk_offset, chunk_rows
 from .dtensor import is_dtensor
 from ..utils.tracing import nvtx_range
+from ..optim.errors import SparseGradientError
 
 MODE_COPY, MODE_EMA, MODE_HEAVYBALL = 0, 1, 2
 
@@ -186,7 +187,7 @@ class MuonEngine:
             return
         for t in tasks:
             if t.grad.is_sparse:
-                raise RuntimeError("Muon does not support sparse gradients")
+                raise SparseGradientError("Muon does not support sparse gradients")
             t.local_param = _local(t.param)
             t.local_grad = _local(t.grad)
         world, rank, group = self._world(tasks)

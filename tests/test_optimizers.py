@@ -330,3 +330,23 @@ def test_nvtx_ranges_are_noops_when_disabled():
     with tracing.nvtx_range("x"):
         pass
     assert not tracing.enabled()
+
+
+def test_documented_exceptions():
+    """muon_fsdp.exceptions (the reference's API guide) with the built-in bases kept."""
+    import torch.nn as nn
+
+    from my_muon_fsdp2_b200 import MuonOptimizer, SpectralSphereOptimizer
+    from my_muon_fsdp2_b200.muon_fsdp.exceptions import InvalidParameterError, OptimizerError, SparseGradientError
+
+    assert issubclass(InvalidParameterError, (OptimizerError, ValueError))
+    assert issubclass(SparseGradientError, (OptimizerError, RuntimeError))
+    with pytest.raises(InvalidParameterError):
+        MuonOptimizer(nn.Linear(2, 2).parameters(), lr=-1.0)
+    with pytest.raises(InvalidParameterError):
+        SpectralSphereOptimizer(nn.Linear(2, 2).parameters(), radius_mode="nope")
+    emb = nn.Embedding(10, 4, sparse=True)
+    opt = MuonOptimizer(emb.parameters(), lr=0.01)
+    emb(torch.tensor([1, 2])).sum().backward()
+    with pytest.raises(SparseGradientError):
+        opt.step()
