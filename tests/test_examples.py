@@ -15,12 +15,17 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def _run(args, nproc=None, timeout=400):
     env = dict(os.environ, PYTHONPATH=ROOT, OMP_NUM_THREADS="2")
     env["CUDA_VISIBLE_DEVICES"] = ""  # the CPU paths, also on a machine with GPUs
-    if nproc is None:
-        cmd = [sys.executable] + args
-    else:
-        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
-               "--master-addr=127.0.0.1", f"--master-port={free_port()}"] + args
-    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=timeout)
+    for attempt in range(3):
+        if nproc is None:
+            cmd = [sys.executable] + args
+        else:
+            cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
+                   "--master-addr=127.0.0.1", f"--master-port={free_port()}"] + args
+        r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=timeout)
+        # another test process may take the free port before the rendezvous binds it: new port
+        if r.returncode != 0 and nproc is not None and "EADDRINUSE" in r.stderr and attempt < 2:
+            continue
+        break
     assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-3000:])
     return r.stdout
 
