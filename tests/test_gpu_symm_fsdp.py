@@ -18,10 +18,13 @@ ROOT = os.path.dirname(HERE)
 
 def _run(world, mode, out):
     env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
-    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
-           os.path.join(HERE, "symm_fsdp_worker.py"), "--mode", mode, "--out", out]
-    r = subprocess.run(cmd, env=env, capture_output=True, text=True, cwd=ROOT)
+    for attempt in range(3):  # a rendezvous port taken meanwhile: pick another
+        cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
+               os.path.join(HERE, "symm_fsdp_worker.py"), "--mode", mode, "--out", out]
+        r = subprocess.run(cmd, env=env, capture_output=True, text=True, cwd=ROOT)
+        if r.returncode == 0 or "EADDRINUSE" not in r.stderr:
+            break
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     return torch.load(out)
 
