@@ -350,3 +350,28 @@ def test_documented_exceptions():
     emb(torch.tensor([1, 2])).sum().backward()
     with pytest.raises(SparseGradientError):
         opt.step()
+
+
+def test_grad_scaler_drives_muon_like_a_plain_step():
+    """torch.amp.GradScaler (the reference's mixed-precision recipe) unscales the gradients
+    before MuonOptimizer.step: the update equals the one without scaling."""
+    import copy
+
+    import torch.nn as nn
+
+    from my_muon_fsdp2_b200 import MuonOptimizer
+
+    torch.manual_seed(0)
+    a = nn.Sequential(nn.Linear(16, 32), nn.GELU(), nn.Linear(32, 8))
+    b = copy.deepcopy(a)
+    x, y = torch.randn(4, 16), torch.randn(4, 8)
+    oa = MuonOptimizer(a.parameters(), lr=0.02, weight_decay=0.01)
+    ob = MuonOptimizer(b.parameters(), lr=0.02, weight_decay=0.01)
+    scaler = torch.amp.GradScaler("cpu", init_scale=1024.0)
+    scaler.scale(((a(x) - y) ** 2).mean()).backward()
+    scaler.step(oa)
+    scaler.update()
+    ((b(x) - y) ** 2).mean().backward()
+    ob.step()
+    for p, q in zip(a.parameters(), b.parameters()):
+        assert torch.allclose(p, q, rtol=1e-5, atol=1e-6)
