@@ -153,3 +153,41 @@ def test_hsdp_2x2_matches_single_process():
     _train(model, opt, 3, 16, 8)
     for p, q in zip(res["params"], model.parameters()):
         assert rel_err(p, q.detach()) < 1e-4
+
+
+def _scaled_worker(rank, world, use_scaler):
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.fsdp import fully_shard
+    from torch.distributed.fsdp.sharded_grad_scaler import ShardedGradScaler
+
+    from my_muon_fsdp2_b200 import MuonOptimizer
+
+    model = _mlp(0, 64, 128, 32)
+    mesh = init_device_mesh("cpu", (world,))
+    for m in model:
+        if isinstance(m, nn.Linear):
+            fully_shard(m, mesh=mesh)
+    fully_shard(model, mesh=mesh)
+    opt = MuonOptimizer(model.parameters(), lr=0.02, momentum=0.95, weight_decay=0.01)
+    scaler = ShardedGradScaler(device="cpu", init_scale=256.0) if use_scaler else None
+    for s in range(2):
+        x, y = _data(s, 64, 32, batch=8)
+        opt.zero_grad()
+        loss = ((model(x) - y) ** 2).mean()
+        if scaler is None:
+            loss.backward()
+            opt.step()
+        else:
+            scaler.scale(loss).backward()
+            scaler.step(opt)
+            scaler.update()
+    return [p.full_tensor().detach().clone() for p in model.parameters()]
+
+
+def test_sharded_grad_scaler_with_fsdp2():
+    """The reference trainer's FSDP + AMP recipe (ShardedGradScaler, train_gpt.py:324,343)
+    drives the sharded Muon step like an unscaled one."""
+    plain = run_ranks(_scaled_worker, 2, False)
+    scaled = run_ranks(_scaled_worker, 2, True)
+    for p, q in zip(scaled, plain):
+        assert rel_err(p, q) < 1e-5
