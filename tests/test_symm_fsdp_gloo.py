@@ -456,3 +456,31 @@ def test_symm_fsdp_frozen_weight():
             assert rel_err(got["grads"][n], p.grad) < 1e-5, n
     shard = ((H // 2) * D + (D // 2) * H) * 4  # one up and one down weight: the other rank's rows
     assert got["reduced"] == 2 * shard - (H // 2) * D * 4
+
+
+def _pure_replication(rank, world):
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    mesh = init_device_mesh("cpu", (2, 1), mesh_dim_names=("replicate", "shard"))
+    model = Net()
+    ctl = apply_symm_fsdp(model, mesh=mesh)
+    assert ctl.world == 1 and ctl.replicas == 2
+    for mb in range(2):
+        model.set_requires_gradient_sync(mb == 1)
+        x, y = _data(mb, rank)
+        ((model(x) - y) ** 2).mean().div(2).backward()
+    return {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+
+
+def test_symm_fsdp_replicas_of_one_shard():
+    """A (2, 1) mesh: every rank holds whole weights and only the replica average moves
+    gradients; the result equals one process on the union of the data."""
+    got = run_ranks(_pure_replication, 2)
+    ref = Net()
+    for mb in range(2):
+        xs, ys = zip(*[_data(mb, r) for r in range(2)])
+        ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
+    for n, p in ref.named_parameters():
+        assert rel_err(got[n], p.grad) < 1e-5, n
