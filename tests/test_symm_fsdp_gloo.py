@@ -484,3 +484,41 @@ def test_symm_fsdp_replicas_of_one_shard():
         ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().div(2).backward()
     for n, p in ref.named_parameters():
         assert rel_err(got[n], p.grad) < 1e-5, n
+
+
+def _hdsp_on_symm(rank, world, steps):
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from my_muon_fsdp2_b200 import HDSPMuonOptimizer
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    mesh = init_device_mesh("cpu", (2, 2), mesh_dim_names=("replicate", "shard"))
+    model = Net()
+    ctl = apply_symm_fsdp(model, mesh=mesh)
+    opt = HDSPMuonOptimizer(model, lr=0.02)
+    assert opt.device_mesh is not None and opt.device_mesh.ndim == 2
+    ctl.attach_optimizer(opt)
+    for s in range(steps):
+        x, y = _data(20 + s, rank)
+        ((model(x) - y) ** 2).mean().backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+    return {n: _full(p.detach()).clone() for n, p in model.named_parameters()}
+
+
+def test_hdsp_optimizer_on_fused_fsdp_hsdp():
+    """HDSPMuonOptimizer finds the 2-D mesh of the fused-FSDP parameters and exchanges inside the
+    shard groups: training equals one process on the union of the data."""
+    from my_muon_fsdp2_b200 import HDSPMuonOptimizer
+
+    steps = 2
+    got = run_ranks(_hdsp_on_symm, 4, steps)
+    ref = Net()
+    opt = HDSPMuonOptimizer(ref, lr=0.02)
+    for s in range(steps):
+        xs, ys = zip(*[_data(20 + s, r) for r in range(4)])
+        ((ref(torch.cat(xs)) - torch.cat(ys)) ** 2).mean().backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+    for n, p in ref.named_parameters():
+        assert rel_err(got[n], p.detach()) < 1e-4, n
