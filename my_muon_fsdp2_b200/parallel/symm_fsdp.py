@@ -382,6 +382,18 @@ class SymmFSDP:
         return {"bytes_gathered": self.bytes_gathered, "bytes_reduced": self.bytes_reduced,
                 "bytes_replica": self.bytes_replica}
 
+    def memory_bytes(self) -> Dict[str, int]:
+        """Device memory this controller holds on this rank: the weight shards, the resident full
+        weights gathered so far, the gradient accumulators (unsharded, for no-sync micro-batches
+        and the overlapped reduce-scatter) and the receive slots of ``rs_mode="fused"``."""
+        def nbytes(t: Optional[torch.Tensor]) -> int:
+            return 0 if t is None else t.numel() * t.element_size()
+
+        acc_buf = getattr(self, "acc_buf", None)
+        acc = nbytes(acc_buf) if acc_buf is not None else sum(nbytes(a) for a in self.acc)
+        return {"shards": nbytes(self.shard_buf), "full_weights": sum(nbytes(f) for f in self.full),
+                "grad_accumulators": acc, "rs_slots": nbytes(getattr(self, "slot_buf", None))}
+
     def _replica_average(self, g: torch.Tensor) -> None:
         """HSDP: average a gradient shard over the replicas (no-op on a 1-D mesh)."""
         if self.rgroup is None or self.replicas == 1:

@@ -522,3 +522,23 @@ def test_hdsp_optimizer_on_fused_fsdp_hsdp():
         opt.zero_grad(set_to_none=True)
     for n, p in ref.named_parameters():
         assert rel_err(got[n], p.detach()) < 1e-4, n
+
+
+def _memory(rank, world):
+    from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+
+    model = Net()
+    ctl = apply_symm_fsdp(model)
+    before = ctl.memory_bytes()
+    x, y = _data(0, rank)
+    model.set_requires_gradient_sync(False)
+    ((model(x) - y) ** 2).mean().backward()
+    return before, ctl.memory_bytes()
+
+
+def test_symm_fsdp_memory_report():
+    before, after = run_ranks(_memory, 2)
+    weights = 2 * (H * D + D * H) * 4  # two blocks of up + down, fp32
+    assert before == {"shards": weights // 2, "full_weights": 0, "grad_accumulators": 0, "rs_slots": 0}
+    # after a no-sync micro-batch: every weight gathered once and an unsharded accumulator each
+    assert after["full_weights"] == weights and after["grad_accumulators"] == weights
