@@ -113,6 +113,7 @@ class Trainer:
             m["symm_fsdp/world"] = ctl.world
             m["symm_fsdp/rs_mode"] = ctl.rs_mode
             m["symm_fsdp/resident_weights"] = sum(1 for f in ctl.full if f is not None)
+            m["symm_fsdp/memory_bytes"] = sum(ctl.memory_bytes().values())
             cur = ctl.stats()
             prev = self._prev_comm or {k: 0 for k in cur}
             for k, v in cur.items():  # this step's traffic
@@ -139,6 +140,8 @@ class Trainer:
                 out[k.replace("timer", "ms")] = v.mean_ms()
             else:
                 out[k] = v
+        if self.device.type == "cuda":  # the monitoring the reference's performance guide suggests
+            out["max_memory_allocated_gb"] = torch.cuda.max_memory_allocated(self.device) / 2**30
         ms = self.last_step_ms()
         if ms:
             out["step_ms"] = ms
