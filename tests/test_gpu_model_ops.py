@@ -17,8 +17,10 @@ def _grads(y, dy, *xs):
     return torch.autograd.grad(y, xs, dy)
 
 
-def test_rmsnorm_fwd_bwd():
-    x, w = _bf(64, 1024), _bf(1024)
+@pytest.mark.parametrize("rows,cols", [(64, 1024), (300, 4096), (37, 1001)],
+                         ids=["vec", "llama_width_many_rows", "scalar_path"])
+def test_rmsnorm_fwd_bwd(rows, cols):
+    x, w = _bf(rows, cols), _bf(cols)
     y = M.rms_norm(x, w, 1e-5)
     xf, wf = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
     yr = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * wf
