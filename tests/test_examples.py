@@ -35,6 +35,11 @@ def test_simple_muon():
     assert "step 19 loss" in out
 
 
+def test_single_process_fsdp2_utils():
+    out = _run(["examples/single_gpu.py"])
+    assert "world size: 1" in out and "step 3: loss" in out and "single-process example done" in out
+
+
 def test_sso_vs_muon():
     out = _run(["examples/train_sso.py"])
     assert "muon" in out and "sso" in out
