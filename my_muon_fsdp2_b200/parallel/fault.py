@@ -7,7 +7,9 @@ The reference has none (its only robustness code swallows exceptions, hdsp.py:13
   heartbeat is older than a limit, so the survivors learn of a dead or hung rank *between steps*
   (before their next collective) instead of blocking in it.
 * :func:`guarded_barrier` — a barrier with a deadline (gloo ``monitored_barrier`` names the
-  missing ranks; NCCL groups fall back to a heartbeat check + barrier).
+  missing ranks; when a peer's process died and the barrier fails with a transport error instead,
+  the heartbeat names the rank that went quiet; NCCL groups fall back to a heartbeat check +
+  barrier).
 * :func:`verify_replicas` — detects corrupted/diverged replicated tensors by comparing
   checksums across ranks.
 * :class:`StepWatchdog` — fires a callback (default: dump stacks) when a step exceeds a limit.
@@ -108,9 +110,24 @@ def guarded_barrier(timeout_s: float = 30.0, group: Optional[dist.ProcessGroup] 
         try:
             dist.monitored_barrier(group=group, timeout=datetime.timedelta(seconds=timeout_s), wait_all_ranks=True)
         except RuntimeError as e:
-            raise RankFailure(_ranks_from_message(str(e)), f"barrier timed out: {e}") from e
+            ranks = _ranks_from_message(str(e))
+            if not ranks and heartbeat is not None:
+                # a peer whose process died closes its connections: the barrier then fails with a
+                # transport error that names no rank, and the heartbeat tells which rank went quiet
+                ranks = _quiet_ranks(heartbeat, timeout_s)
+            raise RankFailure(ranks, f"barrier failed: {e}") from e
     else:
         dist.barrier(group=group)
+
+
+def _quiet_ranks(heartbeat: Heartbeat, limit_s: float) -> List[int]:
+    """Ranks whose heartbeat is older than ``limit_s``, polled for up to ``2 * limit_s``."""
+    end = time.monotonic() + 2.0 * limit_s
+    while True:
+        dead = heartbeat.dead_ranks(limit_s)
+        if dead or time.monotonic() > end:
+            return dead
+        time.sleep(min(0.05, limit_s / 4))
 
 
 def _ranks_from_message(msg: str) -> List[int]:

@@ -1,13 +1,16 @@
-"""Failure detection on CPU gloo ranks (host-side faults only): a rank that raises, a rank that
-stops heart-beating, a delayed rank caught by a monitored barrier, a corrupted replica."""
+"""Failure detection on CPU gloo ranks (host-side faults only): a rank that raises, a rank whose
+process is killed, a rank that stops heart-beating, a delayed rank caught by a monitored
+barrier, a corrupted replica."""
 import datetime
+import os
+import signal
 import time
 
 import pytest
 import torch
 import torch.distributed as dist
 
-from tests.dist_util import run_ranks
+from tests.dist_util import run_ranks, run_ranks_some_die
 
 pytestmark = pytest.mark.distributed
 
@@ -72,6 +75,31 @@ def _raising_rank(rank, world):
 
 def test_raising_rank_detected_before_next_collective():
     out = run_ranks(_raising_rank, 2)
+    assert out is not None and out["step"] == 1 and out["ranks"] == [1]
+
+
+def _killed_rank(rank, world):
+    from my_muon_fsdp2_b200.parallel.fault import Heartbeat, RankFailure, guarded_barrier
+
+    store = dist.distributed_c10d._get_default_store()  # served by rank 0's process
+    hb = Heartbeat(store, rank, world, interval_s=0.05).start()
+    dist.barrier()  # both ranks start together, however late either process came up
+    out = None
+    for step in range(3):
+        if rank == 1 and step == 1:
+            os.kill(os.getpid(), signal.SIGKILL)  # the process dies between steps
+        try:
+            guarded_barrier(timeout_s=1.0 if step > 0 else 10.0, heartbeat=hb if step > 0 else None)
+        except RankFailure as e:
+            out = {"step": step, "ranks": e.ranks}
+            break
+    hb.stop()
+    return out
+
+
+def test_killed_rank_detected_and_named():
+    out, codes = run_ranks_some_die(_killed_rank, 2)
+    assert codes == [0, -signal.SIGKILL]
     assert out is not None and out["step"] == 1 and out["ranks"] == [1]
 
 
