@@ -39,19 +39,23 @@ def run_ranks(fn, world, *args):
             return torch.load(path, weights_only=False)
 
 
-def run_ranks_some_die(fn, world, *args, timeout_s=120.0):
+def run_ranks_some_die(fn, world, *args, timeout_s=120.0, attempts=3):
     """Like :func:`run_ranks`, but a rank may end its own process (a killed rank): returns rank 0's
-    value and every rank's exit code (negative = the signal that ended it).  Rank 0 must survive."""
-    with tempfile.TemporaryDirectory() as d:
-        path = os.path.join(d, "result.pt")
-        ctx = mp.start_processes(_entry, args=(world, free_port(), fn, path, args), nprocs=world, join=False,
-                                 start_method="spawn")
-        for p in ctx.processes:
-            p.join(timeout_s)
-        codes = []
-        for p in ctx.processes:
-            if p.is_alive():  # a hung rank: end this test's own child, by its PID
-                p.kill()
-                p.join(5)
-            codes.append(p.exitcode)
-        return (torch.load(path, weights_only=False) if os.path.exists(path) else None), codes
+    value and every rank's exit code (negative = the signal that ended it).  Rank 0 must survive;
+    a run whose rank 0 failed (e.g. its rendezvous port was taken by a parallel test) is retried."""
+    for attempt in range(attempts):
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "result.pt")
+            ctx = mp.start_processes(_entry, args=(world, free_port(), fn, path, args), nprocs=world, join=False,
+                                     start_method="spawn")
+            for p in ctx.processes:
+                p.join(timeout_s)
+            codes = []
+            for p in ctx.processes:
+                if p.is_alive():  # a hung rank: end this test's own child, by its PID
+                    p.kill()
+                    p.join(5)
+                codes.append(p.exitcode)
+            if codes[0] != 0 and attempt + 1 < attempts:
+                continue
+            return (torch.load(path, weights_only=False) if os.path.exists(path) else None), codes
