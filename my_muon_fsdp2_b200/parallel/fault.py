@@ -16,6 +16,8 @@ The reference has none (its only robustness code swallows exceptions, hdsp.py:13
 * :class:`FaultInjector` — host-side injection for tests: raise on a given rank/step, delay a
   rank, stop heart-beating (simulated hang), corrupt a tensor.  Nothing here faults a GPU.
 * :func:`check_device` — reads the device error word written by our kernels' bounded waits.
+* :func:`init_distributed` — joins a torchrun job with a collective timeout, NCCL async error
+  handling and an eagerly created communicator.
 """
 from __future__ import annotations
 
@@ -208,3 +210,41 @@ def check_device(device: int = 0) -> None:
     from .._ext import check_device_error
 
     check_device_error(device)
+
+
+def init_distributed(backend: Optional[str] = None, timeout_s: float = 300.0,
+                     async_error_handling: bool = True) -> dict:
+    """Join the job that ``torchrun`` described in the environment (RANK, WORLD_SIZE, LOCAL_RANK,
+    MASTER_ADDR, MASTER_PORT) with failure handling switched on; a plain single process (no RANK)
+    joins nothing.  Returns ``{"rank", "world", "local_rank", "device"}``.
+
+    * backend: ``"nccl"`` when CUDA is available, else ``"gloo"``.
+    * ``timeout_s`` bounds every collective: a rank that died or hung ends the others' next
+      collective with an error instead of a wait forever.
+    * ``async_error_handling`` sets ``TORCH_NCCL_ASYNC_ERROR_HANDLING=1`` (unless already set):
+      NCCL's watchdog then aborts the communicator and ends the process on a failed or timed-out
+      collective, so no GPU stream stays blocked on a dead peer.
+    * NCCL groups are bound to this rank's GPU (``device_id``), which creates the communicator
+      eagerly: a missing peer fails here, at start-up, not in the first training step.
+    """
+    import os
+
+    if "RANK" not in os.environ or "WORLD_SIZE" not in os.environ:
+        dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+        return {"rank": 0, "world": 1, "local_rank": 0, "device": dev}
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    if backend is None:
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+    kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if backend == "nccl":
+        if async_error_handling:
+            os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
+        torch.cuda.set_device(local)
+        dev = torch.device("cuda", local)
+        kw["device_id"] = dev
+    else:
+        dev = torch.device("cpu")
+    if not dist.is_initialized():
+        dist.init_process_group(backend, rank=rank, world_size=world, **kw)
+    return {"rank": rank, "world": world, "local_rank": local, "device": dev}

@@ -145,3 +145,56 @@ def test_step_watchdog_fires():
     with StepWatchdog(0.1, on_timeout=lambda: fired.append(1)) as w:
         time.sleep(0.3)
     assert w.fired and fired
+
+
+def _init_entry(rank, world, port, path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    torch.set_num_threads(1)
+    from my_muon_fsdp2_b200.parallel.fault import init_distributed
+
+    info = init_distributed(timeout_s=2.0)
+    t = torch.tensor([float(rank + 1)])
+    dist.all_reduce(t)
+    res = {"info": info, "sum": float(t), "backend": dist.get_backend()}
+    # rank 1 leaves without taking the next collective: rank 0's all_reduce must end with an
+    # error once the group's timeout has passed, not wait forever
+    if rank == 0:
+        t0 = time.time()
+        try:
+            dist.all_reduce(torch.ones(1))
+            res["late"] = "completed"
+        except RuntimeError:
+            res["late"] = round(time.time() - t0, 1)
+        torch.save(res, path)
+    else:
+        time.sleep(5.0)
+    dist.destroy_process_group()
+
+
+def test_init_distributed_joins_with_a_collective_timeout(tmp_path):
+    import torch.multiprocessing as mp
+
+    from tests.conftest import free_port
+
+    for attempt in range(3):
+        path = str(tmp_path / f"r{attempt}.pt")
+        try:
+            mp.spawn(_init_entry, args=(2, free_port(), path), nprocs=2, join=True)
+        except mp.ProcessRaisedException as e:
+            if attempt < 2 and "address already in use" in str(e).lower():
+                continue
+            raise
+        break
+    res = torch.load(path, weights_only=False)
+    assert res["backend"] == "gloo" and res["sum"] == 3.0
+    assert res["info"]["rank"] == 0 and res["info"]["world"] == 2 and str(res["info"]["device"]) == "cpu"
+    assert res["late"] != "completed" and res["late"] < 4.5
+
+
+def test_init_distributed_single_process(monkeypatch):
+    from my_muon_fsdp2_b200.parallel.fault import init_distributed
+
+    monkeypatch.delenv("RANK", raising=False)
+    info = init_distributed()
+    assert info["rank"] == 0 and info["world"] == 1 and not dist.is_initialized()
