@@ -22,6 +22,7 @@ import torch.distributed as dist
 from my_muon_fsdp2_b200 import FusedAdamW, MuonOptimizer
 from my_muon_fsdp2_b200.models.llama import Llama, LlamaConfig
 from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
+from my_muon_fsdp2_b200.parallel.fault import init_distributed
 from my_muon_fsdp2_b200.train import Trainer
 
 
@@ -34,11 +35,9 @@ def main():
                     help="HSDP: a (replicas, world / replicas) mesh; the linears are sharded over the second dim")
     a = ap.parse_args()
     cuda = torch.cuda.is_available()
-    dist.init_process_group("nccl" if cuda else "gloo")
-    rank = dist.get_rank()
-    if cuda:
-        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-    dev = torch.device("cuda" if cuda else "cpu")
+    # NCCL on GPUs (gloo on CPU) with a collective timeout and async error handling
+    job = init_distributed(timeout_s=300.0)
+    rank, dev = job["rank"], job["device"]
     torch.manual_seed(0)
     cfg = LlamaConfig.tiny(dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab_size=2048, n_layers=2)
     model = Llama(cfg).to(dev, torch.bfloat16 if cuda else torch.float32)
