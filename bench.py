@@ -236,16 +236,23 @@ def main():
     clocks = ClockSampler(physical_gpu_index(local))
     clocks.start()
     n0 = count() if count else 0
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # one event per step boundary (recording an event adds no work between the steps)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    start, end = marks[0], marks[-1]
     start.record()
     for s in range(args.steps):
         loss = trainer.step_on_device(dev_batches[s % 2])
-    end.record()
+        marks[s + 1].record()
     torch.cuda.synchronize()
     launches = (count() - n0) if count else None
     clk = clocks.stop()
     dist.barrier()
     dev_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    # per-step spread (each step's max over ranks), so that a few-percent change between runs
+    # can be told apart from step-to-step noise
+    per_step = [max_over_ranks(marks[i].elapsed_time(marks[i + 1])) for i in range(args.steps)]
+    srt = sorted(per_step)
+    spread = {"min": srt[0], "median": srt[len(srt) // 2], "max": srt[-1]}
     opt_ms = max_over_ranks(opt_timer.mean_ms())
     final_loss = float(loss.item())
 
@@ -279,7 +286,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / base) if base else None, "dtype": "bf16",
             "data": "synthetic uniform random tokens; random-init weights",
-            "optimizer_step_ms": opt_ms,
+            "optimizer_step_ms": opt_ms, "step_ms_spread": spread,
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",

@@ -37,6 +37,9 @@ def main():
     cuda = torch.cuda.is_available()
     # NCCL on GPUs (gloo on CPU) with a collective timeout and async error handling
     job = init_distributed(timeout_s=300.0)
+    if not dist.is_initialized():
+        sys.exit("llama_symm_fsdp.py shards the model over a process group: launch it with torchrun "
+                 "(e.g. torchrun --nproc-per-node 2 --master-addr 127.0.0.1 examples/llama_symm_fsdp.py)")
     rank, dev = job["rank"], job["device"]
     torch.manual_seed(0)
     cfg = LlamaConfig.tiny(dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab_size=2048, n_layers=2)

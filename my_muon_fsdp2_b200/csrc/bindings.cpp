@@ -184,6 +184,139 @@ void wgrad_out(Tensor dY, Tensor X, Tensor out_ptrs, int64_t nseg, Tensor out_me
   mmf::tc_gemm_out(a, cur_stream());
 }
 
+// Grouped transformer-linear GEMM (linear_gemm.cu).  Shapes are read from the tensors:
+//   forward         (a_mn=0, b_mn=0): A = [X [M, K]],        B = [W_s [N_s, K]],  out = [Y_s [M, N_s]]
+//   input gradient  (a_mn=0, b_mn=1): A = [dY_s [M, K_s]],   B = [W_s [K_s, N]],  out = [dX [M, N]]
+//   weight gradient (a_mn=1, b_mn=1): A = [dY_s [T, N_s]],   B = [X [T, K]],      out = [dW_s [N_s, K]]
+// SWIGLU: B = [W1, W3] ([F, K] each), out = [h, g, u] ([M, F] each).  SWIGLU_BWD: out = [dg, du],
+// aux0 = g, aux1 = u.  GELU: out = [gelu(z), z].  GELU_BWD: out = [dz], aux0 = z.
+void linear_gemm(std::vector<Tensor> A, std::vector<Tensor> B, bool a_mn, bool b_mn, std::vector<Tensor> out,
+                 int64_t epilogue, c10::optional<Tensor> C, c10::optional<Tensor> aux0, c10::optional<Tensor> aux1,
+                 c10::optional<Tensor> bias, double alpha, bool accumulate, int64_t rope_mask, int64_t seq_len,
+                 int64_t head_dim, double rope_theta) {
+  TORCH_CHECK(!A.empty() && !B.empty() && !out.empty(), "mmf: linear_gemm needs operands and outputs");
+  TORCH_CHECK(A.size() <= 3 && B.size() <= 3 && out.size() <= 3, "mmf: linear_gemm takes at most 3 segments");
+  for (auto& t : A) check_bf16_contig(t, "A");
+  for (auto& t : B) check_bf16_contig(t, "B");
+  for (auto& t : A) TORCH_CHECK(t.dim() == 2, "mmf: linear_gemm operands are 2-D");
+  for (auto& t : B) TORCH_CHECK(t.dim() == 2, "mmf: linear_gemm operands are 2-D");
+  const auto dev = A[0].device();
+  for (auto& t : out) {
+    check_cuda(t, "out");
+    TORCH_CHECK(t.device() == dev && t.dim() == 2 && t.is_contiguous(), "mmf: outputs must be contiguous 2-D on A's device");
+    TORCH_CHECK(t.scalar_type() == out[0].scalar_type(), "mmf: outputs must share one dtype");
+  }
+  const bool f32 = out[0].scalar_type() == torch::kFloat32;
+  TORCH_CHECK(f32 || out[0].scalar_type() == torch::kBFloat16, "mmf: outputs must be bf16 or fp32");
+  const c10::cuda::CUDAGuard guard(dev);
+  mmf::LinearGemmArgs a{};
+  a.a_mn = a_mn;
+  a.b_mn = b_mn;
+  a.epilogue = static_cast<int>(epilogue);
+  a.alpha = static_cast<float>(alpha);
+  a.accumulate = accumulate;
+  a.out_f32 = f32;
+  const int na = static_cast<int>(A.size()), nb = static_cast<int>(B.size());
+  for (int s = 0; s < na; ++s) {
+    a.A[s] = A[s].data_ptr();
+    a.a_outer[s] = A[s].size(0);
+    a.a_inner[s] = A[s].size(1);
+  }
+  for (int s = 0; s < nb; ++s) {
+    a.B[s] = B[s].data_ptr();
+    a.b_outer[s] = B[s].size(0);
+    a.b_inner[s] = B[s].size(1);
+  }
+  for (size_t s = 0; s < out.size(); ++s) {
+    a.out[s] = out[s].data_ptr();
+    a.ldo[s] = out[s].size(1);
+  }
+  if (!a_mn && !b_mn) {  // forward
+    TORCH_CHECK(na == 1, "mmf: forward takes one input X");
+    a.M = static_cast<int>(A[0].size(0));
+    a.K[0] = static_cast<int>(A[0].size(1));
+    for (int s = 0; s < nb; ++s) TORCH_CHECK(B[s].size(1) == a.K[0], "mmf: weight in-features mismatch");
+    if (epilogue == mmf::LIN_EPI_SWIGLU) {
+      TORCH_CHECK(nb == 2 && B[0].sizes() == B[1].sizes() && out.size() == 3, "mmf: SWIGLU takes W1, W3 -> h, g, u");
+      a.axis = mmf::LIN_SEG_N;
+      a.nseg = 2;
+      a.N = static_cast<int>(B[0].size(0));
+      for (auto& t : out) TORCH_CHECK(t.size(0) == a.M && t.size(1) == a.N, "mmf: SWIGLU outputs are [M, F]");
+    } else if (epilogue == mmf::LIN_EPI_GELU) {
+      TORCH_CHECK(nb == 1 && out.size() == 2, "mmf: GELU takes one weight -> gelu(z), z");
+      a.axis = mmf::LIN_SEG_NONE;
+      a.nseg = 1;
+      a.N = static_cast<int>(B[0].size(0));
+      for (auto& t : out) TORCH_CHECK(t.size(0) == a.M && t.size(1) == a.N, "mmf: GELU outputs are [M, N]");
+    } else {
+      TORCH_CHECK(static_cast<int>(out.size()) == nb, "mmf: one output per weight");
+      a.axis = nb > 1 ? mmf::LIN_SEG_N : mmf::LIN_SEG_NONE;
+      a.nseg = nb;
+      a.N = 0;
+      for (int s = 0; s < nb; ++s) {
+        TORCH_CHECK(out[s].size(0) == a.M && out[s].size(1) == B[s].size(0), "mmf: output shape mismatch");
+        a.seg_len[s] = static_cast<int>(B[s].size(0));
+        a.N += a.seg_len[s];
+      }
+    }
+  } else if (!a_mn && b_mn) {  // input gradient
+    TORCH_CHECK(na == nb, "mmf: one weight per output gradient");
+    a.M = static_cast<int>(A[0].size(0));
+    a.N = static_cast<int>(B[0].size(1));
+    for (int s = 0; s < na; ++s) {
+      TORCH_CHECK(A[s].size(0) == a.M && B[s].size(1) == a.N && A[s].size(1) == B[s].size(0),
+                  "mmf: input-gradient operand shapes mismatch");
+      a.K[s] = static_cast<int>(A[s].size(1));
+    }
+    a.axis = na > 1 ? mmf::LIN_SEG_K : mmf::LIN_SEG_NONE;
+    a.nseg = na;
+    const size_t nout = epilogue == mmf::LIN_EPI_SWIGLU_BWD ? 2 : 1;
+    TORCH_CHECK(out.size() == nout, "mmf: wrong number of outputs for this epilogue");
+    for (auto& t : out) TORCH_CHECK(t.size(0) == a.M && t.size(1) == a.N, "mmf: output shape mismatch");
+  } else {  // weight gradient
+    TORCH_CHECK(a_mn && b_mn && nb == 1, "mmf: weight gradient takes dY segments and one X");
+    TORCH_CHECK(static_cast<int>(out.size()) == na, "mmf: one weight gradient per dY segment");
+    a.K[0] = static_cast<int>(B[0].size(0));
+    a.N = static_cast<int>(B[0].size(1));
+    a.M = 0;
+    for (int s = 0; s < na; ++s) {
+      TORCH_CHECK(A[s].size(0) == a.K[0], "mmf: dY and X token counts differ");
+      TORCH_CHECK(out[s].size(0) == A[s].size(1) && out[s].size(1) == a.N, "mmf: weight-gradient shape mismatch");
+      a.seg_len[s] = static_cast<int>(A[s].size(1));
+      a.M += a.seg_len[s];
+    }
+    a.axis = na > 1 ? mmf::LIN_SEG_M : mmf::LIN_SEG_NONE;
+    a.nseg = na;
+  }
+  if (C.has_value()) {
+    check_bf16_contig(*C, "C");
+    TORCH_CHECK(C->dim() == 2 && C->size(0) == a.M && C->size(1) == a.N, "mmf: C must be [M, N]");
+    a.C = C->data_ptr();
+    a.ldc = C->size(1);
+  }
+  if (aux0.has_value()) {
+    check_bf16_contig(*aux0, "aux0");
+    TORCH_CHECK(aux0->dim() == 2 && aux0->size(0) == a.M && aux0->size(1) == a.N, "mmf: aux0 must be [M, N]");
+    a.aux0 = aux0->data_ptr();
+    a.ld_aux = aux0->size(1);
+  }
+  if (aux1.has_value()) {
+    check_bf16_contig(*aux1, "aux1");
+    TORCH_CHECK(aux1->sizes() == aux0->sizes(), "mmf: aux1 must match aux0");
+    a.aux1 = aux1->data_ptr();
+  }
+  if (bias.has_value()) {
+    check_bf16_contig(*bias, "bias");
+    TORCH_CHECK(bias->numel() == a.N, "mmf: bias must have N elements");
+    a.bias = bias->data_ptr();
+  }
+  a.rope_mask = static_cast<int>(rope_mask);
+  a.seq_len = static_cast<int>(seq_len);
+  a.head_dim = static_cast<int>(head_dim);
+  a.rope_theta = static_cast<float>(rope_theta);
+  mmf::linear_gemm(a, cur_stream());
+}
+
 // Y = X @ W^T with W row-sharded over the group (shard_ptrs: every rank's shard address in this
 // process's address space); also assembles the full W into G.  ready: int32 [N / 128] scratch.
 Tensor ag_gemm(Tensor X, std::vector<int64_t> shard_ptrs, int64_t rank, Tensor G, Tensor ready, double wait_s) {
@@ -649,6 +782,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_gemm_out", &tc_gemm_out);
   m.def("wgrad_out", &wgrad_out);
   m.def("ag_gemm", &ag_gemm);
+  m.def("linear_gemm", &linear_gemm);
   m.def("rs_reduce", &rs_reduce);
   m.def("rs_pull_reduce", &rs_pull_reduce);
   m.def("muon_prep", &muon_prep);

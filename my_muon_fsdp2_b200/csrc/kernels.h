@@ -83,6 +83,55 @@ struct GemmOutArgs {
 void tc_gemm_out(const GemmOutArgs& args, cudaStream_t stream);
 
 // ----------------------------------------------------------------------------------------
+// Grouped GEMM of the transformer linears (linear_gemm.cu), CTA-pair tiles of 256 x 256:
+//   out = epilogue(alpha * sum_k A[m, k] B[k, n])
+// Operand storage (bf16, row-major, row pitch a multiple of 8 elements, 16-byte aligned):
+//   a_mn == false: A segment s is [a_outer = rows, a_inner = K_s]          (K-major)
+//   a_mn == true : A segment s is [a_outer = K,    a_inner = rows_s]       (the product uses A^T)
+//   b_mn == false: B segment s is [b_outer = cols_s, b_inner = K]          (the product uses B^T)
+//   b_mn == true : B segment s is [b_outer = K_s,  b_inner = cols]
+// Supported pairs: (false, false) forward, (false, true) input gradient, (true, true) weight
+// gradient.  Segments concatenate up to three operands along one axis:
+//   LIN_SEG_M: A segments (rows seg_len[s]) -> out[s];  LIN_SEG_N: B segments (columns
+//   seg_len[s]) -> out[s];  LIN_SEG_K: (A, B) pairs with reduction K[s], summed into out[0].
+// Epilogues: see linear_gemm.cu.  Ragged M, N, K are handled (zero-filled loads, checked stores).
+enum LinSegAxis : int { LIN_SEG_NONE = 0, LIN_SEG_M = 1, LIN_SEG_N = 2, LIN_SEG_K = 3 };
+enum LinEpilogue : int {
+  LIN_EPI_STORE = 0,
+  LIN_EPI_ROPE = 1,
+  LIN_EPI_SWIGLU = 2,
+  LIN_EPI_SWIGLU_BWD = 3,
+  LIN_EPI_GELU = 4,
+  LIN_EPI_GELU_BWD = 5,
+};
+struct LinearGemmArgs {
+  int M, N;       // output rows and columns (SWIGLU: N = hidden units; LIN_SEG_M/N: the sum of seg_len)
+  int K[3];       // reduction length (per segment for LIN_SEG_K, else K[0])
+  bool a_mn, b_mn;
+  int axis, nseg;
+  int seg_len[3];
+  const void* A[3];
+  int64_t a_inner[3], a_outer[3];
+  const void* B[3];
+  int64_t b_inner[3], b_outer[3];
+  int epilogue;
+  void* out[3];   // STORE/ROPE: one per segment (or out[0]); SWIGLU: h, g, u; SWIGLU_BWD: dg, du; GELU: a, z
+  int64_t ldo[3];
+  bool out_f32, accumulate;
+  float alpha;
+  const void* C;  // STORE: + C (residual; may alias out[0]), pitch ldc
+  int64_t ldc;
+  const void* aux0;  // SWIGLU_BWD: g, GELU_BWD: z
+  const void* aux1;  // SWIGLU_BWD: u
+  int64_t ld_aux;
+  const void* bias;  // STORE / GELU: + bias[col]
+  int rope_mask;     // ROPE: bit s set -> rotate the heads of segment s
+  int seq_len, head_dim;
+  float rope_theta;
+};
+void linear_gemm(const LinearGemmArgs& args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------------
 // FSDP all-gather fused with the consuming GEMM:  Y[M, N] = X[M, K] @ W^T, where W [N, K] is
 // row-sharded over `ws` ranks (rank s holds rows [s*N/ws, (s+1)*N/ws) at shard_ptrs[s], a
 // peer-mapped address for s != rank).  The same launch assembles the full W into the local

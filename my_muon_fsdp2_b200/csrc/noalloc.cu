@@ -10,6 +10,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <string>
 
 #include "noalloc.h"
 
@@ -20,7 +21,16 @@ static __device__ __align__(256) float g_noalloc_scratch[MMF_NOALLOC_MAX_PARTS *
 constexpr int kMaxDevices = 64;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
 std::mutex g_mu;
-thread_local const char* g_last_error = "";
+thread_local std::string g_last_error;
+
+int fail(int code, const char* what, cudaError_t e = cudaSuccess) {
+  g_last_error = what;
+  if (e != cudaSuccess) {
+    g_last_error += ": ";
+    g_last_error += cudaGetErrorString(e);
+  }
+  return code;
+}
 
 __device__ __forceinline__ float bfv(__nv_bfloat16 v) { return __bfloat162float(v); }
 
@@ -101,32 +111,44 @@ float* scratch_for_current_device() {
 
 }  // namespace
 
-extern "C" __attribute__((visibility("default"))) const char* mmf_noalloc_last_error(void) { return g_last_error; }
+extern "C" __attribute__((visibility("default"))) const char* mmf_noalloc_last_error(void) {
+  return g_last_error.c_str();
+}
 
 extern "C" __attribute__((visibility("default"))) int mmf_rmsnorm_bwd_noalloc(const void* dy, const void* x,
                                                                              const void* w, const float* rstd, void* dx,
                                                                              void* dw, int rows, int cols,
                                                                              cudaStream_t stream) {
-  if (rows < 1 || cols < 1 || cols > MMF_NOALLOC_MAX_COLS) {
-    g_last_error = "mmf_rmsnorm_bwd_noalloc: rows must be >= 1 and cols in [1, MMF_NOALLOC_MAX_COLS = 8192]";
-    return 1;
+  if (rows < 1 || cols < 1 || cols > MMF_NOALLOC_MAX_COLS)
+    return fail(1, "mmf_rmsnorm_bwd_noalloc: rows must be >= 1 and cols in [1, MMF_NOALLOC_MAX_COLS = 8192]");
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return fail(2, "mmf_rmsnorm_bwd_noalloc: cudaGetDevice failed", e);
+  if (stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread) {
+    // the scratch address belongs to the current device: a stream of another device cannot use it
+    int sdev = -1;
+    e = cudaStreamGetDevice(stream, &sdev);
+    if (e != cudaSuccess) return fail(4, "mmf_rmsnorm_bwd_noalloc: cudaStreamGetDevice failed", e);
+    if (sdev != cur) return fail(4, "mmf_rmsnorm_bwd_noalloc: the stream belongs to another device than the current one");
   }
   float* part = scratch_for_current_device();
-  if (part == nullptr) {
-    g_last_error = "mmf_rmsnorm_bwd_noalloc: cudaGetSymbolAddress for the static scratch array failed";
-    return 2;
-  }
+  if (part == nullptr)
+    return fail(2, "mmf_rmsnorm_bwd_noalloc: cudaGetSymbolAddress for the static scratch array failed");
   const int parts = rows < MMF_NOALLOC_MAX_PARTS ? rows : MMF_NOALLOC_MAX_PARTS;
-  rmsnorm_bwd_partials<<<parts, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(dy),
-                                                   static_cast<const __nv_bfloat16*>(x),
-                                                   static_cast<const __nv_bfloat16*>(w), rstd,
-                                                   static_cast<__nv_bfloat16*>(dx), part, rows, cols);
-  colsum_to_bf16<<<(cols + 255) / 256, 256, 0, stream>>>(part, parts, cols, static_cast<__nv_bfloat16*>(dw));
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    g_last_error = "mmf_rmsnorm_bwd_noalloc: kernel launch failed";
-    return 3;
-  }
-  g_last_error = "";
+  // cudaLaunchKernelEx returns the error of this launch (or a sticky error of the context),
+  // not an unrelated earlier one left in the per-thread error slot
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(parts);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  e = cudaLaunchKernelEx(&cfg, rmsnorm_bwd_partials, static_cast<const __nv_bfloat16*>(dy),
+                         static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), rstd,
+                         static_cast<__nv_bfloat16*>(dx), part, rows, cols);
+  if (e != cudaSuccess) return fail(3, "mmf_rmsnorm_bwd_noalloc: partials kernel launch failed", e);
+  cfg.gridDim = dim3((cols + 255) / 256);
+  e = cudaLaunchKernelEx(&cfg, colsum_to_bf16, static_cast<const float*>(part), parts, cols,
+                         static_cast<__nv_bfloat16*>(dw));
+  if (e != cudaSuccess) return fail(3, "mmf_rmsnorm_bwd_noalloc: column-sum kernel launch failed", e);
+  g_last_error.clear();
   return 0;
 }

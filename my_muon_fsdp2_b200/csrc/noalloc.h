@@ -27,7 +27,9 @@ extern "C" {
 // message from mmf_noalloc_last_error():
 //   1: cols outside [1, MMF_NOALLOC_MAX_COLS] or rows < 1
 //   2: scratch set-up failed (cudaGetSymbolAddress) on the current device
-//   3: kernel launch failed
+//   3: kernel launch failed (the message carries CUDA's error string)
+//   4: `stream` belongs to another device than the current one (the scratch address is looked
+//      up for the current device, so make the stream's device current before the call)
 // The first call on each device looks up the scratch address with that device current; make
 // that first call before any stream capture.  All calls share one scratch array per device
 // and it keeps the last call's contents: calls that overlap on the GPU (different streams

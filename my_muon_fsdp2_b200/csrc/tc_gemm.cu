@@ -24,8 +24,37 @@
 
 #include "kernels.h"
 #include "tc_common.cuh"
+#include "tma_host.h"
 
 namespace mmf {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  if (!fn) throw std::runtime_error("mmf: cuTensorMapEncodeTiled is not available from the CUDA driver");
+  return fn;
+}
+
+CUtensorMap make_map_bf16_3d(const void* base, uint64_t inner, uint64_t outer, uint64_t batch, uint32_t box_inner,
+                             uint32_t box_outer) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("mmf: TMA base must be 16-byte aligned");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {inner, outer, batch};
+  cuuint64_t strides[2] = {inner * 2, inner * outer * 2};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("mmf: cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+  return m;
+}
 
 namespace {
 
@@ -1128,34 +1157,6 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
 }
 
 // ------------------------------------ host side ------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
-    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  if (!fn) throw std::runtime_error("mmf: cuTensorMapEncodeTiled is not available from the CUDA driver");
-  return fn;
-}
-
-CUtensorMap make_map_bf16_3d(const void* base, uint64_t inner, uint64_t outer, uint64_t batch, uint32_t box_inner,
-                             uint32_t box_outer) {
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("mmf: TMA base must be 16-byte aligned");
-  CUtensorMap m;
-  cuuint64_t dims[3] = {inner, outer, batch};
-  cuuint64_t strides[2] = {inner * 2, inner * outer * 2};
-  cuuint32_t box[3] = {box_inner, box_outer, 1};
-  cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) throw std::runtime_error("mmf: cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
-  return m;
-}
-
 struct DeviceInfo {
   int sms = 0;
   bool attr_set[12] = {};

@@ -2,8 +2,10 @@
 
 The reference has no Llama; this is the model of the Llama-3 8B FSDP2+Muon workload
 (32 layers, d=4096, 32 query / 8 KV heads, head_dim 128, FFN 14336, vocab 128256).
-Linear projections are plain library GEMMs (``F.linear``); RMSNorm, RoPE, SwiGLU and the fused
-LM-head cross entropy are this library's sm_100a kernels (``ops.model_ops``).
+Every projection runs on this library's grouped tcgen05 GEMM (``ops.linear``): q | k | v in one
+launch with RoPE in its epilogue, W1 | W3 with SwiGLU in the epilogue, and the residual adds of
+the attention output projection and of W2 fused into their GEMMs.  RMSNorm, attention and the
+LM-head cross entropy are this library's sm_100a kernels as well (``ops.model_ops``).
 """
 from __future__ import annotations
 
@@ -13,8 +15,8 @@ from typing import Optional
 import torch
 import torch.nn as nn
 
-from ..ops.model_ops import apply_rope, causal_attention, fused_linear_cross_entropy, rms_norm, swiglu
-from ..parallel.symm_fsdp import multi_linear
+from ..ops.linear import linear, qkv_rope, swiglu_ffn
+from ..ops.model_ops import causal_attention, fused_linear_cross_entropy, rms_norm
 
 
 @dataclass
@@ -71,17 +73,16 @@ class Attention(nn.Module):
         self.wv = nn.Linear(cfg.dim, cfg.n_kv_heads * hd, bias=False)
         self.wo = nn.Linear(cfg.n_heads * hd, cfg.dim, bias=False)
 
-    def forward(self, x):
+    def forward(self, x, residual: Optional[torch.Tensor] = None):
+        """wo(attention(rope(wq x), rope(wk x), wv x)) (+ residual, added in wo's epilogue)."""
         B, T, _ = x.shape
         c = self.cfg
-        q, k, v = multi_linear(x, (self.wq, self.wk, self.wv))
+        q, k, v = qkv_rope(x, (self.wq, self.wk, self.wv), T, c.head_dim, c.rope_theta)
         q = q.view(B, T, c.n_heads, c.head_dim)
         k = k.view(B, T, c.n_kv_heads, c.head_dim)
         v = v.view(B, T, c.n_kv_heads, c.head_dim)
-        q = apply_rope(q, c.rope_theta)
-        k = apply_rope(k, c.rope_theta)
         o = causal_attention(q, k, v)
-        return self.wo(o.reshape(B, T, -1))
+        return linear(o.reshape(B, T, -1), self.wo, residual)
 
 
 class FeedForward(nn.Module):
@@ -91,9 +92,9 @@ class FeedForward(nn.Module):
         self.w3 = nn.Linear(cfg.dim, cfg.ffn_dim, bias=False)
         self.w2 = nn.Linear(cfg.ffn_dim, cfg.dim, bias=False)
 
-    def forward(self, x):
-        gate, up = multi_linear(x, (self.w1, self.w3))
-        return self.w2(swiglu(gate, up))
+    def forward(self, x, residual: Optional[torch.Tensor] = None):
+        """w2(silu(w1 x) * w3 x) (+ residual)."""
+        return swiglu_ffn(x, self.w1, self.w3, self.w2, residual)
 
 
 class TransformerBlock(nn.Module):
@@ -105,8 +106,8 @@ class TransformerBlock(nn.Module):
         self.feed_forward = FeedForward(cfg)
 
     def forward(self, x):
-        x = x + self.attention(self.attention_norm(x))
-        return x + self.feed_forward(self.ffn_norm(x))
+        h = self.attention(self.attention_norm(x), residual=x)
+        return self.feed_forward(self.ffn_norm(h), residual=h)
 
 
 class Llama(nn.Module):

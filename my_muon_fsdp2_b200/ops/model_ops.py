@@ -148,9 +148,11 @@ def gelu(x: torch.Tensor) -> torch.Tensor:
 class _LinearCEFn(torch.autograd.Function):
     """loss = mean_t CE(x_t @ W^T, y_t) with the logits computed chunk by chunk.
 
-    Forward computes the gradients as well (the loss is terminal): per chunk one library GEMM
-    for the logits, the fused softmax-CE kernel that turns the bf16 logits into their gradient in
-    place, and two library GEMMs for dX and dW.  Backward only scales by the incoming gradient.
+    Forward computes the gradients as well (the loss is terminal): per chunk the tcgen05 GEMM
+    for the bf16 logits (``ops.linear``), the fused softmax-CE kernel that turns them into their
+    gradient in place, then the tcgen05 GEMMs for dX (written into its row block) and dW (fp32
+    accumulation across chunks, or bf16 for a single chunk).  Backward only scales by the
+    incoming gradient.
     """
 
     @staticmethod
@@ -164,17 +166,18 @@ class _LinearCEFn(torch.autograd.Function):
         loss_sum = torch.zeros((), dtype=torch.float32, device=x.device)
         E = ext()
         inv = 1.0 / N  # kernel writes d(sum/N)/dlogits; rescaled by N/valid in backward
+        from .linear import EPI_STORE, gemm, mm_dw, mm_fwd
+
+        if single:
+            dw = torch.empty(V, D, dtype=w.dtype, device=x.device)
         for s in range(0, N, chunk):
             e = min(N, s + chunk)
             xs = x[s:e]
-            logits = xs @ w.t()  # [n, V] bf16 (library GEMM)
+            (logits,) = mm_fwd(xs, [w])  # [n, V] bf16
             rows = E.cross_entropy_(logits, targets[s:e].contiguous(), V, inv, ignore_index)
             loss_sum += rows.sum()
-            torch.matmul(logits, w, out=dx[s:e])
-            if single:
-                dw = logits.t() @ xs
-            else:
-                dw.add_(torch.mm(logits.t(), xs, out_dtype=torch.float32))
+            gemm([logits], [w], False, True, [dx[s:e]], EPI_STORE)  # dX rows of this chunk
+            mm_dw([logits], xs, [dw], accumulate=(s > 0))
         scale = N / valid.float()
         ctx.save_for_backward(dx, dw, scale)
         ctx.w_dtype = w.dtype

@@ -326,19 +326,52 @@ class SymmFSDP:
     def _local(self, i: int) -> torch.Tensor:
         return self.params[i].to_local()
 
+    def resident(self, idxs: Sequence[int]) -> bool:
+        """True when the full weights of ``idxs`` are usable without a gather: one rank, or
+        already gathered in this step."""
+        return self.world == 1 or all(self.valid[i] for i in idxs)
+
+    def full_weight(self, i: int) -> torch.Tensor:
+        """The full weight i (the local shard on one rank, else the resident gathered copy)."""
+        return self._local(i) if self.world == 1 else self.full[i]
+
+    @staticmethod
+    def _native(*ts) -> bool:
+        return all(t.is_cuda and t.dtype == torch.bfloat16 for t in ts)
+
+    def _mm(self, x2: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x2 @ w^T: this library's tcgen05 GEMM for CUDA bf16, PyTorch otherwise (CPU tests)."""
+        if self._native(x2, w):
+            from ..ops.linear import mm_fwd
+
+            return mm_fwd(x2, [w])[0]
+        return F.linear(x2, w)
+
+    def _dw(self, dy2: torch.Tensor, x2: torch.Tensor, out: torch.Tensor, accumulate: bool) -> torch.Tensor:
+        """out (+)= dy2^T x2 (weight gradient of one linear)."""
+        if self._native(dy2, x2):
+            from ..ops.linear import mm_dw
+
+            mm_dw([dy2], x2, [out], accumulate)
+        elif accumulate:
+            out.addmm_(dy2.t(), x2)
+        else:
+            torch.mm(dy2.t(), x2, out=out)
+        return out
+
     # ------------------------------------------------------------------ forward
     def linear_forward(self, i: int, x2: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
-            return F.linear(x2, self._local(i))
+            return self._mm(x2, self._local(i))
         if self.valid[i]:
-            return F.linear(x2, self.full[i])
+            return self._mm(x2, self.full[i])
         n, k = self.shapes[i]
         if self.full[i] is None:
             self.full[i] = torch.empty(n, k, dtype=x2.dtype, device=x2.device)
         self.bytes_gathered += self._shard_bytes(i, self.full[i].element_size())
         if self.peer and not self.fused_ok[i]:
             dist.all_gather_into_tensor(self.full[i], self._local(i).contiguous(), group=self.group)
-            y = F.linear(x2, self.full[i])
+            y = self._mm(x2, self.full[i])
         elif self.peer:
             if not self._step_synced:
                 # every rank has finished writing its shards (optimizer step) before any reads them
@@ -362,8 +395,12 @@ class SymmFSDP:
     def linear_backward(self, i: int, dy2: torch.Tensor, x2: torch.Tensor,
                         dx_acc: Optional[torch.Tensor] = None) -> torch.Tensor:
         """dX (added to ``dx_acc`` in place when given) and the weight-gradient path."""
-        w = self._local(i) if self.world == 1 else self.full[i]
-        if dx_acc is None:
+        w = self.full_weight(i)
+        if self._native(dy2, w):
+            from ..ops.linear import mm_dx
+
+            dx = mm_dx([dy2], [w], add_to=dx_acc)
+        elif dx_acc is None:
             dx = dy2 @ w
         else:
             dx = dx_acc.addmm_(dy2, w)
@@ -435,21 +472,15 @@ class SymmFSDP:
             # no-sync micro-batch: accumulate this rank's unsharded partial dW locally
             if self.acc[i] is None:
                 self.acc[i] = torch.empty(n, k, dtype=dy2.dtype, device=dy2.device)
-            if self.acc_live[i]:
-                self.acc[i].addmm_(dy2.t(), x2)
-            else:
-                torch.mm(dy2.t(), x2, out=self.acc[i])
-                self.acc_live[i] = True
+            self._dw(dy2, x2, self.acc[i], self.acc_live[i])
+            self.acc_live[i] = True
             return
         carry = self.acc[i] if self.acc_live[i] else None
         self.acc_live[i] = False
         g, acc = self._grad_local(i)
         self.bytes_reduced += self._shard_bytes(i, g.element_size())
         if self.world == 1:
-            if acc:
-                g.addmm_(dy2.t(), x2)
-            else:
-                torch.mm(dy2.t(), x2, out=g)
+            self._dw(dy2, x2, g, acc)
             if self.sync_grads:
                 self._replica_average(g)
             return
@@ -481,14 +512,66 @@ class SymmFSDP:
         ext.rs_reduce(slots, self.world, self.slot_elems // self.world, g, acc, 1.0 / self.world)
         self._replica_average(g)
 
+    def accumulate_grads(self, idxs: Sequence[int], dys: Sequence[torch.Tensor], x2: torch.Tensor) -> None:
+        """Weight gradients of several linears that share the input ``x2`` (q/k/v, w1/w3).
+        The partial products that go to a local buffer (the gradient shard on one rank, the
+        no-sync accumulators, the overlapped reduce-scatter's partials) are computed by one
+        grouped GEMM launch per accumulate flag; the rest go weight by weight."""
+        pairs = [(i, dy) for i, dy in zip(idxs, dys) if self.params[i].requires_grad]
+        if not pairs:
+            return
+        idxs = [i for i, _ in pairs]
+        dys = [dy for _, dy in pairs]
+        if len(idxs) == 1 or not self._native(x2, *dys):
+            for i, dy in zip(idxs, dys):
+                self._accumulate_grad(i, dy, x2)
+            return
+        groups: Dict[bool, List[Tuple[int, torch.Tensor, torch.Tensor, str]]] = {True: [], False: []}
+        for i, dy in zip(idxs, dys):
+            n, k = self.shapes[i]
+            overlap = self.peer and self.rs_mode == "overlap" and self.fused_ok[i]
+            if self.world == 1:
+                g, acc = self._grad_local(i)
+                groups[acc].append((i, dy, g, "local"))
+            elif overlap and self.sync_grads:
+                if self.acc[i] is None:
+                    o = self.acc_offsets[i]
+                    self.acc[i] = self.acc_buf[o:o + n * k].view(n, k)
+                groups[self.acc_live[i]].append((i, dy, self.acc[i], "overlap"))
+            elif not self.sync_grads:
+                if self.acc[i] is None:
+                    if overlap:
+                        o = self.acc_offsets[i]
+                        self.acc[i] = self.acc_buf[o:o + n * k].view(n, k)
+                    else:
+                        self.acc[i] = torch.empty(n, k, dtype=dy.dtype, device=dy.device)
+                groups[self.acc_live[i]].append((i, dy, self.acc[i], "nosync"))
+            else:
+                self._accumulate_grad(i, dy, x2)
+        from ..ops.linear import mm_dw
+
+        for accumulate, items in groups.items():
+            if not items:
+                continue
+            mm_dw([it[1] for it in items], x2, [it[2] for it in items], accumulate)
+            for i, _, g, kind in items:
+                if kind == "local":
+                    if self.sync_grads:
+                        self._replica_average(g)
+                elif kind == "nosync":
+                    self.acc_live[i] = True
+                else:
+                    with nvtx_range("symm_fsdp/reduce_scatter_overlap"):
+                        self._overlap_reduce(i)
+
     def _nccl_reduce_scatter(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         """Weights the fused kernels do not take: partial dW (+ the no-sync accumulation), then
         NCCL's averaging reduce-scatter into the gradient shard."""
         n, k = self.shapes[i]
         if self.acc_live[i]:
-            part = self.acc[i].addmm_(dy2.t(), x2)
+            part = self._dw(dy2, x2, self.acc[i], True)
         else:
-            part = dy2.t() @ x2
+            part = self._dw(dy2, x2, torch.empty(n, k, dtype=dy2.dtype, device=dy2.device), False)
         self.acc_live[i] = False
         g, acc = self._grad_local(i)
         self.bytes_reduced += self._shard_bytes(i, part.element_size())
@@ -503,14 +586,16 @@ class SymmFSDP:
     def _overlapped_reduce_scatter(self, i: int, dy2: torch.Tensor, x2: torch.Tensor) -> None:
         """Synchronising backward of weight i (overlap mode): local partial GEMM, then the
         reduce-scatter on the side stream, overlapped with the rest of the backward."""
+        # 1. this rank's complete partial dW (+ the no-sync accumulation), local GEMM
+        self._dw(dy2, x2, self.acc[i], self.acc_live[i])
+        self._overlap_reduce(i)
+
+    def _overlap_reduce(self, i: int) -> None:
+        """Second half of the overlapped reduce-scatter of weight i, whose complete partial dW
+        is in ``acc[i]``: the pull-reduce on the side stream."""
         n, k = self.shapes[i]
         r = self.rows[i]
         acc_i = self.acc[i]
-        # 1. this rank's complete partial dW (+ the no-sync accumulation), local GEMM
-        if self.acc_live[i]:
-            acc_i.addmm_(dy2.t(), x2)
-        else:
-            torch.mm(dy2.t(), x2, out=acc_i)
         self.acc_live[i] = False
         g, acc = self._grad_local(i)
         self.bytes_reduced += self._shard_bytes(i, acc_i.element_size())

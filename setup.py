@@ -29,6 +29,7 @@ if os.environ.get("MMF_DEVICE_CHECKS", "0") == "1":
 SOURCES = [
     "bindings.cpp",
     "tc_gemm.cu",
+    "linear_gemm.cu",
     "optim_kernels.cu",
     "model_kernels.cu",
     "attention.cu",

@@ -153,7 +153,7 @@ def _init_entry(rank, world, port, path):
     torch.set_num_threads(1)
     from my_muon_fsdp2_b200.parallel.fault import init_distributed
 
-    info = init_distributed(timeout_s=2.0)
+    info = init_distributed(backend="gloo", timeout_s=2.0)
     t = torch.tensor([float(rank + 1)])
     dist.all_reduce(t)
     res = {"info": info, "sum": float(t), "backend": dist.get_backend()}

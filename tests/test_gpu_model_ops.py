@@ -114,7 +114,8 @@ def test_muon_optimizer_cuda_matches_cpu_oracle():
     torch.manual_seed(0)
     shapes = [(256, 512), (512, 256), (300, 200), (64,)]
     ps = [torch.nn.Parameter(torch.randn(*s, device="cuda")) for s in shapes]
-    ref = [p.detach().double().cpu().clone() for p in ps]
+    p0 = [p.detach().double().cpu().clone() for p in ps]
+    ref = [p.clone() for p in p0]
     bufs = [torch.zeros_like(r) for r in ref]
     opt = MuonOptimizer(ps, lr=0.02, momentum=0.9, weight_decay=0.1, nesterov=True)
     for step in range(2):
@@ -123,6 +124,12 @@ def test_muon_optimizer_cuda_matches_cpu_oracle():
             p.grad = g
         opt.step()
         muon_reference_step(ref, [g.double().cpu() for g in grads], bufs, 0.02, 0.9, 0.1, True, 5)
-    for p, r in zip(ps, ref):
-        # parameters move by lr*O per step; compare the accumulated change
-        assert rel_err(p.detach().cpu(), r) < 5e-3
+    for p, r, q in zip(ps, ref, p0):
+        # compare the parameter CHANGE with the oracle's change: the update is about 0.2 % of
+        # the parameter, so a whole-parameter comparison would pass even with a zero NS output
+        d_ours, d_ref = p.detach().cpu().double() - q, r - q
+        assert rel_err(d_ours, d_ref) < 0.06, f"update mismatch for shape {tuple(p.shape)}"
+        # and the NS part alone (the change minus weight decay), for the matrices
+        if p.dim() == 2:
+            decay = (1 - 0.02 * 0.1) ** 2 - 1
+            assert rel_err(d_ours - decay * q, d_ref - decay * q) < 0.06

@@ -5,6 +5,9 @@ runtime with its own pre-planned memory arena, or code without PyTorch's allocat
 its scratch in a fixed static device array.  The test calls the exported C symbol through
 ctypes, twice in a row (the second call reuses the scratch left by the first), and compares
 with ``rmsnorm_bwd`` of the extension within the tolerance used by the other kernel tests.
+Both are also checked against a plain fp32 PyTorch restatement of the RMSNorm backward.
+The cases include the documented maximum row width (8192, every slot of the per-thread
+accumulator and the whole 64 x 8192 scratch in use) and a width that is not a multiple of 256.
 This file is collected last on purpose.
 """
 import ctypes
@@ -28,13 +31,21 @@ def _lib():
     return lib, fn
 
 
+def _rmsnorm_bwd_fp32(dy, x, w, rstd):
+    """dx = rstd * (dy * w) - x * rstd^3 * mean(dy * w * x); dw = sum_rows dy * x * rstd."""
+    dy, x, w, r = dy.float(), x.float(), w.float(), rstd.float()[:, None]
+    gw = dy * w
+    dx = r * gw - x * r.pow(3) * (gw * x).mean(-1, keepdim=True)
+    return dx, (dy * x * r).sum(0)
+
+
 def test_noalloc_rmsnorm_bwd_matches_regular_entry_point_twice():
     from my_muon_fsdp2_b200._ext import ext
 
     lib, fn = _lib()
     torch.manual_seed(0)
     stream = torch.cuda.current_stream()
-    for rows, cols in [(300, 4096), (37, 768)]:
+    for rows, cols in [(300, 4096), (37, 768), (200, 8192), (64, 8000)]:
         x = torch.randn(rows, cols, device="cuda").to(torch.bfloat16)
         w = torch.randn(cols, device="cuda").to(torch.bfloat16)
         _, rstd = ext().rmsnorm_fwd(x, w, 1e-5)
@@ -49,6 +60,20 @@ def test_noalloc_rmsnorm_bwd_matches_regular_entry_point_twice():
             torch.cuda.synchronize()
             assert rel_err(dx, ref_dx) < 1e-2, f"dx mismatch on call {call}"
             assert rel_err(dw, ref_dw) < 1e-2, f"dw mismatch on call {call}"
+            f_dx, f_dw = _rmsnorm_bwd_fp32(dy, x, w, rstd)
+            assert rel_err(dx, f_dx) < 1e-2, f"dx differs from fp32 on call {call} ({rows}x{cols})"
+            assert rel_err(dw, f_dw) < 1e-2, f"dw differs from fp32 on call {call} ({rows}x{cols})"
+
+
+def test_noalloc_rejects_a_stream_of_another_device():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    lib, fn = _lib()
+    t = torch.zeros(8, device="cuda:0")
+    with torch.cuda.device(1):
+        s1 = torch.cuda.Stream()
+    rc = fn(t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), t.data_ptr(), 1, 8, s1.cuda_stream)
+    assert rc == 4, lib.mmf_noalloc_last_error()
 
 
 def test_noalloc_rejects_oversized_rows():
