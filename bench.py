@@ -51,6 +51,9 @@ def parse():
                     help="symm: reduce-scatter on a side stream (overlap) or from the GEMM epilogue (fused)")
     ap.add_argument("--keep-gathered", action="store_true",
                     help="FSDP2 modules stay gathered between the micro-batches of a step (Trainer keep_gathered)")
+    ap.add_argument("--phases", action="store_true",
+                    help="also report the device time of each step phase (forward / backward per micro-batch, "
+                         "optimizer), max over ranks, averaged over the timed steps")
     ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="symm",
                     help="fsdp2: fully_shard everywhere; symm: block linears on symmetric memory with the "
                          "fused all-gather GEMM / GEMM reduce-scatter kernels, the rest fully_shard")
@@ -220,7 +223,8 @@ def main():
     else:
         from my_muon_fsdp2_b200.train import Trainer
 
-        trainer = Trainer(model, opts, grad_accum=ga, step_timer=opt_timer, keep_gathered=args.keep_gathered)
+        trainer = Trainer(model, opts, grad_accum=ga, step_timer=opt_timer, keep_gathered=args.keep_gathered,
+                          time_phases=args.phases)
 
     dev_batches = [synthetic_tokens(s, ga, mbs, seq, vocab, rank, device="cuda") for s in range(2)]
     for s in range(args.warmup):
@@ -240,9 +244,13 @@ def main():
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     start, end = marks[0], marks[-1]
     start.record()
+    phase_sum: dict = {}
     for s in range(args.steps):
         loss = trainer.step_on_device(dev_batches[s % 2])
         marks[s + 1].record()
+        if args.phases and hasattr(trainer, "phase_ms"):
+            for k, v in trainer.phase_ms().items():  # reading the events waits for this step
+                phase_sum[k] = phase_sum.get(k, 0.0) + v
     torch.cuda.synchronize()
     launches = (count() - n0) if count else None
     clk = clocks.stop()
@@ -253,6 +261,7 @@ def main():
     per_step = [max_over_ranks(marks[i].elapsed_time(marks[i + 1])) for i in range(args.steps)]
     srt = sorted(per_step)
     spread = {"min": srt[0], "median": srt[len(srt) // 2], "max": srt[-1]}
+    phases = {k: max_over_ranks(v / args.steps) for k, v in sorted(phase_sum.items())} if phase_sum else None
     opt_ms = max_over_ranks(opt_timer.mean_ms())
     final_loss = float(loss.item())
 
@@ -287,6 +296,7 @@ def main():
             "vs_baseline": (value / base) if base else None, "dtype": "bf16",
             "data": "synthetic uniform random tokens; random-init weights",
             "optimizer_step_ms": opt_ms, "step_ms_spread": spread,
+            **({"phase_ms": phases} if phases else {}),
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",

@@ -2,7 +2,7 @@
 PyTorch SDPA (cuDNN / flash backend, a library kernel) on the Llama-3-8B attention shape.
 
     python bench_attn.py [--B 1 --T 4096 --Hq 32 --Hkv 8 --D 128 --iters 20]
-    python bench_attn.py --sweep 'fwd=0,2,3,4;bwd=0,1'     # kernel variants, one process
+    python bench_attn.py --sweep 'fwd=0,1'                 # forward kernels, one process
 
 Causal FLOPs: forward 2 * 2 * B * Hq * T^2 * D / 2, backward 2.5x forward.  CUDA events on the
 launching stream after warm-up.  The inputs (32 MB per tensor at the default shape) fit in the
@@ -39,18 +39,16 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--only", choices=["all", "ours_fwd", "ours_bwd"], default="all")
     ap.add_argument("--fwd-variant", type=int, default=0,
-                    help="0: two query tiles per CTA (packed-arithmetic softmax), 1: one, 2: two (plain softmax)")
-    ap.add_argument("--bwd-variant", type=int, default=0, help="0: plain elementwise, 1: packed f32x2 arithmetic")
+                    help="0: three warpgroups with whole score rows (default), 1: two softmax warpgroups")
     ap.add_argument("--sweep", default="",
-                    help="time several kernels in one process, e.g. 'fwd=0,2,3,4;bwd=0,1' (checks each "
-                         "against the default kernels' output first)")
+                    help="time several forward kernels in one process, e.g. 'fwd=0,1' (checks each against "
+                         "the default kernel's output first)")
     a = ap.parse_args()
     if a.sweep:
         return sweep(a)
     from my_muon_fsdp2_b200._ext import ext
 
     ext().set_attention_fwd_variant(a.fwd_variant)
-    ext().set_attention_bwd_variant(a.bwd_variant)
     torch.manual_seed(0)
     q = torch.randn(a.B, a.T, a.Hq, a.D, device="cuda", dtype=torch.bfloat16)
     k = torch.randn(a.B, a.T, a.Hkv, a.D, device="cuda", dtype=torch.bfloat16)
@@ -82,23 +80,19 @@ def main():
 
 
 def sweep(a):
-    """Time the listed forward / backward variants at one shape, interleaved twice, after
-    checking that each gives the default kernel's result (relative Frobenius difference)."""
+    """Time the listed forward variants at one shape, interleaved twice, after checking that each
+    gives the default kernel's result (relative Frobenius difference)."""
     from my_muon_fsdp2_b200._ext import check_device_error, ext
 
     spec = dict(part.split("=") for part in a.sweep.split(";") if part)
     fwd = [int(v) for v in spec.get("fwd", "").split(",") if v != ""]
-    bwd = [int(v) for v in spec.get("bwd", "").split(",") if v != ""]
     torch.manual_seed(0)
     q = torch.randn(a.B, a.T, a.Hq, a.D, device="cuda", dtype=torch.bfloat16)
     k = torch.randn(a.B, a.T, a.Hkv, a.D, device="cuda", dtype=torch.bfloat16)
     v = torch.randn(a.B, a.T, a.Hkv, a.D, device="cuda", dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(a.D)
     ext().set_attention_fwd_variant(0)
-    ext().set_attention_bwd_variant(0)
     o0, lse0 = ext().attention_fwd(q, k, v, scale)
-    do = torch.randn_like(o0)
-    g0 = ext().attention_bwd(do, q, k, v, o0, lse0, scale)
     torch.cuda.synchronize()
 
     def rel(x, y):
@@ -114,15 +108,6 @@ def sweep(a):
             res.setdefault(f"fwd{fv}_rel_diff", rel(o, o0))
             res.setdefault(f"fwd{fv}_ms", []).append(timeit(lambda: ext().attention_fwd(q, k, v, scale), a.iters))
         ext().set_attention_fwd_variant(0)
-        for bv in bwd:
-            ext().set_attention_bwd_variant(bv)
-            g = ext().attention_bwd(do, q, k, v, o0, lse0, scale)
-            torch.cuda.synchronize()
-            check_device_error(0)
-            res.setdefault(f"bwd{bv}_rel_diff", max(rel(x, y) for x, y in zip(g, g0)))
-            res.setdefault(f"bwd{bv}_ms", []).append(
-                timeit(lambda: ext().attention_bwd(do, q, k, v, o0, lse0, scale), a.iters))
-        ext().set_attention_bwd_variant(0)
     res["shape"] = dict(B=a.B, T=a.T, Hq=a.Hq, Hkv=a.Hkv, D=a.D)
     print(json.dumps(res))
 

@@ -19,7 +19,6 @@
 #include <string>
 
 #include "attention.h"
-#include "exp2_poly.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
 
@@ -29,7 +28,6 @@ namespace {
 
 constexpr int QB = 128;  // query rows per CTA
 constexpr int KB = 128;  // keys per block
-constexpr int ATT_THREADS = 192;
 constexpr int BWD_THREADS = 320;  // TMA warp, MMA warp, 8 elementwise warps (2 per TMEM lane quarter)
 
 struct AttnParams {
@@ -40,18 +38,6 @@ struct AttnParams {
   int* err;
 };
 
-template <int D>
-struct AttnSmem {
-  static constexpr int CH = D / 64;                 // 64-column swizzle chunks per row
-  static constexpr int TILE = 128 * D * 2;          // one [128 x D] bf16 tile
-  static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + TILE;        // 2 stages
-  static constexpr int V_OFF = K_OFF + 2 * TILE;    // 2 stages
-  static constexpr int BAR_OFF = V_OFF + 2 * TILE;  // P_j lives in TMEM (over S_j), not in smem
-  // >= 120 KB so that only one CTA (which holds all 512 TMEM columns) fits on an SM
-  static constexpr int BYTES = (BAR_OFF + 256 + 1024) > 120 * 1024 ? (BAR_OFF + 256 + 1024) : 120 * 1024;
-};
-
 // byte offset of element (row, col) inside a K-major 128B-swizzled tile made of [rows x 64]
 // chunks of 16 KB each (128 rows): the 16-byte unit index is XORed with (row % 8).
 __device__ __forceinline__ uint32_t swz_offset(int row, int col) {
@@ -60,224 +46,6 @@ __device__ __forceinline__ uint32_t swz_offset(int row, int col) {
   const int unit = (c >> 3) ^ (row & 7);
   return static_cast<uint32_t>(chunk * (128 * 128) + row * 128 + unit * 16 + (c & 7) * 2);
 }
-
-template <int D>
-__global__ void __launch_bounds__(ATT_THREADS, 1)
-    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
-  using L = AttnSmem<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem + L::Q_OFF;
-  uint8_t* sK = smem + L::K_OFF;
-  uint8_t* sV = smem + L::V_OFF;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2] S_j in TMEM buffer j&1
-  uint64_t* p_full = bars + 7;    // [2] P_j (bf16, packed) written over S_j
-  uint64_t* pv_done = bars + 9;
-  uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqb = p.T / QB;
-  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);  // heaviest blocks first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int hk = h / (p.Hq / p.Hkv);
-  const int nblk = qb + 1;  // causal: key blocks 0..qb
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-    }
-    mbar_init(pv_done, 1);
-    mbar_init(drain, 1);
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // S_j buffer of block j: tmem + (j & 1) * 128 (arithmetic, so no local-memory array)
-  auto ts_buf = [tmem](int st) { return tmem + static_cast<uint32_t>(st) * 128u; };
-  const uint32_t tO = tmem + 256;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      constexpr uint32_t TILE = L::TILE;
-      mbar_arrive_expect_tx(q_full, TILE);
-#pragma unroll
-      for (int c = 0; c < L::CH; ++c) tma_load_4d(sQ + c * 16384, &tmQ, q_full, c * 64, h, qb * QB, b);
-      for (int j = 0; j < nblk; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, ERR_TMA_EMPTY_TIMEOUT)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
-#pragma unroll
-        for (int c = 0; c < L::CH; ++c) {
-          tma_load_4d(sK + st * TILE + c * 16384, &tmK, &kv_full[st], c * 64, hk, j * KB, b);
-          tma_load_4d(sV + st * TILE + c * 16384, &tmV, &kv_full[st], c * 64, hk, j * KB, b);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(128, KB, false, false);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, false, true);
-      const uint32_t q_addr = smem_u32(sQ);
-      // S_j = Q K_j^T into TMEM buffer j&1.  The buffer last held P_{j-2}, whose P V MMA was
-      // issued earlier by this thread, and tcgen05 MMAs of one thread execute in order.
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + st * L::TILE);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(ts_buf(st), sdesc_kmajor(q_addr + off), sdesc_kmajor(k_addr + off), idesc_s, kk ? 1u : 0u);
-        }
-        umma_commit(&s_full[st]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, p.err, ERR_MMA_FULL_TIMEOUT) && issue_s(0);
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int st = j & 1;
-        // S_{j+1} overlaps the softmax of block j
-        if (j + 1 < nblk && !(ok = issue_s(j + 1))) break;
-        // O += P_j V_j with P_j read from TMEM (bf16 pairs over S_j's first 64 columns)
-        if (!mbar_wait(&p_full[st], (j >> 1) & 1, p.err, ERR_MMA_FULL_TIMEOUT)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + st * L::TILE);
-#pragma unroll
-        for (int kk = 0; kk < KB / 16; ++kk)
-          umma_bf16_ts(tO, ts_buf(st) + static_cast<uint32_t>(kk * 8), sdesc_mnmajor(v_addr + kk * 16 * 128, 16384),
-                       idesc_o, (j | kk) ? 1u : 0u);
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
-      }
-      umma_commit(drain);
-      mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
-    }
-  } else {
-    // ------------------------------ softmax / epilogue ---------------------------------
-    const int q = warp & 3;
-    const int r = q * 32 + lane;            // row inside the query block
-    const int qi = qb * QB + r;             // query position
-    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    float m2 = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nblk && ok; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait(&s_full[st], (j >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool diag = (j == qb);
-      // the whole 128-column S row in registers: 4 loads, one wait
-      float sv[KB];
-#pragma unroll
-      for (int c = 0; c < KB / 32; ++c) tmem_ld_32cols_async(ts_buf(st) + lane_off + c * 32, sv + c * 32);
-      tmem_ld_wait();
-      float mx = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < KB; ++e) {
-        sv[e] *= p.scale_log2;
-        if (diag && (j * KB + e > qi)) sv[e] = -INFINITY;
-        mx = fmaxf(mx, sv[e]);
-      }
-      // The reference max only moves when the row max grows by more than 2^8: probabilities stay
-      // below 256 and O / l is unchanged (both use the same reference), while O rarely needs a
-      // rescale in TMEM.
-      const bool grow = (m2 == -INFINITY) || (mx > m2 + 8.f);
-      const float m_new = grow ? mx : m2;
-      const float alpha = (m2 == -INFINITY) ? 0.f : (grow ? fast_exp2(m2 - m_new) : 1.f);
-      // O may only be rescaled once P_{j-1} V_{j-1} has landed (rare: threshold above)
-      if (__any_sync(0xffffffffu, j >= 1 && alpha != 1.f)) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int hh = 0; hh < D / 64; ++hh) {
-          float o[64];
-          tmem_ld_32cols_async(tO + lane_off + hh * 64, o);
-          tmem_ld_32cols_async(tO + lane_off + hh * 64 + 32, o + 32);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 64; ++e) o[e] *= alpha;
-          tmem_st_32cols_async(tO + lane_off + hh * 64, o);
-          tmem_st_32cols_async(tO + lane_off + hh * 64 + 32, o + 32);
-        }
-      }
-      // probabilities as bf16 pairs over the first 64 columns of S_j's TMEM buffer; row sum
-      float sum = 0.f;
-      float pk[KB / 2];
-#pragma unroll
-      for (int e2 = 0; e2 < KB / 2; ++e2) {
-        const float p0 = fast_exp2(sv[2 * e2] - m_new);
-        const float p1 = fast_exp2(sv[2 * e2 + 1] - m_new);
-        sum += p0 + p1;
-        __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-        pk[e2] = *reinterpret_cast<float*>(&pb);
-      }
-      tmem_st_32cols_async(ts_buf(st) + lane_off, pk);
-      tmem_st_32cols_async(ts_buf(st) + lane_off + 32, pk + 32);
-      tmem_st_wait();
-      l = l * alpha + sum;
-      m2 = m_new;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[st]);
-    }
-    // epilogue: wait for the last P V, then O / l
-    if (ok && mbar_wait(pv_done, (nblk - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-      tc_fence_after();
-      const float inv = (l > 0.f) ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = p.o + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D;
-      float o[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) tmem_ld_32cols_async(tO + lane_off + c * 32, o + c * 32);
-      tmem_ld_wait();
-#pragma unroll
-      for (int g = 0; g < D / 8; ++g) {
-        uint4 w;
-        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(o[g * 8 + 2 * e2] * inv, o[g * 8 + 2 * e2 + 1] * inv);
-        *reinterpret_cast<uint4*>(orow + g * 8) = w;
-      }
-      // natural-log LSE: (m2 + log2(l)) * ln 2
-      p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + qi] = (m2 + log2f(l)) * 0.69314718055994531f;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 
 // ======================================================================================
 // Forward with two query tiles per CTA (query blocks 2x and 2x+1 of one head): two softmax
@@ -301,114 +69,13 @@ struct Attn2Smem {
 constexpr int ATT2_THREADS = 320;
 
 // Online softmax of one query tile (128 rows, one per thread of the 4 calling warps) over key
-// blocks 0..nblk-1; P into TMEM over S; O rescale in TMEM when the reference max moves; epilogue.
-template <int D>
-__device__ __forceinline__ void fwd_softmax_tile(const AttnParams& p, uint32_t tS, uint32_t tO, uint64_t* s_full,
-                                                 uint64_t* p_full, uint64_t* pv_done, int qb, int nblk, int h, int b,
-                                                 int q, int lane) {
-  const int r = q * 32 + lane;
-  const int qi = qb * QB + r;
-  const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-  float m2 = -INFINITY, l = 0.f;
-  bool ok = true;
-  for (int j = 0; j < nblk && ok; ++j) {
-    if (!mbar_wait(s_full, j & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-      ok = false;
-      break;
-    }
-    tc_fence_after();
-    const bool diag = (j == qb);
-    // Two 64-column halves keep the register footprint at one half: the row max reads keys
-    // 64..127 then 0..63; the probabilities of keys 0..63 come from the registers, those of
-    // keys 64..127 from a second TMEM read (their S columns are not overwritten before that).
-    float sv[64];
-    auto load_half = [&](int hf) {
-      tmem_ld_32cols_async(tS + lane_off + hf * 64, sv);
-      tmem_ld_32cols_async(tS + lane_off + hf * 64 + 32, sv + 32);
-      tmem_ld_wait();
-#pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        sv[e] *= p.scale_log2;
-        if (diag && (j * KB + hf * 64 + e > qi)) sv[e] = -INFINITY;
-      }
-    };
-    float mx = -INFINITY;
-    load_half(1);
-#pragma unroll
-    for (int e = 0; e < 64; ++e) mx = fmaxf(mx, sv[e]);
-    load_half(0);
-#pragma unroll
-    for (int e = 0; e < 64; ++e) mx = fmaxf(mx, sv[e]);
-    // the reference max moves only when the row max grows by more than 2^8 (see attn_fwd_kernel)
-    const bool grow = (m2 == -INFINITY) || (mx > m2 + 8.f);
-    const float m_new = grow ? mx : m2;
-    const float alpha = (m2 == -INFINITY) ? 0.f : (grow ? fast_exp2(m2 - m_new) : 1.f);
-    if (__any_sync(0xffffffffu, j >= 1 && alpha != 1.f)) {
-      if (!mbar_wait(pv_done, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        tmem_ld_32cols(tO + lane_off + c * 32, o);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] *= alpha;
-        tmem_st_32cols_async(tO + lane_off + c * 32, o);
-      }
-    }
-    float sum = 0.f;
-#pragma unroll 1
-    for (int hf = 0; hf < 2; ++hf) {
-      if (hf == 1) {
-        tmem_st_wait();  // keys 0..63 stored over S columns 0..31, which were read already
-        load_half(1);
-      }
-      float pk[32];
-#pragma unroll
-      for (int e2 = 0; e2 < 32; ++e2) {
-        const float p0 = fast_exp2(sv[2 * e2] - m_new);
-        const float p1 = fast_exp2(sv[2 * e2 + 1] - m_new);
-        sum += p0 + p1;
-        __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-        pk[e2] = *reinterpret_cast<float*>(&pb);
-      }
-      tmem_st_32cols_async(tS + lane_off + hf * 32, pk);
-    }
-    tmem_st_wait();
-    l = l * alpha + sum;
-    m2 = m_new;
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(p_full);
-  }
-  if (ok && nblk > 0 && mbar_wait(pv_done, (nblk - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-    tc_fence_after();
-    const float inv = (l > 0.f) ? 1.f / l : 0.f;
-    __nv_bfloat16* orow = p.o + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D;
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float o[32];
-      tmem_ld_32cols(tO + lane_off + c * 32, o);
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        uint4 w;
-        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
-#pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) hw[e2] = __floats2bfloat162_rn(o[g * 8 + 2 * e2] * inv, o[g * 8 + 2 * e2 + 1] * inv);
-        *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = w;
-      }
-    }
-    p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.T + qi] = (m2 + log2f(l)) * 0.69314718055994531f;
-  }
-}
-
-// Same contract as fwd_softmax_tile, with fewer instructions per score: the row max is taken
-// on the raw scores (the scale is positive), three at a time; the exponent argument is one
-// packed fma s*scale - m per pair of scores; the row sum is a packed add; the causal mask is
-// applied only on the diagonal block.
-template <int D, bool FULL_ROW, int EMU = 0>
+// blocks 0..nblk-1; P into TMEM over S; O rescaled in TMEM when the reference max moves;
+// epilogue O / l -> bf16 and the row log-sum-exp.  The row max is taken on the raw scores (the
+// scale is positive), three at a time; the exponent argument is one packed fma s*scale - m per
+// pair of scores; the row sum is a packed add; the causal mask is applied only on the diagonal
+// block.  FULL_ROW: the whole row of 128 scores in registers (one TMEM read per key block, for
+// the 3-warpgroup kernel whose softmax threads hold 224 registers), else two 64-score halves.
+template <int D, bool FULL_ROW>
 __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_t tS, uint32_t tO, uint64_t* s_full,
                                                     uint64_t* p_full, uint64_t* pv_done, int qb, int nblk, int h,
                                                     int b, int q, int lane) {
@@ -460,7 +127,7 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
       for (int e = 0; e < 64; e += 2) mx = fmax3(mx, sv[e], sv[e + 1]);
     }
     const float mxs = mx * c;
-    // the reference max moves only when the row max grows by more than 2^8 (see attn_fwd_kernel)
+    // the reference max moves only when the row max grows by more than 2^8 (then the exponentials stay below 2^8 and fp32 sums cannot overflow)
     const bool grow = (m2 == -INFINITY) || (mxs > m2 + 8.f);
     const float m_new = grow ? mxs : m2;
     const float alpha = (m2 == -INFINITY) ? 0.f : (grow ? fast_exp2(m2 - m_new) : 1.f);
@@ -488,11 +155,7 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
 #pragma unroll
       for (int e2 = 0; e2 < 32; ++e2) {
         const float2 x = ffma2(make_float2(v[2 * e2], v[2 * e2 + 1]), c2, nm);
-        // with EMU > 0, every EMU-th pair takes the FMA-pipe exponential (exp2_poly.cuh) so that
-        // the MUFU unit is not the only one computing exponentials
-        const bool emu = (EMU > 0) && (e2 % (EMU > 0 ? EMU : 1) == (EMU > 0 ? EMU : 1) - 1);
-        const float2 pp = emu ? make_float2(exp2_poly(x.x), exp2_poly(x.y))
-                              : make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        const float2 pp = make_float2(fast_exp2(x.x), fast_exp2(x.y));
         sum2 = fadd2(sum2, pp);
         __nv_bfloat162 pb = __floats2bfloat162_rn(pp.x, pp.y);
         pk[e2] = *reinterpret_cast<float*>(&pb);
@@ -540,7 +203,7 @@ __device__ __forceinline__ void fwd_softmax_tile_v2(const AttnParams& p, uint32_
   }
 }
 
-template <int D, bool V2, bool FULL_ROW = false, int EMU = 0>
+template <int D>
 __global__ void __launch_bounds__(ATT2_THREADS, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -684,12 +347,8 @@ __global__ void __launch_bounds__(ATT2_THREADS, 1)
     const int t = (warp - 2) >> 2;  // tile of this warpgroup (one call site keeps the code small)
     const int q = warp & 3;
     if (t == 0 || has_b) {
-      if constexpr (V2)
-        fwd_softmax_tile_v2<D, FULL_ROW, EMU>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
-                               t ? nblk_b : nblk_a, h, b, q, lane);
-      else
-        fwd_softmax_tile<D>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
-                            t ? nblk_b : nblk_a, h, b, q, lane);
+      fwd_softmax_tile_v2<D, false>(p, ts_of(t), to_of(t), s_full + t, p_full + t, pv_done + t, t ? qbb : qa,
+                                    t ? nblk_b : nblk_a, h, b, q, lane);
     }
   }
   tc_fence_before();
@@ -902,7 +561,7 @@ struct BwdSmem {
   static constexpr int BYTES = BYTES0 > 120 * 1024 ? BYTES0 : 120 * 1024;
 };
 
-template <int D, bool V2, bool PING = false, int EMU = 0>
+template <int D>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -945,7 +604,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&do_full[t], 1);
       mbar_init(&do_empty[t], 1);
       mbar_init(&sp_full[t], 1);
-      mbar_init(&ds_full[t], PING ? 4 : 8);
+      mbar_init(&ds_full[t], 8);
       mbar_init(&ds_empty[t], 1);
     }
     mbar_init(drain, 1);
@@ -1051,123 +710,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, p.err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
     }
-  } else if constexpr (PING) {
-    // Ping-pong: warpgroup wg (warps 2-5 / 6-9) owns the units of query half wg, i.e. queries
-    // wg*64 .. wg*64+63 of every query block, all 64 of them per warp (two 32-query passes), so
-    // the two warpgroups work on consecutive units at the same time.  Packed arithmetic as V2.
-    const int q = warp & 3;
-    const int wg = (warp - 2) >> 2;
-    const int kr = q * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const int wt = threadIdx.x - 64 - wg * 128;  // 0..127 inside the warpgroup
-    // this warpgroup's statistics of the current block: [0, 64) = -lse*log2e, [64, 128) = -delta
-    float* sStat = sLse + wg * 128;
-    const float* stat_src = (wt < 64) ? p.lse : p.delta;
-    const float stat_mul = (wt < 64) ? -1.4426950408889634f : -1.f;
-    const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + wg * 64 + (wt & 63);
-    float stat_next = stat_src[stat_base + j * QB] * stat_mul;
-    const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-    bool ok = true;
-    for (int u = wg; u < n_units && ok; u += 2) {
-      const int n = u >> 1, h = u & 1;  // h == wg
-      const int i = j + n;
-      // publish this block's statistics (the previous block's readers are past the barrier)
-      if (wg == 0)
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      else
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-      sStat[wt] = stat_next;
-      if (wg == 0)
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      else
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-      if (n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
-      if (!mbar_wait(&sp_full[h], (u >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool diag = (i == j);
-      uint8_t* dst_tile = sDSt + h * 16384;
-#pragma unroll 1
-      for (int pass = 0; pass < 2; ++pass) {
-        const int c0 = pass * 32;  // queries c0 .. c0+31 of this unit
-        float sv[32], dp[32];
-        tmem_ld_32cols_async(ts_h(h) + lane_off + c0, sv);
-        tmem_ld_32cols_async(tdp_h(h) + lane_off + c0, dp);
-        tmem_ld_wait();
-        float ppk[16];
-        uint4 wds[4];  // dS^T of this pass, stored once the buffer is free
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4& wd = wds[g];
-          __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
-          const int qu = c0 + g * 8;  // query column inside the unit
-          float st_l[8], st_d[8];
-          *reinterpret_cast<float4*>(st_l) = *reinterpret_cast<const float4*>(sStat + qu);
-          *reinterpret_cast<float4*>(st_l + 4) = *reinterpret_cast<const float4*>(sStat + qu + 4);
-          *reinterpret_cast<float4*>(st_d) = *reinterpret_cast<const float4*>(sStat + 64 + qu);
-          *reinterpret_cast<float4*>(st_d + 4) = *reinterpret_cast<const float4*>(sStat + 64 + qu + 4);
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const int e = g * 8 + e2 * 2;
-            const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, make_float2(st_l[e2 * 2], st_l[e2 * 2 + 1]));
-            // with EMU > 0, every EMU-th pair of exponentials on the FMA pipe (exp2_poly.cuh)
-            const bool emu = (EMU > 0) && ((g * 4 + e2) % (EMU > 0 ? EMU : 1) == (EMU > 0 ? EMU : 1) - 1);
-            float2 pr = emu ? make_float2(exp2_poly(x.x), exp2_poly(x.y)) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
-            if (diag) {
-              const int qc = h * 64 + qu + e2 * 2;  // query column inside the block
-              if (qc < kr) pr.x = 0.f;
-              if (qc + 1 < kr) pr.y = 0.f;
-            }
-            const float2 dd =
-                fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), make_float2(st_d[e2 * 2], st_d[e2 * 2 + 1])));
-            __nv_bfloat162 pb = __floats2bfloat162_rn(pr.x, pr.y);
-            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
-            hd[e2] = __floats2bfloat162_rn(dd.x, dd.y);
-          }
-        }
-        // packed P^T of queries c0 .. c0+31 over their own (consumed) S^T columns [c0, c0 + 16);
-        // the dV MMA that read this half's previous P^T completed before S^T of this unit
-        tmem_st_16cols_async(ts_h(h) + lane_off + c0, ppk);
-        // the dS^T buffer of this half was last read by the dK MMA of unit u-2
-        if (pass == 0 && u >= 2 &&
-            !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS,
-                       false)) {
-          tmem_st_wait();  // leave no TMEM store in flight on the way out
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wds[g];
-      }
-      if (!ok) break;
-      tmem_st_wait();
-      tc_fence_before();
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ds_full[h]);
-    }
-    // the last dV/dK MMAs: wait for the final Q/dO release (committed after them)
-    if (ok) ok = mbar_wait(&q_empty[(n_iter - 1) & 1], ((n_iter - 1) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
-                           MMF_WAIT_TIMEOUT_NS, false);
-    if (ok) {
-      tc_fence_after();
-      const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hq + hq;
-#pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
-        float* dst = (which == 0 ? p.dv_h : p.dk_h) + row * D + wg * (D / 2);
-        const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off + wg * (D / 2);
-        const float f = which == 0 ? 1.f : p.scale;
-        float v[D / 2];
-#pragma unroll
-        for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tb + c * 32, v + c * 32);
-        tmem_ld_wait();
-#pragma unroll
-        for (int g = 0; g < D / 8; ++g)
-          *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4] * f, v[g * 4 + 1] * f, v[g * 4 + 2] * f, v[g * 4 + 3] * f);
-      }
-    }
   } else {
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;  // which 32 queries of a 64-query unit (and D/2 output columns)
@@ -1182,8 +724,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     bool ok = true;
     // row statistics of each query block, prefetched one block ahead (one value per thread)
     const float* stat_src = (tid < 128) ? p.lse : p.delta;
-    // V2 keeps the statistics negated (-lse*log2e, -delta) so that both enter as addends
-    const float stat_mul = ((tid < 128) ? 1.4426950408889634f : 1.f) * (V2 ? -1.f : 1.f);
+    // the statistics are kept negated (-lse*log2e, -delta) so that both enter as addends
+    const float stat_mul = (tid < 128) ? -1.4426950408889634f : -1.f;
     const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + (tid & 127);
     float stat_next = stat_src[stat_base + j * QB] * stat_mul;
     for (int u = 0; u < n_units && ok; ++u) {
@@ -1228,43 +770,24 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         *reinterpret_cast<float4*>(st_l + 4) = *reinterpret_cast<const float4*>(sLse + q0 + 4);
         *reinterpret_cast<float4*>(st_d) = *reinterpret_cast<const float4*>(sDelta + q0);
         *reinterpret_cast<float4*>(st_d + 4) = *reinterpret_cast<const float4*>(sDelta + q0 + 4);
-        if constexpr (V2) {
-          // one packed fma per pair for the exponent argument, packed add + mul for dS; the
-          // causal mask only on the diagonal block
-          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        // one packed fma per pair for the exponent argument, packed add + mul for dS; the
+        // causal mask only on the diagonal block
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
 #pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const int e = g * 8 + e2 * 2;
-            const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, make_float2(st_l[e2 * 2], st_l[e2 * 2 + 1]));
-            float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-            if (diag) {
-              const int qc = q0 + e2 * 2;  // query column inside the block
-              if (qc < kr) pr.x = 0.f;
-              if (qc + 1 < kr) pr.y = 0.f;
-            }
-            const float2 dd =
-                fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), make_float2(st_d[e2 * 2], st_d[e2 * 2 + 1])));
-            __nv_bfloat162 pb = __floats2bfloat162_rn(pr.x, pr.y);
-            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
-            hd[e2] = __floats2bfloat162_rn(dd.x, dd.y);
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const int e = g * 8 + e2 * 2;
+          const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, make_float2(st_l[e2 * 2], st_l[e2 * 2 + 1]));
+          float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          if (diag) {
+            const int qc = q0 + e2 * 2;  // query column inside the block
+            if (qc < kr) pr.x = 0.f;
+            if (qc + 1 < kr) pr.y = 0.f;
           }
-        } else {
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            float pv[2], dv[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int e = g * 8 + e2 * 2 + t;
-              const int qc = q0 + e2 * 2 + t;  // query column inside the block
-              const bool masked = diag && (qc < kr);
-              const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - st_l[e2 * 2 + t]);
-              pv[t] = pr;
-              dv[t] = pr * (dp[e] - st_d[e2 * 2 + t]);
-            }
-            __nv_bfloat162 pb = __floats2bfloat162_rn(pv[0], pv[1]);
-            ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
-            hd[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
-          }
+          const float2 dd =
+              fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), make_float2(st_d[e2 * 2], st_d[e2 * 2 + 1])));
+          __nv_bfloat162 pb = __floats2bfloat162_rn(pr.x, pr.y);
+          ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
+          hd[e2] = __floats2bfloat162_rn(dd.x, dd.y);
         }
         *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wd;
       }
@@ -1339,7 +862,7 @@ struct AttnDqParams {
   int* err;
 };
 
-template <int D, bool V2, bool EARLY = false, int EMU = 0>
+template <int D>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -1498,40 +1021,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         mbar_arrive(&s_empty[st]);
         mbar_arrive(dp_empty);
       }
-      if constexpr (EARLY) {
-        // dS of this block into registers first (packed bf16 pairs), so that the math overlaps
-        // the previous block's dQ MMA; then wait for it to release the dS buffer and store
-        uint32_t packed[32];
-        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-        const float2 nl = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
-#pragma unroll
-        for (int e2 = 0; e2 < 32; ++e2) {
-          const int e = e2 * 2;
-          const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nl);
-          const bool emu = (EMU > 0) && (e2 % (EMU > 0 ? EMU : 1) == (EMU > 0 ? EMU : 1) - 1);
-          float2 pr = emu ? make_float2(exp2_poly(x.x), exp2_poly(x.y)) : make_float2(fast_exp2(x.x), fast_exp2(x.y));
-          if (diag) {
-            const int key = j * KB + c0 + e;
-            if (key > qi) pr.x = 0.f;
-            if (key + 1 > qi) pr.y = 0.f;
-          }
-          const float2 dd = fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), nd));
-          __nv_bfloat162 hb = __floats2bfloat162_rn(dd.x, dd.y);
-          packed[e2] = *reinterpret_cast<uint32_t*>(&hb);
-        }
-        if (j >= 1 && !mbar_wait(ds_empty, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int g = 0; g < 8; ++g)
-          *reinterpret_cast<uint4*>(sDS + swz_offset(r, c0 + g * 8)) =
-              make_uint4(packed[g * 4], packed[g * 4 + 1], packed[g * 4 + 2], packed[g * 4 + 3]);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(ds_full);
-        continue;
-      }
       // the dS buffer must have been consumed by the previous dQ MMA
       if (j >= 1 && !mbar_wait(ds_empty, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
         ok = false;
@@ -1541,35 +1030,20 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       for (int g = 0; g < 8; ++g) {
         uint4 w;
         __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
-        if constexpr (V2) {
-          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-          const float2 nl = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nl = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
 #pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const int e = g * 8 + e2 * 2;
-            const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nl);
-            float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-            if (diag) {
-              const int key = j * KB + c0 + e;
-              if (key > qi) pr.x = 0.f;
-              if (key + 1 > qi) pr.y = 0.f;
-            }
-            const float2 dd = fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), nd));
-            hw[e2] = __floats2bfloat162_rn(dd.x, dd.y);
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const int e = g * 8 + e2 * 2;
+          const float2 x = ffma2(make_float2(sv[e], sv[e + 1]), sc2, nl);
+          float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          if (diag) {
+            const int key = j * KB + c0 + e;
+            if (key > qi) pr.x = 0.f;
+            if (key + 1 > qi) pr.y = 0.f;
           }
-        } else {
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            float dv[2];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int e = g * 8 + e2 * 2 + t;
-              const bool masked = diag && (j * KB + c0 + e > qi);
-              const float pr = masked ? 0.f : fast_exp2(sv[e] * p.scale_log2 - lse2);
-              dv[t] = pr * (dp[e] - dlt);
-            }
-            hw[e2] = __floats2bfloat162_rn(dv[0], dv[1]);
-          }
+          const float2 dd = fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), nd));
+          hw[e2] = __floats2bfloat162_rn(dd.x, dd.y);
         }
         *reinterpret_cast<uint4*>(sDS + swz_offset(r, c0 + g * 8)) = w;
       }
@@ -1676,34 +1150,29 @@ CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
   return m;
 }
 
-// 0: two query tiles per CTA with the packed-arithmetic softmax (fwd_softmax_tile_v2),
-// 1: one tile per CTA, 2: two tiles with the plain softmax (fwd_softmax_tile),
-// 3: as 0 with the whole score row held in registers (one TMEM read per key block),
-// 4: as 3 in 3 warpgroups with the registers moved to the softmax warps (attn_fwd3_kernel),
-// 5 / 6: as 0 with every 4th / 2nd pair of exponentials on the FMA pipe (exp2_poly.cuh)
+// Forward kernel: 0 (default) = the 3-warpgroup kernel (whole score rows in registers; at the
+// Llama-3-8B shape 0.1776 ms against 0.1794 ms for the 2-warpgroup kernel, 1 B200), which runs
+// only when its compiled register count is the one its register split assumes, else the
+// 2-warpgroup kernel; 1 = always the 2-warpgroup kernel.
 std::atomic<int> g_fwd_variant{0};
-// backward elementwise: 0 plain, 1 packed arithmetic (f32x2 fma/add/mul, diagonal-only mask),
-// 2 as 1 with the dK/dV kernel's two warpgroups on alternate 64-query units (ping-pong) and
-// the dQ kernel computing dS before it waits for the dS buffer, 3 as 2 with every 4th pair of
-// exponentials on the FMA pipe (exp2_poly.cuh)
-std::atomic<int> g_bwd_variant{0};
+// The backward's elementwise arithmetic is packed (f32x2 fma/add/mul, diagonal-only mask): the
+// fastest of the versions swept at the 8B shape (0.742 ms against 0.786 / 0.762 / 0.769 ms for
+// the plain, ping-pong and FMA-pipe-exponential versions, which were removed).
 
 template <int D>
 void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   static bool attr_set[64] = {false};
+  static int regs3[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    cudaFuncSetAttribute(attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_fwd2_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
-    cudaFuncSetAttribute(attn_fwd2_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
-    cudaFuncSetAttribute(attn_fwd2_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Attn2Smem<D>::BYTES);
+    cudaFuncSetAttribute(attn_fwd2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
     cudaFuncSetAttribute(attn_fwd3_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Attn2Smem<D>::BYTES);
-    cudaFuncSetAttribute(attn_fwd2_kernel<D, true, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Attn2Smem<D>::BYTES);
-    cudaFuncSetAttribute(attn_fwd2_kernel<D, true, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Attn2Smem<D>::BYTES);
+    // the register split of attn_fwd3_kernel assumes its launch allocation; an increase beyond
+    // the block's pool would wait forever, so it only runs when the compiled count matches
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, attn_fwd3_kernel<D>);
+    regs3[dev] = fa.numRegs;
     attr_set[dev] = true;
   }
   AttnParams p{};
@@ -1719,39 +1188,11 @@ void launch_fwd(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap mq = map_bthd(a.q, a.B, a.T, a.Hq, D);
   CUtensorMap mk = map_bthd(a.k, a.B, a.T, a.Hkv, D);
   CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
-  if (g_fwd_variant.load() == 1) {
-    dim3 grid(a.T / QB, a.Hq, a.B);
-    attn_fwd_kernel<D><<<grid, ATT_THREADS, AttnSmem<D>::BYTES, stream>>>(mq, mk, mv, p);
-  } else if (g_fwd_variant.load() == 2) {
-    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
-    attn_fwd2_kernel<D, false><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
-  } else if (g_fwd_variant.load() == 4) {
-    // the register split assumes the launch allocation; an increase beyond the block's pool
-    // would wait forever, so refuse to launch if the compiled kernel differs
-    static int regs[64] = {0};
-    if (!regs[dev]) {
-      cudaFuncAttributes fa{};
-      cudaFuncGetAttributes(&fa, attn_fwd3_kernel<D>);
-      regs[dev] = fa.numRegs;
-    }
-    if (regs[dev] != static_cast<int>(ATT3_REGS_LAUNCH))
-      throw std::runtime_error("mmf: attn_fwd3_kernel compiled with " + std::to_string(regs[dev]) +
-                               " registers per thread; its register split needs " + std::to_string(ATT3_REGS_LAUNCH));
-    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+  dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
+  if (g_fwd_variant.load() == 0 && regs3[dev] == static_cast<int>(ATT3_REGS_LAUNCH))
     attn_fwd3_kernel<D><<<grid, ATT3_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
-  } else if (g_fwd_variant.load() == 5) {
-    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
-    attn_fwd2_kernel<D, true, false, 4><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
-  } else if (g_fwd_variant.load() == 6) {
-    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
-    attn_fwd2_kernel<D, true, false, 2><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
-  } else if (g_fwd_variant.load() == 3) {
-    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
-    attn_fwd2_kernel<D, true, true><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
-  } else {
-    dim3 grid((a.T / QB + 1) / 2, a.Hq, a.B);
-    attn_fwd2_kernel<D, true><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
-  }
+  else
+    attn_fwd2_kernel<D><<<grid, ATT2_THREADS, Attn2Smem<D>::BYTES, stream>>>(mq, mk, mv, p);
   count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: attention launch failed: ") + cudaGetErrorString(e));
@@ -1764,18 +1205,8 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    cudaFuncSetAttribute(attn_bwd_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         BwdSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_kernel<D, true, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         BwdSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         DqSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
-    cudaFuncSetAttribute(attn_bwd_dq_kernel<D, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         DqSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem<D>::BYTES);
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, DqSmem<D>::BYTES);
     attr_set[dev] = true;
   }
   const int64_t rows = static_cast<int64_t>(a.B) * a.T * a.Hq;
@@ -1800,16 +1231,7 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   CUtensorMap mv = map_bthd(a.v, a.B, a.T, a.Hkv, D);
   CUtensorMap mdo = map_bthd(a.dout, a.B, a.T, a.Hq, D);
   dim3 grid(a.T / KB, a.Hq, a.B);
-  const int bv = g_bwd_variant.load();
-  const bool v2 = bv >= 1;
-  if (bv == 3)
-    attn_bwd_kernel<D, true, true, 4><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
-  else if (bv == 2)
-    attn_bwd_kernel<D, true, true><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
-  else if (v2)
-    attn_bwd_kernel<D, true><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
-  else
-    attn_bwd_kernel<D, false><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
+  attn_bwd_kernel<D><<<grid, BWD_THREADS, BwdSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, p);
   count_launch();
   AttnDqParams pq{};
   pq.B = a.B;
@@ -1822,17 +1244,7 @@ void launch_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
   pq.delta = a.delta;
   pq.dq = static_cast<__nv_bfloat16*>(a.dq);
   pq.err = p.err;
-  if (bv == 3)
-    attn_bwd_dq_kernel<D, true, true, 4><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(
-        mq, mk, mv, mdo, pq);
-  else if (bv == 2)
-    attn_bwd_dq_kernel<D, true, true><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(
-        mq, mk, mv, mdo, pq);
-  else if (v2)
-    attn_bwd_dq_kernel<D, true><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, pq);
-  else
-    attn_bwd_dq_kernel<D, false><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo,
-                                                                                                       pq);
+  attn_bwd_dq_kernel<D><<<dim3(a.T / QB, a.Hq, a.B), BWD_THREADS, DqSmem<D>::BYTES, stream>>>(mq, mk, mv, mdo, pq);
   count_launch();
   const int64_t rows_kv = static_cast<int64_t>(a.B) * a.T * a.Hkv;
   gqa_reduce_kernel<<<static_cast<unsigned>(std::min<int64_t>((rows_kv * D + 255) / 256, 148 * 16)), 256, 0, stream>>>(
@@ -1869,6 +1281,5 @@ void attention_bwd(const AttnBwdArgs& a, cudaStream_t stream) {
     throw std::runtime_error("mmf: attention supports head_dim 64 or 128");
 }
 void set_attention_fwd_variant(int v) { g_fwd_variant.store(v); }
-void set_attention_bwd_variant(int v) { g_bwd_variant.store(v); }
 
 }  // namespace mmf

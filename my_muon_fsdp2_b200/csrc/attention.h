@@ -15,11 +15,10 @@ struct AttnArgs {
   float scale;
 };
 void attention_fwd(const AttnArgs& a, cudaStream_t stream);
-// Forward kernel choice: 0 = two query tiles per CTA with the packed-arithmetic softmax
-// (default), 1 = one query tile per CTA, 2 = two query tiles with the plain softmax.
+// Forward kernel choice: 0 = three warpgroups, whole score rows in registers (default; falls
+// back to 1 when its compiled register count differs from the one its register split assumes),
+// 1 = two softmax warpgroups over score-row halves.  Both take two query tiles per CTA.
 void set_attention_fwd_variant(int v);
-// Backward elementwise choice: 0 = plain (default), 1 = packed f32x2 arithmetic.
-void set_attention_bwd_variant(int v);
 
 struct AttnBwdArgs {
   const void* q;

@@ -783,6 +783,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wgrad_out", &wgrad_out);
   m.def("ag_gemm", &ag_gemm);
   m.def("linear_gemm", &linear_gemm);
+  m.def("set_linear_tile_n", [](int64_t tn) { mmf::set_linear_tile_n(static_cast<int>(tn)); });
   m.def("rs_reduce", &rs_reduce);
   m.def("rs_pull_reduce", &rs_pull_reduce);
   m.def("muon_prep", &muon_prep);
@@ -805,7 +806,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_bwd", &attention_bwd);
   m.def("set_attention_fwd_variant", [](int64_t v) { mmf::set_attention_fwd_variant(static_cast<int>(v)); });
   m.def("set_ag_gemm_variant", [](int64_t v) { mmf::set_ag_gemm_variant(static_cast<int>(v)); });
-  m.def("set_attention_bwd_variant", [](int64_t v) { mmf::set_attention_bwd_variant(static_cast<int>(v)); });
   m.def("set_gemm_variant", [](int64_t v) { mmf::set_gemm_variant(static_cast<int>(v)); });
   m.def("gemm_variant", []() { return static_cast<int64_t>(mmf::gemm_variant()); });
   m.def("device_error", &device_error);

@@ -130,6 +130,8 @@ struct LinearGemmArgs {
   float rope_theta;
 };
 void linear_gemm(const LinearGemmArgs& args, cudaStream_t stream);
+// Tile width of linear_gemm: 0 = automatic (default), 128 or 256 = forced (for benchmarks).
+void set_linear_tile_n(int tn);
 
 // ----------------------------------------------------------------------------------------
 // FSDP all-gather fused with the consuming GEMM:  Y[M, N] = X[M, K] @ W^T, where W [N, K] is

@@ -30,7 +30,11 @@
 // SMs.  No TMA multicast; every wait is bounded (tc_common.cuh) and records an error code.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <atomic>
+#include <cmath>
 #include <mutex>
+#include <type_traits>
 #include <stdexcept>
 #include <string>
 
@@ -43,16 +47,24 @@ namespace mmf {
 namespace {
 
 constexpr int L_BK = 64;
-constexpr int L_STAGES = 6;
-constexpr int L_HALF = 128;  // rows of A and of B staged by each CTA of the pair
+constexpr int L_HALF = 128;  // rows of A staged by each CTA of the pair
 constexpr int L_TM = 256;    // output rows per pair tile
-constexpr int L_TN = 256;    // output columns per pair tile (MMA N)
-constexpr int L_A_BYTES = L_HALF * L_BK * 2;
-constexpr int L_B_BYTES = L_HALF * L_BK * 2;
-constexpr int L_STAGE_BYTES = L_A_BYTES + L_B_BYTES;
-constexpr int L_SMEM_BYTES = L_STAGES * L_STAGE_BYTES + 1024 + 256;
 constexpr int L_THREADS = 192;
 constexpr uint32_t L_TMEM_COLS = 512;
+
+// Tile geometry for TN output columns per pair tile (MMA N): 256 (the default) or 128 (more
+// tiles, for shapes whose 256-wide tile count leaves a mostly idle last wave).  Each CTA stages
+// 128 rows of A and TN/2 rows of B per 64-deep k-block; the ring takes as many stages as fit in
+// 192 KB of shared memory (6 for TN = 256, 8 for TN = 128).
+template <int TN>
+struct LinTile {
+  static constexpr int BH = TN / 2;
+  static constexpr int A_BYTES = L_HALF * L_BK * 2;
+  static constexpr int B_BYTES = BH * L_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
 
 struct LinMaps {
   CUtensorMap a[3];
@@ -62,6 +74,7 @@ struct LinMaps {
 struct LinDev {
   int M, N;  // output extents (rows, columns of the concatenated problem; SWIGLU: N = hidden units)
   int tiles_m, tiles_n, num_tiles, band;
+  int row_bands;     // raster: 1 = bands of `band` tile rows with columns fastest, 0 = column bands
   int axis, nseg;    // segment axis (LIN_SEG_*) and count
   int seg_tile[4];   // segment s covers tiles (K: k-blocks) [seg_tile[s], seg_tile[s+1])
   int seg_len[3];    // true rows / columns of each segment (axis M / N)
@@ -90,14 +103,20 @@ __device__ __forceinline__ int seg_of(const LinDev& p, int tile) {
 }
 
 __device__ __forceinline__ void lin_tile(const LinDev& p, int t, int& tm, int& tn) {
-  // column bands of `band` tile columns, rows fastest inside a band: the pairs running at the
-  // same time share a narrow slab of B and all of A, so B is read from DRAM about once
-  const int span = p.band * p.tiles_m;
+  // Bands of `band` tile columns with rows fastest inside a band (the pairs running at the same
+  // time share a narrow slab of B and walk all of A), or the transpose: bands of tile rows with
+  // columns fastest (they share a slab of A and walk all of B).  The host picks the order that
+  // keeps the walked operand in L2, so each operand comes from DRAM about once.
+  const int n_inner = p.row_bands ? p.tiles_n : p.tiles_m;
+  const int n_outer = p.row_bands ? p.tiles_m : p.tiles_n;
+  const int span = p.band * n_inner;
   const int bi = t / span;
   const int rr = t - bi * span;
-  const int w = min(p.band, p.tiles_n - bi * p.band);
-  tn = bi * p.band + rr % w;
-  tm = rr / w;
+  const int w = min(p.band, n_outer - bi * p.band);
+  const int outer = bi * p.band + rr % w;
+  const int inner = rr / w;
+  tm = p.row_bands ? outer : inner;
+  tn = p.row_bands ? inner : outer;
 }
 
 __device__ __forceinline__ void ld_bf16x32(const __nv_bfloat16* src, float* v, bool vec, int n) {
@@ -183,13 +202,13 @@ __device__ __forceinline__ void store_chunk(const LinDev& p, int s, int64_t r, i
   st_bf16x32(o, v, vec, n);
 }
 
-template <int EPI>
+template <int EPI, int TN>
 __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, int row_in_tile, uint32_t t_row) {
   const int grow = tm * L_TM + row_in_tile;  // row of the concatenated output
   int s = 0;
   int64_t r = grow;
   int rlim = p.M;
-  int cbase = tn * L_TN;
+  int cbase = tn * TN;
   int clim = p.N;
   if (p.axis == LIN_SEG_M) {
     s = seg_of(p, tm);
@@ -197,21 +216,21 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
     rlim = p.seg_len[s];
   } else if (p.axis == LIN_SEG_N) {
     s = seg_of(p, tn);
-    cbase = (tn - p.seg_tile[s]) * L_TN;
+    cbase = (tn - p.seg_tile[s]) * TN;
     clim = p.seg_len[s];
   }
   const bool row_ok = r < rlim;
 
   if constexpr (EPI == LIN_EPI_SWIGLU) {
-    // TMEM columns [0, 128): gate of hidden units tn*128 + c; [128, 256): up of the same units
-    const int h0 = tn * (L_TN / 2);
+    // TMEM columns [0, TN/2): gate of hidden units tn*TN/2 + c; [TN/2, TN): up of the same units
+    const int h0 = tn * (TN / 2);
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < TN / 64; ++c) {
       const int col = h0 + c * 32;
       if (col >= p.N) break;  // uniform across the warp
       float g[32], u[32];
       tmem_ld_32cols(t_row + c * 32, g);
-      tmem_ld_32cols(t_row + 128 + c * 32, u);
+      tmem_ld_32cols(t_row + TN / 2 + c * 32, u);
       if (!row_ok) continue;
       const int n = min(32, p.N - col);
       float h[32];
@@ -228,7 +247,7 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
     return;
   } else if constexpr (EPI == LIN_EPI_SWIGLU_BWD || EPI == LIN_EPI_GELU_BWD) {
 #pragma unroll 1
-    for (int c = 0; c < L_TN / 32; ++c) {
+    for (int c = 0; c < TN / 32; ++c) {
       const int col = cbase + c * 32;
       if (col >= clim) break;
       float d[32];
@@ -266,7 +285,7 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
     return;
   } else if constexpr (EPI == LIN_EPI_GELU) {
 #pragma unroll 1
-    for (int c = 0; c < L_TN / 32; ++c) {
+    for (int c = 0; c < TN / 32; ++c) {
       const int col = cbase + c * 32;
       if (col >= clim) break;
       float z[32];
@@ -296,7 +315,7 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       const int half_c = hc / 2;
       const float pos = static_cast<float>(r % p.seq_len);
 #pragma unroll 1
-      for (int a = 0; a < L_TN / 32; ++a) {
+      for (int a = 0; a < TN / 32; ++a) {
         if ((a % hc) >= half_c) continue;
         const int b = a + half_c;
         const int col_a = cbase + a * 32;
@@ -321,7 +340,7 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       return;
     }
 #pragma unroll 1
-    for (int c = 0; c < L_TN / 32; ++c) {
+    for (int c = 0; c < TN / 32; ++c) {
       const int col = cbase + c * 32;
       if (col >= clim) break;
       float v[32];
@@ -346,9 +365,12 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int TN>
 __global__ void __launch_bounds__(L_THREADS, 1)
     linear_gemm_kernel(const __grid_constant__ LinMaps maps, const LinDev p) {
+  using G = LinTile<TN>;
+  constexpr int L_STAGES = G::STAGES, L_A_BYTES = G::A_BYTES, L_B_BYTES = G::B_BYTES;
+  constexpr int L_STAGE_BYTES = G::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -411,13 +433,13 @@ __global__ void __launch_bounds__(L_THREADS, 1)
           a_row -= p.seg_tile[am] * L_TM;
         }
         // rows (K-major) or columns (MN-major) of B this CTA stages, and which B map
-        int bm = 0, b_row = tn * L_TN + static_cast<int>(rank) * L_HALF;
+        int bm = 0, b_row = tn * TN + static_cast<int>(rank) * G::BH;
         if (EPI == LIN_EPI_SWIGLU) {
           bm = static_cast<int>(rank);  // CTA 0: W1 (gate) rows, CTA 1: W3 (up) rows
-          b_row = tn * L_HALF;
+          b_row = tn * G::BH;
         } else if (p.axis == LIN_SEG_N) {
           bm = seg_of(p, tn);
-          b_row -= p.seg_tile[bm] * L_TN;
+          b_row -= p.seg_tile[bm] * TN;
         }
         int ks = 0;  // K segment
         int ks_end = (p.axis == LIN_SEG_K) ? p.seg_tile[1] : p.total_kb;
@@ -437,6 +459,12 @@ __global__ void __launch_bounds__(L_THREADS, 1)
           }
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L_STAGE_BYTES);
+          // debug builds: every innermost TMA coordinate on its 16-byte boundary and every map
+          // index inside the segment tables (a failed check records its code and skips; the
+          // bounded wait on the stage's barrier then unwinds the kernel)
+          if (!MMF_DCHECK_TMA_X(A_MN ? a_row : kl * L_BK, 2, err) || !MMF_DCHECK_TMA_X(B_MN ? b_row : kl * L_BK, 2, err) ||
+              !MMF_DCHECK(am >= 0 && am < 3 && bm >= 0 && bm < 3, err, ERR_CHECK_BOUNDS))
+            continue;
           if (A_MN) {
 #pragma unroll
             for (int c = 0; c < 2; ++c)
@@ -447,7 +475,7 @@ __global__ void __launch_bounds__(L_THREADS, 1)
           }
           if (B_MN) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+            for (int c = 0; c < G::BH / 64; ++c)
               tma_load_3d_pair(sB + stage * L_B_BYTES + c * (L_BK * 64 * 2), &maps.b[bm], fb, b_row + c * 64,
                                kl * L_BK, 0);
           } else {
@@ -463,7 +491,7 @@ __global__ void __launch_bounds__(L_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer (leader CTA only) ---------------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(L_TM, L_TN, A_MN, B_MN);
+      constexpr uint32_t idesc = idesc_bf16_f32(L_TM, TN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -475,7 +503,7 @@ __global__ void __launch_bounds__(L_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * L_TN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TN);
         for (int kb = 0; kb < p.total_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, ERR_MMA_FULL_TIMEOUT)) {
             ok = false;
@@ -519,8 +547,8 @@ __global__ void __launch_bounds__(L_THREADS, 1)
       lin_tile(p, t, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
       tc_fence_after();
-      lin_epilogue<EPI>(p, tm, tn, static_cast<int>(rank) * L_HALF + q * 32 + lane,
-                        tmem_base + static_cast<uint32_t>(acc * L_TN) + (static_cast<uint32_t>(q * 32) << 16));
+      lin_epilogue<EPI, TN>(p, tm, tn, static_cast<int>(rank) * L_HALF + q * 32 + lane,
+                            tmem_base + static_cast<uint32_t>(acc * TN) + (static_cast<uint32_t>(q * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
@@ -547,21 +575,21 @@ int num_sms(int dev) {
   return sms[dev];
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int TN>
 cudaError_t launch_lin(const LinMaps& maps, const LinDev& p, int clusters, cudaStream_t stream) {
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(linear_gemm_kernel<A_MN, B_MN, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L_SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(linear_gemm_kernel<A_MN, B_MN, EPI, TN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, LinTile<TN>::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters, 1, 1);
   cfg.blockDim = dim3(L_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = L_SMEM_BYTES;
+  cfg.dynamicSmemBytes = LinTile<TN>::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -570,14 +598,18 @@ cudaError_t launch_lin(const LinMaps& maps, const LinDev& p, int clusters, cudaS
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, linear_gemm_kernel<A_MN, B_MN, EPI>, maps, p);
+  return cudaLaunchKernelEx(&cfg, linear_gemm_kernel<A_MN, B_MN, EPI, TN>, maps, p);
 }
 
-void fail(const std::string& what) { throw std::runtime_error("mmf: linear_gemm: " + what); }
+[[noreturn]] void fail(const std::string& what) { throw std::runtime_error("mmf: linear_gemm: " + what); }
+
+std::atomic<int> g_linear_tile_n{0};  // 0 automatic, 128 or 256 forced (benchmarks)
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
 }  // namespace
+
+void set_linear_tile_n(int tn) { g_linear_tile_n.store(tn); }
 
 void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0) fail("empty output");
@@ -598,7 +630,7 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   if (epi == LIN_EPI_SWIGLU && (a.axis != LIN_SEG_N || a.nseg != 2)) fail("SWIGLU takes the two weights W1, W3");
   if (epi != LIN_EPI_STORE && epi != LIN_EPI_ROPE && (a.out_f32 || a.accumulate))
     fail("fp32 / accumulating output only with the STORE epilogue");
-  if ((a.C || a.bias) && a.nseg != 1) fail("residual / bias need one segment");
+  if ((a.C || a.bias) && a.nseg != 1 && a.axis != LIN_SEG_K) fail("residual / bias need one output segment");
   if (epi == LIN_EPI_ROPE && (a.head_dim != 64 && a.head_dim != 128)) fail("fused RoPE needs head_dim 64 or 128");
 
   int dev = 0;
@@ -635,13 +667,67 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   }
   if (a.C) p.in_vec = aligned16(a.C) && (a.ldc % 8) == 0;
 
-  // tiles along each axis, segment starts
-  int tiles_m = (a.M + L_TM - 1) / L_TM;
-  int tiles_n = (epi == LIN_EPI_SWIGLU) ? (a.N + L_HALF - 1) / L_HALF : (a.N + L_TN - 1) / L_TN;
-  p.total_kb = 0;
+  // k-blocks and K-segment starts (independent of the tile width)
+  int total_kb = 0;
+  if (a.axis == LIN_SEG_K) {
+    for (int s = 0; s < a.nseg; ++s) {
+      p.seg_tile[s] = total_kb;
+      total_kb += (a.K[s] + L_BK - 1) / L_BK;
+    }
+    p.seg_tile[a.nseg] = total_kb;
+  } else {
+    total_kb = (a.K[0] + L_BK - 1) / L_BK;
+  }
+  if (total_kb <= 0) fail("empty reduction");
+  p.total_kb = total_kb;
+  const int units = num_sms(dev) / 2;
+
+  // Tile width: 256 columns unless 128 fills the last wave of pairs clearly better (the narrow
+  // tile costs a little per tile: more shared-memory traffic per MMA).  SWIGLU keeps 256 (gate
+  // and up halves of 128 hidden units); N segments must start on tile boundaries, so every
+  // segment but the last must be a multiple of the width.
+  auto n_tiles_for = [&](int tn) {
+    if (epi == LIN_EPI_SWIGLU) return (a.N + tn / 2 - 1) / (tn / 2);
+    if (a.axis != LIN_SEG_N) return (a.N + tn - 1) / tn;
+    int t = 0;
+    for (int s = 0; s < a.nseg; ++s) t += (a.seg_len[s] + tn - 1) / tn;
+    return t;
+  };
+  const int tiles_m0 = [&] {
+    if (a.axis != LIN_SEG_M) return (a.M + L_TM - 1) / L_TM;
+    int t = 0;
+    for (int s = 0; s < a.nseg; ++s) t += (a.seg_len[s] + L_TM - 1) / L_TM;
+    return t;
+  }();
+  int TN = 256;
+  const int forced = g_linear_tile_n.load();
+  if (forced == 128 || forced == 256) {
+    TN = forced;
+  } else if (epi != LIN_EPI_SWIGLU) {
+    auto wave_eff = [&](int tn) {
+      const double tiles = static_cast<double>(tiles_m0) * n_tiles_for(tn);
+      const double waves = tiles / units;
+      return waves / std::ceil(waves);
+    };
+    if (wave_eff(128) * 0.96 > wave_eff(256)) TN = 128;
+  }
+  if (epi == LIN_EPI_SWIGLU) TN = 256;
+  if (a.axis == LIN_SEG_N && TN == 128) {
+    for (int s = 0; s + 1 < a.nseg; ++s)
+      if (a.seg_len[s] % 128) TN = 256;
+  }
+  if (a.axis == LIN_SEG_N && epi != LIN_EPI_SWIGLU) {
+    for (int s = 0; s + 1 < a.nseg; ++s)
+      if (a.seg_len[s] % TN) fail("column segments must be multiples of the tile width (all but the last)");
+  }
+  if (epi == LIN_EPI_ROPE && (TN % a.head_dim)) TN = 256;
+
+  // tiles along each axis, row / column segment starts
+  int tiles_m = tiles_m0;
+  int tiles_n = n_tiles_for(TN);
   if (a.axis == LIN_SEG_M || a.axis == LIN_SEG_N) {
     int acc = 0;
-    const int unit = (a.axis == LIN_SEG_M) ? L_TM : L_TN;
+    const int unit = (a.axis == LIN_SEG_M) ? L_TM : TN;
     for (int s = 0; s < a.nseg; ++s) {
       p.seg_tile[s] = acc;
       p.seg_len[s] = a.seg_len[s];
@@ -653,33 +739,31 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
       p.seg_len[0] = p.seg_len[1] = a.N;
     }
     p.seg_tile[a.nseg] = acc;
-    if (a.axis == LIN_SEG_M) tiles_m = acc;
-    else tiles_n = acc;
-    p.total_kb = (a.K[0] + L_BK - 1) / L_BK;
-  } else if (a.axis == LIN_SEG_K) {
-    int acc = 0;
-    for (int s = 0; s < a.nseg; ++s) {
-      p.seg_tile[s] = acc;
-      acc += (a.K[s] + L_BK - 1) / L_BK;
-    }
-    p.seg_tile[a.nseg] = acc;
-    p.total_kb = acc;
-  } else {
+  } else if (a.axis != LIN_SEG_K) {
     p.seg_tile[0] = 0;
     p.seg_tile[1] = 1 << 30;
-    p.total_kb = (a.K[0] + L_BK - 1) / L_BK;
   }
-  if (p.total_kb <= 0) fail("empty reduction");
   p.tiles_m = tiles_m;
   p.tiles_n = tiles_n;
   p.num_tiles = tiles_m * tiles_n;
-  const int units = num_sms(dev) / 2;
   {
-    int band = (units + tiles_m - 1) / tiles_m;
-    p.band = band < 1 ? 1 : (band > tiles_n ? tiles_n : band);
+    // Operand bytes walked per band: column bands re-read A (all rows) once per band, row bands
+    // re-read B.  An operand that fits in half the L2 is read from DRAM once either way.
+    auto ceil_div = [](int64_t x, int64_t y) { return (x + y - 1) / y; };
+    const int64_t kbytes = static_cast<int64_t>(p.total_kb) * L_BK * 2;
+    const int64_t a_bytes = static_cast<int64_t>(tiles_m) * L_TM * kbytes;
+    const int64_t b_bytes = static_cast<int64_t>(tiles_n) * TN * kbytes;
+    const int64_t l2_half = 60ll << 20;
+    const int band_c = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles_n, ceil_div(units, tiles_m))));
+    const int band_r = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles_m, ceil_div(units, tiles_n))));
+    const int64_t cost_c = (a_bytes <= l2_half ? a_bytes : a_bytes * ceil_div(tiles_n, band_c)) + b_bytes;
+    const int64_t cost_r = (b_bytes <= l2_half ? b_bytes : b_bytes * ceil_div(tiles_m, band_r)) + a_bytes;
+    p.row_bands = cost_r < cost_c ? 1 : 0;
+    p.band = p.row_bands ? band_r : band_c;
   }
 
-  // tensor maps: K-major operands [rows, K] with 64 x 128 boxes; MN-major [K, cols] with 64 x 64
+  // tensor maps: K-major operands [rows, K] with 64-wide boxes of 128 (A) or TN/2 (B) rows;
+  // MN-major [K, cols] with 64 x 64 boxes
   LinMaps maps;
   const int na = (a.axis == LIN_SEG_M || a.axis == LIN_SEG_K) ? a.nseg : 1;
   const int nb = (a.axis == LIN_SEG_N || a.axis == LIN_SEG_K) ? a.nseg : 1;
@@ -691,30 +775,34 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
     maps.a[s] = a.a_mn ? make_map_bf16_3d(a.A[sa], a.a_inner[sa], a.a_outer[sa], 1, 64, L_BK)
                        : make_map_bf16_3d(a.A[sa], a.a_inner[sa], a.a_outer[sa], 1, L_BK, L_HALF);
     maps.b[s] = a.b_mn ? make_map_bf16_3d(a.B[sb], a.b_inner[sb], a.b_outer[sb], 1, 64, L_BK)
-                       : make_map_bf16_3d(a.B[sb], a.b_inner[sb], a.b_outer[sb], 1, L_BK, L_HALF);
+                       : make_map_bf16_3d(a.B[sb], a.b_inner[sb], a.b_outer[sb], 1, L_BK, TN / 2);
   }
 
   const int clusters = p.num_tiles < units ? p.num_tiles : units;
   cudaError_t e = cudaSuccess;
-  if (fwd_kind) {
-    switch (epi) {
-      case LIN_EPI_STORE: e = launch_lin<false, false, LIN_EPI_STORE>(maps, p, clusters, stream); break;
-      case LIN_EPI_ROPE: e = launch_lin<false, false, LIN_EPI_ROPE>(maps, p, clusters, stream); break;
-      case LIN_EPI_SWIGLU: e = launch_lin<false, false, LIN_EPI_SWIGLU>(maps, p, clusters, stream); break;
-      case LIN_EPI_GELU: e = launch_lin<false, false, LIN_EPI_GELU>(maps, p, clusters, stream); break;
-      default: fail("epilogue not available for the forward GEMM");
+  auto go = [&](auto tn_tag) {
+    constexpr int W = decltype(tn_tag)::value;
+    if (fwd_kind) {
+      switch (epi) {
+        case LIN_EPI_STORE: return launch_lin<false, false, LIN_EPI_STORE, W>(maps, p, clusters, stream);
+        case LIN_EPI_ROPE: return launch_lin<false, false, LIN_EPI_ROPE, W>(maps, p, clusters, stream);
+        case LIN_EPI_SWIGLU: return launch_lin<false, false, LIN_EPI_SWIGLU, 256>(maps, p, clusters, stream);
+        case LIN_EPI_GELU: return launch_lin<false, false, LIN_EPI_GELU, W>(maps, p, clusters, stream);
+        default: fail("epilogue not available for the forward GEMM");
+      }
+    } else if (dx_kind) {
+      switch (epi) {
+        case LIN_EPI_STORE: return launch_lin<false, true, LIN_EPI_STORE, W>(maps, p, clusters, stream);
+        case LIN_EPI_SWIGLU_BWD: return launch_lin<false, true, LIN_EPI_SWIGLU_BWD, W>(maps, p, clusters, stream);
+        case LIN_EPI_GELU_BWD: return launch_lin<false, true, LIN_EPI_GELU_BWD, W>(maps, p, clusters, stream);
+        default: fail("epilogue not available for the input-gradient GEMM");
+      }
+    } else if (epi != LIN_EPI_STORE) {
+      fail("the weight-gradient GEMM takes the STORE epilogue");
     }
-  } else if (dx_kind) {
-    switch (epi) {
-      case LIN_EPI_STORE: e = launch_lin<false, true, LIN_EPI_STORE>(maps, p, clusters, stream); break;
-      case LIN_EPI_SWIGLU_BWD: e = launch_lin<false, true, LIN_EPI_SWIGLU_BWD>(maps, p, clusters, stream); break;
-      case LIN_EPI_GELU_BWD: e = launch_lin<false, true, LIN_EPI_GELU_BWD>(maps, p, clusters, stream); break;
-      default: fail("epilogue not available for the input-gradient GEMM");
-    }
-  } else {
-    if (epi != LIN_EPI_STORE) fail("the weight-gradient GEMM takes the STORE epilogue");
-    e = launch_lin<true, true, LIN_EPI_STORE>(maps, p, clusters, stream);
-  }
+    return launch_lin<true, true, LIN_EPI_STORE, W>(maps, p, clusters, stream);
+  };
+  e = (TN == 128) ? go(std::integral_constant<int, 128>{}) : go(std::integral_constant<int, 256>{});
   count_launch();
   if (e != cudaSuccess) fail(std::string("launch failed: ") + cudaGetErrorString(e));
 }

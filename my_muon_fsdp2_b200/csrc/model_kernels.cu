@@ -133,7 +133,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
   for (int c = threadIdx.x; c < cols; c += blockDim.x) dw_part[static_cast<int64_t>(blockIdx.x) * cols + c] = dw_acc[c];
 }
 
-// Vector variant of the backward (cols % 8 == 0 and cols <= 256 * 8 * RV).
+// Vector variant of the backward (cols % 8 == 0 and cols <= 256 * 8 * RV).  Each block walks its
+// rows with the next row's dy and x loaded before the current row's block reduction, so that the
+// DRAM latency of one row overlaps the reduction and the stores of the previous one.
 template <int RV>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(const __nv_bfloat16* __restrict__ dy,
                                                               const __nv_bfloat16* __restrict__ x,
@@ -150,21 +152,35 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(const __nv_bfloat1
     for (int e = 0; e < 8; ++e) acc[k][e] = 0.f;
     if (c < cols) ld_bf8(w + c, wv[k]);
   }
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+  float g[RV][8], xv[RV][8];  // current row
+  float gn[RV][8], xn[RV][8];  // next row (prefetched)
+  auto load_row = [&](int r, float (*gd)[8], float (*xd)[8]) {
+    const int64_t off = static_cast<int64_t>(r) * cols;
+#pragma unroll
+    for (int k = 0; k < RV; ++k) {
+      const int c = (threadIdx.x + 256 * k) * 8;
+      if (c < cols) {
+        ld_bf8(dy + off + c, gd[k]);
+        ld_bf8(x + off + c, xd[k]);
+      }
+    }
+  };
+  int r = blockIdx.x;
+  if (r < rows) load_row(r, g, xv);
+  for (; r < rows; r += gridDim.x) {
     const int64_t off = static_cast<int64_t>(r) * cols;
     const float rs = rstd[r];
-    float g[RV][8], xv[RV][8];
     float dot = 0.f;
 #pragma unroll
     for (int k = 0; k < RV; ++k) {
       const int c = (threadIdx.x + 256 * k) * 8;
       if (c < cols) {
-        ld_bf8(dy + off + c, g[k]);
-        ld_bf8(x + off + c, xv[k]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) dot = fmaf(g[k][e] * wv[k][e], xv[k][e], dot);
       }
     }
+    const int rn = r + gridDim.x;
+    if (rn < rows) load_row(rn, gn, xn);  // in flight during the reduction below
     dot = block_allsum(dot, red);
     const float k3 = dot * rs * rs * rs / cols;
 #pragma unroll
@@ -180,6 +196,13 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_vec_kernel(const __nv_bfloat1
         st_bf8(dx + off + c, o);
       }
     }
+#pragma unroll
+    for (int k = 0; k < RV; ++k)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        g[k][e] = gn[k][e];
+        xv[k][e] = xn[k][e];
+      }
   }
 #pragma unroll
   for (int k = 0; k < RV; ++k) {
@@ -510,9 +533,15 @@ void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd
                  int rows, int cols, int partial_rows, cudaStream_t stream) {
   if (rows <= 0) return;
   if ((cols % 8 == 0) && cols <= 256 * 8 * 4 && aligned16(dy) && aligned16(x) && aligned16(w) && aligned16(dx)) {
-    rmsnorm_bwd_vec_kernel<4><<<partial_rows, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
-        static_cast<const __nv_bfloat16*>(w), rstd, static_cast<__nv_bfloat16*>(dx), dw_partial, rows, cols);
+    auto go = [&](auto kern) {
+      kern<<<partial_rows, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
+                                             static_cast<const __nv_bfloat16*>(w), rstd, static_cast<__nv_bfloat16*>(dx),
+                                             dw_partial, rows, cols);
+    };
+    if (cols <= 256 * 8 * 2)
+      go(rmsnorm_bwd_vec_kernel<2>);
+    else
+      go(rmsnorm_bwd_vec_kernel<4>);
     check_launch("rmsnorm_bwd");
     return;
   }

@@ -2,8 +2,9 @@
 
 Same architecture and configs as the reference example (``examples/train_gpt.py:49-268``:
 small 768/12/12, medium 1024/24/16, large 1280/36/20, vocab 50257, ctx 1024), with the naive
-O(T^2) masked attention replaced by causal flash attention, LayerNorm / GELU on this library's
-kernels and the tied head fused with the cross entropy.  ``configure_fsdp`` shards every block
+O(T^2) masked attention replaced by causal flash attention, the linears on this library's
+grouped tcgen05 GEMM (GELU, biases and residual adds in its epilogues), LayerNorm on its kernels
+and the tied head fused with the cross entropy.  ``configure_fsdp`` shards every block
 *and* the root (the reference leaves the root unsharded, train_gpt.py:265-268).
 """
 from __future__ import annotations
@@ -14,6 +15,7 @@ from typing import Optional
 import torch
 import torch.nn as nn
 
+from ..ops.linear import gelu_mlp, linear
 from ..ops.model_ops import causal_attention, fused_linear_cross_entropy, gelu, layer_norm
 
 
@@ -62,14 +64,19 @@ class CausalSelfAttention(nn.Module):
         self.c_proj = nn.Linear(cfg.n_embd, cfg.n_embd)
         self.resid_dropout = nn.Dropout(cfg.resid_pdrop)
 
-    def forward(self, x):
+    def forward(self, x, residual: Optional[torch.Tensor] = None):
+        """c_proj(attention(c_attn(x))) (+ residual: added in c_proj's GEMM epilogue when the
+        dropout between them is inactive)."""
         B, T, C = x.shape
-        q, k, v = self.c_attn(x).split(C, dim=2)
+        q, k, v = linear(x, self.c_attn).split(C, dim=2)
         q = q.reshape(B, T, self.n_head, self.head_dim)
         k = k.reshape(B, T, self.n_head, self.head_dim)
         v = v.reshape(B, T, self.n_head, self.head_dim)
         y = causal_attention(q, k, v).reshape(B, T, C)
-        return self.resid_dropout(self.c_proj(y))
+        if self.training and self.resid_dropout.p > 0:
+            y = self.resid_dropout(linear(y, self.c_proj))
+            return y if residual is None else residual + y
+        return linear(y, self.c_proj, residual)
 
 
 class MLP(nn.Module):
@@ -79,8 +86,12 @@ class MLP(nn.Module):
         self.c_proj = nn.Linear(4 * cfg.n_embd, cfg.n_embd)
         self.dropout = nn.Dropout(cfg.resid_pdrop)
 
-    def forward(self, x):
-        return self.dropout(self.c_proj(gelu(self.c_fc(x))))
+    def forward(self, x, residual: Optional[torch.Tensor] = None):
+        """c_proj(gelu(c_fc(x))) (+ residual), GELU and its derivative in the GEMM epilogues."""
+        if self.training and self.dropout.p > 0:
+            y = self.dropout(self.c_proj(gelu(self.c_fc(x))))
+            return y if residual is None else residual + y
+        return gelu_mlp(x, self.c_fc, self.c_proj, residual)
 
 
 class Block(nn.Module):
@@ -92,8 +103,8 @@ class Block(nn.Module):
         self.mlp = MLP(cfg)
 
     def forward(self, x):
-        x = x + self.attn(self.ln_1(x))
-        return x + self.mlp(self.ln_2(x))
+        x = self.attn(self.ln_1(x), residual=x)
+        return self.mlp(self.ln_2(x), residual=x)
 
 
 class GPTModel(nn.Module):

@@ -139,7 +139,7 @@ class Llama(nn.Module):
             x = layer(x)
         x = self.norm(x)
         if targets is None:
-            return self.output(x)
+            return linear(x, self.output)
         return fused_linear_cross_entropy(x, self.output.weight, targets)
 
     def muon_param_names(self):

@@ -101,9 +101,12 @@ class _Source:
         """The products through the controller's own forward (fused all-gather GEMM)."""
         return [self.ctl.linear_forward(i, x2) for i in self.idxs]
 
-    def weight_grads(self, dys, x2, need) -> Tuple[Optional[torch.Tensor], ...]:
+    def weight_grads(self, dys, x2, need, sel: Optional[Sequence[int]] = None) -> Tuple[Optional[torch.Tensor], ...]:
+        """Gradients of the weights at positions ``sel`` of this source (default: all) from their
+        output gradients ``dys`` and the shared input ``x2``."""
         if self.ctl is not None:
-            self.ctl.accumulate_grads(self.idxs, list(dys), x2)
+            sel = range(len(self.idxs)) if sel is None else sel
+            self.ctl.accumulate_grads([self.idxs[k] for k in sel], list(dys), x2)
             return (None,) * len(dys)
         if not any(need):
             return (None,) * len(dys)
@@ -205,9 +208,9 @@ class _SwiGLUFFNFn(torch.autograd.Function):
         # dH = dY W2 never leaves the tensor memory: the epilogue writes dg and du
         gemm([dy], [W2], False, True, [dg, du], EPI_SWIGLU_BWD, aux0=g, aux1=u)
         need = ctx.needs_input_grad
-        gw2 = src.weight_grads([dy], h, need[5:6])
+        gw2 = src.weight_grads([dy], h, need[5:6], sel=(2,))
         dx = mm_dx([dg, du], [W1, W3]) if need[0] else None
-        gw13 = src.weight_grads([dg, du], x2, need[3:5])
+        gw13 = src.weight_grads([dg, du], x2, need[3:5], sel=(0, 1))
         return (dx, dy if ctx.has_res else None, None) + gw13 + gw2
 
 
@@ -305,9 +308,9 @@ class _GeluMLPFn(torch.autograd.Function):
         gemm([dy], [W2], False, True, [dz], EPI_GELU_BWD, aux0=z)
         db2 = dy.sum(0) if ctx.has_b2 and need[3] else None
         db1 = dz.sum(0) if ctx.has_b1 and need[2] else None
-        (gw2,) = src.weight_grads([dy], a, need[6:7])
+        (gw2,) = src.weight_grads([dy], a, need[6:7], sel=(1,))
         dx = mm_dx([dz], [W1]) if need[0] else None
-        (gw1,) = src.weight_grads([dz], x2, need[5:6])
+        (gw1,) = src.weight_grads([dz], x2, need[5:6], sel=(0,))
         return dx, (dy if ctx.has_res else None), db1, db2, None, gw1, gw2
 
 

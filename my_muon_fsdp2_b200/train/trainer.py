@@ -19,7 +19,7 @@ from ..utils.tracing import nvtx_range
 class Trainer:
     def __init__(self, model: nn.Module, optimizers: Sequence, grad_accum: int = 1, device=None,
                  step_timer=None, max_grad_norm: Optional[float] = None, time_steps: bool = False,
-                 keep_gathered: bool = False):
+                 keep_gathered: bool = False, time_phases: bool = False):
         """``max_grad_norm``: clip the global gradient norm before the optimizer steps, as the
         reference trainers do with 1.0 (examples/train_gpt.py:367-371); None disables it.
         ``time_steps``: bracket every step with CUDA events (read by ``last_step_ms`` and
@@ -28,7 +28,10 @@ class Trainer:
         micro-batch, so the next micro-batch's forward needs no all-gather (FSDP2's
         ``set_reshard_after_backward``; the root module then gathers once per step) at the cost
         of holding the gathered parameters through the accumulation; the last micro-batch
-        reshards as usual."""
+        reshards as usual.
+        ``time_phases``: CUDA events between the phases of every step (each micro-batch's
+        forward and backward, gradient clipping, the optimizer step); ``phase_ms()`` reads the
+        last step's durations.  Events add no work and no synchronisation inside the step."""
         self.model = model
         self.max_grad_norm = max_grad_norm
         self.last_grad_norm: Optional[torch.Tensor] = None
@@ -42,6 +45,8 @@ class Trainer:
         self.keep_gathered = bool(keep_gathered) and self.fsdp and self.grad_accum > 1
         self.time_steps = bool(time_steps) and self.device.type == "cuda"
         self._step_events = None
+        self.time_phases = bool(time_phases) and self.device.type == "cuda"
+        self._phase_marks: list = []
         self._prev_comm: Optional[dict] = None
         ctl = getattr(model, "_symm_fsdp", None)  # fused-collective linears: regather after each step
         if ctl is not None:
@@ -59,9 +64,28 @@ class Trainer:
         t = tokens[i]
         with nvtx_range(f"trainer/micro_batch_{i}/forward"):
             loss = self.model(t[:, :-1], t[:, 1:]) / self.grad_accum
+        self._mark(f"forward_{i}")
         with nvtx_range(f"trainer/micro_batch_{i}/backward"):
             loss.backward()
+        self._mark(f"backward_{i}")
         return loss
+
+    def _mark(self, name: str) -> None:
+        if self.time_phases:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._phase_marks.append((name, ev))
+
+    def phase_ms(self) -> dict:
+        """Device time of each phase of the last step (waits for it); {} unless ``time_phases``.
+        The backward phases include the weight-gradient collectives joined at their end."""
+        if len(self._phase_marks) < 2:
+            return {}
+        self._phase_marks[-1][1].synchronize()
+        out = {}
+        for (_, a), (name, b) in zip(self._phase_marks[:-1], self._phase_marks[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
 
     def step_on_device(self, tokens: torch.Tensor) -> torch.Tensor:
         """One optimizer step on a device batch [grad_accum, micro_bs, seq+1]; returns the loss
@@ -69,6 +93,8 @@ class Trainer:
         if self.time_steps:
             t0 = torch.cuda.Event(enable_timing=True)
             t0.record()
+        self._phase_marks = []
+        self._mark("start")
         total = None
         for i in range(self.grad_accum):
             l = self._micro(tokens, i).detach()
@@ -76,6 +102,7 @@ class Trainer:
         if self.max_grad_norm is not None:
             params = [p for p in self.model.parameters() if p.grad is not None]
             self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.max_grad_norm)
+            self._mark("grad_clip")
         if self.step_timer is not None:
             self.step_timer.start()
         with nvtx_range("trainer/optimizer_step"):
@@ -83,6 +110,7 @@ class Trainer:
                 opt.step()
         if self.step_timer is not None:
             self.step_timer.stop()
+        self._mark("optimizer")
         for opt in self.optimizers:
             opt.zero_grad(set_to_none=True)
         if self.time_steps:

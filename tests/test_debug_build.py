@@ -12,7 +12,7 @@ CSRC = os.path.join(os.path.dirname(HERE), "my_muon_fsdp2_b200", "csrc")
 
 
 @pytest.mark.skipif(shutil.which("nvcc") is None, reason="needs nvcc")
-@pytest.mark.parametrize("src", ["tc_gemm.cu"])
+@pytest.mark.parametrize("src", ["tc_gemm.cu", "linear_gemm.cu"])
 def test_device_checks_build_compiles(src, tmp_path):
     from torch.utils.cpp_extension import include_paths
 

@@ -40,6 +40,18 @@ def test_fused_allgather_gemm_and_reduce_scatter():
             assert v < 1e-2, f"{k}: relative error {v}"
 
 
+def test_symm_fsdp_one_rank_training_matches_fsdp2():
+    """One rank: SymmFSDP's weight sources and grouped gradient GEMMs (q|k|v, w1|w3 partial sums
+    into the gradient shards) against FSDP2's autograd-returned gradients, same fused kernels."""
+    with tempfile.TemporaryDirectory() as d:
+        res = _run(1, "train", os.path.join(d, "t1.pt"))
+    a, b = res["symm"], res["fsdp2"]
+    for x, y in zip(a["losses"], b["losses"]):
+        assert abs(x - y) < 2e-2 * abs(y), (a["losses"], b["losses"])
+    for n in b["params"]:
+        assert rel_err(a["params"][n], b["params"][n]) < 2e-2, n
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_symm_fsdp_training_matches_fsdp2():
     with tempfile.TemporaryDirectory() as d:
