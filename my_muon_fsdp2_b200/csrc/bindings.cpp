@@ -317,6 +317,47 @@ void linear_gemm(std::vector<Tensor> A, std::vector<Tensor> B, bool a_mn, bool b
   mmf::linear_gemm(a, cur_stream());
 }
 
+// GEMM -> reduce-scatter, first half: dW = dY^T X (+ C, an unsharded gradient accumulator),
+// row r stored to owner_ptrs[r / rows_per_owner] + ((r % rows_per_owner) * K + col) elements
+// (owner_ptrs: device int64 table, e.g. this rank's sub-slot in every owner's receive buffer).
+void wgrad_scatter(Tensor dY, Tensor X, Tensor owner_ptrs, int64_t rows_per_owner, c10::optional<Tensor> C) {
+  check_bf16_contig(dY, "dY");
+  check_bf16_contig(X, "X");
+  check_cuda(owner_ptrs, "owner_ptrs");
+  TORCH_CHECK(dY.dim() == 2 && X.dim() == 2 && dY.size(0) == X.size(0), "mmf: wgrad_scatter needs dY [T, N], X [T, K]");
+  TORCH_CHECK(owner_ptrs.scalar_type() == torch::kInt64 && owner_ptrs.is_contiguous(), "mmf: owner_ptrs must be int64");
+  TORCH_CHECK(rows_per_owner >= 1 && owner_ptrs.numel() * rows_per_owner >= dY.size(1),
+              "mmf: the owner table does not cover every output row");
+  const c10::cuda::CUDAGuard guard(dY.device());
+  mmf::LinearGemmArgs a{};
+  a.a_mn = true;
+  a.b_mn = true;
+  a.epilogue = mmf::LIN_EPI_SCATTER;
+  a.alpha = 1.f;
+  a.axis = mmf::LIN_SEG_NONE;
+  a.nseg = 1;
+  a.A[0] = dY.data_ptr();
+  a.a_outer[0] = dY.size(0);
+  a.a_inner[0] = dY.size(1);
+  a.B[0] = X.data_ptr();
+  a.b_outer[0] = X.size(0);
+  a.b_inner[0] = X.size(1);
+  a.K[0] = static_cast<int>(dY.size(0));
+  a.M = static_cast<int>(dY.size(1));
+  a.N = static_cast<int>(X.size(1));
+  a.ldo[0] = X.size(1);
+  if (C.has_value()) {
+    check_bf16_contig(*C, "C");
+    TORCH_CHECK(C->dim() == 2 && C->size(0) == a.M && C->size(1) == a.N, "mmf: C must be [N, K]");
+    a.C = C->data_ptr();
+    a.ldc = a.N;
+  }
+  a.scatter_ptrs = owner_ptrs.data_ptr<int64_t>();
+  a.scatter_nseg = static_cast<int>(owner_ptrs.numel());
+  a.scatter_rows = rows_per_owner;
+  mmf::linear_gemm(a, cur_stream());
+}
+
 // Y = X @ W^T with W row-sharded over the group (shard_ptrs: every rank's shard address in this
 // process's address space); also assembles the full W into G.  ready: int32 [N / 128] scratch.
 Tensor ag_gemm(Tensor X, std::vector<int64_t> shard_ptrs, int64_t rank, Tensor G, Tensor ready, double wait_s) {
@@ -570,6 +611,40 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
   return {dx, dw};
 }
 
+// out[..., :] = table[tokens[...]]   (table [V, D] bf16, tokens int64)
+Tensor embedding_fwd(Tensor table, Tensor tokens) {
+  check_bf16_contig(table, "table");
+  check_cuda(tokens, "tokens");
+  TORCH_CHECK(table.dim() == 2 && tokens.scalar_type() == torch::kInt64, "mmf: embedding takes a [V, D] table, int64 tokens");
+  const c10::cuda::CUDAGuard guard(table.device());
+  Tensor tok = tokens.contiguous();
+  auto shape = tok.sizes().vec();
+  shape.push_back(table.size(1));
+  Tensor out = torch::empty(shape, table.options());
+  mmf::embedding_fwd(table.data_ptr(), tok.data_ptr<int64_t>(), out.data_ptr(), tok.numel(),
+                     static_cast<int>(table.size(1)), table.size(0), cur_stream());
+  return out;
+}
+
+// Dense gradient of the table: row v = sum of dy over the positions whose token is v (fp32, in
+// a fixed order), zeros elsewhere.  The token sort is a library sort of the (small) token list.
+Tensor embedding_bwd(Tensor dy, Tensor tokens, int64_t vocab) {
+  check_bf16_contig(dy, "dy");
+  check_cuda(tokens, "tokens");
+  const c10::cuda::CUDAGuard guard(dy.device());
+  const int64_t D = dy.size(-1);
+  Tensor tok = tokens.reshape({-1});
+  TORCH_CHECK(tok.numel() * D == dy.numel(), "mmf: embedding_bwd: dy must be [..., D] over the tokens");
+  auto sorted = torch::sort(tok, /*stable=*/true, /*dim=*/0, /*descending=*/false);
+  Tensor s_tok = std::get<0>(sorted).contiguous();
+  Tensor perm = std::get<1>(sorted).contiguous();
+  Tensor first = torch::empty({vocab}, dy.options().dtype(torch::kInt32));
+  Tensor dtable = torch::empty({vocab, D}, dy.options());
+  mmf::embedding_bwd(dy.data_ptr(), s_tok.data_ptr<int64_t>(), perm.data_ptr<int64_t>(), first.data_ptr<int>(),
+                     dtable.data_ptr(), tok.numel(), vocab, static_cast<int>(D), cur_stream());
+  return dtable;
+}
+
 std::vector<Tensor> layernorm_fwd(Tensor x, Tensor w, c10::optional<Tensor> b, double eps) {
   check_bf16_contig(x, "x");
   check_bf16_contig(w, "w");
@@ -783,7 +858,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wgrad_out", &wgrad_out);
   m.def("ag_gemm", &ag_gemm);
   m.def("linear_gemm", &linear_gemm);
-  m.def("set_linear_tile_n", [](int64_t tn) { mmf::set_linear_tile_n(static_cast<int>(tn)); });
+  m.def("wgrad_scatter", &wgrad_scatter);
   m.def("rs_reduce", &rs_reduce);
   m.def("rs_pull_reduce", &rs_pull_reduce);
   m.def("muon_prep", &muon_prep);
@@ -793,6 +868,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
   m.def("layernorm_bwd", &layernorm_bwd);
   m.def("rope_", &rope_);
   m.def("swiglu_fwd", &swiglu_fwd);

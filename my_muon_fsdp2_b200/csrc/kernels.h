@@ -103,6 +103,7 @@ enum LinEpilogue : int {
   LIN_EPI_SWIGLU_BWD = 3,
   LIN_EPI_GELU = 4,
   LIN_EPI_GELU_BWD = 5,
+  LIN_EPI_SCATTER = 6,
 };
 struct LinearGemmArgs {
   int M, N;       // output rows and columns (SWIGLU: N = hidden units; LIN_SEG_M/N: the sum of seg_len)
@@ -128,10 +129,14 @@ struct LinearGemmArgs {
   int rope_mask;     // ROPE: bit s set -> rotate the heads of segment s
   int seq_len, head_dim;
   float rope_theta;
+  // SCATTER (weight gradient, bf16): output row r goes to scatter_ptrs[r / scatter_rows] +
+  // ((r % scatter_rows) * ldo[0] + col) elements (device table of nseg owner addresses, e.g. this
+  // rank's sub-slot in every owner's receive buffer, peer-mapped); + C when given.
+  const int64_t* scatter_ptrs;
+  int scatter_nseg;
+  int64_t scatter_rows;
 };
 void linear_gemm(const LinearGemmArgs& args, cudaStream_t stream);
-// Tile width of linear_gemm: 0 = automatic (default), 128 or 256 = forced (for benchmarks).
-void set_linear_tile_n(int tn);
 
 // ----------------------------------------------------------------------------------------
 // FSDP all-gather fused with the consuming GEMM:  Y[M, N] = X[M, K] @ W^T, where W [N, K] is
@@ -265,6 +270,13 @@ void swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate,
                 cudaStream_t stream);
 void gelu_fwd(const void* x, void* y, int64_t n, cudaStream_t stream);
 void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t stream);
+// Embedding rows (bf16, D % 8 == 0): out[t] = table[tokens[t]] (a token outside the table gives
+// zeros and records ERR_BAD_ARGUMENT).  Backward: the dense table gradient in one pass from the
+// sorted tokens and their permutation; `first` is int32 scratch of vocab entries.
+void embedding_fwd(const void* table, const int64_t* tokens, void* out, int64_t n_tokens, int D, int64_t vocab,
+                   cudaStream_t stream);
+void embedding_bwd(const void* dy, const int64_t* sorted, const int64_t* perm, int* first, void* dtable,
+                   int64_t n_tokens, int64_t vocab, int D, cudaStream_t stream);
 // Softmax cross entropy over bf16 logits rows; writes per-row loss (fp32) and, when
 // grad_scale != 0, overwrites logits with d(loss_sum*grad_scale)/dlogits (bf16).
 void cross_entropy_fwd_bwd(void* logits, const int64_t* targets, float* loss_rows, int rows, int vocab,

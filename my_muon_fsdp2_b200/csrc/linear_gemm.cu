@@ -23,6 +23,10 @@
 //   SWIGLU_BWD  dH = dY W2 in TMEM; reads g, u; writes dg = dh u s (1 + g (1 - s)), du = dh g s
 //   GELU        z = acc + bias; writes gelu(z) (erf form) and z
 //   GELU_BWD    dA = dY Wproj in TMEM; reads z; writes dz = da (Phi(z) + z phi(z))
+//   SCATTER     weight gradient (+ C) stored straight into each row's owner (GEMM -> reduce-
+//               scatter): every warp stages 32 rows x 64 columns in shared memory (XOR-swizzled)
+//               and stores whole 128-byte row segments, four rows per instruction, to the owner
+//               addresses (peer-mapped receive slots over NVLink)
 //
 // Warp roles per CTA (192 threads): warp 0 TMA producer, warp 1 TMEM allocator and (leader CTA)
 // MMA issuer, warps 2..5 epilogue.  6-stage ring of 32 KB per CTA, 2 x 256 TMEM columns so the
@@ -52,10 +56,9 @@ constexpr int L_TM = 256;    // output rows per pair tile
 constexpr int L_THREADS = 192;
 constexpr uint32_t L_TMEM_COLS = 512;
 
-// Tile geometry for TN output columns per pair tile (MMA N): 256 (the default) or 128 (more
-// tiles, for shapes whose 256-wide tile count leaves a mostly idle last wave).  Each CTA stages
-// 128 rows of A and TN/2 rows of B per 64-deep k-block; the ring takes as many stages as fit in
-// 192 KB of shared memory (6 for TN = 256, 8 for TN = 128).
+// Tile geometry for TN output columns per pair tile (MMA N, 256).  Each CTA stages 128 rows of
+// A and TN/2 rows of B per 64-deep k-block; the ring takes as many stages as fit in 192 KB of
+// shared memory (6).
 template <int TN>
 struct LinTile {
   static constexpr int BH = TN / 2;
@@ -64,7 +67,13 @@ struct LinTile {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int STAGING_BYTES = 4 * 32 * 128;  // SCATTER: 32 rows x 64 bf16 per epilogue warp
 };
+template <int TN, int EPI>
+constexpr int lin_smem_bytes() {
+  // SCATTER: 1 KB reserved after the barriers, then the 1 KB-aligned staging
+  return LinTile<TN>::SMEM_BYTES + (EPI == LIN_EPI_SCATTER ? 1024 + LinTile<TN>::STAGING_BYTES : 0);
+}
 
 struct LinMaps {
   CUtensorMap a[3];
@@ -93,6 +102,9 @@ struct LinDev {
   const __nv_bfloat16* bias;
   int rope_mask, seq_len, head_dim;
   float log2_theta;
+  const int64_t* scatter_ptrs;
+  int scatter_nseg;
+  int64_t scatter_rows;
   int* err;
 };
 
@@ -203,7 +215,8 @@ __device__ __forceinline__ void store_chunk(const LinDev& p, int s, int64_t r, i
 }
 
 template <int EPI, int TN>
-__device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, int row_in_tile, uint32_t t_row) {
+__device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, int row_in_tile, uint32_t t_row,
+                                             uint8_t* staging) {
   const int grow = tm * L_TM + row_in_tile;  // row of the concatenated output
   int s = 0;
   int64_t r = grow;
@@ -306,6 +319,58 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       st_bf16x32(out_bf(p, 1, r, col), z, p.vec_ok[1] != 0, n);
     }
     return;
+  } else if constexpr (EPI == LIN_EPI_SCATTER) {
+    // stage[row][unit ^ (row & 7)]: 32 rows x 8 units of 16 bytes (64 bf16) for this warp
+    uint8_t* stage = staging;
+    const int lane = row_in_tile & 31;
+    const int64_t warp_row0 = grow - lane;  // first output row of this warp
+#pragma unroll 1
+    for (int c64 = 0; c64 < TN / 64; ++c64) {
+      const int col = cbase + c64 * 64;
+      if (col >= clim) break;  // uniform across the warp
+      float v[64];
+      tmem_ld_32cols(t_row + c64 * 64, v);
+      tmem_ld_32cols(t_row + c64 * 64 + 32, v + 32);
+      const int n = min(64, clim - col);
+      if (row_ok && p.C != nullptr) {
+        float c_[32];
+        ld_bf16x32(p.C + r * p.ldc + col, c_, p.in_vec != 0, n);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += c_[i];
+        if (n > 32) {
+          ld_bf16x32(p.C + r * p.ldc + col + 32, c_, p.in_vec != 0, n - 32);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[32 + i] += c_[i];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        uint4 w;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[u * 8 + 2 * e] * p.alpha, v[u * 8 + 2 * e + 1] * p.alpha);
+        *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) * 16)) = w;
+      }
+      __syncwarp();
+      const int u = lane & 7;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = (lane >> 3) + 4 * i;  // row of the warp's 32 this lane stores now
+        const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((u ^ (rr & 7)) * 16));
+        const int64_t orow = warp_row0 + rr;
+        const int c = col + u * 8;
+        if (orow < p.M && c < clim) {
+          const int owner = static_cast<int>(orow / p.scatter_rows);
+          if (MMF_DCHECK(owner < p.scatter_nseg, p.err, ERR_CHECK_BOUNDS)) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[owner]) +
+                                 (orow - static_cast<int64_t>(owner) * p.scatter_rows) * p.ldo[0] + c;
+            *reinterpret_cast<uint4*>(dst) = w;
+          }
+        }
+      }
+      __syncwarp();
+    }
+    return;
   } else {
     // STORE and ROPE
     const bool rope = (EPI == LIN_EPI_ROPE) && ((p.rope_mask >> s) & 1);
@@ -381,6 +446,8 @@ __global__ void __launch_bounds__(L_THREADS, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  // SCATTER staging after the barriers (1 KB reserved for them), 1 KB-aligned
+  uint8_t* staging = sB + L_STAGES * L_B_BYTES + 1024;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -548,7 +615,8 @@ __global__ void __launch_bounds__(L_THREADS, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
       tc_fence_after();
       lin_epilogue<EPI, TN>(p, tm, tn, static_cast<int>(rank) * L_HALF + q * 32 + lane,
-                            tmem_base + static_cast<uint32_t>(acc * TN) + (static_cast<uint32_t>(q * 32) << 16));
+                            tmem_base + static_cast<uint32_t>(acc * TN) + (static_cast<uint32_t>(q * 32) << 16),
+                            staging + q * (32 * 128));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
@@ -582,14 +650,14 @@ cudaError_t launch_lin(const LinMaps& maps, const LinDev& p, int clusters, cudaS
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(linear_gemm_kernel<A_MN, B_MN, EPI, TN>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, LinTile<TN>::SMEM_BYTES);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, lin_smem_bytes<TN, EPI>());
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters, 1, 1);
   cfg.blockDim = dim3(L_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = LinTile<TN>::SMEM_BYTES;
+  cfg.dynamicSmemBytes = lin_smem_bytes<TN, EPI>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -603,13 +671,11 @@ cudaError_t launch_lin(const LinMaps& maps, const LinDev& p, int clusters, cudaS
 
 [[noreturn]] void fail(const std::string& what) { throw std::runtime_error("mmf: linear_gemm: " + what); }
 
-std::atomic<int> g_linear_tile_n{0};  // 0 automatic, 128 or 256 forced (benchmarks)
+
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
 }  // namespace
-
-void set_linear_tile_n(int tn) { g_linear_tile_n.store(tn); }
 
 void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0) fail("empty output");
@@ -618,7 +684,7 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
     fail("bad segment axis");
   if (a.axis == LIN_SEG_NONE && a.nseg != 1) fail("segments need a segment axis");
   const int epi = a.epilogue;
-  if (epi < LIN_EPI_STORE || epi > LIN_EPI_GELU_BWD) fail("bad epilogue");
+  if (epi < LIN_EPI_STORE || epi > LIN_EPI_SCATTER) fail("bad epilogue");
   const bool fwd_kind = !a.a_mn && !a.b_mn;
   const bool dx_kind = !a.a_mn && a.b_mn;
   const bool dw_kind = a.a_mn && a.b_mn;
@@ -627,6 +693,12 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
     fail("ROPE / SWIGLU / GELU epilogues are forward epilogues");
   if ((epi == LIN_EPI_SWIGLU_BWD || epi == LIN_EPI_GELU_BWD) && !dx_kind)
     fail("SWIGLU_BWD / GELU_BWD epilogues follow an input-gradient GEMM");
+  if (epi == LIN_EPI_SCATTER) {
+    if (!dw_kind || a.nseg != 1) fail("SCATTER is the epilogue of one weight-gradient GEMM");
+    if (a.out_f32 || a.accumulate) fail("SCATTER stores bf16 without reading the destination");
+    if (a.scatter_ptrs == nullptr || a.scatter_nseg < 1 || a.scatter_rows < 1) fail("SCATTER needs its owner table");
+    if (a.N % 8 || a.ldo[0] % 8) fail("SCATTER needs N % 8 == 0 and a 16-byte row pitch");
+  }
   if (epi == LIN_EPI_SWIGLU && (a.axis != LIN_SEG_N || a.nseg != 2)) fail("SWIGLU takes the two weights W1, W3");
   if (epi != LIN_EPI_STORE && epi != LIN_EPI_ROPE && (a.out_f32 || a.accumulate))
     fail("fp32 / accumulating output only with the STORE epilogue");
@@ -653,6 +725,9 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   p.seq_len = a.seq_len > 0 ? a.seq_len : 1;
   p.head_dim = a.head_dim;
   p.log2_theta = a.rope_theta > 0.f ? log2f(a.rope_theta) : 0.f;
+  p.scatter_ptrs = a.scatter_ptrs;
+  p.scatter_nseg = a.scatter_nseg;
+  p.scatter_rows = a.scatter_rows;
   p.err = device_error_word(dev);
 
   const int elt = a.out_f32 ? 4 : 2;
@@ -682,49 +757,14 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   p.total_kb = total_kb;
   const int units = num_sms(dev) / 2;
 
-  // Tile width: 256 columns unless 128 fills the last wave of pairs clearly better (the narrow
-  // tile costs a little per tile: more shared-memory traffic per MMA).  SWIGLU keeps 256 (gate
-  // and up halves of 128 hidden units); N segments must start on tile boundaries, so every
-  // segment but the last must be a multiple of the width.
-  auto n_tiles_for = [&](int tn) {
-    if (epi == LIN_EPI_SWIGLU) return (a.N + tn / 2 - 1) / (tn / 2);
-    if (a.axis != LIN_SEG_N) return (a.N + tn - 1) / tn;
-    int t = 0;
-    for (int s = 0; s < a.nseg; ++s) t += (a.seg_len[s] + tn - 1) / tn;
-    return t;
-  };
-  const int tiles_m0 = [&] {
-    if (a.axis != LIN_SEG_M) return (a.M + L_TM - 1) / L_TM;
-    int t = 0;
-    for (int s = 0; s < a.nseg; ++s) t += (a.seg_len[s] + L_TM - 1) / L_TM;
-    return t;
-  }();
-  int TN = 256;
-  const int forced = g_linear_tile_n.load();
-  if (forced == 128 || forced == 256) {
-    TN = forced;
-  } else if (epi != LIN_EPI_SWIGLU) {
-    auto wave_eff = [&](int tn) {
-      const double tiles = static_cast<double>(tiles_m0) * n_tiles_for(tn);
-      const double waves = tiles / units;
-      return waves / std::ceil(waves);
-    };
-    if (wave_eff(128) * 0.96 > wave_eff(256)) TN = 128;
-  }
-  if (epi == LIN_EPI_SWIGLU) TN = 256;
-  if (a.axis == LIN_SEG_N && TN == 128) {
-    for (int s = 0; s + 1 < a.nseg; ++s)
-      if (a.seg_len[s] % 128) TN = 256;
-  }
-  if (a.axis == LIN_SEG_N && epi != LIN_EPI_SWIGLU) {
-    for (int s = 0; s + 1 < a.nseg; ++s)
-      if (a.seg_len[s] % TN) fail("column segments must be multiples of the tile width (all but the last)");
-  }
-  if (epi == LIN_EPI_ROPE && (TN % a.head_dim)) TN = 256;
-
-  // tiles along each axis, row / column segment starts
-  int tiles_m = tiles_m0;
-  int tiles_n = n_tiles_for(TN);
+  // Tile width: 256 columns.  A 128-wide variant (more tiles, a fuller last wave) measured
+  // 0.52-0.65x of the 256-wide kernel on every Llama-3-8B linear (1 B200, bench_gemm.py), so it
+  // is not built.
+  constexpr int TN = 256;
+  // tiles along each axis, row / column segment starts (a segment occupies whole tiles; the
+  // part of its last tile past the segment's end is zero-filled on load and never stored)
+  int tiles_m = (a.M + L_TM - 1) / L_TM;
+  int tiles_n = (epi == LIN_EPI_SWIGLU) ? (a.N + TN / 2 - 1) / (TN / 2) : (a.N + TN - 1) / TN;
   if (a.axis == LIN_SEG_M || a.axis == LIN_SEG_N) {
     int acc = 0;
     const int unit = (a.axis == LIN_SEG_M) ? L_TM : TN;
@@ -739,6 +779,10 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
       p.seg_len[0] = p.seg_len[1] = a.N;
     }
     p.seg_tile[a.nseg] = acc;
+    if (a.axis == LIN_SEG_M)
+      tiles_m = acc;
+    else
+      tiles_n = acc;
   } else if (a.axis != LIN_SEG_K) {
     p.seg_tile[0] = 0;
     p.seg_tile[1] = 1 << 30;
@@ -780,29 +824,28 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
 
   const int clusters = p.num_tiles < units ? p.num_tiles : units;
   cudaError_t e = cudaSuccess;
-  auto go = [&](auto tn_tag) {
-    constexpr int W = decltype(tn_tag)::value;
-    if (fwd_kind) {
-      switch (epi) {
-        case LIN_EPI_STORE: return launch_lin<false, false, LIN_EPI_STORE, W>(maps, p, clusters, stream);
-        case LIN_EPI_ROPE: return launch_lin<false, false, LIN_EPI_ROPE, W>(maps, p, clusters, stream);
-        case LIN_EPI_SWIGLU: return launch_lin<false, false, LIN_EPI_SWIGLU, 256>(maps, p, clusters, stream);
-        case LIN_EPI_GELU: return launch_lin<false, false, LIN_EPI_GELU, W>(maps, p, clusters, stream);
-        default: fail("epilogue not available for the forward GEMM");
-      }
-    } else if (dx_kind) {
-      switch (epi) {
-        case LIN_EPI_STORE: return launch_lin<false, true, LIN_EPI_STORE, W>(maps, p, clusters, stream);
-        case LIN_EPI_SWIGLU_BWD: return launch_lin<false, true, LIN_EPI_SWIGLU_BWD, W>(maps, p, clusters, stream);
-        case LIN_EPI_GELU_BWD: return launch_lin<false, true, LIN_EPI_GELU_BWD, W>(maps, p, clusters, stream);
-        default: fail("epilogue not available for the input-gradient GEMM");
-      }
-    } else if (epi != LIN_EPI_STORE) {
-      fail("the weight-gradient GEMM takes the STORE epilogue");
+  if (fwd_kind) {
+    switch (epi) {
+      case LIN_EPI_STORE: e = launch_lin<false, false, LIN_EPI_STORE, TN>(maps, p, clusters, stream); break;
+      case LIN_EPI_ROPE: e = launch_lin<false, false, LIN_EPI_ROPE, TN>(maps, p, clusters, stream); break;
+      case LIN_EPI_SWIGLU: e = launch_lin<false, false, LIN_EPI_SWIGLU, TN>(maps, p, clusters, stream); break;
+      case LIN_EPI_GELU: e = launch_lin<false, false, LIN_EPI_GELU, TN>(maps, p, clusters, stream); break;
+      default: fail("epilogue not available for the forward GEMM");
     }
-    return launch_lin<true, true, LIN_EPI_STORE, W>(maps, p, clusters, stream);
-  };
-  e = (TN == 128) ? go(std::integral_constant<int, 128>{}) : go(std::integral_constant<int, 256>{});
+  } else if (dx_kind) {
+    switch (epi) {
+      case LIN_EPI_STORE: e = launch_lin<false, true, LIN_EPI_STORE, TN>(maps, p, clusters, stream); break;
+      case LIN_EPI_SWIGLU_BWD: e = launch_lin<false, true, LIN_EPI_SWIGLU_BWD, TN>(maps, p, clusters, stream); break;
+      case LIN_EPI_GELU_BWD: e = launch_lin<false, true, LIN_EPI_GELU_BWD, TN>(maps, p, clusters, stream); break;
+      default: fail("epilogue not available for the input-gradient GEMM");
+    }
+  } else if (epi == LIN_EPI_SCATTER) {
+    e = launch_lin<true, true, LIN_EPI_SCATTER, TN>(maps, p, clusters, stream);
+  } else if (epi == LIN_EPI_STORE) {
+    e = launch_lin<true, true, LIN_EPI_STORE, TN>(maps, p, clusters, stream);
+  } else {
+    fail("the weight-gradient GEMM takes the STORE or SCATTER epilogue");
+  }
   count_launch();
   if (e != cudaSuccess) fail(std::string("launch failed: ") + cudaGetErrorString(e));
 }

@@ -389,6 +389,67 @@ __global__ void gelu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv
   }
 }
 
+// ------------------------------- embedding -----------------------------------------------
+// Forward: out[t] = table[tok[t]], one 16-byte vector per thread (D % 8 == 0).
+__global__ void embedding_fwd_kernel(const __nv_bfloat16* __restrict__ table, const int64_t* __restrict__ tok,
+                                     __nv_bfloat16* __restrict__ out, int64_t tokens, int D, int64_t vocab,
+                                     int* __restrict__ err) {
+  const int vpr = D / 8;  // vectors per row
+  const int64_t total = tokens * vpr;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = e / vpr;
+    const int c = static_cast<int>(e - t * vpr) * 8;
+    const int64_t v = tok[t];
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (v >= 0 && v < vocab)
+      w = *reinterpret_cast<const uint4*>(table + v * D + c);
+    else if (c == 0)
+      atomicCAS(err, 0, ERR_BAD_ARGUMENT);  // a token outside the table: zeros, and say so
+    *reinterpret_cast<uint4*>(out + t * D + c) = w;
+  }
+}
+
+// Backward, step 1: first[v] = position of vocabulary row v's first occurrence in the sorted
+// token list (rows that never occur keep -1 from the memset before).
+__global__ void embedding_first_kernel(const int64_t* __restrict__ sorted, int64_t tokens, int64_t vocab,
+                                       int* __restrict__ first) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < tokens;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t v = sorted[i];
+    if (v >= 0 && v < vocab && (i == 0 || sorted[i - 1] != v)) first[v] = static_cast<int>(i);
+  }
+}
+
+// Backward, step 2: every row of the dense table gradient in one pass: zeros for rows without
+// tokens, else the fp32 sum of their tokens' output gradients in sorted (then original) order,
+// so the result does not depend on scheduling.  One warp per row, 16-byte vectors.
+__global__ void embedding_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const int64_t* __restrict__ sorted,
+                                     const int64_t* __restrict__ perm, const int* __restrict__ first,
+                                     __nv_bfloat16* __restrict__ dtable, int64_t tokens, int64_t vocab, int D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t v = warp; v < vocab; v += nwarps) {
+    const int f = first[v];
+    __nv_bfloat16* row = dtable + v * D;
+    for (int c = lane * 8; c < D; c += 256) {
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      if (f >= 0) {
+        for (int64_t i = f; i < tokens && sorted[i] == v; ++i) {
+          float g[8];
+          ld_bf8(dy + perm[i] * D + c, g);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += g[e];
+        }
+      }
+      st_bf8(row + c, acc);
+    }
+  }
+}
+
 // ------------------------------- cross entropy -------------------------------------------
 // One block per row.  Online (max, sum-exp) over the row, then the gradient pass.
 template <bool VEC>
@@ -638,6 +699,31 @@ void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t s
   gelu_bwd_kernel<<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(dx), n);
   check_launch("gelu_bwd");
+}
+
+void embedding_fwd(const void* table, const int64_t* tokens, void* out, int64_t n_tokens, int D, int64_t vocab,
+                   cudaStream_t stream) {
+  if (n_tokens <= 0) return;
+  if (D % 8 || !aligned16(table) || !aligned16(out)) throw std::runtime_error("mmf: embedding needs D % 8 == 0, 16-byte rows");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  embedding_fwd_kernel<<<grid_for(n_tokens * (D / 8), 256, 148 * 16), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(table), tokens, static_cast<__nv_bfloat16*>(out), n_tokens, D, vocab,
+      device_error_word(dev));
+  check_launch("embedding_fwd");
+}
+
+void embedding_bwd(const void* dy, const int64_t* sorted, const int64_t* perm, int* first, void* dtable,
+                   int64_t n_tokens, int64_t vocab, int D, cudaStream_t stream) {
+  if (D % 8 || !aligned16(dy) || !aligned16(dtable)) throw std::runtime_error("mmf: embedding needs D % 8 == 0, 16-byte rows");
+  cudaMemsetAsync(first, 0xff, sizeof(int) * vocab, stream);  // -1: the row has no tokens
+  if (n_tokens > 0)
+    embedding_first_kernel<<<grid_for(n_tokens, 256, 148 * 4), 256, 0, stream>>>(sorted, n_tokens, vocab, first);
+  check_launch("embedding_first");
+  embedding_bwd_kernel<<<grid_for(vocab * 32, 256, 148 * 16), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(dy), sorted, perm, first, static_cast<__nv_bfloat16*>(dtable), n_tokens, vocab,
+      D);
+  check_launch("embedding_bwd");
 }
 
 void cross_entropy_fwd_bwd(void* logits, const int64_t* targets, float* loss_rows, int rows, int vocab, int64_t ld,

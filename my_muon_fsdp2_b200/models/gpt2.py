@@ -16,7 +16,7 @@ import torch
 import torch.nn as nn
 
 from ..ops.linear import gelu_mlp, linear
-from ..ops.model_ops import causal_attention, fused_linear_cross_entropy, gelu, layer_norm
+from ..ops.model_ops import causal_attention, embedding, fused_linear_cross_entropy, gelu, layer_norm
 
 
 @dataclass
@@ -130,7 +130,7 @@ class GPTModel(nn.Module):
         if T > self.config.n_positions:
             raise ValueError(f"Sequence length {T} exceeds maximum {self.config.n_positions}")
         pos = torch.arange(T, device=input_ids.device)
-        x = self.drop(self.wte(input_ids) + self.wpe(pos))
+        x = self.drop(embedding(input_ids, self.wte.weight) + embedding(pos, self.wpe.weight))
         for blk in self.h:
             x = blk(x)
         x = self.ln_f(x)

@@ -4,8 +4,9 @@ The reference has no Llama; this is the model of the Llama-3 8B FSDP2+Muon workl
 (32 layers, d=4096, 32 query / 8 KV heads, head_dim 128, FFN 14336, vocab 128256).
 Every projection runs on this library's grouped tcgen05 GEMM (``ops.linear``): q | k | v in one
 launch with RoPE in its epilogue, W1 | W3 with SwiGLU in the epilogue, and the residual adds of
-the attention output projection and of W2 fused into their GEMMs.  RMSNorm, attention and the
-LM-head cross entropy are this library's sm_100a kernels as well (``ops.model_ops``).
+the attention output projection and of W2 fused into their GEMMs.  The embedding lookup, RMSNorm,
+attention and the LM-head cross entropy are this library's sm_100a kernels as well
+(``ops.model_ops``).
 """
 from __future__ import annotations
 
@@ -16,7 +17,7 @@ import torch
 import torch.nn as nn
 
 from ..ops.linear import linear, qkv_rope, swiglu_ffn
-from ..ops.model_ops import causal_attention, fused_linear_cross_entropy, rms_norm
+from ..ops.model_ops import causal_attention, embedding, fused_linear_cross_entropy, rms_norm
 
 
 @dataclass
@@ -134,7 +135,7 @@ class Llama(nn.Module):
                 local.normal_(0.0, self.cfg.init_std, generator=gen)
 
     def forward(self, tokens: torch.Tensor, targets: Optional[torch.Tensor] = None):
-        x = self.tok_embeddings(tokens)
+        x = embedding(tokens, self.tok_embeddings.weight)
         for layer in self.layers:
             x = layer(x)
         x = self.norm(x)

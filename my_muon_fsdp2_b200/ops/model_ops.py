@@ -62,6 +62,30 @@ def layer_norm(x, weight, bias=None, eps: float = 1e-5):
     return F.layer_norm(x, (x.shape[-1],), weight, bias, eps)
 
 
+# -------------------------------------------------------------------------------- embedding
+class _EmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tokens, weight):
+        ctx.save_for_backward(tokens)
+        ctx.vocab = weight.shape[0]
+        return ext().embedding_fwd(weight, tokens)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (tokens,) = ctx.saved_tensors
+        if not ctx.needs_input_grad[1]:
+            return None, None
+        return None, ext().embedding_bwd(dy.contiguous(), tokens, ctx.vocab)
+
+
+def embedding(tokens: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """``weight[tokens]`` (an ``nn.Embedding`` lookup without padding_idx / max_norm); CUDA bf16
+    tables run this library's gather and its one-pass dense backward."""
+    if _cuda_bf16(weight) and tokens.is_cuda and weight.shape[1] % 8 == 0:
+        return _EmbeddingFn.apply(tokens.long(), weight)
+    return F.embedding(tokens, weight)
+
+
 # ------------------------------------------------------------------------------------- RoPE
 def _rope_torch(x: torch.Tensor, seq_len: int, theta: float, inverse: bool = False) -> torch.Tensor:
     """x: [B, T, H, D]; rotate-half convention (pairs (i, i + D/2))."""

@@ -19,10 +19,12 @@ moves the two collectives into this library's kernels:
   GEMM writes this rank's unsharded partial ``dW`` into a peer-readable buffer, then a side
   stream runs a bounded barrier and ``ext.rs_pull_reduce`` (each rank pulls its rows from every
   rank with P2P loads and sums them in rank order) while the backward continues on the compute
-  stream.  ``rs_mode="fused"``: the GEMM epilogue itself stores each rank's row block into that
-  rank's receive slot (``ext.wgrad_out``), then barrier + ``ext.rs_reduce`` on the compute
-  stream.  Both accumulate ``1/world`` of the rank-order sum into the gradient shard, which is
-  what FSDP2's averaging reduce-scatter produces, deterministically.
+  stream.  ``rs_mode="fused"``: the weight-gradient GEMM's epilogue itself stores each owner's
+  rows of the partial into this rank's sub-slot of that owner's receive region
+  (``ext.wgrad_scatter``: 128-byte row segments over NVLink, staged in shared memory), then a
+  barrier and the local rank-order sum (``ext.rs_reduce``) on the side stream.  Both accumulate
+  ``1/world`` of the rank-order sum into the gradient shard, which is what FSDP2's averaging
+  reduce-scatter produces, deterministically.
 
 The remaining parameters (embeddings, norms, LM head) stay under ``fully_shard`` with the fused
 linears passed as ``ignored_params``.  Without CUDA (gloo tests) the same module runs its
@@ -217,17 +219,21 @@ class SymmFSDP:
             if not any(self.fused_ok):
                 self.ready = None
             if rs_mode == "fused":
-                # receive slots, double-buffered: [2][world][largest shard] (epilogue P2P stores)
-                slot_elems = max(sizes) * self.world
-                self.slot_elems = slot_elems
-                self.slot_buf = symm_mem.empty(2 * slot_elems, dtype=dtype, device=self.device)
+                # one receive region per weight on every owner: [world sources][rows][K]; the
+                # weight-gradient GEMM's epilogue stores each owner's rows of this rank's partial
+                # into sub-slot [rank] of that owner's region (P2P stores, 128-byte row segments)
+                self.slot_offsets, o = [], 0
+                for (n, k), r in zip(self.shapes, self.rows):
+                    self.slot_offsets.append(o)
+                    o += (self.world * r * k + 7) // 8 * 8
+                self.slot_buf = symm_mem.empty(max(o, 8), dtype=dtype, device=self.device)
                 sync_handle = self._rendezvous(self.slot_buf)
-                self._slot_ptrs = [
-                    torch.tensor([int(sync_handle.buffer_ptrs[s_]) + 2 * (b * slot_elems + self.rank * (slot_elems // self.world))
+                bptrs = [int(sync_handle.buffer_ptrs[s_]) for s_ in range(self.world)]
+                self._owner_ptrs = [
+                    torch.tensor([bptrs[s_] + 2 * (self.slot_offsets[i] + self.rank * self.rows[i] * k)
                                   for s_ in range(self.world)], dtype=torch.int64, device=self.device)
-                    for b in range(2)
+                    for i, (_, k) in enumerate(self.shapes)
                 ]
-                self._meta: Dict[int, torch.Tensor] = {}
             else:
                 # unsharded partial dW of every weight, peer-readable: the reduce-scatter pulls
                 # each rank's rows from all ranks on a side stream while backward continues
@@ -239,15 +245,15 @@ class SymmFSDP:
                 sync_handle = self._rendezvous(self.acc_buf)
                 self._acc_ptrs = torch.tensor([int(sync_handle.buffer_ptrs[s_]) for s_ in range(self.world)],
                                               dtype=torch.int64, device=self.device)
-                self.comm = torch.cuda.Stream(device=self.device)
-                self.comm_epoch = 0
-                self._join_queued = False
+            # the reductions run on a side stream, overlapped with the rest of the backward
+            self.comm = torch.cuda.Stream(device=self.device)
+            self.comm_epoch = 0
+            self._join_queued = False
             # barriers use the signal pads of the synchronisation buffer's allocation
             self.pad_ptrs = torch.tensor(list(sync_handle.signal_pad_ptrs), dtype=torch.int64, device=self.device)
         else:
             self.shard_buf = torch.empty(total, dtype=dtype, device=self.device)
         self.epoch = 0
-        self.parity = 0
         self.sync_grads = True
         # cumulative bytes this rank received from its peers (algorithmic counts): weight
         # all-gathers, gradient reduce-scatters, and the replica all-reduces of HSDP
@@ -496,21 +502,40 @@ class SymmFSDP:
                 g.copy_(dw)
             self._replica_average(g)
             return
-        ext = _ext()
-        meta = self._meta.get(i)
-        if meta is None:
-            meta = torch.tensor([k, 0, r], dtype=torch.int64, device=self.device)
-            self._meta[i] = meta
-        b = self.parity
-        self.parity ^= 1
-        # rank s's rows of this rank's partial dW (+ the no-sync accumulation) -> slot [b][rank]
-        # of rank s, by P2P stores from the GEMM epilogue
-        ext.wgrad_out(_pad_rows(dy2, 64), _pad_rows(x2, 64), self._slot_ptrs[b], self.world, meta, False, 0.0,
-                      carry, 1.0)
-        self._barrier()
-        slots = self.slot_buf[b * self.slot_elems:(b + 1) * self.slot_elems]
-        ext.rs_reduce(slots, self.world, self.slot_elems // self.world, g, acc, 1.0 / self.world)
-        self._replica_average(g)
+        # rs_mode "fused": owner s's rows of this rank's partial dW (+ the no-sync accumulation)
+        # go straight into sub-slot [rank] of owner s's region for this weight, by P2P stores
+        # from the GEMM epilogue; the rank-order sum of the region runs on the side stream
+        with nvtx_range("symm_fsdp/wgrad_scatter"):
+            _ext().wgrad_scatter(dy2, x2, self._owner_ptrs[i], r, carry)
+        self._side_reduce(i, g, acc)
+
+    def _side_reduce(self, i: int, g: torch.Tensor, acc: bool) -> None:
+        """rs_mode "fused", second half: on the side stream, a barrier (every rank's scatter of
+        weight i has landed in this rank's region) and the rank-order sum of the region's
+        ``world`` sub-slots into the gradient shard (x 1/world, accumulated when ``acc``).  The
+        region is rewritten only in the next step, after the all-gather's start-of-step barrier,
+        which every rank passes after its optimizer step, so no second barrier is needed."""
+        n, k = self.shapes[i]
+        r = self.rows[i]
+        cur = torch.cuda.current_stream(self.device)
+        self.comm.wait_stream(cur)
+        g.record_stream(self.comm)
+        with torch.cuda.stream(self.comm):
+            self._comm_barrier()
+            o = self.slot_offsets[i]
+            region = self.slot_buf[o:o + self.world * r * k]
+            _ext().rs_reduce(region, self.world, r * k, g, acc, 1.0 / self.world)
+            self._replica_average(g)
+        self._queue_join()
+
+    def _queue_join(self) -> None:
+        """Join the side stream into the compute stream at the end of this backward pass."""
+        if not self._join_queued:
+            self._join_queued = True
+            try:
+                torch.autograd.Variable._execution_engine.queue_callback(self._join)
+            except RuntimeError:  # called outside a backward pass
+                self._join()
 
     def accumulate_grads(self, idxs: Sequence[int], dys: Sequence[torch.Tensor], x2: torch.Tensor) -> None:
         """Weight gradients of several linears that share the input ``x2`` (q/k/v, w1/w3).
@@ -609,12 +634,7 @@ class SymmFSDP:
             _ext().rs_pull_reduce(self._acc_ptrs, self.acc_offsets[i] + self.rank * r * k, g, acc, 1.0 / self.world)
             self._comm_barrier()
             self._replica_average(g)
-        if not self._join_queued:
-            self._join_queued = True
-            try:
-                torch.autograd.Variable._execution_engine.queue_callback(self._join)
-            except RuntimeError:  # called outside a backward pass
-                self._join()
+        self._queue_join()
 
 
 def block_linears(model: nn.Module, blocks_attr: str = "layers") -> List[nn.Linear]:

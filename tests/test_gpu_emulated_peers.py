@@ -47,10 +47,15 @@ def test_rs_pull_reduce_emulated(ws, rank, rows, cols, accumulate):
     assert rel_err(out, ref) < 1e-2
 
 
-@pytest.mark.parametrize("ws,T,N,K", [(2, 256, 1024, 512), (4, 320, 4096, 1024), (8, 4096, 14336, 4096)])
-def test_wgrad_epilogue_scatter_then_rank_order_reduce(ws, T, N, K):
+@pytest.mark.parametrize("kernel", ["linear_scatter", "tc_gemm_out"])
+@pytest.mark.parametrize("ws,T,N,K", [(2, 256, 1024, 512), (4, 320, 4096, 1024), (8, 4096, 14336, 4096),
+                                      (8, 200, 1024, 136)])
+def test_wgrad_epilogue_scatter_then_rank_order_reduce(ws, T, N, K, kernel):
     """Every emulated rank j computes its partial dW_j = dY_j^T X_j; the GEMM epilogue stores rows
-    of owner s into slot [j] of owner s; each owner then sums its ws slots (x 1/ws)."""
+    of owner s into slot [j] of owner s; each owner then sums its ws slots (x 1/ws).  Both the
+    grouped linear kernel's coalesced scatter and the NS kernel's row-segment output mode."""
+    if kernel == "tc_gemm_out" and (T % 64 or K % 256):
+        pytest.skip("the NS kernel's output mode takes T % 64 == 0 and K % 256 == 0")
     torch.manual_seed(T + N + ws)
     r = N // ws
     dys = [(torch.randn(T, N, device="cuda") * 0.1).to(torch.bfloat16) for _ in range(ws)]
@@ -60,7 +65,10 @@ def test_wgrad_epilogue_scatter_then_rank_order_reduce(ws, T, N, K):
     for j in range(ws):
         ptrs = torch.tensor([slots[s].data_ptr() + 2 * j * r * K for s in range(ws)], dtype=torch.int64,
                             device="cuda")
-        _E().wgrad_out(dys[j], xs[j], ptrs, ws, meta, False, 0.0, None, 1.0)
+        if kernel == "linear_scatter":
+            _E().wgrad_scatter(dys[j], xs[j], ptrs, r, None)
+        else:
+            _E().wgrad_out(dys[j], xs[j], ptrs, ws, meta, False, 0.0, None, 1.0)
     grads = [torch.zeros(r, K, dtype=torch.bfloat16, device="cuda") for _ in range(ws)]
     for s in range(ws):
         _E().rs_reduce(slots[s], ws, r * K, grads[s], False, 1.0 / ws)
@@ -139,3 +147,21 @@ def test_p2p_muon_exchange_direct_update_emulated(ws):
         d_ours = torch.cat([params[r][j].double().cpu() - p0[r][j].double().cpu() for r in range(ws)])
         d_ref = ref[j] - full_p[j]
         assert rel_err(d_ours, d_ref) < 0.06, f"matrix {j} {shapes[j]}"
+
+
+def test_wgrad_scatter_adds_the_carry():
+    """The scatter epilogue adds the unsharded no-sync accumulator C before storing."""
+    torch.manual_seed(3)
+    ws, T, N, K = 4, 256, 512, 384
+    r = N // ws
+    dy = (torch.randn(T, N, device="cuda") * 0.1).to(torch.bfloat16)
+    x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
+    carry = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+    slots = [torch.zeros(r * K, dtype=torch.bfloat16, device="cuda") for _ in range(ws)]
+    ptrs = torch.tensor([t.data_ptr() for t in slots], dtype=torch.int64, device="cuda")
+    _E().wgrad_scatter(dy, x, ptrs, r, carry)
+    torch.cuda.synchronize()
+    _check()
+    full = dy.float().t() @ x.float() + carry.float()
+    got = torch.cat([t.view(r, K) for t in slots])
+    assert rel_err(got, full) < 1e-2

@@ -10,16 +10,6 @@ from tests.conftest import rel_err
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=[0, 128, 256], ids=["tile_auto", "tile_n128", "tile_n256"], autouse=True)
-def tile_width(request):
-    """Every test with the automatic tile width and with each width forced (SWIGLU keeps 256)."""
-    from my_muon_fsdp2_b200._ext import ext
-
-    ext().set_linear_tile_n(request.param)
-    yield request.param
-    ext().set_linear_tile_n(0)
-
-
 def _bf(*shape, scale=1.0):
     return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
 

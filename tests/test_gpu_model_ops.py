@@ -133,3 +133,26 @@ def test_muon_optimizer_cuda_matches_cpu_oracle():
         if p.dim() == 2:
             decay = (1 - 0.02 * 0.1) ** 2 - 1
             assert rel_err(d_ours - decay * q, d_ref - decay * q) < 0.06
+
+
+@pytest.mark.parametrize("V,D,shape", [(1000, 256, (4, 300)), (128256, 4096, (1, 4096)), (50, 64, (3, 97))])
+def test_embedding_gather_and_dense_backward(V, D, shape):
+    """Forward equals the table rows exactly; the backward equals an fp32 index_add of the output
+    gradient (repeated tokens included: V=50 with 291 tokens repeats every row)."""
+    from my_muon_fsdp2_b200.ops.model_ops import embedding
+
+    torch.manual_seed(V)
+    w = (torch.randn(V, D, device="cuda") * 0.02).to(torch.bfloat16).requires_grad_()
+    tok = torch.randint(0, V, shape, device="cuda")
+    y = embedding(tok, w)
+    assert torch.equal(y, w.detach()[tok])
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    from my_muon_fsdp2_b200._ext import check_device_error
+
+    check_device_error(0)
+    ref = torch.zeros(V, D, device="cuda").index_add_(0, tok.reshape(-1), dy.reshape(-1, D).float())
+    assert rel_err(w.grad, ref) < 1e-2
+    untouched = torch.ones(V, dtype=torch.bool, device="cuda")
+    untouched[tok.reshape(-1)] = False
+    assert torch.count_nonzero(w.grad[untouched]) == 0
