@@ -2,8 +2,10 @@
 
 For each weight W [N, K] (row-sharded over the ranks) and T tokens per rank:
   * forward  : NCCL all_gather_into_tensor(W) + F.linear     vs  ag_gemm (one kernel)
-  * weight-gradient: dY^T X (cuBLAS) + NCCL reduce_scatter_tensor(avg)  vs
-                     wgrad_out (P2P stores from the epilogue) + bounded barrier + rs_reduce
+  * weight-gradient: dY^T X (cuBLAS) + NCCL reduce_scatter_tensor(avg)  vs the SymmFSDP path of
+                     --rs-mode: "fused" = wgrad_scatter (the GEMM epilogue stores each owner's rows
+                     over NVLink) + side-stream barrier + rs_reduce; "overlap" = local GEMM +
+                     side-stream barrier + rs_pull_reduce (both joined before the end event)
 CUDA events on the launching stream, max over ranks, after warm-up; inputs are larger than L2
 for the big shapes (weights 32-117 MB bf16, activations 32-117 MB).
 
@@ -138,11 +140,10 @@ def main():
         r["wgrad_nccl_ms"] = timed(nccl_wgrad, args.iters, args.warmup)
         r["wgrad_fused_ms"] = timed(fused_wgrad, args.iters, args.warmup)
         r["wgrad_gemm_only_ms"] = timed(lambda: dy.t() @ x, args.iters, args.warmup)
+        from my_muon_fsdp2_b200.ops.linear import mm_dw
+
         loc = torch.empty(n, k, device=dev, dtype=torch.bfloat16)
-        loc_ptrs = torch.tensor([loc.data_ptr()], dtype=torch.int64, device=dev)
-        loc_meta = torch.tensor([k, 0, n], dtype=torch.int64, device=dev)
-        r["wgrad_own_gemm_ms"] = timed(lambda: ext().wgrad_out(dy, x, loc_ptrs, 1, loc_meta, False, 0.0, None, 0.0),
-                                       args.iters, args.warmup)
+        r["wgrad_own_gemm_ms"] = timed(lambda: mm_dw([dy], x, [loc], False), args.iters, args.warmup)
         ref_dw = (dy.t() @ x).float()
         r["wgrad_own_rel_err"] = float((loc.float() - ref_dw).norm() / ref_dw.norm())
         # correctness spot check of the fused forward

@@ -54,11 +54,14 @@ def main():
     ap.add_argument("--variant", type=int, default=0, help="0 auto, 1 single-CTA tiles, 2 CTA-pair tiles")
     ap.add_argument("--only", default="", help="comma-separated case names")
     ap.add_argument("--lin-only", action="store_true", help="only the grouped transformer-linear kernel (and cuBLAS)")
+    ap.add_argument("--no-split", action="store_true", help="grouped kernel: whole tiles only (no split last wave)")
     a = ap.parse_args()
     from my_muon_fsdp2_b200._ext import ext
 
     E = ext()
     E.set_gemm_variant(a.variant)
+    E.set_linear_split_tail(not a.no_split)
+    print(json.dumps({"resident_cta_pairs": int(E.linear_resident_pairs())}), flush=True)
     T = a.tokens
     bf = torch.bfloat16
     shapes = {  # name: (N out features, K in features)
@@ -107,7 +110,7 @@ def main():
                    "cublas_ms": round(t_lib, 4), "tflops": round(flops / t_ours / 1e9, 1),
                    "cublas_tflops": round(flops / t_lib / 1e9, 1),
                    "frac_of_measured_peak": round(flops / t_ours / 1e9 / peak, 3),
-                   "speedup_vs_cublas": round(t_lib / t_ours, 3), "variant": a.variant}
+                   "speedup_vs_cublas": round(t_lib / t_ours, 3), "variant": a.variant, "split_last_wave": not a.no_split}
             print(json.dumps(rec), flush=True)
         del X, W, dY
         torch.cuda.empty_cache()

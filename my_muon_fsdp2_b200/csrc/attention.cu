@@ -21,6 +21,7 @@
 #include "attention.h"
 #include "kernels.h"
 #include "tc_common.cuh"
+#include "tma_host.h"
 
 namespace mmf {
 
@@ -1136,6 +1137,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode() {
 // [B, T, H, D] bf16 tensor, box {64 (D), 1 (head), 128 (T), 1}
 CUtensorMap map_bthd(const void* base, int B, int T, int H, int D) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("mmf: attention tensors must be 16B aligned");
+  ensure_context();
   CUtensorMap m;
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(T),
                         static_cast<cuuint64_t>(B)};

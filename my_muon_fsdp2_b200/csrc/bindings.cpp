@@ -611,6 +611,15 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
   return {dx, dw};
 }
 
+// x *= s (bf16 x in place; s a one-element fp32 CUDA tensor, read on the device)
+void scale_(Tensor x, Tensor s) {
+  check_bf16_contig(x, "x");
+  check_cuda(s, "s");
+  TORCH_CHECK(s.scalar_type() == torch::kFloat32 && s.numel() == 1, "mmf: scale_ takes a one-element fp32 scale");
+  const c10::cuda::CUDAGuard guard(x.device());
+  mmf::scale_bf16(x.data_ptr(), s.data_ptr<float>(), x.numel(), cur_stream());
+}
+
 // out[..., :] = table[tokens[...]]   (table [V, D] bf16, tokens int64)
 Tensor embedding_fwd(Tensor table, Tensor tokens) {
   check_bf16_contig(table, "table");
@@ -859,6 +868,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ag_gemm", &ag_gemm);
   m.def("linear_gemm", &linear_gemm);
   m.def("wgrad_scatter", &wgrad_scatter);
+  m.def("set_linear_split_tail", [](bool on) { mmf::set_linear_split_tail(on); });
+  m.def("linear_resident_pairs", []() { return static_cast<int64_t>(mmf::linear_resident_pairs()); });
   m.def("rs_reduce", &rs_reduce);
   m.def("rs_pull_reduce", &rs_pull_reduce);
   m.def("muon_prep", &muon_prep);
@@ -869,6 +880,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("layernorm_fwd", &layernorm_fwd);
   m.def("embedding_fwd", &embedding_fwd);
+  m.def("scale_", &scale_);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("layernorm_bwd", &layernorm_bwd);
   m.def("rope_", &rope_);

@@ -137,6 +137,10 @@ struct LinearGemmArgs {
   int64_t scatter_rows;
 };
 void linear_gemm(const LinearGemmArgs& args, cudaStream_t stream);
+// Split the tiles of a last, partly filled wave along K over the idle CTA pairs (default on).
+void set_linear_split_tail(bool on);
+// CTA pairs of the linear GEMM resident at once on the current device (its persistent grid).
+int linear_resident_pairs();
 
 // ----------------------------------------------------------------------------------------
 // FSDP all-gather fused with the consuming GEMM:  Y[M, N] = X[M, K] @ W^T, where W [N, K] is
@@ -270,6 +274,8 @@ void swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate,
                 cudaStream_t stream);
 void gelu_fwd(const void* x, void* y, int64_t n, cudaStream_t stream);
 void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t stream);
+// x (bf16, 16-byte aligned) *= s[0] (a device fp32 scalar).
+void scale_bf16(void* x, const float* s, int64_t n, cudaStream_t stream);
 // Embedding rows (bf16, D % 8 == 0): out[t] = table[tokens[t]] (a token outside the table gives
 // zeros and records ERR_BAD_ARGUMENT).  Backward: the dense table gradient in one pass from the
 // sorted tokens and their permutation; `first` is int32 scratch of vocab entries.

@@ -36,6 +36,8 @@
 
 #include <algorithm>
 #include <atomic>
+#include <map>
+#include <utility>
 #include <cmath>
 #include <mutex>
 #include <type_traits>
@@ -105,8 +107,55 @@ struct LinDev {
   const int64_t* scatter_ptrs;
   int scatter_nseg;
   int64_t scatter_rows;
+  // Split last wave: work items [0, full_tiles) are whole tiles; the remaining tiles are each
+  // split into `split` parts along K (items full_tiles + j * split + part).  Part 0 owns the
+  // tile's epilogue; parts 1.. write fp32 partial sums to part_ws and count up part_flags.
+  int full_tiles, split, num_items;
+  float* part_ws;
+  uint32_t* part_flags;
   int* err;
 };
+
+// Work item w -> tile t, split part (-1 = whole tile), and its k-block range [kb0, kb1).
+__device__ __forceinline__ void lin_item(const LinDev& p, int w, int& t, int& part, int& kb0, int& kb1) {
+  if (w < p.full_tiles) {
+    t = w;
+    part = -1;
+    kb0 = 0;
+    kb1 = p.total_kb;
+    return;
+  }
+  const int r = w - p.full_tiles;
+  const int j = r / p.split;
+  part = r - j * p.split;
+  t = p.full_tiles + j;
+  kb0 = static_cast<int>((static_cast<int64_t>(part) * p.total_kb) / p.split);
+  kb1 = static_cast<int>((static_cast<int64_t>(part + 1) * p.total_kb) / p.split);
+}
+
+constexpr int64_t L_PART_FLOATS = static_cast<int64_t>(L_TM) * 256;  // one fp32 partial tile
+
+// The accumulator of one thread's row for the epilogue: its TMEM lane, plus (when this is the
+// owning part of a split tile) the other parts' fp32 partial rows, added on every load.
+struct AccRow {
+  uint32_t t_row;
+  const float* part;  // this thread's row in the first partial slot of the tile, or nullptr
+  int nparts;
+};
+__device__ __forceinline__ void acc_ld(const AccRow& a, int col, float* v) {
+  tmem_ld_32cols(a.t_row + col, v);
+  for (int q = 0; q < a.nparts; ++q) {
+    const float4* src = reinterpret_cast<const float4*>(a.part + q * L_PART_FLOATS + col);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 w = src[i];
+      v[4 * i] += w.x;
+      v[4 * i + 1] += w.y;
+      v[4 * i + 2] += w.z;
+      v[4 * i + 3] += w.w;
+    }
+  }
+}
 
 __device__ __forceinline__ int seg_of(const LinDev& p, int tile) {
   int s = 0;
@@ -215,7 +264,7 @@ __device__ __forceinline__ void store_chunk(const LinDev& p, int s, int64_t r, i
 }
 
 template <int EPI, int TN>
-__device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, int row_in_tile, uint32_t t_row,
+__device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, int row_in_tile, const AccRow& t_row,
                                              uint8_t* staging) {
   const int grow = tm * L_TM + row_in_tile;  // row of the concatenated output
   int s = 0;
@@ -242,8 +291,8 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       const int col = h0 + c * 32;
       if (col >= p.N) break;  // uniform across the warp
       float g[32], u[32];
-      tmem_ld_32cols(t_row + c * 32, g);
-      tmem_ld_32cols(t_row + TN / 2 + c * 32, u);
+      acc_ld(t_row, c * 32, g);
+      acc_ld(t_row, TN / 2 + c * 32, u);
       if (!row_ok) continue;
       const int n = min(32, p.N - col);
       float h[32];
@@ -264,7 +313,7 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       const int col = cbase + c * 32;
       if (col >= clim) break;
       float d[32];
-      tmem_ld_32cols(t_row + c * 32, d);
+      acc_ld(t_row, c * 32, d);
       if (!row_ok) continue;
       const int n = min(32, clim - col);
       const bool vin = p.in_vec != 0;
@@ -302,7 +351,7 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       const int col = cbase + c * 32;
       if (col >= clim) break;
       float z[32];
-      tmem_ld_32cols(t_row + c * 32, z);
+      acc_ld(t_row, c * 32, z);
       if (!row_ok) continue;
       const int n = min(32, clim - col);
       float a[32];
@@ -329,8 +378,8 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       const int col = cbase + c64 * 64;
       if (col >= clim) break;  // uniform across the warp
       float v[64];
-      tmem_ld_32cols(t_row + c64 * 64, v);
-      tmem_ld_32cols(t_row + c64 * 64 + 32, v + 32);
+      acc_ld(t_row, c64 * 64, v);
+      acc_ld(t_row, c64 * 64 + 32, v + 32);
       const int n = min(64, clim - col);
       if (row_ok && p.C != nullptr) {
         float c_[32];
@@ -386,8 +435,8 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
         const int col_a = cbase + a * 32;
         if (col_a >= clim) break;
         float x1[32], x2[32];
-        tmem_ld_32cols(t_row + a * 32, x1);
-        tmem_ld_32cols(t_row + b * 32, x2);
+        acc_ld(t_row, a * 32, x1);
+        acc_ld(t_row, b * 32, x2);
         if (!row_ok) continue;
         const int i0 = (a % hc) * 32;
 #pragma unroll
@@ -409,7 +458,7 @@ __device__ __forceinline__ void lin_epilogue(const LinDev& p, int tm, int tn, in
       const int col = cbase + c * 32;
       if (col >= clim) break;
       float v[32];
-      tmem_ld_32cols(t_row + c * 32, v);
+      acc_ld(t_row, c * 32, v);
       if (!row_ok) continue;
       const int n = min(32, clim - col);
 #pragma unroll
@@ -490,7 +539,9 @@ __global__ void __launch_bounds__(L_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = cluster; t < p.num_tiles && ok; t += nclusters) {
+      for (int w = cluster; w < p.num_items && ok; w += nclusters) {
+        int t, part, kb0, kb1;
+        lin_item(p, w, t, part, kb0, kb1);
         int tm, tn;
         lin_tile(p, t, tm, tn);
         // rows of A this CTA stages, and which A map (row segments)
@@ -510,7 +561,7 @@ __global__ void __launch_bounds__(L_THREADS, 1)
         }
         int ks = 0;  // K segment
         int ks_end = (p.axis == LIN_SEG_K) ? p.seg_tile[1] : p.total_kb;
-        for (int kb = 0; kb < p.total_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (p.axis == LIN_SEG_K) {
             while (kb >= ks_end) {
               ++ks;
@@ -564,14 +615,16 @@ __global__ void __launch_bounds__(L_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = cluster; t < p.num_tiles && ok; t += nclusters) {
+      for (int w = cluster; w < p.num_items && ok; w += nclusters) {
+        int t, part, kb0, kb1;
+        lin_item(p, w, t, part, kb0, kb1);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TN);
-        for (int kb = 0; kb < p.total_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, ERR_MMA_FULL_TIMEOUT)) {
             ok = false;
             break;
@@ -585,7 +638,7 @@ __global__ void __launch_bounds__(L_THREADS, 1)
                 A_MN ? sdesc_mnmajor(a_addr + kk * 16 * 128, L_BK * 64 * 2) : sdesc_kmajor(a_addr + kk * 32);
             const uint64_t bd =
                 B_MN ? sdesc_mnmajor(b_addr + kk * 16 * 128, L_BK * 64 * 2) : sdesc_kmajor(b_addr + kk * 32);
-            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk) ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == L_STAGES) {
@@ -609,14 +662,59 @@ __global__ void __launch_bounds__(L_THREADS, 1)
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = cluster; t < p.num_tiles; t += nclusters) {
+    const int row_in_tile = static_cast<int>(rank) * L_HALF + q * 32 + lane;
+    for (int w = cluster; w < p.num_items; w += nclusters) {
+      int t, part, kb0, kb1;
+      lin_item(p, w, t, part, kb0, kb1);
       int tm, tn;
       lin_tile(p, t, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
       tc_fence_after();
-      lin_epilogue<EPI, TN>(p, tm, tn, static_cast<int>(rank) * L_HALF + q * 32 + lane,
-                            tmem_base + static_cast<uint32_t>(acc * TN) + (static_cast<uint32_t>(q * 32) << 16),
-                            staging + q * (32 * 128));
+      AccRow ar{tmem_base + static_cast<uint32_t>(acc * TN) + (static_cast<uint32_t>(q * 32) << 16), nullptr, 0};
+      bool skip = false;
+      if (part >= 0) {
+        const int j = t - p.full_tiles;
+        uint32_t* flag = p.part_flags + j * 8 + static_cast<int>(rank) * 4 + q;  // one per epilogue warp
+        float* rowbase = p.part_ws + static_cast<int64_t>(j) * (p.split - 1) * L_PART_FLOATS +
+                         static_cast<int64_t>(row_in_tile) * 256;
+        if (part > 0) {
+          // a non-owning part: its fp32 partial row to slot (part - 1), then count up the flag
+          float* dst = rowbase + static_cast<int64_t>(part - 1) * L_PART_FLOATS;
+#pragma unroll 1
+          for (int c = 0; c < TN / 32; ++c) {
+            float v[32];
+            tmem_ld_32cols(ar.t_row + c * 32, v);
+            float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) red_release_gpu_add(flag, 1u);
+          skip = true;
+        } else {
+          // the owning part: wait (bounded) until the other parts' rows of this warp have landed
+          bool ready = true;
+          if (lane == 0) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_gpu(flag) < static_cast<uint32_t>(p.split - 1)) {
+              if (globaltimer_ns() - t0 > MMF_WAIT_TIMEOUT_NS) {
+                atomicCAS(err, 0, ERR_PEER_FLAG_TIMEOUT);
+                ready = false;
+                break;
+              }
+              __nanosleep(32);
+            }
+            *flag = 0;  // consumed: zero for the next launch
+          }
+          ready = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
+          if (ready) {
+            ar.part = rowbase;
+            ar.nparts = p.split - 1;
+          }
+        }
+      }
+      if (!skip) lin_epilogue<EPI, TN>(p, tm, tn, row_in_tile, ar, staging + q * (32 * 128));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
@@ -635,12 +733,71 @@ __global__ void __launch_bounds__(L_THREADS, 1)
   }
 }
 
+// Scratch of the split last wave, one per (device, stream) so that launches on different
+// streams never share it: fp32 partial tiles (fewer than 74 of the at most 148 / 2 pairs) and one
+// flag per epilogue warp of each split tile.  The owning part zeroes its flags after use.
+struct SplitScratch {
+  float* ws = nullptr;
+  uint32_t* flags = nullptr;
+};
+constexpr int L_MAX_SPLIT_TILES = 128;
+SplitScratch& split_scratch(int dev, cudaStream_t stream) {
+  static std::map<std::pair<int, cudaStream_t>, SplitScratch> cache;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  SplitScratch& sc = cache[{dev, stream}];
+  if (sc.ws == nullptr) {
+    const size_t ws_bytes = sizeof(float) * static_cast<size_t>(L_PART_FLOATS) * L_MAX_SPLIT_TILES;
+    const size_t fl_bytes = sizeof(uint32_t) * 8 * L_MAX_SPLIT_TILES;
+    if (cudaMalloc(&sc.ws, ws_bytes) != cudaSuccess || cudaMalloc(&sc.flags, fl_bytes) != cudaSuccess)
+      throw std::runtime_error("mmf: linear_gemm: cannot allocate the split-wave scratch");
+    if (cudaMemsetAsync(sc.flags, 0, fl_bytes, stream) != cudaSuccess)
+      throw std::runtime_error("mmf: linear_gemm: cannot clear the split-wave flags");
+  }
+  return sc;
+}
+
+std::atomic<int> g_split_tail{1};  // 1: split the last wave (default), 0: whole tiles only
+
 int num_sms(int dev) {
   static int sms[64] = {0};
   static std::mutex mu;
   std::lock_guard<std::mutex> g(mu);
   if (sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   return sms[dev];
+}
+
+// CTA pairs of this kernel that are resident at the same time (one CTA per SM; a GPC with an
+// odd number of free SMs leaves one idle).  The persistent grid never exceeds it, so every pair
+// runs concurrently: the owner of a split tile can wait for the other parts without deadlock.
+// All instantiations take one CTA per SM; the query uses the largest shared-memory size.
+int resident_pairs(int dev) {
+  static int pairs[64] = {0};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  if (pairs[dev] == 0) {
+    auto kern = linear_gemm_kernel<true, true, LIN_EPI_SCATTER, 256>;
+    const int smem = lin_smem_bytes<256, LIN_EPI_SCATTER>();
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 512, 1, 1);
+    cfg.blockDim = dim3(L_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms(dev) / 2;
+    }
+    pairs[dev] = std::min(n, num_sms(dev) / 2);
+  }
+  return pairs[dev];
 }
 
 template <bool A_MN, bool B_MN, int EPI, int TN>
@@ -676,6 +833,14 @@ cudaError_t launch_lin(const LinMaps& maps, const LinDev& p, int clusters, cudaS
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
 
 }  // namespace
+
+void set_linear_split_tail(bool on) { g_split_tail.store(on ? 1 : 0); }
+
+int linear_resident_pairs() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return resident_pairs(dev);
+}
 
 void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0) fail("empty output");
@@ -755,7 +920,7 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   }
   if (total_kb <= 0) fail("empty reduction");
   p.total_kb = total_kb;
-  const int units = num_sms(dev) / 2;
+  const int units = resident_pairs(dev);
 
   // Tile width: 256 columns.  A 128-wide variant (more tiles, a fuller last wave) measured
   // 0.52-0.65x of the 256-wide kernel on every Llama-3-8B linear (1 B200, bench_gemm.py), so it
@@ -790,6 +955,31 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   p.tiles_m = tiles_m;
   p.tiles_n = tiles_n;
   p.num_tiles = tiles_m * tiles_n;
+  // Split last wave: the tiles of a last, partly filled wave of pairs are split along K over the
+  // pairs that would otherwise idle; the fp32 partial sums go through a per-(device, stream)
+  // scratch area of at most units - 1 tiles.  The fix-up (partials written, then read by the
+  // owning part's epilogue) costs a few microseconds, so each part must keep at least 128
+  // k-blocks (K >= 8192): on a B200 the split made 4096-deep GEMMs 2-5 % slower and the
+  // 128256-deep LM-head input gradient 14 % faster.
+  {
+    const int tail = p.num_tiles % units;
+    int split = tail > 0 ? units / tail : 1;
+    split = std::min(split, p.total_kb / 128);
+    split = std::min(split, 8);
+    if (tail == 0 || split < 2 || g_split_tail.load() == 0 || tail > L_MAX_SPLIT_TILES ||
+        tail * (split - 1) > L_MAX_SPLIT_TILES) {
+      p.full_tiles = p.num_tiles;
+      p.split = 1;
+      p.num_items = p.num_tiles;
+    } else {
+      p.full_tiles = p.num_tiles - tail;
+      p.split = split;
+      p.num_items = p.full_tiles + tail * split;
+      SplitScratch& sc = split_scratch(dev, stream);
+      p.part_ws = sc.ws;
+      p.part_flags = sc.flags;
+    }
+  }
   {
     // Operand bytes walked per band: column bands re-read A (all rows) once per band, row bands
     // re-read B.  An operand that fits in half the L2 is read from DRAM once either way.
@@ -811,18 +1001,27 @@ void linear_gemm(const LinearGemmArgs& a, cudaStream_t stream) {
   LinMaps maps;
   const int na = (a.axis == LIN_SEG_M || a.axis == LIN_SEG_K) ? a.nseg : 1;
   const int nb = (a.axis == LIN_SEG_N || a.axis == LIN_SEG_K) ? a.nseg : 1;
+  // only the maps in use are encoded (host time per launch); unused slots repeat slot 0
   for (int s = 0; s < 3; ++s) {
-    const int sa = s < na ? s : 0;
-    const int sb = s < nb ? s : 0;
-    if (!aligned16(a.A[sa]) || !aligned16(a.B[sb])) fail("operands must be 16-byte aligned");
-    if ((a.a_inner[sa] % 8) || (a.b_inner[sb] % 8)) fail("operand row pitches must be multiples of 8 elements");
-    maps.a[s] = a.a_mn ? make_map_bf16_3d(a.A[sa], a.a_inner[sa], a.a_outer[sa], 1, 64, L_BK)
-                       : make_map_bf16_3d(a.A[sa], a.a_inner[sa], a.a_outer[sa], 1, L_BK, L_HALF);
-    maps.b[s] = a.b_mn ? make_map_bf16_3d(a.B[sb], a.b_inner[sb], a.b_outer[sb], 1, 64, L_BK)
-                       : make_map_bf16_3d(a.B[sb], a.b_inner[sb], a.b_outer[sb], 1, L_BK, TN / 2);
+    if (s < na) {
+      if (!aligned16(a.A[s])) fail("operands must be 16-byte aligned");
+      if (a.a_inner[s] % 8) fail("operand row pitches must be multiples of 8 elements");
+      maps.a[s] = a.a_mn ? make_map_bf16_3d(a.A[s], a.a_inner[s], a.a_outer[s], 1, 64, L_BK)
+                         : make_map_bf16_3d(a.A[s], a.a_inner[s], a.a_outer[s], 1, L_BK, L_HALF);
+    } else {
+      maps.a[s] = maps.a[0];
+    }
+    if (s < nb) {
+      if (!aligned16(a.B[s])) fail("operands must be 16-byte aligned");
+      if (a.b_inner[s] % 8) fail("operand row pitches must be multiples of 8 elements");
+      maps.b[s] = a.b_mn ? make_map_bf16_3d(a.B[s], a.b_inner[s], a.b_outer[s], 1, 64, L_BK)
+                         : make_map_bf16_3d(a.B[s], a.b_inner[s], a.b_outer[s], 1, L_BK, TN / 2);
+    } else {
+      maps.b[s] = maps.b[0];
+    }
   }
 
-  const int clusters = p.num_tiles < units ? p.num_tiles : units;
+  const int clusters = p.num_items < units ? p.num_items : units;
   cudaError_t e = cudaSuccess;
   if (fwd_kind) {
     switch (epi) {

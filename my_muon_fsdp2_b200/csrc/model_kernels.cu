@@ -389,6 +389,25 @@ __global__ void gelu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv
   }
 }
 
+// ------------------------------- scale by a device scalar ---------------------------------
+// x (bf16, n elements) *= *s, 16-byte vectors (the tail element-wise); s stays on the device, so
+// a loss scale known only to the GPU needs no host synchronisation.
+__global__ void scale_bf16_kernel(__nv_bfloat16* __restrict__ x, const float* __restrict__ s, int64_t n) {
+  const float f = *s;
+  const int64_t n8 = n / 8;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v[8];
+    ld_bf8(x + 8 * i, v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] *= f;
+    st_bf8(x + 8 * i, v);
+  }
+  for (int64_t i = 8 * n8 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    x[i] = __float2bfloat16_rn(bf(x[i]) * f);
+}
+
 // ------------------------------- embedding -----------------------------------------------
 // Forward: out[t] = table[tok[t]], one 16-byte vector per thread (D % 8 == 0).
 __global__ void embedding_fwd_kernel(const __nv_bfloat16* __restrict__ table, const int64_t* __restrict__ tok,
@@ -699,6 +718,13 @@ void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t s
   gelu_bwd_kernel<<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(dx), n);
   check_launch("gelu_bwd");
+}
+
+void scale_bf16(void* x, const float* s, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return;
+  if (!aligned16(x)) throw std::runtime_error("mmf: scale_bf16 needs a 16-byte aligned tensor");
+  scale_bf16_kernel<<<grid_for(n / 8 + 1, 256, 148 * 8), 256, 0, stream>>>(static_cast<__nv_bfloat16*>(x), s, n);
+  check_launch("scale_bf16");
 }
 
 void embedding_fwd(const void* table, const int64_t* tokens, void* out, int64_t n_tokens, int D, int64_t vocab,

@@ -41,9 +41,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+void ensure_context() {
+  thread_local int ready_dev = -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) throw std::runtime_error("mmf: no CUDA device");
+  if (ready_dev != dev) {
+    const cudaError_t e = cudaSetDevice(dev);  // initialises and binds the primary context
+    if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: cudaSetDevice failed: ") + cudaGetErrorString(e));
+    ready_dev = dev;
+  }
+}
+
 CUtensorMap make_map_bf16_3d(const void* base, uint64_t inner, uint64_t outer, uint64_t batch, uint32_t box_inner,
                              uint32_t box_outer) {
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("mmf: TMA base must be 16-byte aligned");
+  ensure_context();
   CUtensorMap m;
   cuuint64_t dims[3] = {inner, outer, batch};
   cuuint64_t strides[2] = {inner * 2, inner * outer * 2};

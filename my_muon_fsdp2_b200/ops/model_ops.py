@@ -210,9 +210,13 @@ class _LinearCEFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dx, dw, scale = ctx.saved_tensors
-        s = (g.float() * scale).to(dx.dtype)
-        dx = dx.mul_(s)  # saved gradients are used once: scale in place, no fp32 copies
-        dw = dw.mul_(s.to(dw.dtype)) if dw.dtype == ctx.w_dtype else (dw * s.float()).to(ctx.w_dtype)
+        s = (g.float() * scale).reshape(1)  # stays on the device: no host synchronisation
+        # the saved gradients are used once: scale them in place (one vectorised pass each)
+        ext().scale_(dx, s)
+        if dw.dtype == ctx.w_dtype:
+            ext().scale_(dw, s)
+        else:
+            dw = (dw * s).to(ctx.w_dtype)
         return dx, dw, None, None, None
 
 

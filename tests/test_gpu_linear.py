@@ -242,3 +242,63 @@ def test_fused_linear_with_bias_and_residual_matches_fp32_autograd():
     _check()
     assert rel_err(y, yr) < 2e-2 and rel_err(x.grad, xr.grad) < 3e-2 and rel_err(res.grad, rr.grad) < 1e-2
     assert rel_err(m.weight.grad, mr.weight.grad) < 3e-2 and rel_err(m.bias.grad, mr.bias.grad) < 3e-2
+
+
+def test_launch_from_a_thread_without_cuda_context():
+    """A thread whose first CUDA work is one of this library's GEMMs (autograd's backward worker
+    can be one): the launcher binds the device's context before encoding its tensor maps."""
+    import threading
+
+    from my_muon_fsdp2_b200.ops.linear import mm_fwd
+
+    x, w = _bf(256, 512), _bf(384, 512, scale=0.05)
+    ref = x.float() @ w.float().T
+    out = {}
+
+    def run():
+        try:
+            (out["y"],) = mm_fwd(x, [w])
+            torch.cuda.synchronize()
+        except Exception as e:  # reported below
+            out["e"] = e
+
+    t = threading.Thread(target=run)
+    t.start()
+    t.join()
+    assert "e" not in out, out.get("e")
+    assert rel_err(out["y"], ref) < 1e-2
+
+
+def test_split_last_wave_matches_whole_tiles():
+    """The split last wave (K-parts of the tail tiles on idle CTA pairs, fp32 fix-up; taken when
+    every part keeps >= 8192 of the reduction) gives the whole-tile result for each kernel form,
+    twice in a row (the flags reset themselves)."""
+    from my_muon_fsdp2_b200._ext import ext
+    from my_muon_fsdp2_b200.ops.linear import EPI_SWIGLU_BWD, gemm, mm_dw, mm_dx, mm_fwd
+
+    torch.manual_seed(11)
+    M, N, K = 4096, 4096, 16384  # 256 output tiles: a 34-tile last wave, split in two along K
+    x, w = _bf(M, K), _bf(N, K, scale=0.01)
+    dy, w2 = _bf(M, K), _bf(K, N, scale=0.01)
+    dyt, xt = _bf(K, N, scale=0.1), _bf(K, N)
+    g, u, r = _bf(M, N), _bf(M, N), _bf(M, N)
+    res = {}
+    for split in (False, True):
+        ext().set_linear_split_tail(split)
+        try:
+            for _ in range(2):
+                (y,) = mm_fwd(x, [w], residual=r)
+                dx = mm_dx([dy], [w2])
+                dw = torch.empty(N, N, dtype=torch.bfloat16, device="cuda")
+                mm_dw([dyt], xt, [dw], accumulate=False)
+                dg, du = torch.empty_like(g), torch.empty_like(u)
+                gemm([dy], [w2], False, True, [dg, du], EPI_SWIGLU_BWD, aux0=g, aux1=u)
+                torch.cuda.synchronize()
+                _check()
+        finally:
+            ext().set_linear_split_tail(True)
+        res[split] = (y, dx, dw, dg, du)
+    for a, b in zip(res[False], res[True]):
+        assert rel_err(b, a) < 5e-3
+    ref = x.float() @ w.float().T + r.float()
+    assert rel_err(res[True][0], ref) < 1e-2
