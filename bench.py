@@ -51,9 +51,9 @@ def parse():
                     help="symm: reduce-scatter on a side stream (overlap) or from the GEMM epilogue (fused)")
     ap.add_argument("--keep-gathered", action="store_true",
                     help="FSDP2 modules stay gathered between the micro-batches of a step (Trainer keep_gathered)")
-    ap.add_argument("--phases", action="store_true",
-                    help="also report the device time of each step phase (forward / backward per micro-batch, "
-                         "optimizer), max over ranks, averaged over the timed steps")
+    ap.add_argument("--no-phases", action="store_true",
+                    help="do not record the per-phase events (forward / backward per micro-batch, optimizer); "
+                         "they are read after the timed loop, so they add no synchronisation to it")
     ap.add_argument("--fsdp", choices=["fsdp2", "symm"], default="symm",
                     help="fsdp2: fully_shard everywhere; symm: block linears on symmetric memory with the "
                          "fused all-gather GEMM / GEMM reduce-scatter kernels, the rest fully_shard")
@@ -224,7 +224,7 @@ def main():
         from my_muon_fsdp2_b200.train import Trainer
 
         trainer = Trainer(model, opts, grad_accum=ga, step_timer=opt_timer, keep_gathered=args.keep_gathered,
-                          time_phases=args.phases)
+                          time_phases=not args.no_phases)
 
     dev_batches = [synthetic_tokens(s, ga, mbs, seq, vocab, rank, device="cuda") for s in range(2)]
     for s in range(args.warmup):
@@ -244,14 +244,16 @@ def main():
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     start, end = marks[0], marks[-1]
     start.record()
-    phase_sum: dict = {}
+    step_marks = []
     for s in range(args.steps):
         loss = trainer.step_on_device(dev_batches[s % 2])
         marks[s + 1].record()
-        if args.phases and hasattr(trainer, "phase_ms"):
-            for k, v in trainer.phase_ms().items():  # reading the events waits for this step
-                phase_sum[k] = phase_sum.get(k, 0.0) + v
+        step_marks.append(list(getattr(trainer, "_phase_marks", [])))  # read after the loop
     torch.cuda.synchronize()
+    phase_sum: dict = {}
+    for pm in step_marks:
+        for (_, a), (name, b) in zip(pm[:-1], pm[1:]):
+            phase_sum[name] = phase_sum.get(name, 0.0) + a.elapsed_time(b)
     launches = (count() - n0) if count else None
     clk = clocks.stop()
     dist.barrier()

@@ -80,6 +80,15 @@ def cases(E):
     out["adamw_embed_head"] = (lambda: E.adamw(ps, gs, ms, vs, 1e-3, 0.9, 0.999, 1e-8, 0.01, 0.1, 0.03),
                                n * (2 + 2 + 4 + 4 + 2 + 4 + 4), n * 12)
 
+    # LM-head gradient scaled by a device scalar (128256 x 4096 bf16, in place)
+    sc = torch.ones(1, device=dev, dtype=f32)
+    out["scale_head_grad"] = (lambda: E.scale_(ps[1], sc), 2 * ps[1].numel() * 2, ps[1].numel() * 2)
+    # embedding: gather of 4096 rows; dense table gradient (zeros + 4096 summed rows) in one pass
+    tok = torch.randint(0, V, (T,), device=dev)
+    out["embedding_fwd"] = (lambda: E.embedding_fwd(ps[0], tok), 2 * T * D * 2, T * D * 2)
+    dy_e = torch.randn(T, D, device=dev, dtype=bf)
+    out["embedding_bwd"] = (lambda: E.embedding_bwd(dy_e, tok, V), V * D * 2 + T * D * 2, T * D * 2)
+
     # P2P-style pull-reduce, 8 "ranks" whose buffers are local here (the kernel of the
     # overlapped gradient reduce-scatter): reads 8 x rows, writes 1 x rows
     ws, rows = 8, F * D // 8
