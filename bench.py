@@ -302,6 +302,8 @@ def main():
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",
+                       "root_params": ("fully_shard" if (args.impl == "reference" or world > 1 or args.fsdp != "symm")
+                                       else "unsharded (one rank)"),
                        "fsdp_impl": ((args.fsdp + (f"/{args.rs_mode}" if args.fsdp == "symm" else "")
                                       + ("/keep_gathered" if args.keep_gathered else ""))
                                      if args.impl == "ours" else "fully_shard"),

@@ -650,23 +650,31 @@ def block_linears(model: nn.Module, blocks_attr: str = "layers") -> List[nn.Line
 
 
 def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str = "layers",
-                    reshard_after_forward: Optional[bool] = None, rs_mode: str = "overlap") -> SymmFSDP:
+                    reshard_after_forward: Optional[bool] = None, rs_mode: str = "overlap",
+                    shard_root_alone: bool = False) -> SymmFSDP:
     """Shard the weights of the transformer blocks' linears on symmetric memory (fused
     all-gather/reduce-scatter kernels where the shapes allow, NCCL otherwise; gathered once per
     step either way) and ``fully_shard`` the rest of the model (embeddings, norms, biases, LM
-    head) with FSDP2, the linear weights passed as ``ignored_params``.  A model on the meta
-    device is materialised on ``device``.  Returns the controller (``model._symm_fsdp``)."""
+    head) with FSDP2, the linear weights passed as ``ignored_params``.  On a single rank the rest
+    of the model stays unsharded plain parameters unless ``shard_root_alone``.  A model on the
+    meta device is materialised on ``device``.  Returns the controller (``model._symm_fsdp``)."""
     from torch.distributed.fsdp import fully_shard
 
     lin = block_linears(model, blocks_attr)
-    fully_shard(model, mesh=mesh, reshard_after_forward=reshard_after_forward,
-                ignored_params={m.weight for m in lin})
+    n_ranks = mesh.size() if mesh is not None else (dist.get_world_size() if dist.is_initialized() else 1)
+    # One rank holds everything: FSDP2 on the rest of the model would only copy every parameter
+    # into its unsharded buffer before each forward and backward and every gradient out again,
+    # so the remaining parameters stay plain tensors there.
+    root_fsdp = n_ranks > 1 or shard_root_alone
+    if root_fsdp:
+        fully_shard(model, mesh=mesh, reshard_after_forward=reshard_after_forward,
+                    ignored_params={m.weight for m in lin})
     if device is not None and any(p.device.type == "meta" for p in model.parameters()):
         model.to_empty(device=torch.device(device))
     dev = torch.device(device) if device is not None else next(model.parameters()).device
     ctl = SymmFSDP(lin, mesh=mesh, device=dev, rs_mode=rs_mode)
     model._symm_fsdp = ctl
-    fsdp_sync = model.set_requires_gradient_sync
+    fsdp_sync = model.set_requires_gradient_sync if root_fsdp else (lambda *a, **kw: None)
 
     def set_requires_gradient_sync(flag: bool, *a, **kw):
         fsdp_sync(flag, *a, **kw)
