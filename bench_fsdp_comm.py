@@ -144,6 +144,17 @@ def main():
 
         loc = torch.empty(n, k, device=dev, dtype=torch.bfloat16)
         r["wgrad_own_gemm_ms"] = timed(lambda: mm_dw([dy], x, [loc], False), args.iters, args.warmup)
+        if args.rs_mode == "fused" and ctl.peer and ctl.fused_ok[i]:
+            # the two halves of the fused path on their own: the GEMM whose epilogue stores each
+            # owner's rows over NVLink, and the owner's rank-order sum of its region
+            rr = ctl.rows[i]
+            r["wgrad_scatter_only_ms"] = timed(lambda: ext().wgrad_scatter(dy, x, ctl._owner_ptrs[i], rr, None),
+                                               args.iters, args.warmup)
+            o = ctl.slot_offsets[i]
+            region = ctl.slot_buf[o:o + world * rr * k]
+            gsh = torch.empty(rr, k, device=dev, dtype=torch.bfloat16)
+            r["rs_reduce_only_ms"] = timed(lambda: ext().rs_reduce(region, world, rr * k, gsh, False, 1.0 / world),
+                                           args.iters, args.warmup)
         ref_dw = (dy.t() @ x).float()
         r["wgrad_own_rel_err"] = float((loc.float() - ref_dw).norm() / ref_dw.norm())
         # correctness spot check of the fused forward

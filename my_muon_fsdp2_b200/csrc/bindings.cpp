@@ -527,47 +527,71 @@ void ws_to_out(Tensor X, c10::optional<Tensor> s_vec, Tensor out_ptrs, int64_t n
   mmf::ws_to_out(a, cur_stream());
 }
 
+// Per-tensor descriptors of a multi-tensor optimizer launch: params and grads of one dtype each
+// (fp32 or bf16), two fp32 state tensors per param.  Returns the uploaded table.
+struct OptDescs {
+  Tensor table;
+  int n = 0;
+  int64_t max_numel = 1;
+  bool p32 = false, g32 = false, vec4 = true;
+};
+
+OptDescs opt_descs(const std::vector<Tensor>& params, const std::vector<Tensor>& grads,
+                   const std::vector<Tensor>& st_a, const std::vector<Tensor>& st_b, const char* what) {
+  OptDescs o;
+  o.n = static_cast<int>(params.size());
+  const auto dev = params[0].device();
+  TORCH_CHECK((int)grads.size() == o.n && (int)st_a.size() == o.n && (int)st_b.size() == o.n, "mmf: ", what,
+              " list sizes differ");
+  o.p32 = params[0].scalar_type() == torch::kFloat32;
+  o.g32 = grads[0].scalar_type() == torch::kFloat32;
+  std::vector<mmf::AdamDesc> d(o.n);
+  for (int i = 0; i < o.n; ++i) {
+    TORCH_CHECK(params[i].is_cuda() && params[i].is_contiguous() && grads[i].is_contiguous() &&
+                    st_a[i].is_contiguous() && st_b[i].is_contiguous(),
+                "mmf: ", what, " tensors must be contiguous CUDA tensors");
+    TORCH_CHECK(params[i].device() == dev && grads[i].device() == dev && st_a[i].device() == dev &&
+                    st_b[i].device() == dev,
+                "mmf: ", what, " tensors must be on one device");
+    TORCH_CHECK((params[i].scalar_type() == torch::kFloat32) == o.p32 &&
+                    (grads[i].scalar_type() == torch::kFloat32) == o.g32,
+                "mmf: ", what, " dtypes must be uniform within a launch");
+    TORCH_CHECK(params[i].scalar_type() == torch::kFloat32 || params[i].scalar_type() == torch::kBFloat16,
+                "mmf: ", what, " params must be fp32 or bf16");
+    TORCH_CHECK(grads[i].scalar_type() == torch::kFloat32 || grads[i].scalar_type() == torch::kBFloat16,
+                "mmf: ", what, " grads must be fp32 or bf16");
+    TORCH_CHECK(st_a[i].scalar_type() == torch::kFloat32 && st_b[i].scalar_type() == torch::kFloat32,
+                "mmf: ", what, " state tensors must be fp32");
+    TORCH_CHECK(grads[i].numel() == params[i].numel() && st_a[i].numel() == params[i].numel() &&
+                    st_b[i].numel() == params[i].numel(),
+                "mmf: ", what, " sizes differ");
+    d[i].param = reinterpret_cast<int64_t>(params[i].data_ptr());
+    d[i].grad = reinterpret_cast<int64_t>(grads[i].data_ptr());
+    d[i].exp_avg = reinterpret_cast<int64_t>(st_a[i].data_ptr());
+    d[i].exp_avg_sq = reinterpret_cast<int64_t>(st_b[i].data_ptr());
+    d[i].numel = params[i].numel();
+    if (d[i].numel > o.max_numel) o.max_numel = d[i].numel;
+    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (d[i].numel % 4 != 0 || !al(params[i].data_ptr()) || !al(grads[i].data_ptr()) || !al(st_a[i].data_ptr()) ||
+        !al(st_b[i].data_ptr()))
+      o.vec4 = false;
+  }
+  o.table = upload(d, dev);
+  return o;
+}
+
 void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> exp_avgs,
            std::vector<Tensor> exp_avg_sqs, double lr, double beta1, double beta2, double eps, double weight_decay,
            double bias_correction1, double bias_correction2_sqrt) {
-  const int n = static_cast<int>(params.size());
-  if (n == 0) return;
-  const auto dev = params[0].device();
-  const c10::cuda::CUDAGuard guard(dev);
-  TORCH_CHECK((int)grads.size() == n && (int)exp_avgs.size() == n && (int)exp_avg_sqs.size() == n,
-              "mmf: adamw list sizes differ");
-  const bool p32 = params[0].scalar_type() == torch::kFloat32;
-  const bool g32 = grads[0].scalar_type() == torch::kFloat32;
-  std::vector<mmf::AdamDesc> d(n);
-  int64_t max_numel = 1;
-  bool vec4 = true;
-  for (int i = 0; i < n; ++i) {
-    TORCH_CHECK(params[i].is_cuda() && params[i].is_contiguous() && grads[i].is_contiguous() &&
-                    exp_avgs[i].is_contiguous() && exp_avg_sqs[i].is_contiguous(),
-                "mmf: adamw tensors must be contiguous CUDA tensors");
-    TORCH_CHECK((params[i].scalar_type() == torch::kFloat32) == p32 && (grads[i].scalar_type() == torch::kFloat32) == g32,
-                "mmf: adamw dtypes must be uniform within a launch");
-    TORCH_CHECK(exp_avgs[i].scalar_type() == torch::kFloat32 && exp_avg_sqs[i].scalar_type() == torch::kFloat32,
-                "mmf: adamw moments must be fp32");
-    TORCH_CHECK(grads[i].numel() == params[i].numel(), "mmf: adamw grad size");
-    d[i].param = reinterpret_cast<int64_t>(params[i].data_ptr());
-    d[i].grad = reinterpret_cast<int64_t>(grads[i].data_ptr());
-    d[i].exp_avg = reinterpret_cast<int64_t>(exp_avgs[i].data_ptr());
-    d[i].exp_avg_sq = reinterpret_cast<int64_t>(exp_avg_sqs[i].data_ptr());
-    d[i].numel = params[i].numel();
-    if (d[i].numel > max_numel) max_numel = d[i].numel;
-    auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    if (d[i].numel % 4 != 0 || !al(params[i].data_ptr()) || !al(grads[i].data_ptr()) || !al(exp_avgs[i].data_ptr()) ||
-        !al(exp_avg_sqs[i].data_ptr()))
-      vec4 = false;
-  }
-  Tensor dd = upload(d, dev);
+  if (params.empty()) return;
+  const c10::cuda::CUDAGuard guard(params[0].device());
+  OptDescs o = opt_descs(params, grads, exp_avgs, exp_avg_sqs, "adamw");
   mmf::AdamArgs a{};
-  a.descs = reinterpret_cast<const mmf::AdamDesc*>(dd.data_ptr());
-  a.n = n;
-  a.max_numel = max_numel;
-  a.param_f32 = p32;
-  a.grad_f32 = g32;
+  a.descs = reinterpret_cast<const mmf::AdamDesc*>(o.table.data_ptr());
+  a.n = o.n;
+  a.max_numel = o.max_numel;
+  a.param_f32 = o.p32;
+  a.grad_f32 = o.g32;
   a.lr = static_cast<float>(lr);
   a.beta1 = static_cast<float>(beta1);
   a.beta2 = static_cast<float>(beta2);
@@ -575,8 +599,28 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
   a.weight_decay = static_cast<float>(weight_decay);
   a.bias_correction1 = static_cast<float>(bias_correction1);
   a.bias_correction2_sqrt = static_cast<float>(bias_correction2_sqrt);
-  a.vec4 = vec4 ? 1 : 0;
+  a.vec4 = o.vec4 ? 1 : 0;
   mmf::adamw_multi(a, cur_stream());
+}
+
+void muon_moments(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> bufs,
+                  std::vector<Tensor> second_moments, double momentum, double beta2, double weight_decay,
+                  bool nesterov) {
+  if (params.empty()) return;
+  const c10::cuda::CUDAGuard guard(params[0].device());
+  OptDescs o = opt_descs(params, grads, bufs, second_moments, "muon_moments");
+  mmf::MomentArgs a{};
+  a.descs = reinterpret_cast<const mmf::AdamDesc*>(o.table.data_ptr());
+  a.n = o.n;
+  a.max_numel = o.max_numel;
+  a.param_f32 = o.p32;
+  a.grad_f32 = o.g32;
+  a.momentum = static_cast<float>(momentum);
+  a.beta2 = static_cast<float>(beta2);
+  a.weight_decay = static_cast<float>(weight_decay);
+  a.nesterov = nesterov ? 1 : 0;
+  a.vec4 = o.vec4 ? 1 : 0;
+  mmf::muon_moments_multi(a, cur_stream());
 }
 
 // --------------------------------- model ops --------------------------------------------
@@ -876,6 +920,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ns_scale", &ns_scale);
   m.def("ws_to_out", &ws_to_out);
   m.def("adamw", &adamw);
+  m.def("muon_moments", &muon_moments);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("layernorm_fwd", &layernorm_fwd);

@@ -254,6 +254,21 @@ struct AdamArgs {
 };
 void adamw_multi(const AdamArgs& args, cudaStream_t stream);
 
+// State update of the reference update rule (reference muon_fsdp/fsdp.py:326-345), one pass per
+// tensor: g = grad + wd p; buf = momentum buf + g; u = nesterov ? g + momentum buf : buf;
+// sm = beta2 sm + (1 - beta2) u^2.  The descriptor fields map exp_avg -> momentum buffer and
+// exp_avg_sq -> second moment (both fp32); the parameter is read, not written.
+struct MomentArgs {
+  const AdamDesc* descs;
+  int n;
+  int64_t max_numel;
+  int param_f32, grad_f32;
+  float momentum, beta2, weight_decay;
+  int nesterov;
+  int vec4;
+};
+void muon_moments_multi(const MomentArgs& args, cudaStream_t stream);
+
 // ----------------------------------------------------------------------------------------
 // Model kernels (bf16 activations, fp32 statistics).
 void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int cols, float eps,

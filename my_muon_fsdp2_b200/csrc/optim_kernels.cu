@@ -387,6 +387,46 @@ __global__ void __launch_bounds__(256) adamw_kernel(const AdamArgs a) {
   }
 }
 
+template <bool P_F32, bool G_F32, int VEC>
+__global__ void __launch_bounds__(256) muon_moments_kernel(const MomentArgs a) {
+  const AdamDesc d = a.descs[blockIdx.y];
+  const void* P = reinterpret_cast<const void*>(d.param);
+  const void* G = reinterpret_cast<const void*>(d.grad);
+  float* B = reinterpret_cast<float*>(d.exp_avg);
+  float* S = reinterpret_cast<float*>(d.exp_avg_sq);
+  const int64_t nv = d.numel / VEC;
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < nv;
+       j += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = j * VEC;
+    float g[VEC], b[VEC], s[VEC], p[VEC];
+    if (VEC == 4) {
+      ld4<G_F32>(G, i, g);
+      ld4<true>(B, i, b);
+      ld4<true>(S, i, s);
+      if (a.weight_decay != 0.f) ld4<P_F32>(P, i, p);
+    } else {
+      g[0] = ld_val<G_F32>(G, i);
+      b[0] = B[i];
+      s[0] = S[i];
+      if (a.weight_decay != 0.f) p[0] = ld_val<P_F32>(P, i);
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      if (a.weight_decay != 0.f) g[e] = fmaf(a.weight_decay, p[e], g[e]);
+      b[e] = fmaf(a.momentum, b[e], g[e]);
+      const float u = a.nesterov ? fmaf(a.momentum, b[e], g[e]) : b[e];
+      s[e] = fmaf(a.beta2, s[e], (1.f - a.beta2) * u * u);
+    }
+    if (VEC == 4) {
+      st4<true>(B, i, b);
+      st4<true>(S, i, s);
+    } else {
+      B[i] = b[0];
+      S[i] = s[0];
+    }
+  }
+}
+
 // ---------------------------- power iteration helpers ------------------------------------
 // y[r] = sum_c W[r, c] x[c]     (one warp per row)
 template <bool F32>
@@ -519,6 +559,27 @@ void adamw_multi(const AdamArgs& a, cudaStream_t stream) {
   }
 #undef MMF_ADAM
   check_launch("adamw_multi");
+}
+
+void muon_moments_multi(const MomentArgs& a, cudaStream_t stream) {
+  if (a.n <= 0) return;
+  if (a.n > 65535) throw std::runtime_error("mmf: muon_moments_multi supports at most 65535 tensors per launch");
+  const int vec = a.vec4 ? 4 : 1;
+  dim3 grid(grid_for(a.max_numel / vec, 256, 1184), a.n);
+#define MMF_MOM(PF, GF)                                                       \
+  do {                                                                        \
+    if (a.vec4)                                                               \
+      muon_moments_kernel<PF, GF, 4><<<grid, 256, 0, stream>>>(a);            \
+    else                                                                      \
+      muon_moments_kernel<PF, GF, 1><<<grid, 256, 0, stream>>>(a);            \
+  } while (0)
+  if (a.param_f32) {
+    if (a.grad_f32) MMF_MOM(true, true); else MMF_MOM(true, false);
+  } else {
+    if (a.grad_f32) MMF_MOM(false, true); else MMF_MOM(false, false);
+  }
+#undef MMF_MOM
+  check_launch("muon_moments_multi");
 }
 
 // work must hold max(m, n) + 1 floats.  u [m], v [n] (v holds the start vector on entry).

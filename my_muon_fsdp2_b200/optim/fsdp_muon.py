@@ -39,6 +39,33 @@ from .errors import InvalidParameterError
 logger = logging.getLogger(__name__)
 
 
+def _reference_moments(state, params, mu: float, wd: float, beta2: float, nesterov: bool) -> None:
+    """Momentum and second-moment state of the reference update rule (fsdp.py:326-345):
+    g = grad + wd p, buf = mu buf + g, u = g + mu buf (Nesterov) or buf, sm = beta2 sm + (1-beta2) u^2.
+    On CUDA one ``muon_moments`` launch per (param dtype, grad dtype) bucket reads each tensor once;
+    elsewhere the same steps as PyTorch ops."""
+    live = [p for p in params if p.grad is not None]
+    if not live:
+        return
+    locs = [(get_local_tensor(p), get_local_tensor(p.grad), local_of(state[p]["momentum_buffer"]),
+             local_of(state[p]["second_moment"])) for p in live]
+    if locs[0][0].is_cuda:
+        from .._ext import ext
+
+        buckets: Dict[Any, List[int]] = {}
+        for i, (pd, gd, _, _) in enumerate(locs):
+            buckets.setdefault((pd.dtype, gd.dtype), []).append(i)
+        for idx in buckets.values():
+            ext().muon_moments([locs[i][0].contiguous() for i in idx], [locs[i][1].contiguous() for i in idx],
+                               [locs[i][2] for i in idx], [locs[i][3] for i in idx], mu, beta2, wd, nesterov)
+        return
+    for pd, gd, buf, sm in locs:
+        g = gd + wd * pd if wd != 0 else gd
+        buf.mul_(mu).add_(g.to(buf.dtype))
+        g = g + mu * buf if nesterov else buf.clone()
+        sm.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+
+
 class FSDPMuonOptimizer(Optimizer):
     def __init__(
         self,
@@ -148,17 +175,7 @@ class FSDPMuonOptimizer(Optimizer):
 
         mu, wd, beta2, eps, lr = group["momentum"], group["weight_decay"], group["beta2"], group["eps"], group["lr"]
         params = group["params"]
-        for p in params:
-            if p.grad is None:
-                continue
-            st = self.state[p]
-            pd, gd = get_local_tensor(p), get_local_tensor(p.grad)
-            g = gd + wd * pd if wd != 0 else gd
-            buf = local_of(st["momentum_buffer"])
-            buf.mul_(mu).add_(g.to(buf.dtype))
-            g = g + mu * buf if group["nesterov"] else buf.clone()
-            sm = local_of(st["second_moment"])
-            sm.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+        _reference_moments(self.state, params, mu, wd, beta2, group["nesterov"])
         grads = [get_local_tensor(p.grad) if p.grad is not None else torch.zeros_like(get_local_tensor(p))
                  for p in params]
         ws = get_world_size()
