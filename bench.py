@@ -3,7 +3,9 @@
 Workload (one optimizer step per rank): 4 micro-batches (grad accumulation) of 1 sequence x 4096
 uniform random tokens, bf16 parameters/compute, fp32 Muon momentum; Muon (lr 0.02, momentum
 0.95, weight decay 0.01, 5 NS steps) on every attention/FFN matrix, AdamW (lr 1e-3, wd 0.01) on
-embeddings, norms and the LM head.  FSDP2 ``fully_shard`` on every decoder layer and the root.
+embeddings, norms and the LM head.  The block linears are sharded over the ranks on symmetric
+memory (``apply_symm_fsdp``; ``--fsdp fsdp2`` for plain ``fully_shard`` on every decoder layer);
+the rest of the model is under ``fully_shard`` on several ranks and unsharded on one.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
@@ -17,6 +19,8 @@ Rank 0 prints one JSON line.
 
 ``--impl reference`` runs the unmodified reference package (installed under baseline/_ref) on a
 stock ``transformers`` Llama with the same config, FSDP2 wrapping, data and hyper-parameters.
+Its steps take tens of seconds, so past ``--ref-budget-s`` of wall clock it times fewer steps
+(warm-up 3, at least 1 timed and 1 end-to-end step) and reports the counts it ran.
 """
 from __future__ import annotations
 
@@ -47,6 +51,9 @@ def parse():
     ap.add_argument("--micro-bs", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32, help="debug only: fewer layers is not the named config")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ref-budget-s", type=float, default=900.0,
+                    help="reference arm: wall-clock budget of the whole run; past it the timed steps are cut "
+                         "(to at least 1, warm-up to 3, one end-to-end step) and the JSON line says so")
     ap.add_argument("--rs-mode", choices=["overlap", "fused"], default="overlap",
                     help="symm: reduce-scatter on a side stream (overlap) or from the GEMM epilogue (fused)")
     ap.add_argument("--keep-gathered", action="store_true",
@@ -227,8 +234,31 @@ def main():
                           time_phases=not args.no_phases)
 
     dev_batches = [synthetic_tokens(s, ga, mbs, seq, vocab, rank, device="cuda") for s in range(2)]
-    for s in range(args.warmup):
+    warmup, steps, e2e_cap, settle = args.warmup, args.steps, 3, True
+    budget = None
+    t_begin = time.time()
+    s = 0
+    while s < warmup:
+        t0 = time.time()
         trainer.step_on_device(dev_batches[s % 2])
+        torch.cuda.synchronize()
+        s += 1
+        if args.impl == "reference" and s == 2 and args.ref_budget_s > 0:
+            # the reference's steps take tens of seconds (fp32 larger-Gram Newton-Schulz on every
+            # rank): fit the run into the wall-clock budget, with fewer timed steps if needed.  Every
+            # rank takes the same decision (slowest rank's step time).
+            t_step = torch.tensor([time.time() - t0], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t_step, op=dist.ReduceOp.MAX)
+            t_step = float(t_step.item())
+            elapsed = time.time() - t_begin
+            planned = elapsed + (warmup - 2 + steps + min(steps, 3) + 1) * t_step
+            if planned > args.ref_budget_s:
+                warmup = max(3, s)
+                left = args.ref_budget_s - elapsed - (warmup - s) * t_step
+                steps = max(1, min(args.steps, int(left / t_step) - 1))
+                e2e_cap, settle = 1, False
+                budget = {"budget_s": args.ref_budget_s, "step_s_estimate": t_step, "steps_requested": args.steps,
+                          "warmup_requested": args.warmup}
     torch.cuda.synchronize()
     if args.impl == "ours":
         from my_muon_fsdp2_b200._ext import check_device_error
@@ -241,11 +271,11 @@ def main():
     clocks.start()
     n0 = count() if count else 0
     # one event per step boundary (recording an event adds no work between the steps)
-    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     start, end = marks[0], marks[-1]
     start.record()
     step_marks = []
-    for s in range(args.steps):
+    for s in range(steps):
         loss = trainer.step_on_device(dev_batches[s % 2])
         marks[s + 1].record()
         step_marks.append(list(getattr(trainer, "_phase_marks", [])))  # read after the loop
@@ -257,27 +287,28 @@ def main():
     launches = (count() - n0) if count else None
     clk = clocks.stop()
     dist.barrier()
-    dev_ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    dev_ms = max_over_ranks(start.elapsed_time(end) / steps)
     # per-step spread (each step's max over ranks), so that a few-percent change between runs
     # can be told apart from step-to-step noise
-    per_step = [max_over_ranks(marks[i].elapsed_time(marks[i + 1])) for i in range(args.steps)]
+    per_step = [max_over_ranks(marks[i].elapsed_time(marks[i + 1])) for i in range(steps)]
     srt = sorted(per_step)
     spread = {"min": srt[0], "median": srt[len(srt) // 2], "max": srt[-1]}
-    phases = {k: max_over_ranks(v / args.steps) for k, v in sorted(phase_sum.items())} if phase_sum else None
+    phases = {k: max_over_ranks(v / steps) for k, v in sorted(phase_sum.items())} if phase_sum else None
     opt_ms = max_over_ranks(opt_timer.mean_ms())
     final_loss = float(loss.item())
 
     e2e = None
     if not args.no_e2e:
         host = [synthetic_tokens(100 + s, ga, mbs, seq, vocab, rank).pin_memory() for s in range(2)]
-        trainer.train_step(host[0])  # settle
+        if settle:
+            trainer.train_step(host[0])
         torch.cuda.synchronize()
         dist.barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         # at most 3 timed end-to-end steps: the reference arm's steps take about a minute each
         # at 32 layers (its fp32 larger-Gram Newton-Schulz), and both arms use the same count
-        e2e_steps = min(args.steps, 3)
+        e2e_steps = min(steps, e2e_cap)
         t0.record()
         for s in range(e2e_steps):
             trainer.train_step(host[s % 2])
@@ -293,8 +324,8 @@ def main():
         value = tokens_per_step / (dev_ms / 1e3)
         base = baseline_value()
         out = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, **({"wall_clock_budget": budget} if budget else {}), "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / base) if base else None, "dtype": "bf16",
             "data": "synthetic uniform random tokens; random-init weights",
             "optimizer_step_ms": opt_ms, "step_ms_spread": spread,
