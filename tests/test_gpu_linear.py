@@ -270,18 +270,20 @@ def test_launch_from_a_thread_without_cuda_context():
 
 
 def test_split_last_wave_matches_whole_tiles():
-    """The split last wave (K-parts of the tail tiles on idle CTA pairs, fp32 fix-up; taken when
-    every part keeps >= 8192 of the reduction) gives the whole-tile result for each kernel form,
-    twice in a row (the flags reset themselves)."""
+    """The split last wave (the tail tiles' K-parts on idle CTA pairs with an fp32 fix-up, taken
+    when every part keeps >= 8192 of the reduction) gives the whole-tile result for each kernel
+    form and epilogue, twice in a row (the flags reset themselves).  4096 x 4096 outputs are 256
+    tiles: three full waves of the 74 pairs and 34 tail tiles, split in two along K = 16384."""
     from my_muon_fsdp2_b200._ext import ext
-    from my_muon_fsdp2_b200.ops.linear import EPI_SWIGLU_BWD, gemm, mm_dw, mm_dx, mm_fwd
+    from my_muon_fsdp2_b200.ops.linear import EPI_GELU, EPI_GELU_BWD, EPI_SWIGLU_BWD, gemm, mm_dw, mm_dx, mm_fwd
 
     torch.manual_seed(11)
-    M, N, K = 4096, 4096, 16384  # 256 output tiles: a 34-tile last wave, split in two along K
+    M, N, K = 4096, 4096, 16384
     x, w = _bf(M, K), _bf(N, K, scale=0.01)
     dy, w2 = _bf(M, K), _bf(K, N, scale=0.01)
     dyt, xt = _bf(K, N, scale=0.1), _bf(K, N)
     g, u, r = _bf(M, N), _bf(M, N), _bf(M, N)
+    bias = _bf(N, scale=0.1)
     res = {}
     for split in (False, True):
         ext().set_linear_split_tail(split)
@@ -291,14 +293,21 @@ def test_split_last_wave_matches_whole_tiles():
                 dx = mm_dx([dy], [w2])
                 dw = torch.empty(N, N, dtype=torch.bfloat16, device="cuda")
                 mm_dw([dyt], xt, [dw], accumulate=False)
+                dw32 = torch.ones(N, N, dtype=torch.float32, device="cuda")
+                mm_dw([dyt], xt, [dw32], accumulate=True)
                 dg, du = torch.empty_like(g), torch.empty_like(u)
                 gemm([dy], [w2], False, True, [dg, du], EPI_SWIGLU_BWD, aux0=g, aux1=u)
+                a_, z_ = torch.empty_like(g), torch.empty_like(g)
+                gemm([x], [w], False, False, [a_, z_], EPI_GELU, bias=bias)
+                dz = torch.empty_like(g)
+                gemm([dy], [w2], False, True, [dz], EPI_GELU_BWD, aux0=g)
                 torch.cuda.synchronize()
                 _check()
         finally:
             ext().set_linear_split_tail(True)
-        res[split] = (y, dx, dw, dg, du)
-    for a, b in zip(res[False], res[True]):
-        assert rel_err(b, a) < 5e-3
+        res[split] = (y, dx, dw, dw32, dg, du, a_, z_, dz)
+    for i, (a, b) in enumerate(zip(res[False], res[True])):
+        assert rel_err(b, a) < 5e-3, f"output {i}"
     ref = x.float() @ w.float().T + r.float()
     assert rel_err(res[True][0], ref) < 1e-2
+    assert rel_err(res[True][3], 1.0 + dyt.float().T @ xt.float()) < 1e-2

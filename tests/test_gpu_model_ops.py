@@ -106,8 +106,7 @@ def test_fused_adamw_matches_torch():
     assert rel_err(p, q) < 1e-5
 
 
-@pytest.mark.parametrize("pdt,gdt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16),
-                                     (torch.float32, torch.bfloat16)])
+@pytest.mark.parametrize("pdt,gdt", [(torch.float32, torch.float32), (torch.bfloat16, torch.bfloat16)])
 @pytest.mark.parametrize("nesterov", [False, True])
 def test_reference_rule_moments_kernel(pdt, gdt, nesterov):
     """The reference update rule's momentum + second-moment state (one kernel pass per bucket)
