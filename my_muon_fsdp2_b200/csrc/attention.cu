@@ -29,11 +29,7 @@ namespace {
 
 constexpr int QB = 128;  // query rows per CTA
 constexpr int KB = 128;  // keys per block
-// Backward kernels: TMA warp, MMA warp, 16 elementwise warps (4 per TMEM lane quarter, each on a
-// quarter of the columns), so that while some warps wait on TMEM loads or barriers the others
-// issue.  576 threads at one CTA per SM cap the registers at 112 per thread.
-constexpr int BWD_EW_WARPS = 16;
-constexpr int BWD_THREADS = 64 + 32 * BWD_EW_WARPS;
+constexpr int BWD_THREADS = 320;  // TMA warp, MMA warp, 8 elementwise warps (2 per TMEM lane quarter)
 
 struct AttnParams {
   int B, T, Hq, Hkv, D;
@@ -534,9 +530,8 @@ __global__ void __launch_bounds__(ATT3_THREADS, 1)
 // double-buffered; S^T / dP^T / dS^T are double-buffered per 64-query half, so the tensor core
 // computes one half while the elementwise warps work on the other.
 //   MMA      S^T = K_j Q_u^T  -> TMEM S(h)      dP^T = V_j dO_u^T -> TMEM dP(h)      (N = 64)
-//   softmax  (one key row per TMEM lane, 16 queries per warp) P^T = exp2(S^T*scale*log2e -
-//            lse*log2e) (causal mask on the diagonal block), packed back into TMEM as bf16 (the 16
-//            queries [16g, 16g+16) of a unit in columns [16g, 16g+8)); dS^T = P^T * (dP^T - delta)
+//   softmax  (one key row per TMEM lane) P^T = exp2(S^T*scale*log2e - lse*log2e) (causal mask
+//            on the diagonal block), packed back into TMEM as bf16; dS^T = P^T * (dP^T - delta)
 //            as bf16 into a swizzled smem tile
 //   MMA      dV += P^T dO_u (A from TMEM)      dK += dS^T Q_u   (dO_u, Q_u read MN-major)
 // dK and dV of each query head are written once at the end as fp32 and summed over the GQA
@@ -610,7 +605,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&do_full[t], 1);
       mbar_init(&do_empty[t], 1);
       mbar_init(&sp_full[t], 1);
-      mbar_init(&ds_full[t], BWD_EW_WARPS);
+      mbar_init(&ds_full[t], 8);
       mbar_init(&ds_empty[t], 1);
     }
     mbar_init(drain, 1);
@@ -700,8 +695,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {  // K = the 64 queries of this half
           const uint32_t row = static_cast<uint32_t>(h * 64 + kk * 16) * 128;
-          // P^T packed by the elementwise warps: queries [16kk, 16kk+16) in columns [16kk, 16kk+8)
-          const uint32_t a_tm = ts_h(h) + static_cast<uint32_t>(kk * 16);
+          // P^T packed by the elementwise warps: queries [32w, 32w+32) in columns [32w, 32w+16)
+          const uint32_t a_tm = ts_h(h) + static_cast<uint32_t>((kk >> 1) * 32 + (kk & 1) * 8);
           umma_bf16_ts(tDV, a_tm, sdesc_mnmajor(do_addr + row, 16384), id_kv, (u | kk) ? 1u : 0u);
           umma_bf16(tDK, sdesc_kmajor(ds_addr + kk * 32), sdesc_mnmajor(q_addr + row, 16384), id_kv,
                     (u | kk) ? 1u : 0u);
@@ -718,35 +713,34 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     }
   } else {
     const int q = warp & 3;
-    const int part = (warp - 2) >> 2;  // which 16 queries of a 64-query unit (and D/4 output columns)
+    const int half = (warp - 2) >> 2;  // which 32 queries of a 64-query unit (and D/2 output columns)
     const int kr = q * 32 + lane;      // key row (S^T / dP^T lane)
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const int tid = threadIdx.x - 64;  // 0 .. 32 * BWD_EW_WARPS - 1
-    const int c0 = part * 16;
+    const int tid = threadIdx.x - 64;  // 0..255
+    const int c0 = half * 32;
     // Every warp waits on the same mbarriers with waits that only give up on their own timeout: a
     // phase that completed is seen complete by all of them and one that never completes times
     // out in all of them, so every elementwise warp leaves the loop at the same point and the
     // named barriers stay matched.
     bool ok = true;
-    // row statistics of each query block, prefetched one block ahead (threads 0..255: one value)
-    const bool stat_thread = tid < 256;
+    // row statistics of each query block, prefetched one block ahead (one value per thread)
     const float* stat_src = (tid < 128) ? p.lse : p.delta;
     // the statistics are kept negated (-lse*log2e, -delta) so that both enter as addends
     const float stat_mul = (tid < 128) ? -1.4426950408889634f : -1.f;
     const int64_t stat_base = (static_cast<int64_t>(b) * p.Hq + hq) * p.T + (tid & 127);
-    float stat_next = stat_thread ? stat_src[stat_base + j * QB] * stat_mul : 0.f;
+    float stat_next = stat_src[stat_base + j * QB] * stat_mul;
     for (int u = 0; u < n_units && ok; ++u) {
       const int n = u >> 1, h = u & 1;
       const int i = j + n;
       if (h == 0) {
         // publish this block's statistics (the previous block's readers are past the barrier)
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * BWD_EW_WARPS) : "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (tid < 128)
           sLse[tid] = stat_next;
-        else if (tid < 256)
+        else
           sDelta[tid - 128] = stat_next;
-        asm volatile("bar.sync 1, %0;" ::"n"(32 * BWD_EW_WARPS) : "memory");
-        if (stat_thread && n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        if (n + 1 < n_iter) stat_next = stat_src[stat_base + (i + 1) * QB] * stat_mul;
       }
       if (!mbar_wait(&sp_full[h], (u >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT, MMF_WAIT_TIMEOUT_NS, false)) {
         ok = false;
@@ -754,16 +748,22 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
       tc_fence_after();
       const bool diag = (i == j);
-      float sv[16], dp[16];
-      tmem_ld_16cols_async(ts_h(h) + lane_off + c0, sv);
-      tmem_ld_16cols_async(tdp_h(h) + lane_off + c0, dp);
+      float sv[32], dp[32];
+      tmem_ld_32cols_async(ts_h(h) + lane_off + c0, sv);
+      tmem_ld_32cols_async(tdp_h(h) + lane_off + c0, dp);
       tmem_ld_wait();
-      // P^T and dS^T of this warp's 16 queries, in registers before the buffer wait
-      float ppk[8];  // P^T as bf16 pairs, reinterpreted as 32-bit TMEM words
-      uint4 wds[2];  // dS^T as bf16, 8 queries per 16-byte unit
+      // the dS^T buffer of this half was last read by the dK MMA of unit u-2
+      if (u >= 2 && !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
+                               MMF_WAIT_TIMEOUT_NS, false)) {
+        ok = false;
+        break;
+      }
+      uint8_t* dst_tile = sDSt + h * 16384;
+      float ppk[16];  // P^T as bf16 pairs, reinterpreted as 32-bit TMEM words
 #pragma unroll
-      for (int g = 0; g < 2; ++g) {
-        __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wds[g]);
+      for (int g = 0; g < 4; ++g) {
+        uint4 wd;
+        __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&wd);
         // the 8 query columns' statistics: same address in every lane (broadcast), 16-byte reads
         const int q0 = h * 64 + c0 + g * 8;
         float st_l[8], st_d[8];
@@ -790,19 +790,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           ppk[g * 4 + e2] = *reinterpret_cast<float*>(&pb);
           hd[e2] = __floats2bfloat162_rn(dd.x, dd.y);
         }
+        *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wd;
       }
-      // packed P^T over this warp's own (already consumed) S^T columns [c0, c0 + 8)
-      tmem_st_8cols_async(ts_h(h) + lane_off + c0, ppk);
-      // the dS^T buffer of this half was last read by the dK MMA of unit u-2
-      if (u >= 2 && !mbar_wait(&ds_empty[h], ((u - 2) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
-                               MMF_WAIT_TIMEOUT_NS, false)) {
-        tmem_st_wait();
-        ok = false;
-        break;
-      }
-      uint8_t* dst_tile = sDSt + h * 16384;
-#pragma unroll
-      for (int g = 0; g < 2; ++g) *reinterpret_cast<uint4*>(dst_tile + swz_offset(kr, c0 + g * 8)) = wds[g];
+      // packed P^T over this warp's own (already consumed) S^T columns [c0, c0 + 16)
+      tmem_st_16cols_async(ts_h(h) + lane_off + c0, ppk);
       tmem_st_wait();
       tc_fence_before();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -813,21 +804,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     // final Q/dO release (committed after them)
     if (ok) ok = mbar_wait(&q_empty[(n_iter - 1) & 1], ((n_iter - 1) >> 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT,
                            MMF_WAIT_TIMEOUT_NS, false);
-    // dK_j (x scale) and dV_j of this query head: D/4 columns per warp
+    // dK_j (x scale) and dV_j of this query head
     if (ok) {
       tc_fence_after();
       const int64_t row = (static_cast<int64_t>(b) * p.T + j * KB + kr) * p.Hq + hq;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
-        float* dst = (which == 0 ? p.dv_h : p.dk_h) + row * D + part * (D / 4);
-        const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off + part * (D / 4);
+        float* dst = (which == 0 ? p.dv_h : p.dk_h) + row * D + half * (D / 2);
+        const uint32_t tb = (which == 0 ? tDV : tDK) + lane_off + half * (D / 2);
         const float f = which == 0 ? 1.f : p.scale;
-        float v[D / 4];
+        float v[D / 2];
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) tmem_ld_16cols_async(tb + c * 16, v + c * 16);
+        for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tb + c * 32, v + c * 32);
         tmem_ld_wait();
 #pragma unroll
-        for (int g = 0; g < D / 16; ++g)
+        for (int g = 0; g < D / 8; ++g)
           *reinterpret_cast<float4*>(dst + g * 4) = make_float4(v[g * 4] * f, v[g * 4 + 1] * f, v[g * 4 + 2] * f, v[g * 4 + 3] * f);
       }
     }
@@ -843,7 +834,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // ======================================================================================
 // dQ kernel, one CTA per (128-query block i, query head, batch); loops over key blocks j <= i:
 //   MMA      S = Q_i K_j^T -> TMEM (double buffered)      dP = dO_i V_j^T -> TMEM
-//   softmax  (one query row per TMEM lane, four warps per lane quarter, 32 key columns each)
+//   softmax  (one query row per TMEM lane, two warps per lane quarter splitting the key columns)
 //            P = exp2(S*scale*log2e - lse*log2e) (causal mask on the diagonal), dS = P (dP - delta),
 //            bf16 into a swizzled smem tile
 //   MMA      dQ += dS K_j  (K_j read MN-major from its K-major tile)   -> TMEM, written once (bf16)
@@ -910,10 +901,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&kv_full[t], 1);
       mbar_init(&kv_empty[t], 1);
       mbar_init(&s_full[t], 1);
-      mbar_init(&s_empty[t], BWD_EW_WARPS);
+      mbar_init(&s_empty[t], 8);
     }
-    mbar_init(dp_empty, BWD_EW_WARPS);
-    mbar_init(ds_full, BWD_EW_WARPS);
+    mbar_init(dp_empty, 8);
+    mbar_init(ds_full, 8);
     mbar_init(ds_empty, 1);
     mbar_init(dq_done, 1);
     fence_mbar_init();
@@ -1002,14 +993,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     }
   } else {
     const int q = warp & 3;
-    const int part = (warp - 2) >> 2;  // which 32 key columns this warp owns (and D/4 dQ columns)
+    const int half = (warp - 2) >> 2;  // which 64 key columns this warp owns
     const int r = q * 32 + lane;       // query row in the block
     const int qi = i * QB + r;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int64_t so = (static_cast<int64_t>(b) * p.Hq + h) * p.T + qi;
     const float lse2 = p.lse[so] * 1.4426950408889634f;
     const float dlt = p.delta[so];
-    const int c0 = part * 32;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
       const int st = j & 1;
@@ -1019,9 +1009,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
       tc_fence_after();
       const bool diag = (j == i);
-      float sv[32], dp[32];
+      const int c0 = half * 64;
+      float sv[64], dp[64];
       tmem_ld_32cols_async(tsb(st) + lane_off + c0, sv);
+      tmem_ld_32cols_async(tsb(st) + lane_off + c0 + 32, sv + 32);
       tmem_ld_32cols_async(tDP + lane_off + c0, dp);
+      tmem_ld_32cols_async(tDP + lane_off + c0 + 32, dp + 32);
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
@@ -1029,14 +1022,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         mbar_arrive(&s_empty[st]);
         mbar_arrive(dp_empty);
       }
-      // dS of this warp's 32 keys into registers first; the single dS buffer is written only
-      // after the previous block's dQ MMA has read it
-      uint4 wv[4];
-      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-      const float2 nl = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
+      // the dS buffer must have been consumed by the previous dQ MMA
+      if (j >= 1 && !mbar_wait(ds_empty, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
+        ok = false;
+        break;
+      }
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&wv[g]);
+      for (int g = 0; g < 8; ++g) {
+        uint4 w;
+        __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 nl = make_float2(-lse2, -lse2), nd = make_float2(-dlt, -dlt);
 #pragma unroll
         for (int e2 = 0; e2 < 4; ++e2) {
           const int e = g * 8 + e2 * 2;
@@ -1050,26 +1046,21 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           const float2 dd = fmul2(pr, fadd2(make_float2(dp[e], dp[e + 1]), nd));
           hw[e2] = __floats2bfloat162_rn(dd.x, dd.y);
         }
+        *reinterpret_cast<uint4*>(sDS + swz_offset(r, c0 + g * 8)) = w;
       }
-      if (j >= 1 && !mbar_wait(ds_empty, (j - 1) & 1, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
-        ok = false;
-        break;
-      }
-#pragma unroll
-      for (int g = 0; g < 4; ++g) *reinterpret_cast<uint4*>(sDS + swz_offset(r, c0 + g * 8)) = wv[g];
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full);
     }
     if (ok && mbar_wait(dq_done, 0, p.err, ERR_EPI_TMEM_FULL_TIMEOUT)) {
       tc_fence_after();
-      __nv_bfloat16* dst = p.dq + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D + part * (D / 4);
-      float v[D / 4];
+      __nv_bfloat16* dst = p.dq + ((static_cast<int64_t>(b) * p.T + qi) * p.Hq + h) * D + half * (D / 2);
+      float v[D / 2];
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tmem_ld_16cols_async(tDQ + lane_off + part * (D / 4) + c * 16, v + c * 16);
+      for (int c = 0; c < D / 64; ++c) tmem_ld_32cols_async(tDQ + lane_off + half * (D / 2) + c * 32, v + c * 32);
       tmem_ld_wait();
 #pragma unroll
-      for (int g = 0; g < D / 32; ++g) {
+      for (int g = 0; g < D / 16; ++g) {
         uint4 w;
         __nv_bfloat162* hw = reinterpret_cast<__nv_bfloat162*>(&w);
 #pragma unroll
