@@ -97,7 +97,10 @@ def run_train(rank, world, dev, steps=3, mesh_shape=None):
         torch.manual_seed(0)
         cfg = LlamaConfig.tiny(dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab_size=1024, n_layers=2)
         model = Llama(cfg).to(dev, torch.bfloat16)
-        mesh = init_device_mesh("cuda", mesh_shape or (world,))
+        if mesh_shape:  # (replicate, shard): FSDP2's HSDP wants the dimensions named
+            mesh = init_device_mesh("cuda", mesh_shape, mesh_dim_names=("dp_replicate", "fsdp_shard"))
+        else:
+            mesh = init_device_mesh("cuda", (world,))
         if mode == "symm":
             ctl = apply_symm_fsdp(model, mesh)
         else:
