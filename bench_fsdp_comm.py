@@ -75,7 +75,6 @@ def main():
     ap.add_argument("--emulate-world", type=int, default=0,
                     help="one GPU: run ag_gemm as rank 0 of this many ranks whose shards are all local "
                          "buffers (the kernel's pull / ready-flag / GEMM structure without NVLink, for ncu)")
-    ap.add_argument("--ag-variant", type=int, default=0, help="0: single-CTA all-gather GEMM, 1: CTA pair")
     args = ap.parse_args()
     if "RANK" not in os.environ:  # single process without torchrun
         import socket
@@ -92,7 +91,6 @@ def main():
     from my_muon_fsdp2_b200._ext import check_device_error, ext
     from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmFSDP
 
-    ext().set_ag_gemm_variant(args.ag_variant)
 
     T = args.tokens
     if args.emulate_world > 1:

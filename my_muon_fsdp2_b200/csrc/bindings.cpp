@@ -939,7 +939,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fwd", &attention_fwd);
   m.def("attention_bwd", &attention_bwd);
   m.def("set_attention_fwd_variant", [](int64_t v) { mmf::set_attention_fwd_variant(static_cast<int>(v)); });
-  m.def("set_ag_gemm_variant", [](int64_t v) { mmf::set_ag_gemm_variant(static_cast<int>(v)); });
   m.def("set_gemm_variant", [](int64_t v) { mmf::set_gemm_variant(static_cast<int>(v)); });
   m.def("gemm_variant", []() { return static_cast<int64_t>(mmf::gemm_variant()); });
   m.def("device_error", &device_error);

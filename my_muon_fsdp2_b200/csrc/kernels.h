@@ -164,8 +164,6 @@ struct AgGemmArgs {
   uint64_t wait_ns;
 };
 void ag_gemm(const AgGemmArgs& args, cudaStream_t stream);
-// 0 = single-CTA all-gather GEMM (default), 1 = CTA-pair kernel where M % 256 == 0.
-void set_ag_gemm_variant(int v);
 
 // Deterministic reduction of reduce-scatter slots: out[i] = bf16((accumulate ? out[i] : 0) +
 // scale * sum_{s = 0..ws-1} slots[s * slot_stride + i]) with the sum taken in fp32 in rank order.

@@ -938,236 +938,6 @@ __global__ void __launch_bounds__(AG_THREADS, 1)
   }
 }
 
-// ======================================================================================
-// All-gather GEMM on CTA pairs (cta_group::2): as ag_gemm_kernel, with 256 x 256 tiles per
-// cluster of 2 CTAs.  CTA r stages rows [r*128, r*128+128) of the A block (local X) and the
-// 128-row panel 2*tn + r of the B block (the resident full weight G once that panel has been
-// pulled, else its owner's shard), so each CTA makes one source decision per tile.  The
-// leader issues the M=256 N=256 MMAs; the pullers of all CTAs fill G exactly as in the
-// single-CTA kernel.  5-stage ring of 32 KB (A 16 KB + B 16 KB per CTA) + 2 pull buffers.
-// ======================================================================================
-constexpr int AGP_STAGES = 5;
-constexpr int AGP_SMEM_BYTES = AGP_STAGES * P_STAGE_BYTES + 2 * AG_PIECE_BYTES + 1024 + 256;
-
-__device__ __forceinline__ void ag_tile_pair(const AgParams& p, int t, int& tm, int& tn) {
-  int b;
-  tile_coords_pair(p.g, t, b, tm, tn);
-  tn += p.rot;
-  if (tn >= p.g.tiles_n) tn -= p.g.tiles_n;
-}
-
-__global__ void __launch_bounds__(AG_THREADS, 1)
-    ag_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmG,
-                        const __grid_constant__ AgMaps maps, const AgParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + AGP_STAGES * P_A_BYTES;
-  uint8_t* sP = sB + AGP_STAGES * P_B_BYTES;  // 2 pull buffers
-  uint64_t* full = reinterpret_cast<uint64_t*>(sP + 2 * AG_PIECE_BYTES);
-  uint64_t* empty = full + AGP_STAGES;
-  uint64_t* tfull = empty + AGP_STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint64_t* pfull = drain + 1;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pfull + 2);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t crank = cluster_ctarank();
-  const bool leader = crank == 0;
-  const int cluster = blockIdx.x >> 1;
-  const int nclusters = gridDim.x >> 1;
-  int* err = p.g.err;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < AGP_STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int j = 0; j < 2; ++j) {
-      mbar_init(&tfull[j], 1);
-      mbar_init(&tempty[j], 8);
-      mbar_init(&pfull[j], 1);
-    }
-    mbar_init(drain, 1);
-    fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmG);
-  }
-  if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, TMEM_COLS);
-    tmem_relinquish_pair();
-  }
-  tc_fence_before();
-  cluster_sync();  // barriers of both CTAs initialised before any remote arrive / TMA signal
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const int k_blocks = p.g.K / BK;
-
-  if (warp == 0) {
-    // ------------------------------ TMA producer (both CTAs) -------------------------
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = cluster; t < p.g.num_tiles && ok; t += nclusters) {
-        int tm, tn;
-        ag_tile_pair(p, t, tm, tn);
-        // this CTA's 128-row panel of the B block: local G once pulled, else the owner's shard
-        const int panel = 2 * tn + static_cast<int>(crank);
-        const int owner = panel / p.pps;
-        if (!MMF_DCHECK(owner >= 0 && owner < p.ws && owner < 8, err, ERR_CHECK_BOUNDS)) ok = false;
-        int src = owner;
-        int row = (panel - owner * p.pps) * AG_PANEL;
-        if (owner != p.rank) {
-          const uint32_t* flag = p.ready + panel;
-          bool ready = ld_acquire_gpu(flag) >= static_cast<uint32_t>(p.ppp);
-          if (!ready) {
-            const uint64_t t0 = globaltimer_ns();
-            while (!(ready = ld_acquire_gpu(flag) >= static_cast<uint32_t>(p.ppp))) {
-              if (globaltimer_ns() - t0 > p.wait_ns) break;  // fall back to the owner's memory
-              __nanosleep(64);
-            }
-          }
-          if (ready) {
-            fence_proxy_async_global();
-            src = -1;
-            row = panel * AG_PANEL;
-          }
-        }
-#ifdef MMF_DEVICE_CHECKS
-        if (!ok) break;
-#endif
-        const CUtensorMap* mB = src < 0 ? &tmG : &maps.shard[src];
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, err, ERR_TMA_EMPTY_TIMEOUT)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
-          tma_load_3d_pair(sA + stage * P_A_BYTES, &tmA, fb, kb * BK, tm * P_BM + static_cast<int>(crank) * 128, 0);
-          tma_load_3d_pair(sB + stage * P_B_BYTES, mB, fb, kb * BK, row, 0);
-          if (++stage == AGP_STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------ MMA issuer (leader CTA only) ---------------------
-    if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(P_BM, BN, false, false);
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      bool ok = true;
-      for (int t = cluster; t < p.g.num_tiles && ok; t += nclusters) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, ERR_MMA_TMEM_EMPTY_TIMEOUT)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, err, ERR_MMA_FULL_TIMEOUT)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * P_A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * P_B_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            umma_bf16_pair(d_tmem, sdesc_kmajor(a_addr + kk * 32), sdesc_kmajor(b_addr + kk * 32), idesc,
-                           (kb | kk) ? 1u : 0u);
-          umma_commit_pair(&empty[stage], 0x3);
-          if (++stage == AGP_STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-        umma_commit_pair(&tfull[acc], 0x3);
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
-        }
-      }
-      umma_commit_pair(drain, 0x1);
-      mbar_wait(drain, 0, err, ERR_MMA_FULL_TIMEOUT, 200000000ull);
-    }
-  } else if (warp < 6) {
-    // ------------------------------ epilogue (both CTAs) -----------------------------
-    const int q = warp & 3;
-    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int t = cluster; t < p.g.num_tiles; t += nclusters) {
-      int tm, tn;
-      ag_tile_pair(p, t, tm, tn);
-      if (!mbar_wait(&tfull[acc], acc_phase, err, ERR_EPI_TMEM_FULL_TIMEOUT)) break;
-      tc_fence_after();
-      epilogue_tile(p.g, 0, tm * P_BM + static_cast<int>(crank) * 128 + q * 32 + lane, tn,
-                    tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16));
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(acc * sizeof(uint64_t)));
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
-    }
-  } else {
-    // ------------------------------ puller (as ag_gemm_kernel) ----------------------
-    if (lane == 0) {
-      const int per_shard = p.pps * p.ppp;
-      const int total = p.ws * per_shard;
-      int i = 0, prev_panel = -1;
-      for (int gi = blockIdx.x; gi < total; gi += gridDim.x, ++i) {
-        const int step = gi / per_shard;  // 0 -> shard rank+1, ..., ws-1 -> own shard
-        int src = p.rank + 1 + step;
-        src -= (src >= p.ws) ? p.ws : 0;
-        src -= (src >= p.ws) ? p.ws : 0;
-        const int rem = gi - step * per_shard;
-        const int lp = rem / p.ppp;
-        const int kb = rem - lp * p.ppp;
-        const int buf = i & 1;
-        uint8_t* dst = sP + buf * AG_PIECE_BYTES;
-        if (!MMF_DCHECK(src >= 0 && src < p.ws && src < 8, err, ERR_CHECK_BOUNDS)) break;
-        mbar_arrive_expect_tx(&pfull[buf], AG_PIECE_BYTES);
-        tma_load_3d(dst, &maps.shard[src], &pfull[buf], kb * BK, lp * AG_PANEL, 0);
-        if (!mbar_wait(&pfull[buf], (i >> 1) & 1, err, ERR_TMA_EMPTY_TIMEOUT)) break;
-        tma_store_3d(&tmG, dst, kb * BK, src * p.rows_per_shard + lp * AG_PANEL, 0);
-        bulk_commit_group();
-        bulk_wait_group<1>();  // every store but the newest has completed
-        if (prev_panel >= 0) {
-          fence_proxy_async_global();
-          red_release_gpu_add(p.ready + prev_panel, 1u);
-        }
-        prev_panel = src * p.pps + lp;
-      }
-      bulk_wait_group<0>();
-      if (prev_panel >= 0) {
-        fence_proxy_async_global();
-        red_release_gpu_add(p.ready + prev_panel, 1u);
-      }
-    }
-  }
-
-  tc_fence_before();
-  cluster_sync();  // the leader's MMAs read CTA 1's smem: nobody leaves before both are done
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem_base, TMEM_COLS);
-  }
-}
-
 // ------------------------------------ host side ------------------------------------------
 struct DeviceInfo {
   int sms = 0;
@@ -1221,7 +991,7 @@ void launch(GemmParams& p, const void* A, const void* B, bool b_mn, cudaStream_t
   }
   p.num_tiles = p.tiles_per_batch * p.batch;
   {
-    const int units = pair ? di.sms / 2 : di.sms;  // concurrently running tiles
+    const int units = di.sms;  // concurrently running tiles
     int band = (units + p.tiles_m - 1) / p.tiles_m;
     p.band = band < 1 ? 1 : (band > p.tiles_n ? p.tiles_n : band);
   }
@@ -1370,9 +1140,6 @@ void tc_gemm_out(const GemmOutArgs& a, cudaStream_t stream) {
   launch(p, a.A, a.B, a.b_mn_major, stream, a.a_mn_major);
 }
 
-std::atomic<int> g_ag_variant{0};  // 0 single CTA, 1 CTA pair (needs M % 256 == 0)
-void set_ag_gemm_variant(int v) { g_ag_variant.store(v); }
-
 void ag_gemm(const AgGemmArgs& a, cudaStream_t stream) {
   if (a.ws < 1 || a.ws > AG_MAX_WS || a.rank < 0 || a.rank >= a.ws) throw std::runtime_error("mmf: ag_gemm: bad rank/world");
   check_shape(1, a.M, a.N, a.K);
@@ -1394,12 +1161,11 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t stream) {
   g.alpha = 1.f;
   g.beta = 0.f;
   g.err = device_error_word(dev);
-  const bool pair = g_ag_variant.load() == 1 && a.M % P_BM == 0;
-  g.tiles_m = a.M / (pair ? P_BM : BM);
+  g.tiles_m = a.M / BM;
   g.tiles_n = a.N / BN;
   g.tiles_per_batch = g.tiles_m * g.tiles_n;
   g.num_tiles = g.tiles_per_batch;
-  const int units = pair ? di.sms / 2 : di.sms;  // concurrently running tiles
+  const int units = di.sms;  // concurrently running tiles
   const int band = (units + g.tiles_m - 1) / g.tiles_m;
   g.band = band < 1 ? 1 : (band > g.tiles_n ? g.tiles_n : band);
   p.rank = a.rank;
@@ -1420,34 +1186,13 @@ void ag_gemm(const AgGemmArgs& a, cudaStream_t stream) {
   CUtensorMap ma = make_map_bf16_3d(a.X, a.K, a.M, 1, BK, BM);
   CUtensorMap mg = make_map_bf16_3d(a.G, a.K, a.N, 1, BK, AG_PANEL);
   cudaMemsetAsync(a.ready, 0, sizeof(uint32_t) * (a.N / AG_PANEL), stream);
-  cudaError_t e = cudaSuccess;
-  if (pair) {
-    if (!di.attr_set[9]) {
-      cudaFuncSetAttribute(ag_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AGP_SMEM_BYTES);
-      di.attr_set[9] = true;
-    }
-    const int clusters = g.num_tiles < di.sms / 2 ? g.num_tiles : di.sms / 2;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(AG_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = AGP_SMEM_BYTES;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, ag_gemm_pair_kernel, ma, mg, maps, p);
-  } else {
-    if (!di.attr_set[6]) {
-      cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AG_SMEM_BYTES);
-      di.attr_set[6] = true;
-    }
-    const int grid = g.num_tiles < di.sms ? g.num_tiles : di.sms;
-    ag_gemm_kernel<<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(ma, mg, maps, p);
+  if (!di.attr_set[6]) {
+    cudaFuncSetAttribute(ag_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AG_SMEM_BYTES);
+    di.attr_set[6] = true;
   }
+  const int grid = g.num_tiles < di.sms ? g.num_tiles : di.sms;
+  ag_gemm_kernel<<<grid, AG_THREADS, AG_SMEM_BYTES, stream>>>(ma, mg, maps, p);
+  cudaError_t e = cudaSuccess;
   count_launch();
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("mmf: ag_gemm launch failed: ") + cudaGetErrorString(e));
