@@ -529,80 +529,53 @@ class MuonEngine:
         mine = [j for j in range(n) if owners[j] == rank]
         groups = _group_by(mine, lambda j: (wide_shape(*shapes[j])[:2],
                                             tasks[j].local_param.dtype if direct[j] is not None else None))
-        chunks = []
         for ((mw, nw), direct_dtype), js in groups.items():
             Mp, Np = round_up(mw), round_up(nw)
             per = 2 * Mp * Np * 2 + 2 * Mp * Mp * 2
             chunk = max(1, min(len(js), self.max_workspace_bytes // max(per, 1)))
             for c0 in range(0, len(js), chunk):
-                chunks.append((mw, nw, Mp, Np, direct_dtype, js[c0:c0 + chunk]))
-        # 3. P2P loads: the assembly kernel reads every rank's shard of the chunk's matrices in place
-        #    (cast, transpose of tall ones, zero padding) into a local X0.  Chunk c+1 is assembled on
-        #    a side stream while chunk c's Newton-Schulz chain runs (the assembly's few small CTAs
-        #    fit beside the persistent GEMM's), so only the first pull is exposed.
-        cur = torch.cuda.current_stream(dev)
-        side = self._side_stream(dev) if len(chunks) > 1 else cur
-
-        def assemble(mw, nw, Mp, Np, direct_dtype, sub_js):
-            B = len(sub_js)
-            padded = (Mp != mw) or (Np != nw)
-            X0 = (torch.zeros if padded else torch.empty)(B, Mp, Np, dtype=torch.bfloat16, device=dev)
-            srcs, offs, row0, trs = [], [], [], []
-            for b, j in enumerate(sub_js):
-                rws, cls = shapes[j]
-                for r in range(world):
-                    if rows_of[j][r] == 0:
-                        continue
-                    srcs.append(sw.peer_view(r, off[r][j], (rows_of[j][r], cls)))
-                    offs.append(b * Mp * Np)
-                    row0.append(chunk_offset(rws, world, r))
-                    trs.append(int(rws > cls))
-            ev = None
-            if side is not cur:
-                side.wait_stream(cur)  # X0 allocated and the shards' barrier passed on this stream
-                X0.record_stream(side)
-                with torch.cuda.stream(side):
-                    E.muon_prep(srcs, [], [], X0, offs, row0, trs, [Np], [], [], MODE_COPY, False, 0.0, 0.0, None)
-                    ev = torch.cuda.Event()
-                    ev.record(side)
-            else:
+                sub_js = js[c0:c0 + chunk]
+                tall_group = any(shapes[j][0] > shapes[j][1] for j in sub_js)
+                B = len(sub_js)
+                padded = (Mp != mw) or (Np != nw)
+                X0 = (torch.zeros if padded else torch.empty)(B, Mp, Np, dtype=torch.bfloat16, device=dev)
+                srcs, offs, row0, trs = [], [], [], []
+                for b, j in enumerate(sub_js):
+                    rws, cls = shapes[j]
+                    for r in range(world):
+                        if rows_of[j][r] == 0:
+                            continue
+                        # 3. P2P loads: the assembly kernel reads rank r's shard in place
+                        srcs.append(sw.peer_view(r, off[r][j], (rows_of[j][r], cls)))
+                        offs.append(b * Mp * Np)
+                        row0.append(chunk_offset(rws, world, r))
+                        trs.append(int(rws > cls))
                 E.muon_prep(srcs, [], [], X0, offs, row0, trs, [Np], [], [], MODE_COPY, False, 0.0, 0.0, None)
-            return X0, ev
-
-        pending = assemble(*chunks[0]) if chunks else None
-        for ci, (mw, nw, Mp, Np, direct_dtype, sub_js) in enumerate(chunks):
-            X0, ev = pending
-            if ci + 1 < len(chunks):
-                pending = assemble(*chunks[ci + 1])
-            if ev is not None:
-                cur.wait_event(ev)
-            B = len(sub_js)
-            tall_group = any(shapes[j][0] > shapes[j][1] for j in sub_js)
-            jt = torch.tensor(sub_js, device=dev)
-            ssq = rows_ssq.index_select(1, jt).contiguous()  # [world, B]
-            s = torch.empty(B, dtype=torch.float32, device=dev)
-            s2 = torch.empty_like(s)
-            E.ns_scale(ssq, B, world, NS_EPS, s, s2)
-            addrs, meta = [], []
-            for j in sub_js:
-                rws, cls = shapes[j]
-                for d in range(world):
-                    # 4. P2P stores: rows of rank d go straight into rank d's parameter shard
-                    #    (direct) or into rank d's buffer
-                    addrs.append(direct[j][d] if direct_dtype is not None else sw.peer_addr(d, off[d][j]))
-                meta += [cls, int(rws > cls), (rws + world - 1) // world]
-            ptrs = torch.tensor(addrs, dtype=torch.int64).to(dev, non_blocking=True)
-            meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
-            if direct_dtype is not None:
-                pvec = _decay_vec([tasks[j].decay for j in sub_js], dev)
-                vvec = torch.tensor([-tasks[j].lr_eff for j in sub_js], dtype=torch.float32).to(
-                    dev, non_blocking=True)
-                run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, direct_dtype == torch.float32, False, mw, nw,
-                             p_scale=1.0, v_scale=1.0, p_scale_vec=pvec, v_scale_vec=vvec, nseg=world,
-                             out_meta=meta_t, transposed_dest=tall_group)
-            else:
-                run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
-                             nseg=world, out_meta=meta_t, transposed_dest=tall_group)
+                jt = torch.tensor(sub_js, device=dev)
+                ssq = rows_ssq.index_select(1, jt).contiguous()  # [world, B]
+                s = torch.empty(B, dtype=torch.float32, device=dev)
+                s2 = torch.empty_like(s)
+                E.ns_scale(ssq, B, world, NS_EPS, s, s2)
+                addrs, meta = [], []
+                for j in sub_js:
+                    rws, cls = shapes[j]
+                    for d in range(world):
+                        # 4. P2P stores: rows of rank d go straight into rank d's parameter shard
+                        #    (direct) or into rank d's buffer
+                        addrs.append(direct[j][d] if direct_dtype is not None else sw.peer_addr(d, off[d][j]))
+                    meta += [cls, int(rws > cls), (rws + world - 1) // world]
+                ptrs = torch.tensor(addrs, dtype=torch.int64).to(dev, non_blocking=True)
+                meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
+                if direct_dtype is not None:
+                    pvec = _decay_vec([tasks[j].decay for j in sub_js], dev)
+                    vvec = torch.tensor([-tasks[j].lr_eff for j in sub_js], dtype=torch.float32).to(
+                        dev, non_blocking=True)
+                    run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, direct_dtype == torch.float32, False, mw, nw,
+                                 p_scale=1.0, v_scale=1.0, p_scale_vec=pvec, v_scale_vec=vvec, nseg=world,
+                                 out_meta=meta_t, transposed_dest=tall_group)
+                else:
+                    run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
+                                 nseg=world, out_meta=meta_t, transposed_dest=tall_group)
         # 5. barrier: all owners' results have landed (parameters and buffers)
         sw.barrier()
         # 6. local apply from the own buffer (matrices not updated in place by their owner)
@@ -614,13 +587,6 @@ class MuonEngine:
                         [-tasks[j].lr_eff for j in js], MODE_COPY, False, 0.0, 0.0, None)
         self.last_stats = {"matrices": float(n), "owned": float(len(mine)), "exchange_bytes": float(2 * 2 * total),
                            "comm": "p2p", "direct_updates": float(sum(d is not None for d in direct))}
-
-    def _side_stream(self, dev: torch.device) -> torch.cuda.Stream:
-        """The stream the owner's next-chunk assembly runs on (one per device, kept)."""
-        streams = self.__dict__.setdefault("_side_streams", {})
-        if dev not in streams:
-            streams[dev] = torch.cuda.Stream(device=dev)
-        return streams[dev]
 
     def _direct_targets(self, tasks: List[MuonTask], rows_of, group: dist.ProcessGroup,
                         dev: torch.device) -> List[Optional[List[int]]]:
