@@ -58,6 +58,9 @@ def parse():
                     help="symm: reduce-scatter on a side stream (overlap) or from the GEMM epilogue (fused)")
     ap.add_argument("--keep-gathered", action="store_true",
                     help="FSDP2 modules stay gathered between the micro-batches of a step (Trainer keep_gathered)")
+    ap.add_argument("--root", choices=["shard", "replicate"], default="shard",
+                    help="--fsdp symm on several GPUs: the embedding, norms and LM head under fully_shard, or "
+                         "replicated with one gradient all-reduce per step")
     ap.add_argument("--no-phases", action="store_true",
                     help="do not record the per-phase events (forward / backward per micro-batch, optimizer); "
                          "they are read after the timed loop, so they add no synchronisation to it")
@@ -113,7 +116,7 @@ def build_ours(args, world, local):
     if args.fsdp == "symm":
         from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
 
-        ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local), rs_mode=args.rs_mode)
+        ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local), rs_mode=args.rs_mode, root=args.root)
     else:
         apply_fsdp(model, mesh)
         model.to_empty(device=torch.device("cuda", local))
@@ -333,7 +336,9 @@ def main():
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",
-                       "root_params": ("fully_shard" if (args.impl == "reference" or world > 1 or args.fsdp != "symm")
+                       "root_params": ("fully_shard" if (args.impl == "reference" or args.fsdp != "symm"
+                                                         or (world > 1 and args.root == "shard"))
+                                       else "replicated, one gradient all-reduce per step" if world > 1
                                        else "unsharded (one rank)"),
                        "fsdp_impl": ((args.fsdp + (f"/{args.rs_mode}" if args.fsdp == "symm" else "")
                                       + ("/keep_gathered" if args.keep_gathered else ""))

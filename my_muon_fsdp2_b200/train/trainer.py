@@ -42,6 +42,9 @@ class Trainer:
         self.device = torch.device(device) if device is not None else next(model.parameters()).device
         self.step_timer = step_timer  # optional EventTimer around the optimizer steps
         self.fsdp = is_fsdp_module(model)
+        # gradient synchronisation only on the last micro-batch: FSDP2 modules and models whose
+        # linears are on the fused collectives (whose rest may be replicated, not FSDP2)
+        self.grad_sync = self.fsdp or getattr(model, "_symm_fsdp", None) is not None
         self.keep_gathered = bool(keep_gathered) and self.fsdp and self.grad_accum > 1
         self.time_steps = bool(time_steps) and self.device.type == "cuda"
         self._step_events = None
@@ -55,8 +58,9 @@ class Trainer:
 
     def _micro(self, tokens: torch.Tensor, i: int):
         last = i == self.grad_accum - 1
-        if self.fsdp:
+        if self.grad_sync:
             self.model.set_requires_gradient_sync(last)
+        if self.fsdp:
             if self.keep_gathered and i in (0, self.grad_accum - 1):
                 # no resharding after the backward of a non-final micro-batch: the next forward
                 # finds the parameters still gathered

@@ -50,11 +50,11 @@ def _full(t):
     return t.full_tensor() if hasattr(t, "full_tensor") else t
 
 
-def _symm_grads(rank, world, no_sync):
+def _symm_grads(rank, world, no_sync, root="shard"):
     from my_muon_fsdp2_b200.parallel.symm_fsdp import SymmLinear, apply_symm_fsdp
 
     model = Net()
-    ctl = apply_symm_fsdp(model)
+    ctl = apply_symm_fsdp(model, root=root)
     assert ctl.world == world and not ctl.fused
     assert sum(isinstance(m, SymmLinear) for m in model.modules()) == 4
     for step in range(2):  # two micro-batches: gradients accumulate
@@ -66,10 +66,12 @@ def _symm_grads(rank, world, no_sync):
     return {n: _full(p.grad).clone() for n, p in model.named_parameters()}
 
 
+@pytest.mark.parametrize("root", ["shard", "replicate"])
 @pytest.mark.parametrize("no_sync", [False, True])
-def test_symm_fsdp_grads_match_single_process(no_sync):
+def test_symm_fsdp_grads_match_single_process(no_sync, root):
+    """The rest of the model sharded by FSDP2 or replicated with one gradient all-reduce."""
     world = 2
-    got = run_ranks(_symm_grads, world, no_sync)
+    got = run_ranks(_symm_grads, world, no_sync, root)
     ref = Net()
     for step in range(2):
         xs, ys = zip(*[_data(step, r) for r in range(world)])
@@ -79,12 +81,15 @@ def test_symm_fsdp_grads_match_single_process(no_sync):
         assert rel_err(got[n], p.grad) < 1e-5, n
 
 
-def _symm_train(rank, world, steps):
+def _symm_train(rank, world, steps, root="shard"):
     from my_muon_fsdp2_b200 import MuonOptimizer
     from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
 
     model = Net()
-    ctl = apply_symm_fsdp(model)
+    if root == "replicate" and rank == 1:  # replicas start from rank 0's values
+        with torch.no_grad():
+            model.inp.weight.add_(1.0)
+    ctl = apply_symm_fsdp(model, root=root)
     mats = [p for p in ctl.params]
     rest = [p for p in model.parameters() if all(p is not q for q in mats)]
     opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95, weight_decay=0.01), torch.optim.AdamW(rest, lr=1e-3)]
@@ -102,11 +107,12 @@ def _symm_train(rank, world, steps):
     return {"params": {n: _full(p.detach()).clone() for n, p in model.named_parameters()}, "losses": losses}
 
 
-def test_symm_fsdp_training_matches_single_process():
+@pytest.mark.parametrize("root", ["shard", "replicate"])
+def test_symm_fsdp_training_matches_single_process(root):
     from my_muon_fsdp2_b200 import MuonOptimizer
 
     world, steps = 2, 3
-    got = run_ranks(_symm_train, world, steps)
+    got = run_ranks(_symm_train, world, steps, root)
     ref = Net()
     mats = [m.weight for b in ref.layers for m in (b.up, b.down)]
     rest = [p for p in ref.parameters() if all(p is not q for q in mats)]
