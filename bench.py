@@ -58,7 +58,7 @@ def parse():
                     help="symm: reduce-scatter on a side stream (overlap) or from the GEMM epilogue (fused)")
     ap.add_argument("--keep-gathered", action="store_true",
                     help="FSDP2 modules stay gathered between the micro-batches of a step (Trainer keep_gathered)")
-    ap.add_argument("--root", choices=["shard", "replicate"], default="shard",
+    ap.add_argument("--root", choices=["shard", "replicate"], default="replicate",
                     help="--fsdp symm on several GPUs: the embedding, norms and LM head under fully_shard, or "
                          "replicated with one gradient all-reduce per step")
     ap.add_argument("--no-phases", action="store_true",

@@ -16,6 +16,28 @@ from ..parallel.fsdp_utils import is_fsdp_module
 from ..utils.tracing import nvtx_range
 
 
+def clip_grad_norm(params, max_norm: float) -> torch.Tensor:
+    """``torch.nn.utils.clip_grad_norm_`` for parameter lists that mix sharded DTensor gradients
+    (FSDP2 or SymmFSDP shards) with plain replicated ones (the replicated rest of a SymmFSDP
+    model): the global 2-norm combines the DTensors' norm (reduced over their mesh) with the
+    plain tensors' local norm, and the clip factor scales each gradient in place.  No host
+    synchronisation.  Lists of one kind go to PyTorch's function unchanged."""
+    grads = [p.grad for p in params if p.grad is not None]
+    sharded = [g for g in grads if hasattr(g, "to_local")]
+    plain = [g for g in grads if not hasattr(g, "to_local")]
+    if not sharded or not plain:
+        return torch.nn.utils.clip_grad_norm_(params, max_norm)
+    n_sh = torch.nn.utils.get_total_norm(sharded, 2.0)
+    if hasattr(n_sh, "full_tensor"):
+        n_sh = n_sh.full_tensor()
+    n_pl = torch.nn.utils.get_total_norm(plain, 2.0)
+    total = torch.sqrt(n_sh.float() ** 2 + n_pl.float().to(n_sh.device) ** 2)
+    coef = torch.clamp(max_norm / (total + 1e-6), max=1.0)
+    torch._foreach_mul_([g.to_local() for g in sharded], coef)
+    torch._foreach_mul_(plain, coef.to(plain[0].device))
+    return total
+
+
 class Trainer:
     def __init__(self, model: nn.Module, optimizers: Sequence, grad_accum: int = 1, device=None,
                  step_timer=None, max_grad_norm: Optional[float] = None, time_steps: bool = False,
@@ -105,7 +127,7 @@ class Trainer:
             total = l if total is None else total + l
         if self.max_grad_norm is not None:
             params = [p for p in self.model.parameters() if p.grad is not None]
-            self.last_grad_norm = torch.nn.utils.clip_grad_norm_(params, self.max_grad_norm)
+            self.last_grad_norm = clip_grad_norm(params, self.max_grad_norm)
             self._mark("grad_clip")
         if self.step_timer is not None:
             self.step_timer.start()

@@ -85,7 +85,12 @@ def run_hsdp(rank, world, dev):
     return run_train(rank, world, dev, mesh_shape=(2, world // 2))
 
 
-def run_train(rank, world, dev, steps=3, mesh_shape=None):
+def run_train_shard_root(rank, world, dev):
+    """The same comparison with the rest of the model under FSDP2 instead of replicated."""
+    return run_train(rank, world, dev, root="shard")
+
+
+def run_train(rank, world, dev, steps=3, mesh_shape=None, root="replicate"):
     from torch.distributed.device_mesh import init_device_mesh
 
     from my_muon_fsdp2_b200 import FusedAdamW, MuonOptimizer
@@ -102,7 +107,7 @@ def run_train(rank, world, dev, steps=3, mesh_shape=None):
         else:
             mesh = init_device_mesh("cuda", (world,))
         if mode == "symm":
-            ctl = apply_symm_fsdp(model, mesh)
+            ctl = apply_symm_fsdp(model, mesh, root=root)
         else:
             apply_fsdp(model, mesh)
         names = set(model.muon_param_names())
@@ -172,7 +177,8 @@ def run_split(rank, world, dev, steps=2):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mode", choices=["kernels", "train", "split", "mixed", "hsdp"], required=True)
+    ap.add_argument("--mode", choices=["kernels", "train", "train_shard_root", "split", "mixed", "hsdp"],
+                    required=True)
     ap.add_argument("--out", required=True)
     a = ap.parse_args()
     local = int(os.environ["LOCAL_RANK"])
@@ -181,8 +187,8 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
     try:
-        res = {"kernels": run_kernels, "train": run_train, "split": run_split, "mixed": run_mixed,
-               "hsdp": run_hsdp}[a.mode](
+        res = {"kernels": run_kernels, "train": run_train, "train_shard_root": run_train_shard_root,
+               "split": run_split, "mixed": run_mixed, "hsdp": run_hsdp}[a.mode](
             rank, world, dev)
         if rank == 0:
             torch.save(res, a.out)

@@ -53,9 +53,12 @@ def test_symm_fsdp_one_rank_training_matches_fsdp2():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_symm_fsdp_training_matches_fsdp2():
+@pytest.mark.parametrize("mode", ["train", "train_shard_root"], ids=["root_replicated", "root_fsdp2"])
+def test_symm_fsdp_training_matches_fsdp2(mode):
+    """SymmFSDP linears with the rest of the model replicated (default) or under FSDP2, against
+    plain FSDP2 everywhere, from the same initial weights."""
     with tempfile.TemporaryDirectory() as d:
-        res = _run(2, "train", os.path.join(d, "t.pt"))
+        res = _run(2, mode, os.path.join(d, "t.pt"))
     a, b = res["symm"], res["fsdp2"]
     assert a["direct_updates"] > 0 and b["direct_updates"] == 0  # in-place peer updates on symm shards only
     for x, y in zip(a["losses"], b["losses"]):

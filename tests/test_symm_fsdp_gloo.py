@@ -63,7 +63,11 @@ def _symm_grads(rank, world, no_sync, root="shard"):
         x, y = _data(step, rank)
         loss = ((model(x) - y) ** 2).mean() / 2
         loss.backward()
-    return {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+    from my_muon_fsdp2_b200.train.trainer import clip_grad_norm
+
+    out = {n: _full(p.grad).clone() for n, p in model.named_parameters()}
+    out["_norm"] = float(clip_grad_norm(list(model.parameters()), 1e9))  # norm only (no clipping)
+    return out
 
 
 @pytest.mark.parametrize("root", ["shard", "replicate"])
@@ -79,6 +83,9 @@ def test_symm_fsdp_grads_match_single_process(no_sync, root):
         loss.backward()
     for n, p in ref.named_parameters():
         assert rel_err(got[n], p.grad) < 1e-5, n
+    # the global gradient norm over sharded (DTensor) and replicated (plain) gradients
+    ref_norm = float(torch.nn.utils.get_total_norm([p.grad for p in ref.parameters()], 2.0))
+    assert abs(got["_norm"] - ref_norm) < 1e-5 * ref_norm
 
 
 def _symm_train(rank, world, steps, root="shard"):
