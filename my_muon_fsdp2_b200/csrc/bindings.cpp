@@ -488,6 +488,12 @@ void muon_prep(std::vector<Tensor> grads, std::vector<Tensor> bufs, std::vector<
   a.mu = static_cast<float>(mu);
   a.wd_coupled = static_cast<float>(wd_coupled);
   a.sumsq = sumsq.has_value() ? sumsq->data_ptr<float>() : nullptr;
+  Tensor partials;
+  if (a.sumsq) {
+    partials = torch::empty({static_cast<int64_t>(n) * mmf::muon_prep_blocks(max_tiles)},
+                            torch::dtype(torch::kFloat32).device(dev));
+    a.partials = partials.data_ptr<float>();
+  }
   a.vec8 = vec8 ? 1 : 0;
   mmf::muon_prep(a, cur_stream());
 }
@@ -798,9 +804,13 @@ void power_iteration(Tensor W, Tensor u, Tensor v, Tensor sigma, int64_t iters, 
   TORCH_CHECK(W.scalar_type() == torch::kFloat32 || W.scalar_type() == torch::kBFloat16, "mmf: W dtype");
   const c10::cuda::CUDAGuard guard(W.device());
   TORCH_CHECK(work.numel() >= std::max(W.size(0), W.size(1)) + 1, "mmf: work too small");
+  Tensor col_part = torch::empty({static_cast<int64_t>(mmf::power_iteration_col_blocks(static_cast<int>(W.size(0)))) *
+                                      W.size(1)},
+                                 torch::dtype(torch::kFloat32).device(W.device()));
   mmf::power_iteration(W.data_ptr(), W.scalar_type() == torch::kFloat32, static_cast<int>(W.size(0)),
                        static_cast<int>(W.size(1)), u.data_ptr<float>(), v.data_ptr<float>(), sigma.data_ptr<float>(),
-                       static_cast<int>(iters), static_cast<float>(eps), work.data_ptr<float>(), cur_stream());
+                       static_cast<int>(iters), static_cast<float>(eps), work.data_ptr<float>(),
+                       col_part.data_ptr<float>(), cur_stream());
 }
 
 // pad_ptrs / payload_ptrs: device int64 tensors of per-rank addresses (symmetric memory).

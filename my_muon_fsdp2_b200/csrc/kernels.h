@@ -207,9 +207,14 @@ struct PrepArgs {
   int nesterov;
   float mu;
   float wd_coupled;
-  float* sumsq;           // device [n] (may be null)
+  float* sumsq;           // device [n] (may be null): += sum of squares of each tensor's update
+  float* partials;        // device [n * muon_prep_blocks(max_tiles)] scratch when sumsq is set
   int vec8;               // all tensors allow 16-byte vector access (host-checked)
 };
+// Blocks per tensor of a muon_prep launch (the size of its per-block partial sums).
+int muon_prep_blocks(int max_tiles);
+// The sums of squares are reduced in a fixed order (per-block partials, then one warp per
+// tensor), so the Frobenius scale and everything after it are bitwise reproducible.
 void muon_prep(const PrepArgs& args, cudaStream_t stream);
 
 // s[b] = 1 / (sqrt(sumsq[b]) + eps), s2[b] = s[b]^2 ; optionally sums `nparts` partials per
@@ -303,7 +308,10 @@ void cross_entropy_fwd_bwd(void* logits, const int64_t* targets, float* loss_row
 
 // ----------------------------------------------------------------------------------------
 // Spectral: batched power iteration helpers (GEMV with fused normalisation).
+// work: max(m, n) + 1 floats; col_part: power_iteration_col_blocks(m) * n floats (the W^T u
+// partial sums, added in a fixed order so that sigma is bitwise reproducible).
+int power_iteration_col_blocks(int m);
 void power_iteration(const void* W, bool w_f32, int m, int n, float* u, float* v, float* sigma, int iters,
-                     float eps, float* work, cudaStream_t stream);
+                     float eps, float* work, float* col_part, cudaStream_t stream);
 
 }  // namespace mmf

@@ -186,9 +186,20 @@ __global__ void __launch_bounds__(256) muon_prep_kernel(const PrepArgs a) {
     }
   }
   if (a.sumsq) {
+    // every block writes its partial (zero included); prep_sumsq_kernel adds them in order
     const float s = block_sum_256(sq, red);
-    if (threadIdx.x == 0 && s != 0.f) atomicAdd(&a.sumsq[blockIdx.y], s);
+    if (threadIdx.x == 0) a.partials[static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x] = s;
   }
+}
+
+// sumsq[b] += sum_k partials[b * nblk + k], summed in a fixed order: lane-strided, then a fixed
+// shuffle tree (one warp per tensor).
+__global__ void prep_sumsq_kernel(const float* __restrict__ partials, int nblk, float* __restrict__ sumsq) {
+  const int b = blockIdx.x;
+  float acc = 0.f;
+  for (int k = threadIdx.x; k < nblk; k += 32) acc += partials[static_cast<int64_t>(b) * nblk + k];
+  acc = warp_sum(acc);
+  if (threadIdx.x == 0) sumsq[b] += acc;
 }
 
 __global__ void ns_scale_kernel(const float* sumsq, int n, int nparts, float eps, float* s, float* s2) {
@@ -440,16 +451,25 @@ __global__ void gemv_rows_kernel(const void* W, int m, int n, const float* x, fl
   acc = warp_sum(acc);
   if (l == 0) y[r] = acc;
 }
-// y[c] = sum_r W[r, c] x[r]     (one thread per column, rows split over blockIdx.y, atomics)
+// part[k, c] = sum_{r in row block k} W[r, c] x[r]   (one thread per column, rows split over
+// blockIdx.y); y[c] = sum_k part[k, c] in block order (gemv_cols_sum_kernel): no atomics, so the
+// result is bitwise reproducible.
 template <bool F32>
-__global__ void gemv_cols_kernel(const void* W, int m, int n, const float* x, float* y, int rows_per_block) {
+__global__ void gemv_cols_kernel(const void* W, int m, int n, const float* x, float* part, int rows_per_block) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= n) return;
   const int r0 = blockIdx.y * rows_per_block;
   const int r1 = min(m, r0 + rows_per_block);
   float acc = 0.f;
   for (int r = r0; r < r1; ++r) acc = fmaf(ld_val<F32>(W, static_cast<int64_t>(r) * n + c), x[r], acc);
-  atomicAdd(&y[c], acc);
+  part[static_cast<int64_t>(blockIdx.y) * n + c] = acc;
+}
+__global__ void gemv_cols_sum_kernel(const float* part, int nblk, int n, float* y) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  float acc = 0.f;
+  for (int k = 0; k < nblk; ++k) acc += part[static_cast<int64_t>(k) * n + c];
+  y[c] = acc;
 }
 // x /= max(||x||, eps) in place (single block); optionally also writes ||x|| into *norm_out.
 __global__ void normalize_kernel(float* x, int n, float eps, float* norm_out) {
@@ -499,10 +519,13 @@ void check_launch(const char* what) {
 
 }  // namespace
 
+int muon_prep_blocks(int max_tiles) { return max_tiles < 1 ? 1 : (max_tiles > 4096 ? 4096 : max_tiles); }
+
 void muon_prep(const PrepArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
   if (a.n > 65535) throw std::runtime_error("mmf: muon_prep supports at most 65535 tensors per launch");
-  const int gx = a.max_tiles < 1 ? 1 : (a.max_tiles > 4096 ? 4096 : a.max_tiles);
+  if (a.sumsq && !a.partials) throw std::runtime_error("mmf: muon_prep needs its partial-sum scratch");
+  const int gx = muon_prep_blocks(a.max_tiles);
   dim3 grid(gx, a.n);
 #define MMF_PREP(GF, PF, V) muon_prep_kernel<GF, PF, V><<<grid, 256, 0, stream>>>(a)
   if (a.vec8) {
@@ -520,6 +543,10 @@ void muon_prep(const PrepArgs& a, cudaStream_t stream) {
   }
 #undef MMF_PREP
   check_launch("muon_prep");
+  if (a.sumsq) {
+    prep_sumsq_kernel<<<a.n, 32, 0, stream>>>(a.partials, gx, a.sumsq);
+    check_launch("muon_prep (sum of squares)");
+  }
 }
 
 void ns_scale(const float* sumsq, int n, int nparts, float eps, float* s, float* s2, cudaStream_t stream) {
@@ -583,8 +610,10 @@ void muon_moments_multi(const MomentArgs& a, cudaStream_t stream) {
 }
 
 // work must hold max(m, n) + 1 floats.  u [m], v [n] (v holds the start vector on entry).
+int power_iteration_col_blocks(int m) { return (m + 255) / 256; }
+
 void power_iteration(const void* W, bool w_f32, int m, int n, float* u, float* v, float* sigma, int iters, float eps,
-                     float* work, cudaStream_t stream) {
+                     float* work, float* col_part, cudaStream_t stream) {
   const int rows_per_block = 256;
   auto rows = [&](const float* x, float* y) {
     if (w_f32)
@@ -594,13 +623,14 @@ void power_iteration(const void* W, bool w_f32, int m, int n, float* u, float* v
     check_launch("gemv_rows");
   };
   auto cols = [&](const float* x, float* y) {
-    cudaMemsetAsync(y, 0, sizeof(float) * n, stream);
     dim3 g((n + 255) / 256, (m + rows_per_block - 1) / rows_per_block);
     if (w_f32)
-      gemv_cols_kernel<true><<<g, 256, 0, stream>>>(W, m, n, x, y, rows_per_block);
+      gemv_cols_kernel<true><<<g, 256, 0, stream>>>(W, m, n, x, col_part, rows_per_block);
     else
-      gemv_cols_kernel<false><<<g, 256, 0, stream>>>(W, m, n, x, y, rows_per_block);
+      gemv_cols_kernel<false><<<g, 256, 0, stream>>>(W, m, n, x, col_part, rows_per_block);
     check_launch("gemv_cols");
+    gemv_cols_sum_kernel<<<(n + 255) / 256, 256, 0, stream>>>(col_part, static_cast<int>(g.y), n, y);
+    check_launch("gemv_cols_sum");
   };
   normalize_kernel<<<1, 1024, 0, stream>>>(v, n, eps, nullptr);
   check_launch("normalize");

@@ -189,3 +189,41 @@ def test_embedding_gather_and_dense_backward(V, D, shape):
     untouched = torch.ones(V, dtype=torch.bool, device="cuda")
     untouched[tok.reshape(-1)] = False
     assert torch.count_nonzero(w.grad[untouched]) == 0
+
+
+def test_muon_sum_of_squares_and_power_iteration_are_bitwise_reproducible():
+    """The momentum kernel's per-tensor sums of squares (the Frobenius scale of Newton-Schulz) and
+    the power iteration's W^T u products are reduced in a fixed order: two runs give identical
+    bits, and the values match fp64 sums."""
+    from my_muon_fsdp2_b200._ext import ext
+    from my_muon_fsdp2_b200.parallel.muon_engine import MODE_EMA
+
+    E = ext()
+    torch.manual_seed(5)
+    shapes = [(4096, 4096), (1024, 4096), (300, 200)]
+    grads = [torch.randn(*s, device="cuda").to(torch.bfloat16) for s in shapes]
+    runs = []
+    for _ in range(2):
+        bufs = [torch.zeros(*s, device="cuda") for s in shapes]
+        ssq = torch.zeros(len(shapes), device="cuda")
+        offs = [0]
+        for r, c in shapes[:-1]:
+            offs.append(offs[-1] + r * c)
+        dst = torch.empty(sum(r * c for r, c in shapes), dtype=torch.bfloat16, device="cuda")
+        E.muon_prep(grads, bufs, [], dst, offs, [0] * len(shapes), [0] * len(shapes), [c for _, c in shapes], [], [],
+                    MODE_EMA, False, 0.9, 0.0, ssq)
+        runs.append(ssq.clone())
+    assert torch.equal(runs[0], runs[1])
+    # the sums are those of the update the kernel wrote (the bf16 exchange copy, within rounding)
+    ref = torch.tensor([float((dst[o:o + r * c].double() ** 2).sum()) for o, (r, c) in zip(offs, shapes)])
+    assert rel_err(runs[0].double().cpu(), ref) < 1e-2
+    W = torch.randn(14336, 4096, device="cuda").to(torch.bfloat16)
+    sig = []
+    for _ in range(2):
+        u = torch.empty(14336, device="cuda")
+        v = torch.ones(4096, device="cuda")
+        s = torch.empty(1, device="cuda")
+        work = torch.empty(14336 + 1, device="cuda")
+        E.power_iteration(W, u, v, s, 5, 1e-7, work)
+        sig.append(s.clone())
+    assert torch.equal(sig[0], sig[1])
