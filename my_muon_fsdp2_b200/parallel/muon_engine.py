@@ -297,7 +297,7 @@ class MuonEngine:
                 E.ns_scale(sumsq, B, 1, NS_EPS, s, s2)
                 ptrs = E.ptr_table(params)
                 pvec = _decay_vec([t.decay for t in sub], dev)
-                vvec = torch.tensor([-t.lr_eff for t in sub], dtype=torch.float32).to(dev, non_blocking=True)
+                vvec = _h2d([-t.lr_eff for t in sub], torch.float32, dev)
                 run_ns_group(X0, s, s2, hp.ns_steps, ptrs, cols, pdt == torch.float32, tall, mw, nw,
                              p_scale=1.0, v_scale=1.0, p_scale_vec=pvec, v_scale_vec=vvec)
 
@@ -519,7 +519,7 @@ class MuonEngine:
             E.muon_prep(grads, bufs, params if hp.wd_coupled != 0 else [], sw.buf, [off[rank][j] for j in js],
                         [0] * len(js), [0] * len(js), [shapes[j][1] for j in js], [], [], hp.mode, hp.nesterov,
                         hp.momentum, hp.wd_coupled, sub)
-            part.index_copy_(0, torch.tensor(js, device=dev), sub)
+            part.index_copy_(0, _h2d(js, torch.int64, dev), sub)
         # parameters in peer-mapped storage (the fused FSDP shards): the owner's final epilogue
         # applies p <- decay p - lr_eff O straight into every rank's shard of them
         direct = self._direct_targets(tasks, rows_of, group, dev)
@@ -551,7 +551,7 @@ class MuonEngine:
                         row0.append(chunk_offset(rws, world, r))
                         trs.append(int(rws > cls))
                 E.muon_prep(srcs, [], [], X0, offs, row0, trs, [Np], [], [], MODE_COPY, False, 0.0, 0.0, None)
-                jt = torch.tensor(sub_js, device=dev)
+                jt = _h2d(sub_js, torch.int64, dev)
                 ssq = rows_ssq.index_select(1, jt).contiguous()  # [world, B]
                 s = torch.empty(B, dtype=torch.float32, device=dev)
                 s2 = torch.empty_like(s)
@@ -564,12 +564,11 @@ class MuonEngine:
                         #    (direct) or into rank d's buffer
                         addrs.append(direct[j][d] if direct_dtype is not None else sw.peer_addr(d, off[d][j]))
                     meta += [cls, int(rws > cls), (rws + world - 1) // world]
-                ptrs = torch.tensor(addrs, dtype=torch.int64).to(dev, non_blocking=True)
-                meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
+                ptrs = _h2d(addrs, torch.int64, dev)
+                meta_t = _h2d(meta, torch.int64, dev)
                 if direct_dtype is not None:
                     pvec = _decay_vec([tasks[j].decay for j in sub_js], dev)
-                    vvec = torch.tensor([-tasks[j].lr_eff for j in sub_js], dtype=torch.float32).to(
-                        dev, non_blocking=True)
+                    vvec = _h2d([-tasks[j].lr_eff for j in sub_js], torch.float32, dev)
                     run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, direct_dtype == torch.float32, False, mw, nw,
                                  p_scale=1.0, v_scale=1.0, p_scale_vec=pvec, v_scale_vec=vvec, nseg=world,
                                  out_meta=meta_t, transposed_dest=tall_group)
@@ -629,7 +628,7 @@ class MuonEngine:
                         [0] * len(live), [0] * len(live), [tasks[j].local_param.shape[1] for j in live], [], [],
                         hp.mode, hp.nesterov, hp.momentum,
                         hp.wd_coupled, part)
-            sumsq.index_copy_(0, torch.tensor(live, device=send.device), part)
+            sumsq.index_copy_(0, _h2d(live, torch.int64, send.device), part)
 
     def _cuda_owner_ns(self, tasks, hp, mine, shapes, rows_of, cnt, world, recv, shard_at, back, back_at,
                        parts) -> None:
@@ -664,7 +663,7 @@ class MuonEngine:
                         row0.append(chunk_offset(rws, world, r))
                         trs.append(int(tall))
                 E.muon_prep(srcs, [], [], X0, offs, row0, trs, [Np], [], [], MODE_COPY, False, 0.0, 0.0, None)
-                ssq = parts.index_select(1, torch.tensor(sub, device=dev)).contiguous()  # [world, B]
+                ssq = parts.index_select(1, _h2d(sub, torch.int64, dev)).contiguous()  # [world, B]
                 s = torch.empty(B, dtype=torch.float32, device=dev)
                 s2 = torch.empty_like(s)
                 E.ns_scale(ssq, B, world, NS_EPS, s, s2)
@@ -678,7 +677,7 @@ class MuonEngine:
                         seg_views.append(back[st:st + max(cnt[j][d], 1)] if cnt[j][d] else back[:1])
                     meta += [cls, int(rws > cls), cs]
                 ptrs = E.ptr_table(seg_views)
-                meta_t = torch.tensor(meta, dtype=torch.int64).to(dev, non_blocking=True)
+                meta_t = _h2d(meta, torch.int64, dev)
                 run_ns_group(X0, s, s2, hp.ns_steps, ptrs, 0, False, False, mw, nw, p_scale=0.0, v_scale=1.0,
                              nseg=world, out_meta=meta_t, transposed_dest=tall_group)
 
@@ -733,11 +732,22 @@ def _decay_(p: torch.Tensor, decay) -> None:
         p.mul_(decay)
 
 
+def _h2d(values, dtype, dev) -> torch.Tensor:
+    """A small host-built tensor (pointer tables, indices, per-matrix scalars) on the device
+    without a host synchronisation: staged in pinned memory, so the copy is asynchronous.  From
+    pageable memory the copy waits for the stream's earlier work, which drains the queue and
+    leaves the GPU idle while the host prepares the next launches."""
+    t = torch.tensor(values, dtype=dtype)
+    if torch.device(dev).type != "cuda":
+        return t.to(dev)
+    return t.pin_memory().to(dev, non_blocking=True)
+
+
 def _decay_float(decay) -> float:
     return float(decay.item()) if isinstance(decay, torch.Tensor) else float(decay)
 
 
 def _decay_vec(decays, dev) -> torch.Tensor:
     if all(not isinstance(d, torch.Tensor) for d in decays):
-        return torch.tensor([float(d) for d in decays], dtype=torch.float32).to(dev, non_blocking=True)
+        return _h2d([float(d) for d in decays], torch.float32, dev)
     return torch.stack([torch.as_tensor(d, dtype=torch.float32, device=dev).reshape(()) for d in decays])
