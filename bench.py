@@ -273,6 +273,7 @@ def main():
     clocks = ClockSampler(physical_gpu_index(local))
     clocks.start()
     n0 = count() if count else 0
+    mem0 = torch.cuda.memory_stats()
     # one event per step boundary (recording an event adds no work between the steps)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     start, end = marks[0], marks[-1]
@@ -288,6 +289,13 @@ def main():
         for (_, a), (name, b) in zip(pm[:-1], pm[1:]):
             phase_sum[name] = phase_sum.get(name, 0.0) + a.elapsed_time(b)
     launches = (count() - n0) if count else None
+    mem1 = torch.cuda.memory_stats()
+    # device memory of this rank, and what the caching allocator had to do inside the timed steps
+    # (cudaMalloc calls, and retries that free cached blocks, which synchronise the device)
+    memory = {"max_reserved_gb": round(mem1.get("reserved_bytes.all.peak", 0) / 2**30, 2),
+              "max_allocated_gb": round(mem1.get("allocated_bytes.all.peak", 0) / 2**30, 2),
+              "timed_cuda_mallocs": mem1.get("num_device_alloc", 0) - mem0.get("num_device_alloc", 0),
+              "timed_alloc_retries": mem1.get("num_alloc_retries", 0) - mem0.get("num_alloc_retries", 0)}
     clk = clocks.stop()
     dist.barrier()
     dev_ms = max_over_ranks(start.elapsed_time(end) / steps)
@@ -346,7 +354,7 @@ def main():
                        "tokens_per_step": tokens_per_step,
                        "l2": "no flush: per-step working set (16 GB bf16 weights + activations) >> 126 MB L2",
                        "optimizers": "Muon(attn+FFN matrices, lr .02, mom .95, wd .01, ns 5) + AdamW(rest, lr 1e-3)"},
-            "clocks": clk, "e2e": e2e, "gpu_launches": launches, "final_loss": final_loss,
+            "clocks": clk, "e2e": e2e, "gpu_launches": launches, "final_loss": final_loss, "memory": memory,
         }
         if args.impl == "reference":
             out["impl"] = "reference"
