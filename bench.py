@@ -278,11 +278,14 @@ def main():
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     start, end = marks[0], marks[-1]
     start.record()
-    step_marks = []
+    step_marks, host_marks = [], []
+    host_t0 = time.perf_counter()
     for s in range(steps):
         loss = trainer.step_on_device(dev_batches[s % 2])
         marks[s + 1].record()
         step_marks.append(list(getattr(trainer, "_phase_marks", [])))  # read after the loop
+        host_marks.append(list(getattr(trainer, "_host_marks", [])))
+    host_loop_ms = (time.perf_counter() - host_t0) * 1e3 / steps  # host time to enqueue one step
     torch.cuda.synchronize()
     phase_sum: dict = {}
     for pm in step_marks:
@@ -305,6 +308,11 @@ def main():
     srt = sorted(per_step)
     spread = {"min": srt[0], "median": srt[len(srt) // 2], "max": srt[-1]}
     phases = {k: max_over_ranks(v / steps) for k, v in sorted(phase_sum.items())} if phase_sum else None
+    host_sum: dict = {}
+    for hm in host_marks:
+        for (_, a), (name, b) in zip(hm[:-1], hm[1:]):
+            host_sum[name] = host_sum.get(name, 0.0) + (b - a) * 1e3
+    host_phases = {k: round(v / steps, 2) for k, v in sorted(host_sum.items())} if host_sum else None
     opt_ms = max_over_ranks(opt_timer.mean_ms())
     final_loss = float(loss.item())
 
@@ -341,6 +349,8 @@ def main():
             "data": "synthetic uniform random tokens; random-init weights",
             "optimizer_step_ms": opt_ms, "step_ms_spread": spread,
             **({"phase_ms": phases} if phases else {}),
+            **({"host_phase_ms": host_phases, "host_enqueue_ms_per_step": round(host_loop_ms, 1)}
+               if host_phases else {}),
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",

@@ -7,6 +7,7 @@ gradients and returns the loss as a Python float (one device->host read).
 """
 from __future__ import annotations
 
+import time
 from typing import Optional, Sequence
 
 import torch
@@ -72,6 +73,7 @@ class Trainer:
         self._step_events = None
         self.time_phases = bool(time_phases) and self.device.type == "cuda"
         self._phase_marks: list = []
+        self._host_marks: list = []
         self._prev_comm: Optional[dict] = None
         ctl = getattr(model, "_symm_fsdp", None)  # fused-collective linears: regather after each step
         if ctl is not None:
@@ -101,6 +103,9 @@ class Trainer:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
             self._phase_marks.append((name, ev))
+            # when the host got here: phases whose host time reaches their device time are
+            # launch-bound (the GPU waits for the host)
+            self._host_marks.append((name, time.perf_counter()))
 
     def phase_ms(self) -> dict:
         """Device time of each phase of the last step (waits for it); {} unless ``time_phases``.
@@ -120,6 +125,7 @@ class Trainer:
             t0 = torch.cuda.Event(enable_timing=True)
             t0.record()
         self._phase_marks = []
+        self._host_marks = []
         self._mark("start")
         total = None
         for i in range(self.grad_accum):
