@@ -278,13 +278,14 @@ def main():
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     start, end = marks[0], marks[-1]
     start.record()
-    step_marks, host_marks = [], []
+    step_marks, host_marks, probes = [], [], []
     host_t0 = time.perf_counter()
     for s in range(steps):
         loss = trainer.step_on_device(dev_batches[s % 2])
         marks[s + 1].record()
         step_marks.append(list(getattr(trainer, "_phase_marks", [])))  # read after the loop
         host_marks.append(list(getattr(trainer, "_host_marks", [])))
+        probes.append(list(getattr(trainer, "_probes", [])))
     host_loop_ms = (time.perf_counter() - host_t0) * 1e3 / steps  # host time to enqueue one step
     torch.cuda.synchronize()
     phase_sum: dict = {}
@@ -313,6 +314,12 @@ def main():
         for (_, a), (name, b) in zip(hm[:-1], hm[1:]):
             host_sum[name] = host_sum.get(name, 0.0) + (b - a) * 1e3
     host_phases = {k: round(v / steps, 2) for k, v in sorted(host_sum.items())} if host_sum else None
+    clock_at = {}  # MMF_CLOCK_PROBE=1: mean SM MHz measured at the end of each phase
+    for pr in probes:
+        for name, t in pr:
+            v = t.double()
+            clock_at.setdefault(name, []).append(float((v[:, 0] / v[:, 1]).mean()) * 1e3)
+    clock_at = {k: round(sum(v) / len(v), 1) for k, v in clock_at.items()}
     opt_ms = max_over_ranks(opt_timer.mean_ms())
     final_loss = float(loss.item())
 
@@ -351,6 +358,7 @@ def main():
             **({"phase_ms": phases} if phases else {}),
             **({"host_phase_ms": host_phases, "host_enqueue_ms_per_step": round(host_loop_ms, 1)}
                if host_phases else {}),
+            **({"sm_mhz_after_phase": clock_at} if clock_at else {}),
             "config": {"model": MODEL_DESC if args.layers == 32 else f"{MODEL_DESC} [DEBUG: {args.layers} layers]",
                        "global_batch": world * ga * mbs, "seq_len": seq, "grad_accum": ga,
                        "micro_batch_per_gpu": mbs, "parallelism": f"fsdp{world}",

@@ -936,6 +936,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_fwd", &layernorm_fwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("scale_", &scale_);
+  m.def("clock_probe", [](Tensor out, int64_t cycles) {
+    check_cuda(out, "out");
+    TORCH_CHECK(out.scalar_type() == torch::kInt64 && out.is_contiguous() && out.dim() == 2 && out.size(1) == 2,
+                "mmf: clock_probe writes an int64 [blocks, 2] tensor");
+    const c10::cuda::CUDAGuard guard(out.device());
+    mmf::clock_probe(cycles, static_cast<int>(out.size(0)), reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+                     cur_stream());
+  });
   m.def("embedding_bwd", &embedding_bwd);
   m.def("layernorm_bwd", &layernorm_bwd);
   m.def("rope_", &rope_);

@@ -293,6 +293,9 @@ void swiglu_bwd(const void* dout, const void* gate, const void* up, void* dgate,
 void gelu_fwd(const void* x, void* y, int64_t n, cudaStream_t stream);
 void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t stream);
 // x (bf16, 16-byte aligned) *= s[0] (a device fp32 scalar).
+// Diagnostic: `blocks` single-thread blocks each spin `cycles` SM cycles; out [blocks, 2] int64
+// receives (cycles, nanoseconds) per block.
+void clock_probe(int64_t cycles, int blocks, long long* out, cudaStream_t stream);
 void scale_bf16(void* x, const float* s, int64_t n, cudaStream_t stream);
 // Embedding rows (bf16, D % 8 == 0): out[t] = table[tokens[t]] (a token outside the table gives
 // zeros and records ERR_BAD_ARGUMENT).  Backward: the dense table gradient in one pass from the

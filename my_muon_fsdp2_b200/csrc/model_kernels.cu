@@ -392,6 +392,20 @@ __global__ void gelu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv
 // ------------------------------- scale by a device scalar ---------------------------------
 // x (bf16, n elements) *= *s, 16-byte vectors (the tail element-wise); s stays on the device, so
 // a loss scale known only to the GPU needs no host synchronisation.
+// SM clock probe: one thread per SM spins for `cycles` SM cycles and records the cycles and
+// global-timer nanoseconds it took; out[2 * block] = cycles, out[2 * block + 1] = ns.  The
+// frequency at that moment is cycles / ns GHz (a diagnostic of power-cap clock changes).
+__global__ void clock_probe_kernel(int64_t cycles, long long* __restrict__ out) {
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = globaltimer_ns();
+  const long long c0 = clock64();
+  long long c = c0;
+  while (c - c0 < cycles) c = clock64();
+  const uint64_t t1 = globaltimer_ns();
+  out[2 * blockIdx.x] = c - c0;
+  out[2 * blockIdx.x + 1] = static_cast<long long>(t1 - t0);
+}
+
 __global__ void scale_bf16_kernel(__nv_bfloat16* __restrict__ x, const float* __restrict__ s, int64_t n) {
   const float f = *s;
   const int64_t n8 = n / 8;
@@ -718,6 +732,11 @@ void gelu_bwd(const void* dy, const void* x, void* dx, int64_t n, cudaStream_t s
   gelu_bwd_kernel<<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(dx), n);
   check_launch("gelu_bwd");
+}
+
+void clock_probe(int64_t cycles, int blocks, long long* out, cudaStream_t stream) {
+  clock_probe_kernel<<<blocks, 32, 0, stream>>>(cycles, out);
+  check_launch("clock_probe");
 }
 
 void scale_bf16(void* x, const float* s, int64_t n, cudaStream_t stream) {

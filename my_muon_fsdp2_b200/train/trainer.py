@@ -7,6 +7,7 @@ gradients and returns the loss as a Python float (one device->host read).
 """
 from __future__ import annotations
 
+import os
 import time
 from typing import Optional, Sequence
 
@@ -74,6 +75,8 @@ class Trainer:
         self.time_phases = bool(time_phases) and self.device.type == "cuda"
         self._phase_marks: list = []
         self._host_marks: list = []
+        self._probes: list = []
+        self._clock_probe = self.time_phases and os.environ.get("MMF_CLOCK_PROBE") == "1"
         self._prev_comm: Optional[dict] = None
         ctl = getattr(model, "_symm_fsdp", None)  # fused-collective linears: regather after each step
         if ctl is not None:
@@ -106,6 +109,13 @@ class Trainer:
             # when the host got here: phases whose host time reaches their device time are
             # launch-bound (the GPU waits for the host)
             self._host_marks.append((name, time.perf_counter()))
+            if self._clock_probe:
+                # diagnostic: the SM clock at this phase boundary (clock_probe kernel, 148 SMs)
+                from .._ext import ext
+
+                out = torch.empty(148, 2, dtype=torch.int64, device=self.device)
+                ext().clock_probe(out, 200000)
+                self._probes.append((name, out))
 
     def phase_ms(self) -> dict:
         """Device time of each phase of the last step (waits for it); {} unless ``time_phases``.
@@ -126,6 +136,7 @@ class Trainer:
             t0.record()
         self._phase_marks = []
         self._host_marks = []
+        self._probes = []
         self._mark("start")
         total = None
         for i in range(self.grad_accum):
