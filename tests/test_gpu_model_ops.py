@@ -227,3 +227,16 @@ def test_muon_sum_of_squares_and_power_iteration_are_bitwise_reproducible():
         E.power_iteration(W, u, v, s, 5, 1e-7, work)
         sig.append(s.clone())
     assert torch.equal(sig[0], sig[1])
+
+
+def test_clock_probe_reports_a_plausible_sm_clock():
+    """The diagnostic clock probe: cycles / global-timer ns gives the SM clock of each block."""
+    from my_muon_fsdp2_b200._ext import ext
+
+    out = torch.empty(148, 2, dtype=torch.int64, device="cuda")
+    ext().clock_probe(out, 100000)
+    torch.cuda.synchronize()
+    cyc, ns = out[:, 0].double(), out[:, 1].double()
+    assert bool((cyc >= 100000).all()) and bool((ns > 0).all())
+    mhz = (cyc / ns * 1e3).cpu()
+    assert 200.0 < float(mhz.min()) and float(mhz.max()) < 2500.0, mhz
