@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--root", choices=["shard", "replicate"], default="replicate",
                     help="--fsdp symm on several GPUs: the embedding, norms and LM head under fully_shard, or "
                          "replicated with one gradient all-reduce per step")
+    ap.add_argument("--root-allreduce", choices=["hook", "deferred"], default="hook",
+                    help="--root replicate: launch each gradient's all-reduce from its hook, or all at the "
+                         "end of the backward and wait before the optimizer steps")
     ap.add_argument("--no-phases", action="store_true",
                     help="do not record the per-phase events (forward / backward per micro-batch, optimizer); "
                          "they are read after the timed loop, so they add no synchronisation to it")
@@ -116,7 +119,8 @@ def build_ours(args, world, local):
     if args.fsdp == "symm":
         from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
 
-        ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local), rs_mode=args.rs_mode, root=args.root)
+        ctl = apply_symm_fsdp(model, mesh, device=torch.device("cuda", local), rs_mode=args.rs_mode, root=args.root,
+                              root_allreduce=args.root_allreduce)
     else:
         apply_fsdp(model, mesh)
         model.to_empty(device=torch.device("cuda", local))

@@ -324,7 +324,22 @@ class SymmFSDP:
         if id(opt) in attached:
             return
         attached.add(id(opt))
+
+        def before_step(*a, **k):
+            # only an optimizer that steps replicated parameters needs their all-reduce done
+            ids = getattr(self, "_root_ids", None)
+            if ids and any(id(p) in ids for g in opt.param_groups for p in g["params"]):
+                self.wait_replicated_grads()
+
+        opt.register_step_pre_hook(before_step)
         opt.register_step_post_hook(lambda *a, **k: self.invalidate())
+
+    def wait_replicated_grads(self) -> None:
+        """Make the current stream wait for the all-reduces of the replicated rest of the model
+        (no-op unless ``apply_symm_fsdp(..., root="replicate")`` deferred them)."""
+        w = getattr(self, "_root_wait", None)
+        if w is not None:
+            w()
 
     def shard_ptrs(self, i: int) -> List[int]:
         return [int(self.shard_handle.buffer_ptrs[s]) + 2 * self.shard_offsets[i] for s in range(self.world)]
@@ -649,36 +664,56 @@ def block_linears(model: nn.Module, blocks_attr: str = "layers") -> List[nn.Line
     return out
 
 
-def _replicate_root(model: nn.Module, ctl: "SymmFSDP", skip: set, world: int) -> None:
+def _replicate_root(model: nn.Module, ctl: "SymmFSDP", skip: set, world: int, when: str = "hook") -> None:
     """The rest of the model (embeddings, norms, LM head) as plain parameters replicated on every
     rank: rank 0's values are broadcast before the first forward, and on the gradient-
     synchronising micro-batch each gradient is averaged over all ranks by an asynchronous
-    all-reduce launched as soon as autograd has accumulated it (overlapping the rest of the
-    backward), joined at the end of the backward.  One all-reduce per step instead of FSDP2's
+    all-reduce.  ``when="hook"`` launches each all-reduce as soon as autograd has accumulated
+    that gradient (overlapping the rest of the backward) and joins them at the end of the
+    backward.  ``when="deferred"`` launches them all at the end of the backward and waits only
+    before the first optimizer step that ``ctl.attach_optimizer`` registered (or before
+    ``ctl.wait_replicated_grads()``), so they overlap the start of the optimizer step instead of
+    sharing the SMs with the backward's GEMMs.  One all-reduce per step instead of FSDP2's
     all-gather per micro-batch forward and backward plus a reduce-scatter."""
     params = [p for p in model.parameters() if id(p) not in skip and p.requires_grad]
-    state = {"works": [], "queued": False, "synced": False}
+    state = {"works": [], "ready": [], "queued": False, "synced": False}
 
-    def join():
-        for w in state["works"]:
-            w.wait()
-        state["works"].clear()
-        state["queued"] = False
-
-    def on_grad(p):
-        if not ctl.sync_grads or p.grad is None:
-            return
+    def launch(p):
         if p.grad.is_cuda:
             state["works"].append(dist.all_reduce(p.grad, op=dist.ReduceOp.AVG, async_op=True))
         else:  # gloo has no AVG
             dist.all_reduce(p.grad)
             p.grad.div_(world)
+
+    def wait():
+        for w in state["works"]:
+            w.wait()
+        state["works"].clear()
+
+    def end_of_backward():
+        state["queued"] = False
+        if when == "deferred":
+            for p in state["ready"]:
+                launch(p)
+            state["ready"].clear()
+            if not getattr(ctl, "_attached", None):
+                wait()  # nobody would wait for them later
+        else:
+            wait()
+
+    def on_grad(p):
+        if not ctl.sync_grads or p.grad is None:
+            return
+        if when == "deferred":
+            state["ready"].append(p)
+        else:
+            launch(p)
         if not state["queued"]:
             state["queued"] = True
             try:
-                torch.autograd.Variable._execution_engine.queue_callback(join)
+                torch.autograd.Variable._execution_engine.queue_callback(end_of_backward)
             except RuntimeError:  # outside a backward pass
-                join()
+                end_of_backward()
 
     for p in params:
         p.register_post_accumulate_grad_hook(on_grad)
@@ -693,11 +728,14 @@ def _replicate_root(model: nn.Module, ctl: "SymmFSDP", skip: set, world: int) ->
 
     model.register_forward_pre_hook(broadcast_once)
     model._symm_root_params = params
+    ctl._root_wait = wait
+    ctl._root_ids = {id(p) for p in params}
 
 
 def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str = "layers",
                     reshard_after_forward: Optional[bool] = None, rs_mode: str = "overlap",
-                    shard_root_alone: bool = False, root: str = "replicate") -> SymmFSDP:
+                    shard_root_alone: bool = False, root: str = "replicate",
+                    root_allreduce: str = "hook") -> SymmFSDP:
     """Shard the weights of the transformer blocks' linears on symmetric memory (fused
     all-gather/reduce-scatter kernels where the shapes allow, NCCL otherwise; gathered once per
     step either way).  The rest of the model (embeddings, norms, biases, LM head):
@@ -733,7 +771,9 @@ def apply_symm_fsdp(model: nn.Module, mesh=None, device=None, blocks_attr: str =
     ctl = SymmFSDP(lin, mesh=mesh, device=dev, rs_mode=rs_mode)
     model._symm_fsdp = ctl
     if n_ranks > 1 and not root_fsdp:
-        _replicate_root(model, ctl, {id(m.weight) for m in lin}, dist.get_world_size())
+        if root_allreduce not in ("hook", "deferred"):
+            raise ValueError(f"root_allreduce must be 'hook' or 'deferred', got {root_allreduce!r}")
+        _replicate_root(model, ctl, {id(m.weight) for m in lin}, dist.get_world_size(), root_allreduce)
     fsdp_sync = model.set_requires_gradient_sync if root_fsdp else (lambda *a, **kw: None)
 
     def set_requires_gradient_sync(flag: bool, *a, **kw):

@@ -143,6 +143,9 @@ class Trainer:
             l = self._micro(tokens, i).detach()
             total = l if total is None else total + l
         if self.max_grad_norm is not None:
+            ctl = getattr(self.model, "_symm_fsdp", None)
+            if ctl is not None:
+                ctl.wait_replicated_grads()  # the norm reads every gradient
             params = [p for p in self.model.parameters() if p.grad is not None]
             self.last_grad_norm = clip_grad_norm(params, self.max_grad_norm)
             self._mark("grad_clip")

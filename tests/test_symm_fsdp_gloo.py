@@ -88,7 +88,7 @@ def test_symm_fsdp_grads_match_single_process(no_sync, root):
     assert abs(got["_norm"] - ref_norm) < 1e-5 * ref_norm
 
 
-def _symm_train(rank, world, steps, root="shard"):
+def _symm_train(rank, world, steps, root="shard", root_allreduce="hook"):
     from my_muon_fsdp2_b200 import MuonOptimizer
     from my_muon_fsdp2_b200.parallel.symm_fsdp import apply_symm_fsdp
 
@@ -96,7 +96,7 @@ def _symm_train(rank, world, steps, root="shard"):
     if root == "replicate" and rank == 1:  # replicas start from rank 0's values
         with torch.no_grad():
             model.inp.weight.add_(1.0)
-    ctl = apply_symm_fsdp(model, root=root)
+    ctl = apply_symm_fsdp(model, root=root, root_allreduce=root_allreduce)
     mats = [p for p in ctl.params]
     rest = [p for p in model.parameters() if all(p is not q for q in mats)]
     opts = [MuonOptimizer(mats, lr=0.02, momentum=0.95, weight_decay=0.01), torch.optim.AdamW(rest, lr=1e-3)]
@@ -114,12 +114,12 @@ def _symm_train(rank, world, steps, root="shard"):
     return {"params": {n: _full(p.detach()).clone() for n, p in model.named_parameters()}, "losses": losses}
 
 
-@pytest.mark.parametrize("root", ["shard", "replicate"])
-def test_symm_fsdp_training_matches_single_process(root):
+@pytest.mark.parametrize("root,when", [("shard", "hook"), ("replicate", "hook"), ("replicate", "deferred")])
+def test_symm_fsdp_training_matches_single_process(root, when):
     from my_muon_fsdp2_b200 import MuonOptimizer
 
     world, steps = 2, 3
-    got = run_ranks(_symm_train, world, steps, root)
+    got = run_ranks(_symm_train, world, steps, root, when)
     ref = Net()
     mats = [m.weight for b in ref.layers for m in (b.up, b.down)]
     rest = [p for p in ref.parameters() if all(p is not q for q in mats)]
