@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--micro-bs", type=int, default=1)
     ap.add_argument("--layers", type=int, default=32, help="debug only: fewer layers is not the named config")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--ref-budget-s", type=float, default=450.0,
+    ap.add_argument("--ref-budget-s", type=float, default=520.0,
                     help="reference arm: wall-clock budget of the whole run; past it the timed steps are cut "
                          "(to at least 1, warm-up to 3, one end-to-end step) and the JSON line says so")
     ap.add_argument("--rs-mode", choices=["overlap", "fused"], default="overlap",
